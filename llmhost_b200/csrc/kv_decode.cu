@@ -1,0 +1,608 @@
+// kv_decode.cu -- paged decode attention for sm_100a (split-K over pages).
+//
+// Replaces attention_decode_cached (crates/llm-engine/src/lfm2.rs:1006-1056)
+// plus the q RoPE that precedes it (lfm2.rs:816-822).  Math per query head h
+// (kv head h / g, lfm2.rs:1028): scores = (q . k) / sqrt(d), masked keys get
+// -inf, softmax over the keys, out = sum_s w_s v_s.  Here the softmax is the
+// online (running-max) form, so each split of the key range produces
+// (max, sum, unnormalised out) and splits merge by the log-sum-exp identity
+// (Milakov & Gimelshein 2018); the result equals the reference's to fp32
+// rounding.
+//
+// Work split ("stream-K" over pages): the pages of all sequences are laid
+// end to end (per-sequence page counts, exclusive-scanned in shared memory)
+// and every CTA of a persistent grid (SMs x CTAs/SM) takes an equal slice of
+// that list, so skewed sequence lengths cannot unbalance the SMs.  A sequence
+// wholly inside one slice is finished by that CTA; a sequence cut by slice
+// boundaries leaves one partial per CTA, and the last CTA to finish it
+// (atomic counter, no waiting) merges the partials and resets the counter.
+//
+// Data path per CTA: warp 0 streams whole pages (K and V of all kv heads, one
+// contiguous 4- to 64-KiB block) with TMA 2-D tile loads, 128-byte swizzled,
+// STAGES-1 pages ahead of use, into a ring of STAGES page buffers guarded by
+// full/empty mbarriers.  Two consumer warps own each kv head, one per half
+// page (8 keys): QK^T with 4 lanes per key (16 dims each, FFMA2), page max by
+// warp shuffles, p to shared memory, then PV with each lane owning 2 output
+// dims over the warp's 8 keys.  The two half states merge through shared
+// memory when a sequence's slice ends.
+// Every wait is bounded by %globaltimer; a timeout sets the pool's error word
+// and an abort flag so the CTA drains and exits instead of hanging.
+#include <cmath>
+
+#include "kv_common.cuh"
+#include "kv_pool_impl.h"
+
+namespace kvb200 {
+namespace {
+
+template <typename T, int NKV>
+struct Geom {
+    static constexpr int kElem = sizeof(T);
+    static constexpr int kRowsPerToken = kHeadDim * kElem / 128;  // 1 (bf16) or 2 (f32)
+    static constexpr int kPageRows = 2 * NKV * kPageTokens * kRowsPerToken;
+    static constexpr int kPageBytes = kPageRows * 128;
+    static constexpr int kBoxRows = kPageRows > 256 ? 256 : kPageRows;
+    static constexpr int kLoads = kPageRows / kBoxRows;
+};
+
+struct DecodeArgs {
+    const void* q;
+    void* out;
+    const uint32_t* bt;
+    long long bt_stride;
+    const int32_t* seq_lens;
+    int n_seqs;
+    int window;
+    const float2* rope;
+    int max_pos;
+    uint32_t n_pages;
+    float* part_o;
+    float* part_ml;
+    int* counters;
+    int* err;
+    float qscale;  // log2(e) / sqrt(d): scores come out in log2 units
+};
+
+__device__ __forceinline__ int seq_lo(int n_tok, int window) {
+    return (window > 0 && n_tok > window) ? n_tok - window : 0;
+}
+
+__device__ __forceinline__ int seq_pages(int n_tok, int window) {
+    if (n_tok <= 0) return 0;
+    return (n_tok + kPageTokens - 1) / kPageTokens - seq_lo(n_tok, window) / kPageTokens;
+}
+
+// Largest s in [0, n) with pstart[s] <= g (pstart is nondecreasing, pstart[0] = 0).
+__device__ __forceinline__ int find_seq(const int* pstart, int n, int g) {
+    int lo = 0, hi = n;
+    while (hi - lo > 1) {
+        const int mid = (lo + hi) >> 1;
+        if (pstart[mid] <= g) lo = mid; else hi = mid;
+    }
+    return lo;
+}
+
+// CTA whose slice [floor(c*T/G), floor((c+1)*T/G)) holds global page x.
+__device__ __forceinline__ int cta_of(int x, int grid, int total) {
+    return static_cast<int>(((static_cast<long long>(x) + 1) * grid - 1) / total);
+}
+
+__device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity,
+                                              volatile int* abort_flag, int* err) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (*abort_flag) return false;
+    const uint64_t t0 = global_timer_ns();
+    for (uint32_t i = 1;; ++i) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((i & 127u) == 0) {
+            if (*abort_flag) return false;
+            if (global_timer_ns() - t0 > kWaitLimitNs) {
+                *abort_flag = 1;
+                flag_error(err, kDevErrTimeout);
+                return false;
+            }
+        }
+    }
+}
+
+template <typename T> __device__ __forceinline__ T to_elem(float x);
+template <> __device__ __forceinline__ float to_elem<float>(float x) { return x; }
+template <> __device__ __forceinline__ __nv_bfloat16 to_elem<__nv_bfloat16>(float x) {
+    return __float2bfloat16_rn(x);
+}
+
+// q for heads h*G .. h*G+G-1 of sequence s, dims [16*qd, 16*qd+16), rotated
+// at `pos` exactly as rope.rs:56-81 (two products and a sum, no FMA) and
+// scaled into log2 units.  Two dims at a time to keep few registers live.
+__device__ __forceinline__ float2 load_pair(const __nv_bfloat16* p) {
+    return bf16x2_to_float2(__ldg(reinterpret_cast<const unsigned int*>(p)));
+}
+__device__ __forceinline__ float2 load_pair(const float* p) {
+    return __ldg(reinterpret_cast<const float2*>(p));
+}
+
+template <typename T, int G>
+__device__ __forceinline__ void load_q(const DecodeArgs& a, int s, int nq, int h, int qd, int pos,
+                                       float2 (&q2)[G][8]) {
+    const float4* cs = reinterpret_cast<const float4*>(a.rope + static_cast<size_t>(pos) * (kHeadDim / 2) +
+                                                       ((16 * qd) & 31));
+    const float sgn = qd < 2 ? -1.f : 1.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const float4 c = __ldg(cs + i);  // (cos, sin) of dims 16qd+2i and 16qd+2i+1
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            const T* row = static_cast<const T*>(a.q) + (static_cast<size_t>(s) * nq + h * G + g) * kHeadDim;
+            const float2 x = load_pair(row + 16 * qd + 2 * i);
+            const float2 y = load_pair(row + ((16 * qd + 32) & 63) + 2 * i);
+            const float r0 = __fadd_rn(__fmul_rn(x.x, c.x), __fmul_rn(sgn * y.x, c.y));
+            const float r1 = __fadd_rn(__fmul_rn(x.y, c.z), __fmul_rn(sgn * y.y, c.w));
+            q2[g][i] = make_float2(r0 * a.qscale, r1 * a.qscale);
+        }
+    }
+}
+
+// K row `r` (token row inside the K block), the 16 dims of quarter qd.
+__device__ __forceinline__ void load_krow(const uint8_t* buf, int r, int qd, float2 (&k)[8],
+                                          const __nv_bfloat16*) {
+    const uint32_t lin = static_cast<uint32_t>(r) * 128u + static_cast<uint32_t>(qd) * 32u;
+    const uint4 a = *reinterpret_cast<const uint4*>(buf + swz128(lin));
+    const uint4 b = *reinterpret_cast<const uint4*>(buf + swz128(lin + 16u));
+    k[0] = bf16x2_to_float2(a.x); k[1] = bf16x2_to_float2(a.y);
+    k[2] = bf16x2_to_float2(a.z); k[3] = bf16x2_to_float2(a.w);
+    k[4] = bf16x2_to_float2(b.x); k[5] = bf16x2_to_float2(b.y);
+    k[6] = bf16x2_to_float2(b.z); k[7] = bf16x2_to_float2(b.w);
+}
+__device__ __forceinline__ void load_krow(const uint8_t* buf, int r, int qd, float2 (&k)[8],
+                                          const float*) {
+    const uint32_t lin = static_cast<uint32_t>(r) * 256u + static_cast<uint32_t>(qd) * 64u;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+        const float4 f = *reinterpret_cast<const float4*>(buf + swz128(lin + 16u * c));
+        k[2 * c] = make_float2(f.x, f.y);
+        k[2 * c + 1] = make_float2(f.z, f.w);
+    }
+}
+
+// V row `r`: dims 2*lane, 2*lane+1.
+__device__ __forceinline__ float2 load_vword(const uint8_t* buf, int r, int lane,
+                                             const __nv_bfloat16*) {
+    const uint32_t lin = static_cast<uint32_t>(r) * 128u + static_cast<uint32_t>(lane) * 4u;
+    return bf16x2_to_float2(*reinterpret_cast<const uint32_t*>(buf + swz128(lin)));
+}
+__device__ __forceinline__ float2 load_vword(const uint8_t* buf, int r, int lane, const float*) {
+    const uint32_t lin = static_cast<uint32_t>(r) * 256u + static_cast<uint32_t>(lane) * 8u;
+    return *reinterpret_cast<const float2*>(buf + swz128(lin));
+}
+
+// One page of one kv head, keys [8*half, 8*half+8) of the page; keys
+// [t0, t1) of the page are valid.  Lane (j = lane/4, qd = lane%4) scores key
+// 8*half + j over dims [16qd, 16qd+16); for PV the lane owns output dims
+// 2*lane, 2*lane+1 over the warp's 8 keys.
+template <typename T, int NKV, int G>
+__device__ __forceinline__ void page_step(const uint8_t* buf, int h, int half, int lane, int t0,
+                                          int t1, const float2 (&q2)[G][8], float2 (&o2)[G],
+                                          float (&lp)[G], float (&M)[G], float* pb) {
+    const int j = lane >> 2, qd = lane & 3;
+    const int tk = half * 8 + j;
+    float2 kv[8];
+    load_krow(buf, h * kPageTokens + tk, qd, kv, static_cast<const T*>(nullptr));
+    float sc[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        float2 acc = make_float2(0.f, 0.f);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc = __ffma2_rn(q2[g][i], kv[i], acc);
+        sc[g] = acc.x + acc.y;
+    }
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        sc[g] += __shfl_xor_sync(~0u, sc[g], 1);
+        sc[g] += __shfl_xor_sync(~0u, sc[g], 2);
+    }
+    const bool valid = tk >= t0 && tk < t1;
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        const float x = valid ? sc[g] : -INFINITY;
+        float pm = x;
+        pm = fmaxf(pm, __shfl_xor_sync(~0u, pm, 4));
+        pm = fmaxf(pm, __shfl_xor_sync(~0u, pm, 8));
+        pm = fmaxf(pm, __shfl_xor_sync(~0u, pm, 16));
+        const float mn = fmaxf(M[g], pm);
+        const float mu = (mn == -INFINITY) ? 0.f : mn;
+        const float alpha = exp2f(M[g] - mu);
+        const float p = exp2f(x - mu);
+        lp[g] = lp[g] * alpha + (qd == 0 ? p : 0.f);
+        o2[g] = __fmul2_rn(o2[g], make_float2(alpha, alpha));
+        M[g] = mn;
+        if (qd == 0) pb[g * 8 + j] = p;
+    }
+    __syncwarp();
+    const int vrow = (NKV + h) * kPageTokens + half * 8;
+    const bool full_half = (t0 <= half * 8 && t1 >= half * 8 + 8);
+#pragma unroll
+    for (int t4 = 0; t4 < 2; ++t4) {
+        float4 pq[G];
+#pragma unroll
+        for (int g = 0; g < G; ++g) pq[g] = *reinterpret_cast<const float4*>(pb + g * 8 + 4 * t4);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int t = 4 * t4 + u;
+            float2 v = load_vword(buf, vrow + t, lane, static_cast<const T*>(nullptr));
+            // Slots outside [t0, t1) may hold another sequence's stale values:
+            // zero them so 0 * (inf or nan) cannot leak into the sum.
+            if (!full_half && (half * 8 + t < t0 || half * 8 + t >= t1)) v = make_float2(0.f, 0.f);
+#pragma unroll
+            for (int g = 0; g < G; ++g) {
+                const float pv = u == 0 ? pq[g].x : u == 1 ? pq[g].y : u == 2 ? pq[g].z : pq[g].w;
+                o2[g] = __ffma2_rn(make_float2(pv, pv), v, o2[g]);
+            }
+        }
+    }
+}
+
+// Two warps per kv head (one per half page); warp 0 also issues the loads.
+template <typename T, int NKV, int G, int STAGES>
+struct DecodeShape {
+    using Geo = Geom<T, NKV>;
+    static constexpr int kConsumers = 2 * NKV;
+    static constexpr int kThreads = kConsumers * 32;
+    static size_t smem_bytes(int max_seqs) {
+        return 1024 + static_cast<size_t>(STAGES) * Geo::kPageBytes   // page ring
+               + 2 * STAGES * 8                                         // full/empty barriers
+               + static_cast<size_t>(kConsumers) * 2 * G * 8 * 4        // p buffers
+               + static_cast<size_t>(NKV) * G * (kHeadDim + 2) * 4      // half-merge buffers
+               + 16 + (static_cast<size_t>(max_seqs) + 1) * 4;          // misc + page scan
+    }
+};
+
+template <typename T, int NKV, int G, int STAGES>
+__global__ void __launch_bounds__(DecodeShape<T, NKV, G, STAGES>::kThreads, 1)
+decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeArgs a) {
+    using Geo = Geom<T, NKV>;
+    constexpr int NQ = NKV * G;
+    constexpr int NCW = 2 * NKV;  // consumer warps
+    constexpr int NCONS = NCW * 32;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* stage = reinterpret_cast<uint8_t*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(stage + STAGES * Geo::kPageBytes);
+    uint64_t* empty = full + STAGES;
+    float* pbuf = reinterpret_cast<float*>(empty + STAGES);  // [NCW][2][G][8]
+    float* xbuf = pbuf + NCW * 2 * G * 8;                    // [NKV][G][64 + 2]
+    int* misc = reinterpret_cast<int*>(xbuf + NKV * G * (kHeadDim + 2));  // [0] counter, [1] abort
+    int* pstart = misc + 4;                                               // [n_seqs + 1]
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n = a.n_seqs;
+
+    if (threadIdx.x == 32) {
+        for (int i = 0; i < STAGES; ++i) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], NCW);
+        }
+        fence_mbar_init();
+        prefetch_tmap(&tmap);
+        misc[0] = 0;
+        misc[1] = 0;
+    }
+    if (warp == 0) {  // exclusive scan of per-sequence page counts
+        const int per = (n + 31) >> 5;
+        const int b = min(n, lane * per), e = min(n, b + per);
+        int local = 0;
+        for (int s = b; s < e; ++s) local += seq_pages(__ldg(a.seq_lens + s), a.window);
+        int incl = local;
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) {
+            const int y = __shfl_up_sync(~0u, incl, off);
+            if (lane >= off) incl += y;
+        }
+        int run = incl - local;
+        for (int s = b; s < e; ++s) {
+            pstart[s] = run;
+            run += seq_pages(__ldg(a.seq_lens + s), a.window);
+        }
+        if (lane == 31) pstart[n] = incl;
+    }
+    __syncthreads();
+
+    const int total = pstart[n];
+    const int grid = gridDim.x, cta = blockIdx.x;
+    if (threadIdx.x < NCONS) {  // sequences with no tokens: zeros
+        for (int s = cta; s < n; s += grid) {
+            if (__ldg(a.seq_lens + s) <= 0) {
+                T* o = static_cast<T*>(a.out) + static_cast<size_t>(s) * NQ * kHeadDim;
+                for (int i = threadIdx.x; i < NQ * kHeadDim; i += NCONS) o[i] = to_elem<T>(0.f);
+            }
+        }
+    }
+    const int gb = static_cast<int>((static_cast<long long>(cta) * total) / grid);
+    const int ge = static_cast<int>((static_cast<long long>(cta + 1) * total) / grid);
+    if (gb >= ge) return;
+    volatile int* abort_flag = misc + 1;
+
+    // ---- load issue (warp 0): page i of this slice goes to stage i % STAGES ----
+    // Lane l of warp 0 holds the physical id of slice page bt_base + l.
+    const int n_local = ge - gb;
+    int bt_base = -32;
+    uint32_t bt_batch = 0;
+    int issued = 0;  // pages issued so far (warp 0 only)
+    bool issuing = true;
+    auto issue_upto = [&](int upto) {  // warp 0: issue slice pages [issued, upto)
+        upto = min(upto, n_local);
+        while (issuing && issued < upto) {
+            if (issued >= bt_base + 32) {
+                bt_base = issued & ~31;
+                const int gq = gb + bt_base + lane;
+                bt_batch = 0;
+                if (gq < ge) {
+                    const int sq = find_seq(pstart, n, gq);
+                    const int ntq = __ldg(a.seq_lens + sq);
+                    const int pg = seq_lo(ntq, a.window) / kPageTokens + (gq - pstart[sq]);
+                    // A row holds bt_stride entries: never read past it.
+                    bt_batch = pg < a.bt_stride
+                                   ? __ldg(a.bt + static_cast<size_t>(sq) * a.bt_stride + pg)
+                                   : kPageNone;
+                    if (bt_batch >= a.n_pages) {
+                        flag_error(a.err, kDevErrBadPage);
+                        bt_batch = 0;
+                    }
+                }
+            }
+            const uint32_t ph = __shfl_sync(~0u, bt_batch, issued - bt_base);
+            bool ok = true;
+            if (lane == 0) {
+                const int st = issued % STAGES;
+                if (issued >= STAGES)
+                    ok = wait_or_abort(&empty[st], static_cast<uint32_t>(issued / STAGES - 1) & 1u,
+                                       abort_flag, a.err);
+                if (ok) {
+                    mbar_arrive_expect_tx(&full[st], Geo::kPageBytes);
+                    uint8_t* dst = stage + st * Geo::kPageBytes;
+#pragma unroll
+                    for (int b = 0; b < Geo::kLoads; ++b)
+                        tma_load_2d(dst + b * Geo::kBoxRows * 128, &tmap, &full[st], 0,
+                                    static_cast<int>(ph) * Geo::kPageRows + b * Geo::kBoxRows);
+                }
+            }
+            if (!__shfl_sync(~0u, ok, 0)) {
+                issuing = false;  // stop; consumers' waits on full[] see the abort flag
+                return;
+            }
+            ++issued;
+        }
+    };
+    if (warp == 0) issue_upto(STAGES);
+
+    // ------- consumer warps: warp w owns kv head w/2, keys of half w%2 -------
+    const int h = warp >> 1, half = warp & 1;
+    const int qd = lane & 3;
+    float* my_pb = pbuf + warp * (2 * G * 8);
+    float* my_x = xbuf + h * G * (kHeadDim + 2);
+    float2 q2[G][8];
+    float2 o2[G];
+    float lp[G], M[G];
+    int s = find_seq(pstart, n, gb);
+    int g = gb;
+    int k = 0;
+    while (g < ge) {
+        const int nt = __ldg(a.seq_lens + s);
+        const int lo = seq_lo(nt, a.window);
+        const int plo = lo / kPageTokens;
+        const int s_begin = pstart[s], s_end = pstart[s + 1];
+        const int seg_end = min(ge, s_end);
+        int pos = nt - 1;
+        if (pos >= a.max_pos) {
+            if (lane == 0) flag_error(a.err, kDevErrBadPos);
+            pos = 0;
+        }
+        load_q<T, G>(a, s, NQ, h, qd, pos, q2);
+#pragma unroll
+        for (int gg = 0; gg < G; ++gg) {
+            o2[gg] = make_float2(0.f, 0.f);
+            lp[gg] = 0.f;
+            M[gg] = -INFINITY;
+        }
+        for (; g < seg_end; ++g, ++k) {
+            if (warp == 0) issue_upto(k + STAGES);
+            const int st = k % STAGES;
+            const uint32_t par = static_cast<uint32_t>(k / STAGES) & 1u;
+            if (wait_or_abort(&full[st], par, abort_flag, a.err)) {
+                const int pg = plo + (g - s_begin);
+                const int t0 = max(lo - pg * kPageTokens, 0);
+                const int t1 = min(nt - pg * kPageTokens, kPageTokens);
+                page_step<T, NKV, G>(stage + st * Geo::kPageBytes, h, half, lane, t0, t1, q2, o2,
+                                     lp, M, my_pb + (k & 1) * G * 8);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[st]);
+        }
+        // ---- flush sequence s: lane sums, then merge the two half-page warps ----
+#pragma unroll
+        for (int gg = 0; gg < G; ++gg) {
+            float t = lp[gg];
+            t += __shfl_xor_sync(~0u, t, 16);
+            t += __shfl_xor_sync(~0u, t, 8);
+            t += __shfl_xor_sync(~0u, t, 4);
+            t += __shfl_xor_sync(~0u, t, 2);
+            t += __shfl_xor_sync(~0u, t, 1);
+            lp[gg] = t;
+        }
+        if (half == 1) {
+#pragma unroll
+            for (int gg = 0; gg < G; ++gg) {
+                *reinterpret_cast<float2*>(my_x + gg * (kHeadDim + 2) + 2 * lane) = o2[gg];
+                if (lane == 0) {
+                    my_x[gg * (kHeadDim + 2) + kHeadDim] = M[gg];
+                    my_x[gg * (kHeadDim + 2) + kHeadDim + 1] = lp[gg];
+                }
+            }
+        }
+        named_bar_sync(2 + h, 64);
+        if (half == 0) {
+#pragma unroll
+            for (int gg = 0; gg < G; ++gg) {
+                const float2 ox = *reinterpret_cast<const float2*>(my_x + gg * (kHeadDim + 2) + 2 * lane);
+                const float mx = my_x[gg * (kHeadDim + 2) + kHeadDim];
+                const float lx = my_x[gg * (kHeadDim + 2) + kHeadDim + 1];
+                const float mn = fmaxf(M[gg], mx);
+                const float mu = (mn == -INFINITY) ? 0.f : mn;
+                const float wa = exp2f(M[gg] - mu), wb = exp2f(mx - mu);
+                lp[gg] = lp[gg] * wa + lx * wb;
+                o2[gg] = __ffma2_rn(ox, make_float2(wb, wb), __fmul2_rn(o2[gg], make_float2(wa, wa)));
+                M[gg] = mn;
+            }
+        }
+        named_bar_sync(2 + h, 64);  // xbuf is free again
+        const bool whole = (s_begin >= gb) && (s_end <= ge);
+        if (whole) {
+            if (half == 0) {
+#pragma unroll
+                for (int gg = 0; gg < G; ++gg) {
+                    const float inv = lp[gg] > 0.f ? 1.f / lp[gg] : 0.f;
+                    T* orow = static_cast<T*>(a.out) +
+                              (static_cast<size_t>(s) * NQ + h * G + gg) * kHeadDim + 2 * lane;
+                    const float x = o2[gg].x * inv, y = o2[gg].y * inv;
+                    if constexpr (sizeof(T) == 2)
+                        *reinterpret_cast<uint32_t*>(orow) = float2_to_bf16x2(x, y);
+                    else
+                        *reinterpret_cast<float2*>(orow) = make_float2(x, y);
+                }
+            }
+        } else {
+            const int slot = (s_begin < gb) ? 2 * cta : 2 * cta + 1;
+            if (half == 0) {
+#pragma unroll
+                for (int gg = 0; gg < G; ++gg) {
+                    const size_t row = static_cast<size_t>(slot) * NQ + h * G + gg;
+                    *reinterpret_cast<float2*>(a.part_o + row * kHeadDim + 2 * lane) = o2[gg];
+                    if (lane == 0)
+                        *reinterpret_cast<float2*>(a.part_ml + row * 2) = make_float2(M[gg], lp[gg]);
+                }
+                __threadfence();
+            }
+            named_bar_sync(1, NCONS);
+            if (threadIdx.x == 0) misc[0] = atomicAdd(a.counters + s, 1);
+            named_bar_sync(1, NCONS);
+            const int c_first = cta_of(s_begin, grid, total);
+            const int c_last = cta_of(s_end - 1, grid, total);
+            if (misc[0] == c_last - c_first) {  // last contributor merges the splits
+                __threadfence();
+                for (int idx = threadIdx.x; idx < NQ * kHeadDim; idx += NCONS) {
+                    const int qh = idx / kHeadDim, dd = idx % kHeadDim;
+                    float mx = -INFINITY;
+                    for (int c = c_first; c <= c_last; ++c) {
+                        const int sl = (c == c_first) ? 2 * c + 1 : 2 * c;
+                        mx = fmaxf(mx, __ldcg(a.part_ml + (static_cast<size_t>(sl) * NQ + qh) * 2));
+                    }
+                    const float mu = (mx == -INFINITY) ? 0.f : mx;
+                    float L = 0.f, O = 0.f;
+                    for (int c = c_first; c <= c_last; ++c) {
+                        const int sl = (c == c_first) ? 2 * c + 1 : 2 * c;
+                        const size_t row = static_cast<size_t>(sl) * NQ + qh;
+                        const float w = exp2f(__ldcg(a.part_ml + row * 2) - mu);
+                        L = fmaf(__ldcg(a.part_ml + row * 2 + 1), w, L);
+                        O = fmaf(__ldcg(a.part_o + row * kHeadDim + dd), w, O);
+                    }
+                    static_cast<T*>(a.out)[(static_cast<size_t>(s) * NQ + qh) * kHeadDim + dd] =
+                        to_elem<T>(L > 0.f ? O / L : 0.f);
+                }
+                if (threadIdx.x == 0) a.counters[s] = 0;
+            }
+            named_bar_sync(1, NCONS);  // misc[0] is read by all before the next flush
+        }
+        if (g < ge) s = find_seq(pstart, n, g);
+    }
+    // Warp 0: do not leave while a copy issued here may still be landing
+    // (only possible after an abort; otherwise every page was consumed).
+    if (warp == 0 && lane == 0) {
+        for (int kk = max(0, issued - STAGES); kk < issued; ++kk)
+            mbar_wait(&full[kk % STAGES], static_cast<uint32_t>(kk / STAGES) & 1u);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Host side: one entry per compiled (dtype, n_kv, group) shape.
+struct DecodeVariant {
+    int dtype, nkv, group;
+    const void* fn;
+    size_t (*smem)(int);
+    int threads;
+};
+
+template <typename T, int NKV, int G, int STAGES>
+DecodeVariant make_variant(int dtype) {
+    using S = DecodeShape<T, NKV, G, STAGES>;
+    return DecodeVariant{dtype, NKV, G, reinterpret_cast<const void*>(&decode_kernel<T, NKV, G, STAGES>),
+                         &S::smem_bytes, S::kThreads};
+}
+
+const DecodeVariant* find_variant(int dtype, int nkv, int group) {
+    static const DecodeVariant table[] = {
+        make_variant<__nv_bfloat16, 8, 3, 6>(KV_DTYPE_BF16),
+        make_variant<__nv_bfloat16, 8, 4, 6>(KV_DTYPE_BF16),
+        make_variant<__nv_bfloat16, 1, 4, 8>(KV_DTYPE_BF16),
+        make_variant<float, 8, 3, 3>(KV_DTYPE_F32),
+        make_variant<float, 8, 4, 3>(KV_DTYPE_F32),
+        make_variant<float, 1, 4, 8>(KV_DTYPE_F32),
+    };
+    for (const auto& v : table)
+        if (v.dtype == dtype && v.nkv == nkv && v.group == group) return &v;
+    return nullptr;
+}
+
+}  // namespace
+
+int decode_setup(kv_pool* pool) {
+    const auto& c = pool->cfg;
+    const DecodeVariant* v = find_variant(c.dtype, c.n_kv_heads, c.n_q_heads / c.n_kv_heads);
+    if (!v) return KV_ERR_UNSUPPORTED;
+    const size_t smem = v->smem(c.max_seqs);
+    int optin = 0;
+    if (cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, c.device) != cudaSuccess)
+        return KV_ERR_CUDA;
+    if (smem > static_cast<size_t>(optin)) return KV_ERR_INVALID;  // max_seqs too large
+    if (cudaFuncSetAttribute(v->fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(smem)) != cudaSuccess)
+        return KV_ERR_CUDA;
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, v->fn, v->threads, smem) !=
+            cudaSuccess ||
+        per_sm < 1)
+        return KV_ERR_CUDA;
+    pool->decode_grid = pool->sm_count * per_sm;
+    pool->decode_smem = smem;
+    return KV_OK;
+}
+
+size_t decode_workspace_slots(const kv_pool* pool) { return 2 * static_cast<size_t>(pool->decode_grid); }
+
+int launch_decode(kv_pool* pool, const void* q, const uint32_t* bt, int32_t bt_stride,
+                  const int32_t* seq_lens, int32_t n_seqs, int32_t window, void* out,
+                  cudaStream_t stream) {
+    const auto& c = pool->cfg;
+    const DecodeVariant* v = find_variant(c.dtype, c.n_kv_heads, c.n_q_heads / c.n_kv_heads);
+    if (!v) return KV_ERR_UNSUPPORTED;
+    DecodeArgs a;
+    a.q = q;
+    a.out = out;
+    a.bt = bt;
+    a.bt_stride = bt_stride;
+    a.seq_lens = seq_lens;
+    a.n_seqs = n_seqs;
+    a.window = window;
+    a.rope = pool->rope;
+    a.max_pos = c.max_positions;
+    a.n_pages = c.n_pages;
+    a.part_o = pool->part_o;
+    a.part_ml = pool->part_ml;
+    a.counters = pool->counters;
+    a.err = pool->dev_error;
+    a.qscale = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(c.head_dim)));
+    void* args[] = {&pool->page_map, &a};
+    const cudaError_t e = cudaLaunchKernel(v->fn, dim3(pool->decode_grid), dim3(v->threads), args,
+                                           pool->decode_smem, stream);
+    return e == cudaSuccess ? KV_OK : KV_ERR_CUDA;
+}
+
+}  // namespace kvb200

@@ -1,0 +1,43 @@
+// kv_pool_impl.h -- the pool object behind the opaque `kv_pool` handle.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/llmhost_kv.h"
+
+struct kv_pool {
+    kv_pool_config cfg;
+    int sm_count = 0;
+    size_t page_bytes = 0;
+    size_t elem_bytes = 0;
+    void* pages = nullptr;        // n_pages * page_bytes, device
+    float2* rope = nullptr;       // [max_positions][head_dim / 2] (cos, sin), device
+    int* dev_error = nullptr;     // device error word
+    // decode split workspace
+    float* part_o = nullptr;      // [2 * decode_grid][n_q][head_dim]
+    float* part_ml = nullptr;     // [2 * decode_grid][n_q][2]
+    int* counters = nullptr;      // [max_seqs]
+    int decode_grid = 0;
+    size_t decode_smem = 0;
+    CUtensorMap page_map;         // TMA view of the pool as 128-byte rows
+};
+
+namespace kvb200 {
+
+// Launchers implemented in the .cu files; they return a kv_status.
+int launch_append(kv_pool* pool, const void* k, const void* v, const int32_t* tok_seq,
+                  const int32_t* tok_slot, const int32_t* tok_pos, const int32_t* seq_lens,
+                  int32_t n_tokens, int32_t n_seqs, const uint32_t* bt, int32_t bt_stride,
+                  cudaStream_t stream);
+
+// Sets up the decode kernel for the pool (smem attribute, grid); called once
+// at pool creation.  Returns KV_ERR_UNSUPPORTED for shapes not compiled.
+int decode_setup(kv_pool* pool);
+size_t decode_workspace_slots(const kv_pool* pool);
+int launch_decode(kv_pool* pool, const void* q, const uint32_t* bt, int32_t bt_stride,
+                  const int32_t* seq_lens, int32_t n_seqs, int32_t window, void* out,
+                  cudaStream_t stream);
+
+}  // namespace kvb200

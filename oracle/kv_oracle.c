@@ -1,0 +1,353 @@
+/*
+ * kv_oracle.c -- CPU oracle for the paged KV-cache path (TEST INFRASTRUCTURE).
+ *
+ * Checker only: the product never links or calls this file.  Built with
+ *   gcc -O3 -march=x86-64-v3 -ffp-contract=off -fno-fast-math -pthread
+ * (-march follows the reference's .cargo/config.toml:3-4; -ffp-contract=off
+ * because Rust does not contract a*b+c).  Every restated function cites the
+ * reference lines it follows; the comments give the Rust expression each C
+ * line stands for.
+ */
+#include "kv_oracle.h"
+
+#include <math.h>
+#include <pthread.h>
+#include <stdatomic.h>
+#include <stdlib.h>
+#include <string.h>
+#include <unistd.h>
+
+uint16_t orc_f32_to_bf16(float f) {
+    uint32_t u;
+    memcpy(&u, &f, 4);
+    if ((u & 0x7fffffffu) > 0x7f800000u) return (uint16_t)((u >> 16) | 0x0040u); /* quiet NaN */
+    u += 0x7fffu + ((u >> 16) & 1u);
+    return (uint16_t)(u >> 16);
+}
+
+float orc_bf16_to_f32(uint16_t h) {
+    uint32_t u = (uint32_t)h << 16;
+    float f;
+    memcpy(&f, &u, 4);
+    return f;
+}
+
+/* rope.rs:6-14
+ *   let dim_f = dim as f32;
+ *   for i in (0..dim).step_by(2) { let expo = i as f32 / dim_f;
+ *                                  out.push(1.0 / theta.powf(expo)); } */
+void orc_inv_freq(size_t dim, float theta, float *out) {
+    float dim_f = (float)dim;
+    for (size_t i = 0; i < dim; i += 2) {
+        float expo = (float)i / dim_f;
+        out[i / 2] = 1.0f / powf(theta, expo);
+    }
+}
+
+/* rope.rs:18-43
+ *   let pos = (start + t) as f32; let freq = pos * inv_freq[i];
+ *   cos[t*dim+i] = cos[t*dim+half+i] = freq.cos(); same for sin. */
+void orc_cos_sin(const float *inv_freq, size_t start, size_t tokens, size_t dim,
+                 float *cos_out, float *sin_out) {
+    size_t half = dim / 2;
+    for (size_t t = 0; t < tokens; t++) {
+        float pos = (float)(start + t);
+        for (size_t i = 0; i < half; i++) {
+            float freq = pos * inv_freq[i];
+            float c = cosf(freq);
+            float s = sinf(freq);
+            cos_out[t * dim + i] = c;
+            cos_out[t * dim + half + i] = c;
+            sin_out[t * dim + i] = s;
+            sin_out[t * dim + half + i] = s;
+        }
+    }
+}
+
+/* rope.rs:46-81
+ *   rotated = cat(-x[half:], x[:half]);  rotated[d] = q[d] * c[d] + rotated[d] * s[d]
+ * Two roundings (product, product) and one for the sum: no FMA. */
+void orc_apply_rope_in_place(float *states, const float *cos_t, const float *sin_t,
+                             size_t heads, size_t tokens, size_t dim) {
+    size_t half = dim / 2;
+    float *rot = (float *)malloc(dim * sizeof(float));
+    for (size_t h = 0; h < heads; h++) {
+        for (size_t t = 0; t < tokens; t++) {
+            float *q = states + (h * tokens + t) * dim;
+            for (size_t i = 0; i < half; i++) {
+                rot[i] = -q[half + i];
+                rot[half + i] = q[i];
+            }
+            const float *c = cos_t + t * dim;
+            const float *s = sin_t + t * dim;
+            for (size_t d = 0; d < dim; d++) {
+                float a = q[d] * c[d];
+                float b = rot[d] * s[d];
+                rot[d] = a + b;
+            }
+            memcpy(q, rot, dim * sizeof(float));
+        }
+    }
+    free(rot);
+}
+
+/* ops.rs:64-79
+ *   max = fold(NEG_INFINITY, f32::max); v = (v - max).exp(); sum += v;
+ *   inv = if sum == 0.0 { 0.0 } else { 1.0 / sum }; v *= inv */
+void orc_softmax_last_axis(float *logits, size_t len, size_t n) {
+    if (n == 0) return; /* Rust's chunks_exact_mut(0) panics; callers never pass 0 */
+    for (size_t r = 0; r + n <= len; r += n) {
+        float *row = logits + r;
+        float max = -INFINITY;
+        for (size_t i = 0; i < n; i++) max = fmaxf(max, row[i]);
+        float sum = 0.0f;
+        for (size_t i = 0; i < n; i++) {
+            row[i] = expf(row[i] - max);
+            sum += row[i];
+        }
+        float inv = (sum == 0.0f) ? 0.0f : 1.0f / sum;
+        for (size_t i = 0; i < n; i++) row[i] *= inv;
+    }
+}
+
+/* lfm2.rs:1006-1056 (attention_decode_cached) */
+void orc_attention_decode_cached(const float *q, const float *k_cache, const float *v_cache,
+                                 size_t n_q, size_t n_kv, size_t kv_len, size_t kv_cap,
+                                 size_t dim, const uint8_t *key_valid, size_t key_valid_len,
+                                 float *scores, float *out) {
+    /* let scale = (dim as f32).sqrt().recip(); */
+    float scale = 1.0f / sqrtf((float)dim);
+    size_t n_rep = n_q / n_kv;
+    memset(out, 0, n_q * dim * sizeof(float));
+    for (size_t qh = 0; qh < n_q; qh++) {
+        size_t kv_h = qh / n_rep;
+        const float *qv = q + qh * dim;
+        float *row = scores + qh * kv_len;
+        for (size_t s = 0; s < kv_len; s++) {
+            /* if key_valid.get(s) == Some(&false) */
+            if (key_valid && s < key_valid_len && !key_valid[s]) {
+                row[s] = -INFINITY;
+                continue;
+            }
+            const float *kv = k_cache + (kv_h * kv_cap + s) * dim;
+            float acc = 0.0f;
+            for (size_t d = 0; d < dim; d++) acc = fmaf(qv[d], kv[d], acc); /* mul_add */
+            row[s] = acc * scale;
+        }
+        orc_softmax_last_axis(row, kv_len, kv_len);
+        float *dst = out + qh * dim;
+        for (size_t s = 0; s < kv_len; s++) {
+            float w = row[s];
+            if (w == 0.0f) continue;
+            const float *vv = v_cache + (kv_h * kv_cap + s) * dim;
+            for (size_t d = 0; d < dim; d++) dst[d] = fmaf(w, vv[d], dst[d]);
+        }
+    }
+}
+
+/* Shared body of attention_forward (lfm2.rs:1058-1111): the masked predicate
+ * is `(causal && s > t) || !key_valid[s]` there, `!mask[t*kv_len+s]` here. */
+static void attention_rows(const float *q, const float *k, const float *v, size_t n_q,
+                           size_t n_kv, size_t q_len, size_t kv_len, size_t dim, int causal,
+                           const uint8_t *key_valid, const uint8_t *mask, float *out) {
+    float scale = 1.0f / sqrtf((float)dim);
+    size_t n_rep = n_q / n_kv;
+    memset(out, 0, n_q * q_len * dim * sizeof(float));
+    float *scores = (float *)malloc((q_len * kv_len + 1) * sizeof(float));
+    for (size_t qh = 0; qh < n_q; qh++) {
+        size_t kv_h = qh / n_rep;
+        for (size_t t = 0; t < q_len; t++) {
+            const float *qv = q + (qh * q_len + t) * dim;
+            for (size_t s = 0; s < kv_len; s++) {
+                int masked = mask ? !mask[t * kv_len + s]
+                                  : ((causal && s > t) || (key_valid && !key_valid[s]));
+                if (masked) {
+                    scores[t * kv_len + s] = -INFINITY;
+                    continue;
+                }
+                const float *kv = k + (kv_h * kv_len + s) * dim;
+                float acc = 0.0f;
+                for (size_t d = 0; d < dim; d++) acc = fmaf(qv[d], kv[d], acc);
+                scores[t * kv_len + s] = acc * scale;
+            }
+        }
+        orc_softmax_last_axis(scores, q_len * kv_len, kv_len);
+        for (size_t t = 0; t < q_len; t++) {
+            float *dst = out + (qh * q_len + t) * dim;
+            for (size_t s = 0; s < kv_len; s++) {
+                float w = scores[t * kv_len + s];
+                if (w == 0.0f) continue;
+                const float *vv = v + (kv_h * kv_len + s) * dim;
+                for (size_t d = 0; d < dim; d++) dst[d] = fmaf(w, vv[d], dst[d]);
+            }
+        }
+    }
+    free(scores);
+}
+
+/* lfm2.rs:1058-1111 (attention_forward) */
+void orc_attention_forward(const float *q, const float *k, const float *v, size_t n_q,
+                           size_t n_kv, size_t q_len, size_t kv_len, size_t dim, int causal,
+                           const uint8_t *key_valid, float *out) {
+    attention_rows(q, k, v, n_q, n_kv, q_len, kv_len, dim, causal, key_valid, NULL, out);
+}
+
+void orc_attention_masked(const float *q, const float *k, const float *v, size_t n_q,
+                          size_t n_kv, size_t q_len, size_t kv_len, size_t dim,
+                          const uint8_t *mask, float *out) {
+    attention_rows(q, k, v, n_q, n_kv, q_len, kv_len, dim, 0, NULL, mask, out);
+}
+
+/* ---- paged layout (build-defined) ---------------------------------------- */
+
+static inline float load_elem(const void *base, int dtype, size_t i) {
+    return dtype == ORC_BF16 ? orc_bf16_to_f32(((const uint16_t *)base)[i])
+                             : ((const float *)base)[i];
+}
+
+static inline void store_elem(void *base, int dtype, size_t i, float x) {
+    if (dtype == ORC_BF16)
+        ((uint16_t *)base)[i] = orc_f32_to_bf16(x);
+    else
+        ((float *)base)[i] = x;
+}
+
+void orc_paged_append_token(void *pages, int dtype, size_t n_kv, size_t P, size_t d,
+                            const uint32_t *bt, size_t slot, const void *k_raw,
+                            const void *v, const float *cos_row, const float *sin_row) {
+    size_t page_elems = 2 * n_kv * P * d;
+    uint32_t page = bt[slot / P];
+    size_t j = slot % P;
+    float *kr = (float *)malloc(n_kv * d * sizeof(float));
+    for (size_t i = 0; i < n_kv * d; i++) kr[i] = load_elem(k_raw, dtype, i);
+    /* lfm2.rs:816-825: RoPE on k (heads = n_kv, tokens = 1) before the store
+     * at lfm2.rs:828-832. */
+    orc_apply_rope_in_place(kr, cos_row, sin_row, n_kv, 1, d);
+    for (size_t h = 0; h < n_kv; h++) {
+        size_t kofs = (size_t)page * page_elems + (h * P + j) * d;
+        size_t vofs = (size_t)page * page_elems + ((n_kv + h) * P + j) * d;
+        for (size_t e = 0; e < d; e++) {
+            store_elem(pages, dtype, kofs + e, kr[h * d + e]);
+            store_elem(pages, dtype, vofs + e, load_elem(v, dtype, h * d + e));
+        }
+    }
+    free(kr);
+}
+
+void orc_paged_gather(const void *pages, int dtype, size_t n_kv, size_t P, size_t d,
+                      const uint32_t *bt, size_t n_tokens, float *k_out, float *v_out) {
+    size_t page_elems = 2 * n_kv * P * d;
+    for (size_t t = 0; t < n_tokens; t++) {
+        uint32_t page = bt[t / P];
+        size_t j = t % P;
+        for (size_t h = 0; h < n_kv; h++) {
+            float *kd = k_out + (h * n_tokens + t) * d;
+            float *vd = v_out + (h * n_tokens + t) * d;
+            if (page == ORC_PAGE_NONE) {
+                memset(kd, 0, d * sizeof(float));
+                memset(vd, 0, d * sizeof(float));
+                continue;
+            }
+            size_t kofs = (size_t)page * page_elems + (h * P + j) * d;
+            size_t vofs = (size_t)page * page_elems + ((n_kv + h) * P + j) * d;
+            for (size_t e = 0; e < d; e++) {
+                kd[e] = load_elem(pages, dtype, kofs + e);
+                vd[e] = load_elem(pages, dtype, vofs + e);
+            }
+        }
+    }
+}
+
+void orc_paged_decode(const void *pages, int dtype, size_t n_q, size_t n_kv, size_t P,
+                      size_t d, const uint32_t *bt, size_t seq_len, size_t window,
+                      const void *q_raw, const float *inv_freq, float *out) {
+    if (seq_len == 0) { /* build-defined: an empty sequence attends to nothing */
+        memset(out, 0, n_q * d * sizeof(float));
+        return;
+    }
+    float *k = (float *)malloc(n_kv * seq_len * d * sizeof(float));
+    float *v = (float *)malloc(n_kv * seq_len * d * sizeof(float));
+    float *q = (float *)malloc(n_q * d * sizeof(float));
+    float *cs = (float *)malloc(2 * d * sizeof(float));
+    float *scores = (float *)malloc(n_q * seq_len * sizeof(float));
+    uint8_t *valid = NULL;
+    orc_paged_gather(pages, dtype, n_kv, P, d, bt, seq_len, k, v);
+    for (size_t i = 0; i < n_q * d; i++) q[i] = load_elem(q_raw, dtype, i);
+    /* lfm2.rs:816-822: cos_sin at pos, RoPE on q with heads = n_q, tokens = 1 */
+    orc_cos_sin(inv_freq, seq_len - 1, 1, d, cs, cs + d);
+    orc_apply_rope_in_place(q, cs, cs + d, n_q, 1, d);
+    if (window > 0 && seq_len > window) {
+        valid = (uint8_t *)malloc(seq_len);
+        for (size_t s = 0; s < seq_len; s++) valid[s] = (s + window >= seq_len);
+    }
+    orc_attention_decode_cached(q, k, v, n_q, n_kv, seq_len, seq_len, d, valid,
+                                valid ? seq_len : 0, scores, out);
+    free(valid);
+    free(scores);
+    free(cs);
+    free(q);
+    free(v);
+    free(k);
+}
+
+/* One sequence of orc_decode_step. */
+typedef struct {
+    void *pages;
+    int dtype;
+    size_t n_q, n_kv, P, d, bt_stride, n_seqs, window;
+    const uint32_t *bt;
+    const int32_t *seq_lens;
+    const void *q_raw, *k_raw, *v;
+    const float *inv_freq;
+    float *out;
+    atomic_long next;
+} step_job;
+
+static void step_one(step_job *j, size_t s) {
+    size_t esz = j->dtype == ORC_BF16 ? 2 : 4;
+    size_t len = (size_t)j->seq_lens[s];
+    const uint32_t *row = j->bt + s * j->bt_stride;
+    if (len > 0) {
+        float cs[2 * 256];
+        orc_cos_sin(j->inv_freq, len - 1, 1, j->d, cs, cs + j->d);
+        orc_paged_append_token(j->pages, j->dtype, j->n_kv, j->P, j->d, row, len - 1,
+                               (const char *)j->k_raw + s * j->n_kv * j->d * esz,
+                               (const char *)j->v + s * j->n_kv * j->d * esz, cs, cs + j->d);
+    }
+    orc_paged_decode(j->pages, j->dtype, j->n_q, j->n_kv, j->P, j->d, row, len, j->window,
+                     (const char *)j->q_raw + s * j->n_q * j->d * esz, j->inv_freq,
+                     j->out + s * j->n_q * j->d);
+}
+
+static void *step_worker(void *arg) {
+    step_job *j = (step_job *)arg;
+    for (;;) {
+        long s = atomic_fetch_add(&j->next, 1);
+        if (s >= (long)j->n_seqs) break;
+        step_one(j, (size_t)s);
+    }
+    return NULL;
+}
+
+void orc_decode_step(void *pages, int dtype, size_t n_q, size_t n_kv, size_t P, size_t d,
+                     const uint32_t *bt, size_t bt_stride, const int32_t *seq_lens,
+                     size_t n_seqs, size_t window, const void *q_raw, const void *k_raw,
+                     const void *v, const float *inv_freq, float *out, int n_threads) {
+    step_job j = {pages, dtype, n_q, n_kv, P, d, bt_stride, n_seqs, window, bt, seq_lens,
+                  q_raw, k_raw, v, inv_freq, out, 0};
+    int nt = n_threads > 0 ? n_threads : orc_max_threads();
+    if (nt > (int)n_seqs) nt = (int)n_seqs;
+    if (nt <= 1) {
+        for (size_t s = 0; s < n_seqs; s++) step_one(&j, s);
+        return;
+    }
+    pthread_t *th = (pthread_t *)malloc((size_t)nt * sizeof(pthread_t));
+    for (int i = 0; i < nt; i++) pthread_create(&th[i], NULL, step_worker, &j);
+    for (int i = 0; i < nt; i++) pthread_join(th[i], NULL);
+    free(th);
+}
+
+int orc_max_threads(void) {
+    long n = sysconf(_SC_NPROCESSORS_ONLN);
+    return n > 0 ? (int)n : 1;
+}

@@ -1,0 +1,61 @@
+"""The C-ABI library loads and exports every symbol include/*.h declares.
+
+No compute call is made here (no GPU on the CPU runner).
+"""
+import re
+from pathlib import Path
+
+import pytest
+
+from llmhost_b200 import _capi
+
+ROOT = Path(__file__).resolve().parent.parent
+
+
+def declared_functions() -> set[str]:
+    names = set()
+    for h in (ROOT / "include").glob("*.h"):
+        text = re.sub(r"/\*.*?\*/", "", h.read_text(), flags=re.S)
+        for m in re.finditer(r"^[A-Za-z_][\w\s\*]*?\b(kv_\w+)\s*\(", text, flags=re.M):
+            names.add(m.group(1))
+    return names
+
+
+def test_header_declares_functions():
+    names = declared_functions()
+    assert {"kv_pool_create", "kv_append", "kv_decode_attn"} <= names
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _capi.lib()
+    missing = [n for n in sorted(declared_functions()) if not hasattr(lib, n)]
+    assert not missing, f"not exported: {missing}"
+
+
+def test_python_binding_covers_header():
+    bound = {name for name, _, _ in _capi.SIGNATURES}
+    assert declared_functions() <= bound
+
+
+def test_status_strings_without_gpu():
+    lib = _capi.lib()
+    assert lib.kv_status_str(0) == b"ok"
+    assert lib.kv_api_version() == 1
+    for code in range(8):
+        assert lib.kv_status_str(code)
+
+
+def test_invalid_config_rejected_before_touching_cuda():
+    cfg = _capi.KvPoolConfig(7, 24, 8, 64, 16, 1024, 1e6, 1024, 64, 0)  # bad dtype
+    h = _capi.c_void_p()
+    assert _capi.lib().kv_pool_create(cfg, h) == 1
+    cfg = _capi.KvPoolConfig(1, 24, 8, 128, 16, 1024, 1e6, 1024, 64, 0)  # head_dim 128
+    assert _capi.lib().kv_pool_create(cfg, h) == 1
+    assert h.value is None
+
+
+def test_missing_library_fails_loudly(monkeypatch, tmp_path):
+    monkeypatch.setattr(_capi, "LIB_PATH", tmp_path / "nope.so")
+    monkeypatch.setattr(_capi, "_lib", None)
+    with pytest.raises(RuntimeError, match="no CPU fallback"):
+        _capi.lib()

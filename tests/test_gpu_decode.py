@@ -1,0 +1,116 @@
+"""Parity of the CUDA append + paged decode attention against the CPU oracle.
+
+Tolerances: attention outputs within 1e-5 relative for
+fp32 and 2e-2 for bf16, checked normwise per (sequence, query head) row;
+stored pages bit-exact (RoPE'd K uses the same libm cos/sin as the reference).
+"""
+import numpy as np
+import pytest
+
+from paged_case import DecodeCase, assert_close_rows, to_numpy_f32
+
+pytestmark = pytest.mark.gpu
+
+RTOL = {"f32": 1e-5, "bf16": 2e-2}
+
+
+def run_case(case: DecodeCase, repeat: int = 1):
+    host, ref = case.run_oracle()
+    with case.make_pool() as pool:
+        case.prefill_gpu(pool)
+        out = case.decode_gpu(pool, repeat=repeat)
+        err = pool.last_error()
+        ids = case.used_pages()
+        gpu_pages = pool.read_pages(ids)
+    assert err == 0, f"device error word {err}"
+    np.testing.assert_array_equal(gpu_pages, host.data[ids], err_msg="stored pages differ from the oracle")
+    return to_numpy_f32(out), ref
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "f32"])
+def test_decode_ragged_lengths(cuda, dtype):
+    case = DecodeCase(dtype, 24, 8, [0, 1, 14, 15, 16, 17, 31, 100, 1000, 2999], seed=3)
+    out, ref = run_case(case)
+    assert_close_rows(out, ref, RTOL[dtype], f"{dtype} ragged")
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "f32"])
+def test_decode_group4(cuda, dtype):
+    case = DecodeCase(dtype, 32, 8, [5, 700, 4097, 63], seed=4)
+    out, ref = run_case(case)
+    assert_close_rows(out, ref, RTOL[dtype], f"{dtype} 32q/8kv")
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "f32"])
+def test_decode_single_kv_head_long(cuda, dtype):
+    # One KV head with 4 query heads (the per-GPU shard of the long-context
+    # session): one sequence split over every CTA of the grid.
+    case = DecodeCase(dtype, 4, 1, [40000], seed=5)
+    out, ref = run_case(case)
+    assert_close_rows(out, ref, RTOL[dtype], f"{dtype} 4q/1kv long")
+
+
+def test_decode_one_long_sequence_many_splits(cuda):
+    case = DecodeCase("bf16", 24, 8, [60000], seed=6)
+    out, ref = run_case(case, repeat=3)  # repeated calls: split counters reset
+    assert_close_rows(out, ref, RTOL["bf16"], "bf16 one long sequence")
+
+
+def test_decode_many_short_sequences(cuda):
+    rng = np.random.default_rng(7)
+    lens = rng.integers(0, 200, size=700)
+    case = DecodeCase("bf16", 24, 8, lens, seed=7)
+    out, ref = run_case(case)
+    assert_close_rows(out, ref, RTOL["bf16"], "bf16 700 short sequences")
+
+
+def test_decode_config_shaped_batch(cuda):
+    # 64 sequences with lengths drawn like the batched-decode configuration
+    # (uniform in [128, 8192]), scaled down 4x to keep the oracle quick.
+    rng = np.random.default_rng(1)
+    lens = rng.integers(128, 2048, endpoint=True, size=64)
+    case = DecodeCase("bf16", 24, 8, lens, seed=8)
+    out, ref = run_case(case)
+    assert_close_rows(out, ref, RTOL["bf16"], "bf16 config-shaped")
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "f32"])
+def test_decode_sliding_window_evicted_pages(cuda, dtype):
+    # Pages wholly below the window are marked evicted (KV_PAGE_NONE): the
+    # kernel must not read them (a read would set the bad-page error bit).
+    case = DecodeCase(dtype, 24, 8, [5000, 40, 1030, 2047], seed=9, window=1024, evict_below_window=True)
+    out, ref = run_case(case)
+    assert_close_rows(out, ref, RTOL[dtype], f"{dtype} window")
+
+
+def test_zero_sequences_is_a_noop(cuda):
+    import torch
+
+    case = DecodeCase("bf16", 24, 8, [10], seed=10)
+    with case.make_pool() as pool:
+        empty_i = torch.zeros((0, 1), dtype=torch.int32, device=cuda)
+        q = torch.zeros((0, 24, 64), dtype=torch.bfloat16, device=cuda)
+        out = pool.decode_attn(q, empty_i, torch.zeros(0, dtype=torch.int32, device=cuda))
+        assert out.shape == (0, 24, 64)
+        assert pool.last_error() == 0
+
+
+def test_bad_page_id_sets_error_word(cuda):
+    import torch
+    from llmhost_b200._capi import KV_PAGE_NONE
+
+    case = DecodeCase("bf16", 24, 8, [100, 50], seed=11)
+    with case.make_pool() as pool:
+        case.prefill_gpu(pool)
+        bt = case.bt.copy()
+        bt[1, 1] = np.uint32(case.n_pages + 5)  # out of range: the kernel's bounds check flags it
+        lens = torch.from_numpy(case.seq_lens).to(cuda)
+        from paged_case import to_torch
+
+        pool.decode_attn(to_torch(case.q, "bf16", cuda), torch.from_numpy(bt.view(np.int32)).to(cuda), lens)
+        assert pool.last_error() == 2  # KV_ERR_BAD_PAGE
+        bt[1, 1] = np.uint32(KV_PAGE_NONE)
+        pool.decode_attn(to_torch(case.q, "bf16", cuda), torch.from_numpy(bt.view(np.int32)).to(cuda), lens)
+        assert pool.last_error() == 2
+        # the context stays usable
+        assert pool.last_error() == 0
