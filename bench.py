@@ -49,6 +49,9 @@ def parse_args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=12.0, help="seconds of CPU-baseline work")
     ap.add_argument("--schedule", type=int, default=512, help="decode steps in the workload")
+    ap.add_argument("--layers", type=int, default=6, help="attention layers (6 in the workload)")
+    ap.add_argument("--pool-pages", type=int, default=1 << 20,
+                    help="pool size in pages (2^20 in the workload; smaller only for profiling)")
     return ap.parse_args()
 
 
@@ -227,7 +230,8 @@ def run_ours(args, rank: int, world: int, local_rank: int):
 
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
-    wl = decode_config(steps=args.schedule, seed=1 + 1000 * rank)
+    wl = decode_config(steps=args.schedule, seed=1 + 1000 * rank, n_layers=args.layers,
+                       pool_pages=args.pool_pages)
     n, L = wl.n_seqs, wl.n_layers
     S = wl.steps
     max_pos = int(wl.l0.max()) + S + 16
@@ -390,7 +394,9 @@ def run_ours(args, rank: int, world: int, local_rank: int):
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K,
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": wl.name, "sessions_per_gpu": n, "layers": L, "q_heads": wl.n_q,
+            "config": {"workload": wl.name if (L == 6 and wl.pool_pages == 1 << 20) else
+                       f"{wl.name} (reduced: {L} layers, {wl.pool_pages} pages)",
+                       "sessions_per_gpu": n, "layers": L, "q_heads": wl.n_q,
                        "kv_heads": wl.n_kv, "head_dim": 64, "page_tokens": 16,
                        "pool_pages": wl.pool_pages, "schedule_steps": S,
                        "lengths": "uniform [128, 8192] + step",

@@ -20,11 +20,11 @@
 // Data path per CTA: warp 0 streams whole pages (K and V of all kv heads, one
 // contiguous 4- to 64-KiB block) with TMA 2-D tile loads, 128-byte swizzled,
 // STAGES-1 pages ahead of use, into a ring of STAGES page buffers guarded by
-// full/empty mbarriers.  Two consumer warps own each kv head, one per half
-// page (8 keys): QK^T with 4 lanes per key (16 dims each, FFMA2), page max by
-// warp shuffles, p to shared memory, then PV with each lane owning 2 output
-// dims over the warp's 8 keys.  The two half states merge through shared
-// memory when a sequence's slice ends.
+// full/empty mbarriers.  Two warps own each kv head and take alternate
+// pages: QK^T with 4 lanes per key (16 dims each, FFMA2, 2 keys per lane),
+// the page max in one redux.sync, p to shared memory as (p, p) pairs, then PV
+// with each lane owning 2 output dims over the page's 16 keys.  The two
+// warps' states merge through shared memory when a sequence's slice ends.
 // Every wait is bounded by %globaltimer; a timeout sets the pool's error word
 // and an abort flag so the CTA drains and exits instead of hanging.
 #include <cmath>
@@ -142,106 +142,169 @@ __device__ __forceinline__ void load_q(const DecodeArgs& a, int s, int nq, int h
     }
 }
 
-// K row `r` (token row inside the K block), the 16 dims of quarter qd.
-__device__ __forceinline__ void load_krow(const uint8_t* buf, int r, int qd, float2 (&k)[8],
-                                          const __nv_bfloat16*) {
-    const uint32_t lin = static_cast<uint32_t>(r) * 128u + static_cast<uint32_t>(qd) * 32u;
-    const uint4 a = *reinterpret_cast<const uint4*>(buf + swz128(lin));
-    const uint4 b = *reinterpret_cast<const uint4*>(buf + swz128(lin + 16u));
+// ---- per-lane shared-memory offsets ------------------------------------------
+// The TMA writes each page with the 128-byte swizzle: 16-byte chunk c of
+// 128-byte row R lands at chunk c ^ (R & 7).  The offsets below fold that in
+// once per lane.  K: lane (j = lane/4, qd = lane%4) reads key j of its head,
+// dims [16qd, 16qd+16); key j+8 sits kKey8 bytes further with the same
+// swizzle.  V: lane reads dims 2*lane, 2*lane+1 of key t at vaddr(t), an XOR
+// with a compile-time constant plus an immediate offset.
+template <typename T> struct LaneOffsets;
+
+template <> struct LaneOffsets<__nv_bfloat16> {
+    static constexpr uint32_t kKey8 = 8 * 128;
+    uint32_t k[2];
+    uint32_t v;
+    __device__ __forceinline__ LaneOffsets(int h, int lane, int nkv) {
+        const uint32_t j = lane >> 2, qd = lane & 3;
+        const uint32_t row = h * kPageTokens + j;
+        k[0] = row * 128 + (((2 * qd) ^ j) << 4);
+        k[1] = row * 128 + (((2 * qd + 1) ^ j) << 4);
+        v = (nkv + h) * kPageTokens * 128 + ((lane >> 2) << 4) + (lane & 3) * 4;
+    }
+    __device__ __forceinline__ uint32_t vaddr(int t) const { return (v ^ ((t & 7) << 4)) + t * 128; }
+};
+
+template <> struct LaneOffsets<float> {
+    static constexpr uint32_t kKey8 = 8 * 256;
+    uint32_t k[4];
+    uint32_t v;
+    __device__ __forceinline__ LaneOffsets(int h, int lane, int nkv) {
+        const uint32_t j = lane >> 2, qd = lane & 3;
+        const uint32_t R = (h * kPageTokens + j) * 2 + (qd >> 1);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) k[c] = R * 128 + ((((qd & 1) * 4 + c) ^ (R & 7)) << 4);
+        const uint32_t b = lane >> 4;
+        v = (nkv + h) * kPageTokens * 256 + b * 128 + (((((lane >> 1) & 7) ^ b)) << 4) + (lane & 1) * 8;
+    }
+    __device__ __forceinline__ uint32_t vaddr(int t) const {
+        return (v ^ (((2 * t) & 7) << 4)) + t * 256;
+    }
+};
+
+__device__ __forceinline__ void load_key(const uint8_t* buf, const LaneOffsets<__nv_bfloat16>& o,
+                                         uint32_t extra, float2 (&k)[8]) {
+    const uint4 a = *reinterpret_cast<const uint4*>(buf + o.k[0] + extra);
+    const uint4 b = *reinterpret_cast<const uint4*>(buf + o.k[1] + extra);
     k[0] = bf16x2_to_float2(a.x); k[1] = bf16x2_to_float2(a.y);
     k[2] = bf16x2_to_float2(a.z); k[3] = bf16x2_to_float2(a.w);
     k[4] = bf16x2_to_float2(b.x); k[5] = bf16x2_to_float2(b.y);
     k[6] = bf16x2_to_float2(b.z); k[7] = bf16x2_to_float2(b.w);
 }
-__device__ __forceinline__ void load_krow(const uint8_t* buf, int r, int qd, float2 (&k)[8],
-                                          const float*) {
-    const uint32_t lin = static_cast<uint32_t>(r) * 256u + static_cast<uint32_t>(qd) * 64u;
+__device__ __forceinline__ void load_key(const uint8_t* buf, const LaneOffsets<float>& o,
+                                         uint32_t extra, float2 (&k)[8]) {
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
-        const float4 f = *reinterpret_cast<const float4*>(buf + swz128(lin + 16u * c));
+        const float4 f = *reinterpret_cast<const float4*>(buf + o.k[c] + extra);
         k[2 * c] = make_float2(f.x, f.y);
         k[2 * c + 1] = make_float2(f.z, f.w);
     }
 }
 
-// V row `r`: dims 2*lane, 2*lane+1.
-__device__ __forceinline__ float2 load_vword(const uint8_t* buf, int r, int lane,
-                                             const __nv_bfloat16*) {
-    const uint32_t lin = static_cast<uint32_t>(r) * 128u + static_cast<uint32_t>(lane) * 4u;
-    return bf16x2_to_float2(*reinterpret_cast<const uint32_t*>(buf + swz128(lin)));
+__device__ __forceinline__ float2 load_v(const uint8_t* buf, const LaneOffsets<__nv_bfloat16>& o, int t) {
+    return bf16x2_to_float2(*reinterpret_cast<const uint32_t*>(buf + o.vaddr(t)));
 }
-__device__ __forceinline__ float2 load_vword(const uint8_t* buf, int r, int lane, const float*) {
-    const uint32_t lin = static_cast<uint32_t>(r) * 256u + static_cast<uint32_t>(lane) * 8u;
-    return *reinterpret_cast<const float2*>(buf + swz128(lin));
+__device__ __forceinline__ float2 load_v(const uint8_t* buf, const LaneOffsets<float>& o, int t) {
+    return *reinterpret_cast<const float2*>(buf + o.vaddr(t));
 }
 
-// One page of one kv head, keys [8*half, 8*half+8) of the page; keys
-// [t0, t1) of the page are valid.  Lane (j = lane/4, qd = lane%4) scores key
-// 8*half + j over dims [16qd, 16qd+16); for PV the lane owns output dims
-// 2*lane, 2*lane+1 over the warp's 8 keys.
-template <typename T, int NKV, int G>
-__device__ __forceinline__ void page_step(const uint8_t* buf, int h, int half, int lane, int t0,
-                                          int t1, const float2 (&q2)[G][8], float2 (&o2)[G],
-                                          float (&lp)[G], float (&M)[G], float* pb) {
+// Warp-wide max in one instruction (sm_100a redux.sync on f32).
+__device__ __forceinline__ float warp_max(float x) {
+    float r;
+    asm volatile("redux.sync.max.f32 %0, %1, 0xffffffff;" : "=f"(r) : "f"(x));
+    return r;
+}
+
+// 2^x; 2^-inf = +0.  Scores are already in log2 units.
+__device__ __forceinline__ float ex2(float x) {
+    float r;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+    return r;
+}
+
+// One page (16 keys) of one kv head; keys [t0, t1) of the page are valid
+// (all of them when kMasked is false).  Lane (j, qd) scores keys j and j+8
+// over dims [16qd, 16qd+16) and reduces over the 4 lanes of a key by
+// shuffles; the page max is one redux; p goes to shared memory as (p, p)
+// pairs; for PV the lane owns output dims 2*lane, 2*lane+1 over all 16 keys.
+template <typename T, int G, bool kMasked>
+__device__ __forceinline__ void page_step(const uint8_t* buf, const LaneOffsets<T>& lo, int lane,
+                                          int t0, int t1, const float2 (&q2)[G][8],
+                                          float2 (&o2)[G], float (&lp)[G], float (&M)[G],
+                                          float2* pb) {
     const int j = lane >> 2, qd = lane & 3;
-    const int tk = half * 8 + j;
-    float2 kv[8];
-    load_krow(buf, h * kPageTokens + tk, qd, kv, static_cast<const T*>(nullptr));
-    float sc[G];
+    float sa[G], sb[G];
+    {
+        float2 kv[8];
+        load_key(buf, lo, 0, kv);
 #pragma unroll
-    for (int g = 0; g < G; ++g) {
-        float2 acc = make_float2(0.f, 0.f);
+        for (int g = 0; g < G; ++g) {
+            float2 acc = make_float2(0.f, 0.f);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) acc = __ffma2_rn(q2[g][i], kv[i], acc);
-        sc[g] = acc.x + acc.y;
-    }
+            for (int i = 0; i < 8; ++i) acc = __ffma2_rn(q2[g][i], kv[i], acc);
+            sa[g] = acc.x + acc.y;
+        }
+        load_key(buf, lo, LaneOffsets<T>::kKey8, kv);
 #pragma unroll
-    for (int g = 0; g < G; ++g) {
-        sc[g] += __shfl_xor_sync(~0u, sc[g], 1);
-        sc[g] += __shfl_xor_sync(~0u, sc[g], 2);
-    }
-    const bool valid = tk >= t0 && tk < t1;
+        for (int g = 0; g < G; ++g) {
+            float2 acc = make_float2(0.f, 0.f);
 #pragma unroll
-    for (int g = 0; g < G; ++g) {
-        const float x = valid ? sc[g] : -INFINITY;
-        float pm = x;
-        pm = fmaxf(pm, __shfl_xor_sync(~0u, pm, 4));
-        pm = fmaxf(pm, __shfl_xor_sync(~0u, pm, 8));
-        pm = fmaxf(pm, __shfl_xor_sync(~0u, pm, 16));
-        const float mn = fmaxf(M[g], pm);
-        const float mu = (mn == -INFINITY) ? 0.f : mn;
-        const float alpha = exp2f(M[g] - mu);
-        const float p = exp2f(x - mu);
-        lp[g] = lp[g] * alpha + (qd == 0 ? p : 0.f);
-        o2[g] = __fmul2_rn(o2[g], make_float2(alpha, alpha));
-        M[g] = mn;
-        if (qd == 0) pb[g * 8 + j] = p;
-    }
-    __syncwarp();
-    const int vrow = (NKV + h) * kPageTokens + half * 8;
-    const bool full_half = (t0 <= half * 8 && t1 >= half * 8 + 8);
-#pragma unroll
-    for (int t4 = 0; t4 < 2; ++t4) {
-        float4 pq[G];
-#pragma unroll
-        for (int g = 0; g < G; ++g) pq[g] = *reinterpret_cast<const float4*>(pb + g * 8 + 4 * t4);
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-            const int t = 4 * t4 + u;
-            float2 v = load_vword(buf, vrow + t, lane, static_cast<const T*>(nullptr));
-            // Slots outside [t0, t1) may hold another sequence's stale values:
-            // zero them so 0 * (inf or nan) cannot leak into the sum.
-            if (!full_half && (half * 8 + t < t0 || half * 8 + t >= t1)) v = make_float2(0.f, 0.f);
-#pragma unroll
-            for (int g = 0; g < G; ++g) {
-                const float pv = u == 0 ? pq[g].x : u == 1 ? pq[g].y : u == 2 ? pq[g].z : pq[g].w;
-                o2[g] = __ffma2_rn(make_float2(pv, pv), v, o2[g]);
-            }
+            for (int i = 0; i < 8; ++i) acc = __ffma2_rn(q2[g][i], kv[i], acc);
+            sb[g] = acc.x + acc.y;
         }
     }
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        sa[g] += __shfl_xor_sync(~0u, sa[g], 1);
+        sb[g] += __shfl_xor_sync(~0u, sb[g], 1);
+        sa[g] += __shfl_xor_sync(~0u, sa[g], 2);
+        sb[g] += __shfl_xor_sync(~0u, sb[g], 2);
+    }
+    bool va = true, vb = true;
+    if constexpr (kMasked) {
+        va = j >= t0 && j < t1;
+        vb = j + 8 >= t0 && j + 8 < t1;
+    }
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        const float xa = va ? sa[g] : -INFINITY;
+        const float xb = vb ? sb[g] : -INFINITY;
+        const float mn = fmaxf(M[g], warp_max(fmaxf(xa, xb)));
+        const float mu = (mn == -INFINITY) ? 0.f : mn;
+        const float alpha = ex2(M[g] - mu);
+        const float pa = ex2(xa - mu);
+        const float pbv = ex2(xb - mu);
+        lp[g] = fmaf(lp[g], alpha, qd == 0 ? pa + pbv : 0.f);
+        o2[g].x *= alpha;
+        o2[g].y *= alpha;
+        M[g] = mn;
+        if (qd == 0) {
+            pb[g * 16 + j] = make_float2(pa, pa);
+            pb[g * 16 + j + 8] = make_float2(pbv, pbv);
+        }
+    }
+    __syncwarp();
+#pragma unroll
+    for (int t2 = 0; t2 < kPageTokens / 2; ++t2) {
+        float2 v0 = load_v(buf, lo, 2 * t2);
+        float2 v1 = load_v(buf, lo, 2 * t2 + 1);
+        if constexpr (kMasked) {
+            // Slots outside [t0, t1) may hold another sequence's stale values:
+            // zero them so 0 * (inf or nan) cannot leak into the sum.
+            if (2 * t2 < t0 || 2 * t2 >= t1) v0 = make_float2(0.f, 0.f);
+            if (2 * t2 + 1 < t0 || 2 * t2 + 1 >= t1) v1 = make_float2(0.f, 0.f);
+        }
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            const float4 p = *reinterpret_cast<const float4*>(pb + g * 16 + 2 * t2);
+            o2[g] = __ffma2_rn(make_float2(p.x, p.y), v0, o2[g]);
+            o2[g] = __ffma2_rn(make_float2(p.z, p.w), v1, o2[g]);
+        }
+    }
+    __syncwarp();  // pb is rewritten by this warp's next page
 }
 
-// Two warps per kv head (one per half page); warp 0 also issues the loads.
+// Two warps per kv head, taking alternate pages; warp 0 also issues the loads.
 template <typename T, int NKV, int G, int STAGES>
 struct DecodeShape {
     using Geo = Geom<T, NKV>;
@@ -250,7 +313,7 @@ struct DecodeShape {
     static size_t smem_bytes(int max_seqs) {
         return 1024 + static_cast<size_t>(STAGES) * Geo::kPageBytes   // page ring
                + 2 * STAGES * 8                                         // full/empty barriers
-               + static_cast<size_t>(kConsumers) * 2 * G * 8 * 4        // p buffers
+               + static_cast<size_t>(kConsumers) * G * 16 * 8           // (p, p) buffers
                + static_cast<size_t>(NKV) * G * (kHeadDim + 2) * 4      // half-merge buffers
                + 16 + (static_cast<size_t>(max_seqs) + 1) * 4;          // misc + page scan
     }
@@ -261,15 +324,15 @@ __global__ void __launch_bounds__(DecodeShape<T, NKV, G, STAGES>::kThreads, 1)
 decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeArgs a) {
     using Geo = Geom<T, NKV>;
     constexpr int NQ = NKV * G;
-    constexpr int NCW = 2 * NKV;  // consumer warps
+    constexpr int NCW = 2 * NKV;  // warps
     constexpr int NCONS = NCW * 32;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* stage = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
     uint64_t* full = reinterpret_cast<uint64_t*>(stage + STAGES * Geo::kPageBytes);
     uint64_t* empty = full + STAGES;
-    float* pbuf = reinterpret_cast<float*>(empty + STAGES);  // [NCW][2][G][8]
-    float* xbuf = pbuf + NCW * 2 * G * 8;                    // [NKV][G][64 + 2]
+    float2* pbuf = reinterpret_cast<float2*>(empty + STAGES);  // [NCW][G][16]
+    float* xbuf = reinterpret_cast<float*>(pbuf + NCW * G * 16);  // [NKV][G][64 + 2]
     int* misc = reinterpret_cast<int*>(xbuf + NKV * G * (kHeadDim + 2));  // [0] counter, [1] abort
     int* pstart = misc + 4;                                               // [n_seqs + 1]
 
@@ -279,7 +342,7 @@ decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeArgs a) {
     if (threadIdx.x == 32) {
         for (int i = 0; i < STAGES; ++i) {
             mbar_init(&full[i], 1);
-            mbar_init(&empty[i], NCW);
+            mbar_init(&empty[i], NKV);  // each page is consumed by one warp per kv head
         }
         fence_mbar_init();
         prefetch_tmap(&tmap);
@@ -308,12 +371,10 @@ decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeArgs a) {
 
     const int total = pstart[n];
     const int grid = gridDim.x, cta = blockIdx.x;
-    if (threadIdx.x < NCONS) {  // sequences with no tokens: zeros
-        for (int s = cta; s < n; s += grid) {
-            if (__ldg(a.seq_lens + s) <= 0) {
-                T* o = static_cast<T*>(a.out) + static_cast<size_t>(s) * NQ * kHeadDim;
-                for (int i = threadIdx.x; i < NQ * kHeadDim; i += NCONS) o[i] = to_elem<T>(0.f);
-            }
+    for (int s = cta; s < n; s += grid) {  // sequences with no tokens: zeros
+        if (__ldg(a.seq_lens + s) <= 0) {
+            T* o = static_cast<T*>(a.out) + static_cast<size_t>(s) * NQ * kHeadDim;
+            for (int i = threadIdx.x; i < NQ * kHeadDim; i += NCONS) o[i] = to_elem<T>(0.f);
         }
     }
     const int gb = static_cast<int>((static_cast<long long>(cta) * total) / grid);
@@ -374,17 +435,17 @@ decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeArgs a) {
     };
     if (warp == 0) issue_upto(STAGES);
 
-    // ------- consumer warps: warp w owns kv head w/2, keys of half w%2 -------
+    // ---- consumers: warp w owns kv head w/2 and the slice pages of parity w%2 ----
     const int h = warp >> 1, half = warp & 1;
     const int qd = lane & 3;
-    float* my_pb = pbuf + warp * (2 * G * 8);
+    const LaneOffsets<T> lofs(h, lane, NKV);
+    float2* my_pb = pbuf + warp * (G * 16);
     float* my_x = xbuf + h * G * (kHeadDim + 2);
     float2 q2[G][8];
     float2 o2[G];
     float lp[G], M[G];
     int s = find_seq(pstart, n, gb);
     int g = gb;
-    int k = 0;
     while (g < ge) {
         const int nt = __ldg(a.seq_lens + s);
         const int lo = seq_lo(nt, a.window);
@@ -403,21 +464,25 @@ decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeArgs a) {
             lp[gg] = 0.f;
             M[gg] = -INFINITY;
         }
-        for (; g < seg_end; ++g, ++k) {
+        for (; g < seg_end; ++g) {
+            const int k = g - gb;
             if (warp == 0) issue_upto(k + STAGES);
+            if ((k & 1) != half) continue;
             const int st = k % STAGES;
             const uint32_t par = static_cast<uint32_t>(k / STAGES) & 1u;
             if (wait_or_abort(&full[st], par, abort_flag, a.err)) {
+                const uint8_t* buf = stage + st * Geo::kPageBytes;
                 const int pg = plo + (g - s_begin);
                 const int t0 = max(lo - pg * kPageTokens, 0);
                 const int t1 = min(nt - pg * kPageTokens, kPageTokens);
-                page_step<T, NKV, G>(stage + st * Geo::kPageBytes, h, half, lane, t0, t1, q2, o2,
-                                     lp, M, my_pb + (k & 1) * G * 8);
+                if (t0 == 0 && t1 == kPageTokens)
+                    page_step<T, G, false>(buf, lofs, lane, t0, t1, q2, o2, lp, M, my_pb);
+                else
+                    page_step<T, G, true>(buf, lofs, lane, t0, t1, q2, o2, lp, M, my_pb);
             }
-            __syncwarp();
             if (lane == 0) mbar_arrive(&empty[st]);
         }
-        // ---- flush sequence s: lane sums, then merge the two half-page warps ----
+        // ---- flush sequence s: lane sums, then merge the two warps of a head ----
 #pragma unroll
         for (int gg = 0; gg < G; ++gg) {
             float t = lp[gg];
@@ -447,9 +512,9 @@ decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeArgs a) {
                 const float lx = my_x[gg * (kHeadDim + 2) + kHeadDim + 1];
                 const float mn = fmaxf(M[gg], mx);
                 const float mu = (mn == -INFINITY) ? 0.f : mn;
-                const float wa = exp2f(M[gg] - mu), wb = exp2f(mx - mu);
+                const float wa = ex2(M[gg] - mu), wb = ex2(mx - mu);
                 lp[gg] = lp[gg] * wa + lx * wb;
-                o2[gg] = __ffma2_rn(ox, make_float2(wb, wb), __fmul2_rn(o2[gg], make_float2(wa, wa)));
+                o2[gg] = make_float2(fmaf(ox.x, wb, o2[gg].x * wa), fmaf(ox.y, wb, o2[gg].y * wa));
                 M[gg] = mn;
             }
         }
@@ -500,7 +565,7 @@ decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeArgs a) {
                     for (int c = c_first; c <= c_last; ++c) {
                         const int sl = (c == c_first) ? 2 * c + 1 : 2 * c;
                         const size_t row = static_cast<size_t>(sl) * NQ + qh;
-                        const float w = exp2f(__ldcg(a.part_ml + row * 2) - mu);
+                        const float w = ex2(__ldcg(a.part_ml + row * 2) - mu);
                         L = fmaf(__ldcg(a.part_ml + row * 2 + 1), w, L);
                         O = fmaf(__ldcg(a.part_o + row * kHeadDim + dd), w, O);
                     }
@@ -520,7 +585,6 @@ decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeArgs a) {
             mbar_wait(&full[kk % STAGES], static_cast<uint32_t>(kk / STAGES) & 1u);
     }
 }
-
 // ---------------------------------------------------------------------------
 // Host side: one entry per compiled (dtype, n_kv, group) shape.
 struct DecodeVariant {

@@ -116,6 +116,29 @@ class DecodeCase:
         return np.sort(ids)
 
 
+def truth_decode(host, bt, seq_lens, window, q_raw, dtype: str) -> np.ndarray:
+    """float64 decode attention on the oracle's stored pages (q rotated by the
+    oracle in fp32, as the kernels do), to measure how far each fp32 path is
+    from exact arithmetic."""
+    n = len(seq_lens)
+    out = np.empty((n, host.n_q, host.d), np.float64)
+    g = host.n_q // host.n_kv
+    for s in range(n):
+        L = int(seq_lens[s])
+        k, v = host.gather(bt[s], L)
+        q = (O.bf16_bits_to_f32(q_raw[s]) if dtype == "bf16" else np.asarray(q_raw[s], np.float32)).copy()
+        c, sn = O.cos_sin(host.inv, L - 1, 1, host.d)
+        O.apply_rope_in_place(q, c, sn, host.n_q, 1, host.d)
+        lo = max(L - window, 0) if window else 0
+        for h in range(host.n_q):
+            kk = k[h // g, lo:L].astype(np.float64)
+            vv = v[h // g, lo:L].astype(np.float64)
+            sc = kk @ q[h].astype(np.float64) / np.sqrt(host.d)
+            w = np.exp(sc - sc.max())
+            out[s, h] = (w / w.sum()) @ vv
+    return out
+
+
 def assert_close_rows(got: np.ndarray, ref: np.ndarray, rtol: float, what: str = "") -> float:
     """Normwise per-row check: max|got-ref| <= rtol * max|ref| for every row."""
     got = np.asarray(got, np.float64).reshape(-1, ref.shape[-1])
