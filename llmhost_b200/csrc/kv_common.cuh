@@ -69,14 +69,20 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
                  : "memory");
 }
 
+// Test whether the phase with the given parity has completed.  The waiting
+// thread may be suspended by the hardware for up to kSuspendHintNs (it wakes
+// as soon as the phase completes), so a waiting warp does not spin on the
+// issue slots that computing warps need.
+constexpr uint32_t kSuspendHintNs = 1000000u;
+
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
+        "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(ok)
-        : "r"(smem_addr(bar)), "r"(parity)
+        : "r"(smem_addr(bar)), "r"(parity), "r"(kSuspendHintNs)
         : "memory");
     return ok != 0;
 }
@@ -86,9 +92,9 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = global_timer_ns();
-    for (uint32_t i = 1;; ++i) {
+    for (;;) {
         if (mbar_try_wait(bar, parity)) return true;
-        if ((i & 127u) == 0 && global_timer_ns() - t0 > kWaitLimitNs) return false;
+        if (global_timer_ns() - t0 > kWaitLimitNs) return false;
     }
 }
 

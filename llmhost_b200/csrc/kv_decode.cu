@@ -90,17 +90,14 @@ __device__ __forceinline__ int cta_of(int x, int grid, int total) {
 __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity,
                                               volatile int* abort_flag, int* err) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (*abort_flag) return false;
     const uint64_t t0 = global_timer_ns();
-    for (uint32_t i = 1;; ++i) {
+    for (;;) {
+        if (*abort_flag) return false;
         if (mbar_try_wait(bar, parity)) return true;
-        if ((i & 127u) == 0) {
-            if (*abort_flag) return false;
-            if (global_timer_ns() - t0 > kWaitLimitNs) {
-                *abort_flag = 1;
-                flag_error(err, kDevErrTimeout);
-                return false;
-            }
+        if (global_timer_ns() - t0 > kWaitLimitNs) {
+            *abort_flag = 1;
+            flag_error(err, kDevErrTimeout);
+            return false;
         }
     }
 }
@@ -147,8 +144,9 @@ __device__ __forceinline__ void load_q(const DecodeArgs& a, int s, int nq, int h
 // 128-byte row R lands at chunk c ^ (R & 7).  The offsets below fold that in
 // once per lane.  K: lane (j = lane/4, qd = lane%4) reads key j of its head,
 // dims [16qd, 16qd+16); key j+8 sits kKey8 bytes further with the same
-// swizzle.  V: lane reads dims 2*lane, 2*lane+1 of key t at vaddr(t), an XOR
-// with a compile-time constant plus an immediate offset.
+// swizzle.  V: lane (kh = lane/16, dg = lane%16) reads dims [4dg, 4dg+4) of
+// key 8kh+t at vaddr(t), an XOR with a compile-time constant plus an
+// immediate offset.
 template <typename T> struct LaneOffsets;
 
 template <> struct LaneOffsets<__nv_bfloat16> {
@@ -160,9 +158,11 @@ template <> struct LaneOffsets<__nv_bfloat16> {
         const uint32_t row = h * kPageTokens + j;
         k[0] = row * 128 + (((2 * qd) ^ j) << 4);
         k[1] = row * 128 + (((2 * qd + 1) ^ j) << 4);
-        v = (nkv + h) * kPageTokens * 128 + ((lane >> 2) << 4) + (lane & 3) * 4;
+        const uint32_t kh = lane >> 4, dg = lane & 15;
+        v = ((nkv + h) * kPageTokens + 8 * kh) * 128 + ((dg >> 1) << 4) + (dg & 1) * 8;
     }
-    __device__ __forceinline__ uint32_t vaddr(int t) const { return (v ^ ((t & 7) << 4)) + t * 128; }
+    // key 8kh + t, t in [0, 8): row & 7 == t
+    __device__ __forceinline__ uint32_t vaddr(int t) const { return (v ^ (t << 4)) + t * 128; }
 };
 
 template <> struct LaneOffsets<float> {
@@ -174,8 +174,11 @@ template <> struct LaneOffsets<float> {
         const uint32_t R = (h * kPageTokens + j) * 2 + (qd >> 1);
 #pragma unroll
         for (int c = 0; c < 4; ++c) k[c] = R * 128 + ((((qd & 1) * 4 + c) ^ (R & 7)) << 4);
-        const uint32_t b = lane >> 4;
-        v = (nkv + h) * kPageTokens * 256 + b * 128 + (((((lane >> 1) & 7) ^ b)) << 4) + (lane & 1) * 8;
+        // dims [4dg, 4dg+4) of key row r = 16 bytes at r*256 + 16dg: 128-byte
+        // row 2r + dg/8, chunk dg%8, and (2r + dg/8) & 7 = 2t + dg/8 for
+        // r = 8kh + t (+ multiples of 16).
+        const uint32_t kh = lane >> 4, dg = lane & 15, b = dg >> 3;
+        v = ((nkv + h) * kPageTokens + 8 * kh) * 256 + b * 128 + (((dg & 7) ^ b) << 4);
     }
     __device__ __forceinline__ uint32_t vaddr(int t) const {
         return (v ^ (((2 * t) & 7) << 4)) + t * 256;
@@ -201,11 +204,18 @@ __device__ __forceinline__ void load_key(const uint8_t* buf, const LaneOffsets<f
     }
 }
 
-__device__ __forceinline__ float2 load_v(const uint8_t* buf, const LaneOffsets<__nv_bfloat16>& o, int t) {
-    return bf16x2_to_float2(*reinterpret_cast<const uint32_t*>(buf + o.vaddr(t)));
+// V of one key, the lane's 4 dims, as two float2.
+__device__ __forceinline__ void load_v(const uint8_t* buf, const LaneOffsets<__nv_bfloat16>& o, int t,
+                                       float2& v0, float2& v1) {
+    const uint2 w = *reinterpret_cast<const uint2*>(buf + o.vaddr(t));
+    v0 = bf16x2_to_float2(w.x);
+    v1 = bf16x2_to_float2(w.y);
 }
-__device__ __forceinline__ float2 load_v(const uint8_t* buf, const LaneOffsets<float>& o, int t) {
-    return *reinterpret_cast<const float2*>(buf + o.vaddr(t));
+__device__ __forceinline__ void load_v(const uint8_t* buf, const LaneOffsets<float>& o, int t,
+                                       float2& v0, float2& v1) {
+    const float4 f = *reinterpret_cast<const float4*>(buf + o.vaddr(t));
+    v0 = make_float2(f.x, f.y);
+    v1 = make_float2(f.z, f.w);
 }
 
 // Warp-wide max in one instruction (sm_100a redux.sync on f32).
@@ -223,14 +233,15 @@ __device__ __forceinline__ float ex2(float x) {
 }
 
 // One page (16 keys) of one kv head; keys [t0, t1) of the page are valid
-// (all of them when kMasked is false).  Lane (j, qd) scores keys j and j+8
-// over dims [16qd, 16qd+16) and reduces over the 4 lanes of a key by
+// (all of them when kMasked is false).  QK: lane (j, qd) scores keys j and
+// j+8 over dims [16qd, 16qd+16) and reduces over the 4 lanes of a key by
 // shuffles; the page max is one redux; p goes to shared memory as (p, p)
-// pairs; for PV the lane owns output dims 2*lane, 2*lane+1 over all 16 keys.
+// pairs.  PV: lane (kh, dg) accumulates dims [4dg, 4dg+4) over keys
+// [8kh, 8kh+8); the two key halves are merged when the sequence is flushed.
 template <typename T, int G, bool kMasked>
 __device__ __forceinline__ void page_step(const uint8_t* buf, const LaneOffsets<T>& lo, int lane,
                                           int t0, int t1, const float2 (&q2)[G][8],
-                                          float2 (&o2)[G], float (&lp)[G], float (&M)[G],
+                                          float2 (&o2)[G][2], float (&lp)[G], float (&M)[G],
                                           float2* pb) {
     const int j = lane >> 2, qd = lane & 3;
     float sa[G], sb[G];
@@ -270,13 +281,14 @@ __device__ __forceinline__ void page_step(const uint8_t* buf, const LaneOffsets<
         const float xa = va ? sa[g] : -INFINITY;
         const float xb = vb ? sb[g] : -INFINITY;
         const float mn = fmaxf(M[g], warp_max(fmaxf(xa, xb)));
-        const float mu = (mn == -INFINITY) ? 0.f : mn;
+        // A full page always holds a finite score; a masked one may not.
+        const float mu = (kMasked && mn == -INFINITY) ? 0.f : mn;
         const float alpha = ex2(M[g] - mu);
         const float pa = ex2(xa - mu);
         const float pbv = ex2(xb - mu);
         lp[g] = fmaf(lp[g], alpha, qd == 0 ? pa + pbv : 0.f);
-        o2[g].x *= alpha;
-        o2[g].y *= alpha;
+        o2[g][0] = __fmul2_rn(o2[g][0], make_float2(alpha, alpha));
+        o2[g][1] = __fmul2_rn(o2[g][1], make_float2(alpha, alpha));
         M[g] = mn;
         if (qd == 0) {
             pb[g * 16 + j] = make_float2(pa, pa);
@@ -284,21 +296,33 @@ __device__ __forceinline__ void page_step(const uint8_t* buf, const LaneOffsets<
         }
     }
     __syncwarp();
+    const int kh = lane >> 4;
 #pragma unroll
-    for (int t2 = 0; t2 < kPageTokens / 2; ++t2) {
-        float2 v0 = load_v(buf, lo, 2 * t2);
-        float2 v1 = load_v(buf, lo, 2 * t2 + 1);
-        if constexpr (kMasked) {
-            // Slots outside [t0, t1) may hold another sequence's stale values:
-            // zero them so 0 * (inf or nan) cannot leak into the sum.
-            if (2 * t2 < t0 || 2 * t2 >= t1) v0 = make_float2(0.f, 0.f);
-            if (2 * t2 + 1 < t0 || 2 * t2 + 1 >= t1) v1 = make_float2(0.f, 0.f);
-        }
+    for (int t2 = 0; t2 < 4; ++t2) {
+        float4 pq[G];
 #pragma unroll
-        for (int g = 0; g < G; ++g) {
-            const float4 p = *reinterpret_cast<const float4*>(pb + g * 16 + 2 * t2);
-            o2[g] = __ffma2_rn(make_float2(p.x, p.y), v0, o2[g]);
-            o2[g] = __ffma2_rn(make_float2(p.z, p.w), v1, o2[g]);
+        for (int g = 0; g < G; ++g)
+            pq[g] = *reinterpret_cast<const float4*>(pb + g * 16 + 8 * kh + 2 * t2);
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+            const int t = 2 * t2 + u;
+            float2 v0, v1;
+            load_v(buf, lo, t, v0, v1);
+            if constexpr (kMasked) {
+                // Slots outside [t0, t1) may hold another sequence's stale
+                // values: zero them so 0 * (inf or nan) cannot leak in.
+                const int key = 8 * kh + t;
+                if (key < t0 || key >= t1) {
+                    v0 = make_float2(0.f, 0.f);
+                    v1 = make_float2(0.f, 0.f);
+                }
+            }
+#pragma unroll
+            for (int g = 0; g < G; ++g) {
+                const float2 pp = u == 0 ? make_float2(pq[g].x, pq[g].y) : make_float2(pq[g].z, pq[g].w);
+                o2[g][0] = __ffma2_rn(pp, v0, o2[g][0]);
+                o2[g][1] = __ffma2_rn(pp, v1, o2[g][1]);
+            }
         }
     }
     __syncwarp();  // pb is rewritten by this warp's next page
@@ -307,6 +331,11 @@ __device__ __forceinline__ void page_step(const uint8_t* buf, const LaneOffsets<
 // Two warps per kv head, taking alternate pages; warp 0 also issues the loads.
 template <typename T, int NKV, int G, int STAGES>
 struct DecodeShape {
+    // Warps alternate pages by parity, and a stage's successive pages must
+    // have the same parity: the warps that wait on a stage's next phase then
+    // have seen its previous one, so a parity wait can never pass on a stale
+    // phase.  Hence an even number of stages.
+    static_assert(STAGES % 2 == 0, "the page ring must have an even number of stages");
     using Geo = Geom<T, NKV>;
     static constexpr int kConsumers = 2 * NKV;
     static constexpr int kThreads = kConsumers * 32;
@@ -314,7 +343,7 @@ struct DecodeShape {
         return 1024 + static_cast<size_t>(STAGES) * Geo::kPageBytes   // page ring
                + 2 * STAGES * 8                                         // full/empty barriers
                + static_cast<size_t>(kConsumers) * G * 16 * 8           // (p, p) buffers
-               + static_cast<size_t>(NKV) * G * (kHeadDim + 2) * 4      // half-merge buffers
+               + static_cast<size_t>(NKV) * G * (kHeadDim + 4) * 4      // half-merge buffers
                + 16 + (static_cast<size_t>(max_seqs) + 1) * 4;          // misc + page scan
     }
 };
@@ -332,8 +361,8 @@ decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeArgs a) {
     uint64_t* full = reinterpret_cast<uint64_t*>(stage + STAGES * Geo::kPageBytes);
     uint64_t* empty = full + STAGES;
     float2* pbuf = reinterpret_cast<float2*>(empty + STAGES);  // [NCW][G][16]
-    float* xbuf = reinterpret_cast<float*>(pbuf + NCW * G * 16);  // [NKV][G][64 + 2]
-    int* misc = reinterpret_cast<int*>(xbuf + NKV * G * (kHeadDim + 2));  // [0] counter, [1] abort
+    float* xbuf = reinterpret_cast<float*>(pbuf + NCW * G * 16);  // [NKV][G][64 + 4]
+    int* misc = reinterpret_cast<int*>(xbuf + NKV * G * (kHeadDim + 4));  // [0] counter, [1] abort
     int* pstart = misc + 4;                                               // [n_seqs + 1]
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -440,9 +469,9 @@ decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeArgs a) {
     const int qd = lane & 3;
     const LaneOffsets<T> lofs(h, lane, NKV);
     float2* my_pb = pbuf + warp * (G * 16);
-    float* my_x = xbuf + h * G * (kHeadDim + 2);
+    float* my_x = xbuf + h * G * (kHeadDim + 4);
     float2 q2[G][8];
-    float2 o2[G];
+    float2 o2[G][2];
     float lp[G], M[G];
     int s = find_seq(pstart, n, gb);
     int g = gb;
@@ -460,29 +489,37 @@ decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeArgs a) {
         load_q<T, G>(a, s, NQ, h, qd, pos, q2);
 #pragma unroll
         for (int gg = 0; gg < G; ++gg) {
-            o2[gg] = make_float2(0.f, 0.f);
+            o2[gg][0] = o2[gg][1] = make_float2(0.f, 0.f);
             lp[gg] = 0.f;
             M[gg] = -INFINITY;
         }
-        for (; g < seg_end; ++g) {
-            const int k = g - gb;
+        // This warp's pages of the segment: slice page k = g - gb with k % 2 == half.
+        for (int gw = g + (((g - gb) & 1) ^ half); gw < seg_end; gw += 2) {
+            const int k = gw - gb;
+            // Up to page k + STAGES - 1: it reuses the stage of page k - 1,
+            // never the stage of page k that this warp is about to read.
             if (warp == 0) issue_upto(k + STAGES);
-            if ((k & 1) != half) continue;
             const int st = k % STAGES;
             const uint32_t par = static_cast<uint32_t>(k / STAGES) & 1u;
-            if (wait_or_abort(&full[st], par, abort_flag, a.err)) {
-                const uint8_t* buf = stage + st * Geo::kPageBytes;
-                const int pg = plo + (g - s_begin);
-                const int t0 = max(lo - pg * kPageTokens, 0);
-                const int t1 = min(nt - pg * kPageTokens, kPageTokens);
-                if (t0 == 0 && t1 == kPageTokens)
-                    page_step<T, G, false>(buf, lofs, lane, t0, t1, q2, o2, lp, M, my_pb);
-                else
-                    page_step<T, G, true>(buf, lofs, lane, t0, t1, q2, o2, lp, M, my_pb);
-            }
+            // A failed wait (timeout or abort) keeps the stage: it is never
+            // handed back, so no copy can be issued over one still landing.
+            if (!wait_or_abort(&full[st], par, abort_flag, a.err)) continue;
+            const uint8_t* buf = stage + st * Geo::kPageBytes;
+            const int pg = plo + (gw - s_begin);
+            const int t0 = max(lo - pg * kPageTokens, 0);
+            const int t1 = min(nt - pg * kPageTokens, kPageTokens);
+            if (t0 == 0 && t1 == kPageTokens)
+                page_step<T, G, false>(buf, lofs, lane, t0, t1, q2, o2, lp, M, my_pb);
+            else
+                page_step<T, G, true>(buf, lofs, lane, t0, t1, q2, o2, lp, M, my_pb);
             if (lane == 0) mbar_arrive(&empty[st]);
         }
-        // ---- flush sequence s: lane sums, then merge the two warps of a head ----
+        // Keep the ring full across the flush below; the pages this waits on
+        // are released by the other warps before they reach the flush.
+        if (warp == 0) issue_upto(seg_end - gb + STAGES - 1);
+        g = seg_end;
+        // ---- flush sequence s: sum lane partials, merge the key halves
+        // (lanes l and l^16 hold the same dims), then the two warps of a head.
 #pragma unroll
         for (int gg = 0; gg < G; ++gg) {
             float t = lp[gg];
@@ -492,14 +529,21 @@ decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeArgs a) {
             t += __shfl_xor_sync(~0u, t, 2);
             t += __shfl_xor_sync(~0u, t, 1);
             lp[gg] = t;
+#pragma unroll
+            for (int c = 0; c < 2; ++c) {
+                o2[gg][c].x += __shfl_xor_sync(~0u, o2[gg][c].x, 16);
+                o2[gg][c].y += __shfl_xor_sync(~0u, o2[gg][c].y, 16);
+            }
         }
-        if (half == 1) {
+        const int dg = lane & 15;
+        if (half == 1 && lane < 16) {
 #pragma unroll
             for (int gg = 0; gg < G; ++gg) {
-                *reinterpret_cast<float2*>(my_x + gg * (kHeadDim + 2) + 2 * lane) = o2[gg];
+                *reinterpret_cast<float4*>(my_x + gg * (kHeadDim + 4) + 4 * dg) =
+                    make_float4(o2[gg][0].x, o2[gg][0].y, o2[gg][1].x, o2[gg][1].y);
                 if (lane == 0) {
-                    my_x[gg * (kHeadDim + 2) + kHeadDim] = M[gg];
-                    my_x[gg * (kHeadDim + 2) + kHeadDim + 1] = lp[gg];
+                    my_x[gg * (kHeadDim + 4) + kHeadDim] = M[gg];
+                    my_x[gg * (kHeadDim + 4) + kHeadDim + 1] = lp[gg];
                 }
             }
         }
@@ -507,40 +551,45 @@ decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeArgs a) {
         if (half == 0) {
 #pragma unroll
             for (int gg = 0; gg < G; ++gg) {
-                const float2 ox = *reinterpret_cast<const float2*>(my_x + gg * (kHeadDim + 2) + 2 * lane);
-                const float mx = my_x[gg * (kHeadDim + 2) + kHeadDim];
-                const float lx = my_x[gg * (kHeadDim + 2) + kHeadDim + 1];
+                const float4 ox = *reinterpret_cast<const float4*>(my_x + gg * (kHeadDim + 4) + 4 * dg);
+                const float mx = my_x[gg * (kHeadDim + 4) + kHeadDim];
+                const float lx = my_x[gg * (kHeadDim + 4) + kHeadDim + 1];
                 const float mn = fmaxf(M[gg], mx);
                 const float mu = (mn == -INFINITY) ? 0.f : mn;
                 const float wa = ex2(M[gg] - mu), wb = ex2(mx - mu);
                 lp[gg] = lp[gg] * wa + lx * wb;
-                o2[gg] = make_float2(fmaf(ox.x, wb, o2[gg].x * wa), fmaf(ox.y, wb, o2[gg].y * wa));
+                o2[gg][0] = make_float2(fmaf(ox.x, wb, o2[gg][0].x * wa), fmaf(ox.y, wb, o2[gg][0].y * wa));
+                o2[gg][1] = make_float2(fmaf(ox.z, wb, o2[gg][1].x * wa), fmaf(ox.w, wb, o2[gg][1].y * wa));
                 M[gg] = mn;
             }
         }
         named_bar_sync(2 + h, 64);  // xbuf is free again
         const bool whole = (s_begin >= gb) && (s_end <= ge);
+        const bool writer = (half == 0 && lane < 16);
         if (whole) {
-            if (half == 0) {
+            if (writer) {
 #pragma unroll
                 for (int gg = 0; gg < G; ++gg) {
                     const float inv = lp[gg] > 0.f ? 1.f / lp[gg] : 0.f;
                     T* orow = static_cast<T*>(a.out) +
-                              (static_cast<size_t>(s) * NQ + h * G + gg) * kHeadDim + 2 * lane;
-                    const float x = o2[gg].x * inv, y = o2[gg].y * inv;
+                              (static_cast<size_t>(s) * NQ + h * G + gg) * kHeadDim + 4 * dg;
+                    const float x0 = o2[gg][0].x * inv, x1 = o2[gg][0].y * inv;
+                    const float x2 = o2[gg][1].x * inv, x3 = o2[gg][1].y * inv;
                     if constexpr (sizeof(T) == 2)
-                        *reinterpret_cast<uint32_t*>(orow) = float2_to_bf16x2(x, y);
+                        *reinterpret_cast<uint2*>(orow) =
+                            make_uint2(float2_to_bf16x2(x0, x1), float2_to_bf16x2(x2, x3));
                     else
-                        *reinterpret_cast<float2*>(orow) = make_float2(x, y);
+                        *reinterpret_cast<float4*>(orow) = make_float4(x0, x1, x2, x3);
                 }
             }
         } else {
             const int slot = (s_begin < gb) ? 2 * cta : 2 * cta + 1;
-            if (half == 0) {
+            if (writer) {
 #pragma unroll
                 for (int gg = 0; gg < G; ++gg) {
                     const size_t row = static_cast<size_t>(slot) * NQ + h * G + gg;
-                    *reinterpret_cast<float2*>(a.part_o + row * kHeadDim + 2 * lane) = o2[gg];
+                    *reinterpret_cast<float4*>(a.part_o + row * kHeadDim + 4 * dg) =
+                        make_float4(o2[gg][0].x, o2[gg][0].y, o2[gg][1].x, o2[gg][1].y);
                     if (lane == 0)
                         *reinterpret_cast<float2*>(a.part_ml + row * 2) = make_float2(M[gg], lp[gg]);
                 }
@@ -578,11 +627,14 @@ decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeArgs a) {
         }
         if (g < ge) s = find_seq(pstart, n, g);
     }
-    // Warp 0: do not leave while a copy issued here may still be landing
-    // (only possible after an abort; otherwise every page was consumed).
+    // Warp 0: do not leave while a copy issued here may still be landing.  A
+    // stage is reused only after its previous page was handed back, so the
+    // last page issued into each stage covers every copy in flight.
     if (warp == 0 && lane == 0) {
-        for (int kk = max(0, issued - STAGES); kk < issued; ++kk)
-            mbar_wait(&full[kk % STAGES], static_cast<uint32_t>(kk / STAGES) & 1u);
+        for (int st = 0; st < STAGES && st < issued; ++st) {
+            const int last = st + ((issued - 1 - st) / STAGES) * STAGES;
+            mbar_wait(&full[st], static_cast<uint32_t>(last / STAGES) & 1u);
+        }
     }
 }
 // ---------------------------------------------------------------------------
@@ -606,8 +658,8 @@ const DecodeVariant* find_variant(int dtype, int nkv, int group) {
         make_variant<__nv_bfloat16, 8, 3, 6>(KV_DTYPE_BF16),
         make_variant<__nv_bfloat16, 8, 4, 6>(KV_DTYPE_BF16),
         make_variant<__nv_bfloat16, 1, 4, 8>(KV_DTYPE_BF16),
-        make_variant<float, 8, 3, 3>(KV_DTYPE_F32),
-        make_variant<float, 8, 4, 3>(KV_DTYPE_F32),
+        make_variant<float, 8, 3, 2>(KV_DTYPE_F32),
+        make_variant<float, 8, 4, 2>(KV_DTYPE_F32),
         make_variant<float, 1, 4, 8>(KV_DTYPE_F32),
     };
     for (const auto& v : table)
