@@ -598,20 +598,27 @@ decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeArgs a) {
             named_bar_sync(1, NCONS);
             if (threadIdx.x == 0) misc[0] = atomicAdd(a.counters + s, 1);
             named_bar_sync(1, NCONS);
+            // Contributors: the CTAs whose slice holds a page of s.  With at
+            // least one page per CTA (total >= grid) they are c_first..c_last;
+            // with fewer pages than CTAs some slices are empty and each page
+            // has a CTA of its own, so page s_begin + i belongs to contributor i.
             const int c_first = cta_of(s_begin, grid, total);
-            const int c_last = cta_of(s_end - 1, grid, total);
-            if (misc[0] == c_last - c_first) {  // last contributor merges the splits
+            const bool dense = total >= grid;
+            const int n_contrib = dense ? cta_of(s_end - 1, grid, total) - c_first + 1 : s_end - s_begin;
+            if (misc[0] == n_contrib - 1) {  // last contributor merges the splits
                 __threadfence();
                 for (int idx = threadIdx.x; idx < NQ * kHeadDim; idx += NCONS) {
                     const int qh = idx / kHeadDim, dd = idx % kHeadDim;
                     float mx = -INFINITY;
-                    for (int c = c_first; c <= c_last; ++c) {
+                    for (int i = 0; i < n_contrib; ++i) {
+                        const int c = dense ? c_first + i : cta_of(s_begin + i, grid, total);
                         const int sl = (c == c_first) ? 2 * c + 1 : 2 * c;
                         mx = fmaxf(mx, __ldcg(a.part_ml + (static_cast<size_t>(sl) * NQ + qh) * 2));
                     }
                     const float mu = (mx == -INFINITY) ? 0.f : mx;
                     float L = 0.f, O = 0.f;
-                    for (int c = c_first; c <= c_last; ++c) {
+                    for (int i = 0; i < n_contrib; ++i) {
+                        const int c = dense ? c_first + i : cta_of(s_begin + i, grid, total);
                         const int sl = (c == c_first) ? 2 * c + 1 : 2 * c;
                         const size_t row = static_cast<size_t>(sl) * NQ + qh;
                         const float w = ex2(__ldcg(a.part_ml + row * 2) - mu);

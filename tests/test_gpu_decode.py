@@ -105,6 +105,16 @@ def test_decode_sliding_window_evicted_pages(cuda, dtype):
     assert_close_rows(out, ref, RTOL[dtype], f"{dtype} window")
 
 
+@pytest.mark.parametrize("dtype", ["bf16", "f32"])
+@pytest.mark.parametrize("lens", [[1, 64, 1000], [70], [0, 3, 9, 200]])
+def test_decode_fewer_pages_than_ctas(cuda, dtype, lens):
+    # Fewer pages than CTAs in the persistent grid: some CTA slices are empty
+    # and a split sequence has one contributor per page.
+    case = DecodeCase(dtype, 24, 8, lens, seed=12)
+    out, ref = run_case(case, repeat=2)
+    assert_close_rows(out, ref, RTOL[dtype], f"{dtype} sparse {lens}")
+
+
 def test_zero_sequences_is_a_noop(cuda):
     import torch
 
