@@ -111,6 +111,34 @@ int kv_decode_attn(kv_pool *pool, const void *q, const uint32_t *block_tables, i
                    const int32_t *seq_lens, int32_t n_seqs, int32_t window, void *out,
                    void *stream);
 
+/* Decode attention for callers that cannot allocate device memory.
+ *
+ * No counterpart in the reference.  Same arithmetic and arguments as
+ * kv_decode_attn, but without a pool: some callers cannot call cudaMalloc
+ * (their device memory all comes from a fixed arena they manage, or they may
+ * not grow their footprint after start-up), so they cannot create a kv_pool.
+ * They pass every buffer themselves: the pages (pool layout, n_pages of them,
+ * dtype and head counts as in kv_pool_config), the RoPE table rope_cs
+ * (float pairs (cos, sin) for positions [0, max_positions) and frequency
+ * i < head_dim/2, as kv_pool_create builds it), q, the block tables, the
+ * lengths, out, and `status`, one device int32 that receives the device
+ * error bits of this call (1 bad page id, 2 wait timeout, 4 position out of
+ * range; 0 when clean).
+ *
+ * The call itself allocates nothing.  Its scratch is one 4 MiB array in the
+ * library's device image, held by every GPU that loads the library until
+ * exit.  Limits: n_seqs <= 1024 and n_q_heads <= 32; larger calls return
+ * KV_ERR_INVALID.  All calls on a device share that array: a call clears the
+ * part that must start at zero, but two calls whose kernels overlap on the
+ * GPU (different streams or threads) race on it, so serialise them.  The
+ * first call on a device sets up with that device current (it looks up the
+ * array's address); make that first call before any stream capture. */
+int kv_decode_attn_noalloc(const void *pages, uint32_t n_pages, int32_t dtype, int32_t n_q_heads,
+                           int32_t n_kv_heads, const void *rope_cs, int32_t max_positions,
+                           const void *q, const uint32_t *block_tables, int32_t bt_stride,
+                           const int32_t *seq_lens, int32_t n_seqs, int32_t window, void *out,
+                           int32_t *status, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -71,6 +71,9 @@ SIGNATURES = [
      [c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_void_p, c_int32, c_void_p]),
     ("kv_decode_attn", c_int32,
      [c_void_p, c_void_p, c_void_p, c_int32, c_void_p, c_int32, c_int32, c_void_p, c_void_p]),
+    ("kv_decode_attn_noalloc", c_int32,
+     [c_void_p, c_uint32, c_int32, c_int32, c_int32, c_void_p, c_int32, c_void_p, c_void_p, c_int32,
+      c_void_p, c_int32, c_int32, c_void_p, c_void_p, c_void_p]),
 ]
 
 _lib: ctypes.CDLL | None = None

@@ -728,4 +728,56 @@ int launch_decode(kv_pool* pool, const void* q, const uint32_t* bt, int32_t bt_s
     return e == cudaSuccess ? KV_OK : KV_ERR_CUDA;
 }
 
+// ---- decode on caller-supplied workspace (the allocation-free entry point) ----
+int decode_configure_raw(int dtype, int nkv, int group, int max_seqs, int device, int sm_count,
+                         int* grid, size_t* smem) {
+    const DecodeVariant* v = find_variant(dtype, nkv, group);
+    if (!v) return KV_ERR_UNSUPPORTED;
+    const size_t bytes = v->smem(max_seqs);
+    int optin = 0;
+    if (cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device) != cudaSuccess)
+        return KV_ERR_CUDA;
+    if (bytes > static_cast<size_t>(optin)) return KV_ERR_INVALID;
+    if (cudaFuncSetAttribute(v->fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(bytes)) != cudaSuccess)
+        return KV_ERR_CUDA;
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, v->fn, v->threads, bytes) != cudaSuccess ||
+        per_sm < 1)
+        return KV_ERR_CUDA;
+    *grid = sm_count * per_sm;
+    *smem = bytes;
+    return KV_OK;
+}
+
+int launch_decode_raw(const DecodeRaw& r, cudaStream_t stream) {
+    const DecodeVariant* v = find_variant(r.dtype, r.nkv, r.group);
+    if (!v) return KV_ERR_UNSUPPORTED;
+    DecodeArgs a;
+    a.q = r.q;
+    a.out = r.out;
+    a.bt = r.bt;
+    a.bt_stride = r.bt_stride;
+    a.seq_lens = r.seq_lens;
+    a.n_seqs = r.n_seqs;
+    a.window = r.window;
+    a.rope = r.rope;
+    a.max_pos = r.max_pos;
+    a.n_pages = r.n_pages;
+    a.part_o = r.part_o;
+    a.part_ml = r.part_ml;
+    a.counters = r.counters;
+    a.err = r.err;
+    a.qscale = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(kHeadDim)));
+    // A pool created since the last call may have lowered the kernel's
+    // shared-memory limit to its own size: restore the size this launch needs.
+    if (cudaFuncSetAttribute(v->fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(r.smem)) != cudaSuccess)
+        return KV_ERR_CUDA;
+    CUtensorMap map = *r.map;
+    void* args[] = {&map, &a};
+    const cudaError_t e = cudaLaunchKernel(v->fn, dim3(r.grid), dim3(v->threads), args, r.smem, stream);
+    return e == cudaSuccess ? KV_OK : KV_ERR_CUDA;
+}
+
 }  // namespace kvb200

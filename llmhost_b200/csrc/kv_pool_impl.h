@@ -40,4 +40,32 @@ int launch_decode(kv_pool* pool, const void* q, const uint32_t* bt, int32_t bt_s
                   const int32_t* seq_lens, int32_t n_seqs, int32_t window, void* out,
                   cudaStream_t stream);
 
+// Decode launch on explicit workspace pointers and an explicit tensor map,
+// for the entry point that owns no pool (kv_noalloc.cu).
+struct DecodeRaw {
+    int dtype, nkv, group;
+    const CUtensorMap* map;
+    const void* q;
+    void* out;
+    const uint32_t* bt;
+    long long bt_stride;
+    const int32_t* seq_lens;
+    int n_seqs;
+    int window;
+    const float2* rope;
+    int max_pos;
+    uint32_t n_pages;
+    float* part_o;
+    float* part_ml;
+    int* counters;
+    int* err;
+    int grid;
+    size_t smem;
+};
+// Sets the kernel's shared-memory attribute on the current device and
+// returns its persistent grid size; call once per device and shape.
+int decode_configure_raw(int dtype, int nkv, int group, int max_seqs, int device, int sm_count,
+                         int* grid, size_t* smem);
+int launch_decode_raw(const DecodeRaw& r, cudaStream_t stream);
+
 }  // namespace kvb200
