@@ -19,6 +19,11 @@
  *                       prefill K/V store (lfm2.rs:751-761)
  *   kv_decode_attn      attention_decode_cached (lfm2.rs:1006-1056) with RoPE
  *                       on q (lfm2.rs:816-822) and the key mask (lfm2.rs:1032-1035)
+ *   kv_tree_*           validate_tree_for_tokens, validate_accept_path (tree.rs:48-123)
+ *   kv_state_*          Engine::{open, forward, accept, rollback, committed,
+ *                       session_kv} (batch.rs:128-297) and PagedKv (cache.rs:12-51),
+ *                       with the page allocator, block tables, copy-on-write
+ *                       fork, eviction and compaction the reference lacks
  */
 #ifndef LLMHOST_KV_H
 #define LLMHOST_KV_H
@@ -45,7 +50,11 @@ typedef enum {
     KV_ERR_TIMEOUT = 4,     /* a device-side wait ran past its time limit */
     KV_ERR_CUDA = 5,        /* a CUDA runtime / driver call failed */
     KV_ERR_UNSUPPORTED = 6, /* shape this build does not compile (see kv_pool_create) */
-    KV_ERR_BAD_POS = 7      /* a RoPE position >= max_positions */
+    KV_ERR_BAD_POS = 7,     /* a RoPE position >= max_positions */
+    KV_ERR_UNKNOWN_SEQ = 8, /* EngineError::UnknownSeq (batch.rs:63) */
+    KV_ERR_NO_PENDING = 9,  /* EngineError::NoPendingForward (batch.rs:64) */
+    KV_ERR_INVALID_ACCEPT = 10, /* EngineError::InvalidAccept (batch.rs:65) */
+    KV_ERR_TREE = 11        /* EngineError::Tree / a TreeError (tree.rs:11-19) */
 } kv_status;
 
 typedef struct kv_pool kv_pool; /* opaque */
@@ -110,6 +119,87 @@ int kv_append_decode(kv_pool *pool, const void *k, const void *v, const uint32_t
 int kv_decode_attn(kv_pool *pool, const void *q, const uint32_t *block_tables, int32_t bt_stride,
                    const int32_t *seq_lens, int32_t n_seqs, int32_t window, void *out,
                    void *stream);
+
+/* ---- host-side KV state ----------------------------------------------------
+ * Host-only (no CUDA calls).  It owns the page allocator and every sequence's
+ * per-layer block tables, and mirrors llm-engine's Engine (batch.rs:128-297):
+ * forward() stages draft tokens, accept()/rollback() commit a path of them.
+ * Device work is returned as plans -- page copies (copy-on-write, compaction)
+ * and token-slot moves (accepted draft tokens) -- that the caller runs with
+ * kv_copy_pages / kv_move_slots before its next launch.  Allocation rules:
+ * a LIFO free stack whose first pops follow alloc_order (NULL: 0, 1, 2, ...);
+ * layers are walked in order; a write into a shared partial tail page copies
+ * it first.  Output buffers are checked before the state changes. */
+
+typedef struct kv_state kv_state; /* opaque */
+
+enum {
+    KV_TREE_OK = 0,
+    KV_TREE_LENGTH_MISMATCH = 1,          /* TreeError::LengthMismatch { tree, tokens } */
+    KV_TREE_PARENT_OUT_OF_RANGE = 2,      /* TreeError::ParentOutOfRange { child, parent } */
+    KV_TREE_PARENT_DOES_NOT_PRECEDE = 3   /* TreeError::ParentDoesNotPrecede { child, parent } */
+};
+
+typedef struct {
+    int32_t kind; /* KV_TREE_* */
+    int64_t child;
+    int64_t parent;
+    int64_t tree;
+    int64_t tokens;
+} kv_tree_error;
+
+/* tree.rs:66-73 validate_tree_for_tokens; KV_ERR_TREE with *err filled. */
+int kv_tree_validate(const int32_t *tree, int32_t tree_len, int32_t tokens, kv_tree_error *err);
+/* tree.rs:90-123 validate_accept_path. */
+int kv_tree_validate_accept(const int32_t *tree, int32_t tree_len, const int64_t *accepted, int32_t n,
+                            kv_tree_error *err);
+
+int kv_state_create(uint32_t n_pages, int32_t n_layers, int32_t page_tokens, const uint32_t *alloc_order,
+                    uint32_t n_order, kv_state **out);
+int kv_state_destroy(kv_state *st);
+/* Engine::open: a fresh, empty sequence (replaces existing state). */
+int kv_state_open(kv_state *st, uint64_t seq_id);
+/* Release a sequence and all its pages. */
+int kv_state_close(kv_state *st, uint64_t seq_id);
+/* New sequence dst sharing every committed page of src (copy-on-write). */
+int kv_state_fork(kv_state *st, uint64_t src, uint64_t dst);
+/* Commit n tokens (ids may be NULL) straight into the sequence's KV; cow_*
+ * (capacity >= n_layers) receive the page copies to run first. */
+int kv_state_append(kv_state *st, uint64_t seq_id, const uint32_t *tokens, int32_t n, uint32_t *cow_src,
+                    uint32_t *cow_dst, int32_t cow_cap, int32_t *n_cow);
+/* Engine::forward for one sequence: stage n draft tokens with parent array
+ * tree (NULL: a chain).  slots[i] / positions[i] receive token i's storage
+ * slot and RoPE position; cow_* the page copies to run before the append. */
+int kv_state_forward(kv_state *st, uint64_t seq_id, const uint32_t *tokens, int32_t n, const int32_t *tree,
+                     int32_t tree_len, int32_t *slots, int32_t *positions, uint32_t *cow_src, uint32_t *cow_dst,
+                     int32_t cow_cap, int32_t *n_cow, kv_tree_error *err);
+/* Engine::accept / Engine::rollback: commit a path of the staged tokens.
+ * move_* (capacity >= staged tokens) receive the slot moves to run;
+ * *bad_index is set on KV_ERR_INVALID_ACCEPT. */
+int kv_state_accept(kv_state *st, uint64_t seq_id, const int64_t *accepted, int32_t n, int32_t *move_src,
+                    int32_t *move_dst, int32_t move_cap, int32_t *n_moves, int64_t *bad_index);
+int kv_state_rollback(kv_state *st, uint64_t seq_id, const int64_t *rejected, int32_t n, int32_t *move_src,
+                      int32_t *move_dst, int32_t move_cap, int32_t *n_moves, int64_t *bad_index);
+/* Free the pages wholly below token_count - window (entries become KV_PAGE_NONE). */
+int kv_state_evict_window(kv_state *st, uint64_t seq_id, int64_t window, int64_t *n_freed);
+/* Move used pages into the lowest ids; *n_moves receives the count (also on
+ * KV_ERR_INVALID when cap is too small, with no change made). */
+int kv_state_compact(kv_state *st, uint32_t *src, uint32_t *dst, int32_t cap, int32_t *n_moves);
+/* PagedKv::token_count (cache.rs:31-34). */
+int kv_state_token_count(const kv_state *st, uint64_t seq_id, int64_t *n);
+/* Engine::committed (batch.rs:162-165). */
+int kv_state_committed(const kv_state *st, uint64_t seq_id, uint32_t *tokens, int64_t cap, int64_t *n);
+/* One layer's block table; which = 0 committed, 1 the staged draft. */
+int kv_state_table(const kv_state *st, uint64_t seq_id, int32_t layer, int32_t which, uint32_t *out,
+                   int64_t cap, int64_t *n);
+/* Rows of n_seqs tables for a kernel launch: out[i * stride + j], padded
+ * with KV_PAGE_NONE. */
+int kv_state_export_tables(const kv_state *st, const uint64_t *seq_ids, int32_t n_seqs, int32_t layer,
+                           int32_t which, uint32_t *out, int32_t stride);
+int kv_state_free_list(const kv_state *st, uint32_t *out, int64_t cap, int64_t *n);
+int kv_state_refcount(const kv_state *st, uint32_t page, uint32_t *count);
+/* Token count at which the staged draft starts (its first slot). */
+int kv_state_pending_base(const kv_state *st, uint64_t seq_id, int64_t *base);
 
 /* Decode attention for callers that cannot allocate device memory.
  *

@@ -25,6 +25,10 @@ STATUS = {
     5: "KV_ERR_CUDA",
     6: "KV_ERR_UNSUPPORTED",
     7: "KV_ERR_BAD_POS",
+    8: "KV_ERR_UNKNOWN_SEQ",
+    9: "KV_ERR_NO_PENDING",
+    10: "KV_ERR_INVALID_ACCEPT",
+    11: "KV_ERR_TREE",
 }
 
 

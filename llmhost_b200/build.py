@@ -37,7 +37,7 @@ def nvcc() -> str:
 
 
 def sources() -> list[Path]:
-    return sorted(CSRC.glob("*.cu"))
+    return sorted(CSRC.glob("*.cu")) + sorted(CSRC.glob("*.cpp"))
 
 
 def _deps_mtime() -> float:
@@ -46,7 +46,7 @@ def _deps_mtime() -> float:
 
 
 def _compile(src: Path, ptxas_verbose: bool) -> tuple[Path, str]:
-    obj = BUILD_DIR / (src.stem + ".o")
+    obj = BUILD_DIR / (src.stem + src.suffix.replace(".", "_") + ".o")
     cmd = [nvcc(), *ARCH, *NVCC_FLAGS, "-c", str(src), "-o", str(obj)]
     if ptxas_verbose:
         cmd += ["-Xptxas", "-v"]

@@ -129,6 +129,10 @@ const char* kv_status_str(int status) {
         case KV_ERR_CUDA: return "CUDA error";
         case KV_ERR_UNSUPPORTED: return "shape not supported by this build";
         case KV_ERR_BAD_POS: return "RoPE position out of range";
+        case KV_ERR_UNKNOWN_SEQ: return "unknown sequence";
+        case KV_ERR_NO_PENDING: return "sequence has no pending forward to accept or roll back";
+        case KV_ERR_INVALID_ACCEPT: return "accepted tokens are not a valid path";
+        case KV_ERR_TREE: return "invalid parent-index tree";
         default: return "unknown status";
     }
 }

@@ -33,7 +33,9 @@ def test_library_exports_every_declared_symbol():
 
 
 def test_python_binding_covers_header():
-    bound = {name for name, _, _ in _capi.SIGNATURES}
+    from llmhost_b200 import state
+
+    bound = {name for name, _, _ in _capi.SIGNATURES} | {name for name, _, _ in state.STATE_SIGNATURES}
     assert declared_functions() <= bound
 
 
@@ -41,7 +43,7 @@ def test_status_strings_without_gpu():
     lib = _capi.lib()
     assert lib.kv_status_str(0) == b"ok"
     assert lib.kv_api_version() == 1
-    for code in range(8):
+    for code in range(12):
         assert lib.kv_status_str(code)
 
 
