@@ -120,6 +120,27 @@ int kv_decode_attn(kv_pool *pool, const void *q, const uint32_t *block_tables, i
                    const int32_t *seq_lens, int32_t n_seqs, int32_t window, void *out,
                    void *stream);
 
+/* One token's K/V (every head of one layer) from page slot to page slot. */
+typedef struct {
+    uint32_t src_page;
+    int32_t src_slot;
+    uint32_t dst_page;
+    int32_t dst_slot;
+} kv_token_move;
+
+/* Page copies (copy-on-write, compaction): page src[i] -> dst[i], i < n, src and
+ * dst device arrays.  The copies of one call must be independent (no page is
+ * both a source and a destination). */
+int kv_copy_pages(kv_pool *pool, const uint32_t *src, const uint32_t *dst, int32_t n, void *stream);
+/* Token moves (commit of accepted draft tokens): moves is a device array of
+ * n_moves; group g is moves[group_offsets[g] .. group_offsets[g+1]) (device
+ * array of n_groups + 1), run in order a chunk at a time, every source of a
+ * chunk read before any destination is written -- exact for the moves
+ * kv_state_accept / kv_state_rollback produce.  Groups run in parallel and
+ * must not touch the same slots. */
+int kv_move_tokens(kv_pool *pool, const kv_token_move *moves, int32_t n_moves, const int32_t *group_offsets,
+                   int32_t n_groups, void *stream);
+
 /* ---- host-side KV state ----------------------------------------------------
  * Host-only (no CUDA calls).  It owns the page allocator and every sequence's
  * per-layer block tables, and mirrors llm-engine's Engine (batch.rs:128-297):
@@ -174,12 +195,18 @@ int kv_state_forward(kv_state *st, uint64_t seq_id, const uint32_t *tokens, int3
                      int32_t tree_len, int32_t *slots, int32_t *positions, uint32_t *cow_src, uint32_t *cow_dst,
                      int32_t cow_cap, int32_t *n_cow, kv_tree_error *err);
 /* Engine::accept / Engine::rollback: commit a path of the staged tokens.
- * move_* (capacity >= staged tokens) receive the slot moves to run;
- * *bad_index is set on KV_ERR_INVALID_ACCEPT. */
+ * move_* (capacity >= staged tokens) receive the slot moves (accepted token
+ * order[j] goes from slot L + order[j] to L + j).  tok_moves, if not NULL
+ * (capacity >= staged tokens * n_layers), receives the same moves for every
+ * layer addressed by page, taken before the commit frees the rejected pages:
+ * run them with kv_move_tokens before the next launch.  *bad_index is set on
+ * KV_ERR_INVALID_ACCEPT. */
 int kv_state_accept(kv_state *st, uint64_t seq_id, const int64_t *accepted, int32_t n, int32_t *move_src,
-                    int32_t *move_dst, int32_t move_cap, int32_t *n_moves, int64_t *bad_index);
+                    int32_t *move_dst, int32_t move_cap, int32_t *n_moves, kv_token_move *tok_moves,
+                    int32_t tok_cap, int32_t *n_tok_moves, int64_t *bad_index);
 int kv_state_rollback(kv_state *st, uint64_t seq_id, const int64_t *rejected, int32_t n, int32_t *move_src,
-                      int32_t *move_dst, int32_t move_cap, int32_t *n_moves, int64_t *bad_index);
+                      int32_t *move_dst, int32_t move_cap, int32_t *n_moves, kv_token_move *tok_moves,
+                      int32_t tok_cap, int32_t *n_tok_moves, int64_t *bad_index);
 /* Free the pages wholly below token_count - window (entries become KV_PAGE_NONE). */
 int kv_state_evict_window(kv_state *st, uint64_t seq_id, int64_t window, int64_t *n_freed);
 /* Move used pages into the lowest ids; *n_moves receives the count (also on

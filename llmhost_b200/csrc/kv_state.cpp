@@ -245,12 +245,12 @@ StateStatus KvState::forward(uint64_t seq, const uint32_t* tokens, size_t n, con
 }
 
 StateStatus KvState::accept(uint64_t seq, const int64_t* accepted, size_t na, int64_t* bad_index,
-                            std::vector<SlotMove>* moves) {
-    return commit(seq, std::vector<int64_t>(accepted, accepted + na), bad_index, moves);
+                            std::vector<SlotMove>* moves, std::vector<TokenMove>* pages) {
+    return commit(seq, std::vector<int64_t>(accepted, accepted + na), bad_index, moves, pages);
 }
 
 StateStatus KvState::rollback(uint64_t seq, const int64_t* rejected, size_t nr, int64_t* bad_index,
-                              std::vector<SlotMove>* moves) {
+                              std::vector<SlotMove>* moves, std::vector<TokenMove>* pages) {
     auto it = sessions_.find(seq);
     if (it == sessions_.end()) return StateStatus::UnknownSeq;
     if (!it->second.pending) return StateStatus::NoPending;
@@ -258,11 +258,11 @@ StateStatus KvState::rollback(uint64_t seq, const int64_t* rejected, size_t nr, 
     std::vector<int64_t> acc;
     for (size_t i = 0; i < it->second.pending->tokens.size(); ++i)
         if (!rej.count(static_cast<int64_t>(i))) acc.push_back(static_cast<int64_t>(i));
-    return commit(seq, acc, bad_index, moves);
+    return commit(seq, acc, bad_index, moves, pages);
 }
 
 StateStatus KvState::commit(uint64_t seq, const std::vector<int64_t>& accepted, int64_t* bad_index,
-                            std::vector<SlotMove>* moves) {
+                            std::vector<SlotMove>* moves, std::vector<TokenMove>* pages) {
     auto it = sessions_.find(seq);
     if (it == sessions_.end()) return StateStatus::UnknownSeq;
     Session& s = it->second;
@@ -284,12 +284,16 @@ StateStatus KvState::commit(uint64_t seq, const std::vector<int64_t>& accepted, 
     std::sort(order.begin(), order.end());
     order.erase(std::unique(order.begin(), order.end()), order.end());
     const int64_t a = static_cast<int64_t>(order.size());
-    if (moves) {
-        moves->clear();
-        for (int64_t j = 0; j < a; ++j)
-            if (order[j] != j)
-                moves->push_back({static_cast<int32_t>(d.base + order[j]), static_cast<int32_t>(d.base + j)});
+    std::vector<SlotMove> mv;
+    for (int64_t j = 0; j < a; ++j)
+        if (order[j] != j) mv.push_back({static_cast<int32_t>(d.base + order[j]), static_cast<int32_t>(d.base + j)});
+    if (pages) {
+        pages->clear();
+        for (const auto& t : d.tables)
+            for (const SlotMove& m : mv)
+                pages->push_back({t[m.src / P_], m.src % P_, t[m.dst / P_], m.dst % P_});
     }
+    if (moves) *moves = mv;
     // Free the draft's pages past the accepted tokens (the rejected branches).
     const size_t keep = static_cast<size_t>((d.base + a + P_ - 1) / P_);
     for (auto& t : d.tables) {

@@ -59,6 +59,13 @@ struct PageCopy {
 struct SlotMove {
     int32_t src, dst;
 };
+// One token's K/V (all heads of one layer) from one page slot to another.
+struct TokenMove {
+    uint32_t src_page;
+    int32_t src_slot;
+    uint32_t dst_page;
+    int32_t dst_slot;
+};
 
 enum class StateStatus : int32_t {
     Ok = 0,
@@ -99,10 +106,12 @@ public:
                         std::vector<int32_t>* slots, std::vector<int32_t>* positions,
                         std::vector<PageCopy>* cow);
     // Engine::accept / rollback / commit (batch.rs:230-296).
+    // `pages` receives the same moves per layer (layer-major), addressed by the
+    // draft's pages before the commit frees any of them.
     StateStatus accept(uint64_t seq, const int64_t* accepted, size_t na, int64_t* bad_index,
-                       std::vector<SlotMove>* moves);
+                       std::vector<SlotMove>* moves, std::vector<TokenMove>* pages = nullptr);
     StateStatus rollback(uint64_t seq, const int64_t* rejected, size_t nr, int64_t* bad_index,
-                         std::vector<SlotMove>* moves);
+                         std::vector<SlotMove>* moves, std::vector<TokenMove>* pages = nullptr);
 
     StateStatus evict_window(uint64_t seq, int64_t window, int64_t* freed);
     void compact(std::vector<PageCopy>* moves);
@@ -137,7 +146,7 @@ private:
     int64_t pages_needed(const std::vector<std::vector<uint32_t>>& tables, int64_t start, int64_t n) const;
     void grow(std::vector<std::vector<uint32_t>>& tables, int64_t start, int64_t n, std::vector<PageCopy>* cow);
     StateStatus commit(uint64_t seq, const std::vector<int64_t>& accepted, int64_t* bad_index,
-                       std::vector<SlotMove>* moves);
+                       std::vector<SlotMove>* moves, std::vector<TokenMove>* pages);
 
     uint32_t n_pages_;
     int n_layers_;

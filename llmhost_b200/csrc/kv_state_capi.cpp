@@ -12,6 +12,7 @@ using kvb200::KvState;
 using kvb200::PageCopy;
 using kvb200::SlotMove;
 using kvb200::StateStatus;
+using kvb200::TokenMove;
 using kvb200::TreeError;
 
 struct kv_state {
@@ -147,28 +148,42 @@ int kv_state_forward(kv_state* st, uint64_t seq_id, const uint32_t* tokens, int3
 
 static int finish_commit(kv_state* st, uint64_t seq_id, bool is_accept, const int64_t* idx, int32_t n,
                          int32_t* move_src, int32_t* move_dst, int32_t move_cap, int32_t* n_moves,
-                         int64_t* bad_index) {
+                         kv_token_move* tok_moves, int32_t tok_cap, int32_t* n_tok_moves, int64_t* bad_index) {
     if (!st || n < 0 || (n > 0 && !idx)) return KV_ERR_INVALID;
     int64_t pend = 0;
     const StateStatus ps = st->impl.pending_size(seq_id, &pend);
     if (ps != StateStatus::Ok) return to_status(ps);
     if (pend > 0 && (move_cap < pend || !move_src || !move_dst)) return KV_ERR_INVALID;
+    if (tok_moves && tok_cap < pend * st->impl.n_layers()) return KV_ERR_INVALID;
     std::vector<SlotMove> moves;
-    const StateStatus s = is_accept ? st->impl.accept(seq_id, idx, static_cast<size_t>(n), bad_index, &moves)
-                                    : st->impl.rollback(seq_id, idx, static_cast<size_t>(n), bad_index, &moves);
+    std::vector<TokenMove> pages;
+    std::vector<TokenMove>* pp = tok_moves ? &pages : nullptr;
+    const StateStatus s = is_accept ? st->impl.accept(seq_id, idx, static_cast<size_t>(n), bad_index, &moves, pp)
+                                    : st->impl.rollback(seq_id, idx, static_cast<size_t>(n), bad_index, &moves, pp);
     if (s != StateStatus::Ok) return to_status(s);
     put_moves(moves, move_src, move_dst, n_moves);
+    if (tok_moves) {
+        for (size_t i = 0; i < pages.size(); ++i)
+            tok_moves[i] = kv_token_move{pages[i].src_page, pages[i].src_slot, pages[i].dst_page, pages[i].dst_slot};
+        if (n_tok_moves) *n_tok_moves = static_cast<int32_t>(pages.size());
+    } else if (n_tok_moves) {
+        *n_tok_moves = 0;
+    }
     return KV_OK;
 }
 
 int kv_state_accept(kv_state* st, uint64_t seq_id, const int64_t* accepted, int32_t n, int32_t* move_src,
-                    int32_t* move_dst, int32_t move_cap, int32_t* n_moves, int64_t* bad_index) {
-    return finish_commit(st, seq_id, true, accepted, n, move_src, move_dst, move_cap, n_moves, bad_index);
+                    int32_t* move_dst, int32_t move_cap, int32_t* n_moves, kv_token_move* tok_moves,
+                    int32_t tok_cap, int32_t* n_tok_moves, int64_t* bad_index) {
+    return finish_commit(st, seq_id, true, accepted, n, move_src, move_dst, move_cap, n_moves, tok_moves, tok_cap,
+                         n_tok_moves, bad_index);
 }
 
 int kv_state_rollback(kv_state* st, uint64_t seq_id, const int64_t* rejected, int32_t n, int32_t* move_src,
-                      int32_t* move_dst, int32_t move_cap, int32_t* n_moves, int64_t* bad_index) {
-    return finish_commit(st, seq_id, false, rejected, n, move_src, move_dst, move_cap, n_moves, bad_index);
+                      int32_t* move_dst, int32_t move_cap, int32_t* n_moves, kv_token_move* tok_moves,
+                      int32_t tok_cap, int32_t* n_tok_moves, int64_t* bad_index) {
+    return finish_commit(st, seq_id, false, rejected, n, move_src, move_dst, move_cap, n_moves, tok_moves, tok_cap,
+                         n_tok_moves, bad_index);
 }
 
 int kv_state_evict_window(kv_state* st, uint64_t seq_id, int64_t window, int64_t* n_freed) {

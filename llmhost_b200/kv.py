@@ -151,6 +151,21 @@ class KvPool:
                                          block_tables.shape[-1], _ptr(seq_lens), seq_lens.numel(),
                                          _stream_ptr(stream)), "kv_append_decode")
 
+    def copy_pages(self, src, dst, stream=None) -> None:
+        """Independent page copies src[i] -> dst[i] (device int32 tensors; kv_copy_pages)."""
+        self._check_tensor(src, "src", torch.int32)
+        self._check_tensor(dst, "dst", torch.int32)
+        check(self._lib.kv_copy_pages(self._h, _ptr(src), _ptr(dst), src.numel(), _stream_ptr(stream)),
+              "kv_copy_pages")
+
+    def move_tokens(self, moves, group_offsets, stream=None) -> None:
+        """Token moves (device int32 tensor [n, 4] of src_page, src_slot, dst_page, dst_slot)
+        in groups (device int32 tensor of n_groups + 1 offsets; kv_move_tokens)."""
+        self._check_tensor(moves, "moves", torch.int32)
+        self._check_tensor(group_offsets, "group_offsets", torch.int32)
+        check(self._lib.kv_move_tokens(self._h, _ptr(moves), moves.shape[0], _ptr(group_offsets),
+                                       group_offsets.numel() - 1, _stream_ptr(stream)), "kv_move_tokens")
+
     def decode_attn(self, q, block_tables, seq_lens, window: int = 0, out=None, stream=None):
         """Paged decode attention (kv_decode_attn); returns `out`."""
         dt = self.shape.torch_dtype

@@ -68,9 +68,9 @@ STATE_SIGNATURES = [
                                    c_void_p, c_void_p, c_void_p, c_int32, POINTER(c_int32),
                                    POINTER(KvTreeError)]),
     ("kv_state_accept", c_int32, [c_void_p, c_uint64, c_void_p, c_int32, c_void_p, c_void_p, c_int32,
-                                  POINTER(c_int32), POINTER(c_int64)]),
+                                  POINTER(c_int32), c_void_p, c_int32, POINTER(c_int32), POINTER(c_int64)]),
     ("kv_state_rollback", c_int32, [c_void_p, c_uint64, c_void_p, c_int32, c_void_p, c_void_p, c_int32,
-                                    POINTER(c_int32), POINTER(c_int64)]),
+                                    POINTER(c_int32), c_void_p, c_int32, POINTER(c_int32), POINTER(c_int64)]),
     ("kv_state_evict_window", c_int32, [c_void_p, c_uint64, c_int64, POINTER(c_int64)]),
     ("kv_state_compact", c_int32, [c_void_p, c_void_p, c_void_p, c_int32, POINTER(c_int32)]),
     ("kv_state_token_count", c_int32, [c_void_p, c_uint64, POINTER(c_int64)]),
@@ -204,25 +204,32 @@ class KvState:
                            list(zip(cs[: nc.value].tolist(), cd[: nc.value].tolist())),
                            [[float(t)] for t in tok.tolist()])
 
-    def _commit(self, fn, seq: int, idx) -> list[tuple[int, int]]:
+    def _commit(self, fn, seq: int, idx, with_pages: bool):
         a = np.ascontiguousarray(idx, dtype=np.int64)
         cap = max(self.pending_size(seq), 1)
         ms = np.empty(cap, np.int32)
         md = np.empty(cap, np.int32)
         nm = c_int32(0)
+        tm = np.empty((cap * self.n_layers, 4), np.int32) if with_pages else None
+        ntm = c_int32(0)
         bad = c_int64(0)
         rc = fn(self._h, seq, a.ctypes.data if len(a) else None, len(a), ms.ctypes.data, md.ctypes.data, cap,
-                nm, bad)
+                nm, None if tm is None else tm.ctypes.data, 0 if tm is None else tm.shape[0], ntm, bad)
         if rc == _capi_status("KV_ERR_INVALID_ACCEPT"):
             raise EngineError("InvalidAccept", seq, index=int(bad.value))
         self._engine_check(rc, seq)
-        return list(zip(ms[: nm.value].tolist(), md[: nm.value].tolist()))
+        moves = list(zip(ms[: nm.value].tolist(), md[: nm.value].tolist()))
+        if with_pages:
+            return moves, tm[: ntm.value].copy()
+        return moves
 
-    def accept(self, seq: int, accepted) -> list[tuple[int, int]]:
-        return self._commit(self.lib.kv_state_accept, seq, accepted)
+    def accept(self, seq: int, accepted, with_pages: bool = False):
+        """Commit a path; returns slot moves (and, with_pages, the per-layer
+        page-addressed token moves [n, 4] to run with KvPool.move_tokens)."""
+        return self._commit(self.lib.kv_state_accept, seq, accepted, with_pages)
 
-    def rollback(self, seq: int, rejected) -> list[tuple[int, int]]:
-        return self._commit(self.lib.kv_state_rollback, seq, rejected)
+    def rollback(self, seq: int, rejected, with_pages: bool = False):
+        return self._commit(self.lib.kv_state_rollback, seq, rejected, with_pages)
 
     def evict_window(self, seq: int, window: int) -> int:
         n = c_int64(0)
