@@ -120,6 +120,29 @@ int kv_decode_attn(kv_pool *pool, const void *q, const uint32_t *block_tables, i
                    const int32_t *seq_lens, int32_t n_seqs, int32_t window, void *out,
                    void *stream);
 
+/* Chunked-prefill and tree-verify attention: attention_forward
+ * (lfm2.rs:1058-1111) for T_s new query tokens of sequence s that follow
+ * prefix_lens[s] = L_s cached tokens (the reference only prefills from
+ * position 0, lfm2.rs:730).  The chunk's K/V must already be in the pages at
+ * slots L_s .. L_s + T_s - 1 (kv_append).
+ *   q          [total_q, n_q_heads, head_dim], pool dtype, before RoPE;
+ *              sequence s owns rows q_offsets[s] .. q_offsets[s+1] - 1
+ *   q_pos      [total_q] RoPE position of each query row
+ *   tree_masks NULL: causal chunk (chunk token i sees chunk tokens j <= i);
+ *              else [total_q] bit masks, bit j set when chunk token j is an
+ *              ancestor-or-self of token i (speculative tree verify, T_s <= 64)
+ *   out        [total_q, n_q_heads, head_dim], pool dtype
+ * Every query also sees all L_s cached keys.  max_q_per_seq bounds T_s (the
+ * launch covers that many tokens per sequence; a larger T_s, or T_s > 64 with
+ * tree masks, is flagged in the error word as an invalid argument).  Slots
+ * past L_s + T_s in the sequence's last page must hold finite values (as a
+ * fresh pool and kv_append leave them).  bf16 pools only (tcgen05 tensor
+ * cores); KV_ERR_UNSUPPORTED for f32. */
+int kv_prefill_attn(kv_pool *pool, const void *q, const int32_t *q_pos, const int32_t *q_offsets,
+                    const int32_t *prefix_lens, const uint64_t *tree_masks,
+                    const uint32_t *block_tables, int32_t bt_stride, int32_t n_seqs,
+                    int32_t max_q_per_seq, void *out, void *stream);
+
 /* One token's K/V (every head of one layer) from page slot to page slot. */
 typedef struct {
     uint32_t src_page;

@@ -25,6 +25,7 @@ constexpr uint32_t kPageNone = 0xFFFFFFFFu;
 constexpr int kDevErrBadPage = 1;   // a block-table entry was >= n_pages
 constexpr int kDevErrTimeout = 2;   // an mbarrier wait ran past its time limit
 constexpr int kDevErrBadPos = 4;    // a RoPE position was >= max_positions
+constexpr int kDevErrBadArg = 8;    // a device-side length or offset was out of range
 
 // A bounded wait gives up after this many nanoseconds of %globaltimer.
 constexpr uint64_t kWaitLimitNs = 2000000000ull;

@@ -72,7 +72,8 @@ void build_rope_table(int max_pos, int dim, float theta, std::vector<float2>& ou
     for (auto& t : th) t.join();
 }
 
-int encode_page_map(kv_pool* p) {
+// The pool as 128-byte rows (2D), 128-byte swizzle, boxes of box_rows rows.
+int encode_row_map(kv_pool* p, CUtensorMap* map, cuuint32_t box_rows) {
     PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
     cudaDriverEntryPointQueryResult q;
     if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", reinterpret_cast<void**>(&encode),
@@ -84,15 +85,23 @@ int encode_page_map(kv_pool* p) {
     const cuuint64_t page_rows = p->page_bytes / 128;
     const cuuint64_t gdim[2] = {row_elems, static_cast<cuuint64_t>(p->cfg.n_pages) * page_rows};
     const cuuint64_t gstride[1] = {128};
-    const cuuint32_t box[2] = {static_cast<cuuint32_t>(row_elems),
-                               static_cast<cuuint32_t>(std::min<cuuint64_t>(256, page_rows))};
+    const cuuint32_t box[2] = {static_cast<cuuint32_t>(row_elems), box_rows};
     const cuuint32_t estride[2] = {1, 1};
     const CUtensorMapDataType dt = p->cfg.dtype == KV_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                                                   : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
-    const CUresult r = encode(&p->page_map, dt, 2, p->pages, gdim, gstride, box, estride,
+    const CUresult r = encode(map, dt, 2, p->pages, gdim, gstride, box, estride,
                               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS ? KV_OK : KV_ERR_CUDA;
+}
+
+// page_map: a whole page per box (up to 256 rows; decode).  head_map: one
+// head's page_tokens rows of K or V per box (prefill).
+int encode_page_map(kv_pool* p) {
+    const cuuint64_t page_rows = p->page_bytes / 128;
+    const int rc = encode_row_map(p, &p->page_map, static_cast<cuuint32_t>(std::min<cuuint64_t>(256, page_rows)));
+    if (rc != KV_OK) return rc;
+    return encode_row_map(p, &p->head_map, static_cast<cuuint32_t>(p->cfg.page_tokens * p->elem_bytes / 2));
 }
 
 void free_pool(kv_pool* p) {
@@ -161,6 +170,7 @@ int kv_pool_create(const kv_pool_config* cfg, kv_pool** out) {
         return KV_ERR_CUDA;
     }
     rc = kvb200::decode_setup(p);
+    if (rc == KV_OK) rc = kvb200::prefill_setup(p);
     if (rc != KV_OK) {
         delete p;
         return rc;
@@ -253,6 +263,7 @@ int kv_last_error(kv_pool* pool) {
     if (word & kvb200::kDevErrTimeout) return KV_ERR_TIMEOUT;
     if (word & kvb200::kDevErrBadPage) return KV_ERR_BAD_PAGE;
     if (word & kvb200::kDevErrBadPos) return KV_ERR_BAD_POS;
+    if (word & kvb200::kDevErrBadArg) return KV_ERR_INVALID;
     return KV_ERR_CUDA;
 }
 
@@ -289,6 +300,21 @@ int kv_decode_attn(kv_pool* pool, const void* q, const uint32_t* block_tables, i
     DeviceScope dev(pool->cfg.device);
     return kvb200::launch_decode(pool, q, block_tables, bt_stride, seq_lens, n_seqs, window, out,
                                  static_cast<cudaStream_t>(stream));
+}
+
+int kv_prefill_attn(kv_pool* pool, const void* q, const int32_t* q_pos, const int32_t* q_offsets,
+                    const int32_t* prefix_lens, const uint64_t* tree_masks, const uint32_t* block_tables,
+                    int32_t bt_stride, int32_t n_seqs, int32_t max_q_per_seq, void* out, void* stream) {
+    if (!pool || n_seqs < 0 || max_q_per_seq < 0) return KV_ERR_INVALID;
+    if (pool->cfg.dtype != KV_DTYPE_BF16) return KV_ERR_UNSUPPORTED;
+    if (n_seqs == 0 || max_q_per_seq == 0) return KV_OK;
+    if (!q || !q_pos || !q_offsets || !prefix_lens || !block_tables || !out || bt_stride <= 0 ||
+        n_seqs > 65535 || (tree_masks && max_q_per_seq > 64))
+        return KV_ERR_INVALID;
+    DeviceScope dev(pool->cfg.device);
+    return kvb200::launch_prefill(pool, q, q_pos, q_offsets, prefix_lens,
+                                  reinterpret_cast<const unsigned long long*>(tree_masks), n_seqs,
+                                  max_q_per_seq, block_tables, bt_stride, out, static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

@@ -22,6 +22,7 @@ struct kv_pool {
     int decode_grid = 0;
     size_t decode_smem = 0;
     CUtensorMap page_map;         // TMA view of the pool as 128-byte rows
+    CUtensorMap head_map;         // same rows, one head's page_tokens rows per box (bf16)
 };
 
 namespace kvb200 {
@@ -39,6 +40,12 @@ size_t decode_workspace_slots(const kv_pool* pool);
 int launch_decode(kv_pool* pool, const void* q, const uint32_t* bt, int32_t bt_stride,
                   const int32_t* seq_lens, int32_t n_seqs, int32_t window, void* out,
                   cudaStream_t stream);
+
+// Prefill / tree-verify attention on tcgen05 (kv_prefill.cu); bf16 pools.
+int prefill_setup(kv_pool* pool);
+int launch_prefill(kv_pool* pool, const void* q, const int32_t* q_pos, const int32_t* q_off,
+                   const int32_t* prefix, const unsigned long long* tree, int32_t n_seqs, int32_t max_q,
+                   const uint32_t* bt, int32_t bt_stride, void* out, cudaStream_t stream);
 
 // Decode launch on explicit workspace pointers and an explicit tensor map,
 // for the entry point that owns no pool (kv_noalloc.cu).

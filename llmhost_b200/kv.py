@@ -179,3 +179,48 @@ class KvPool:
                                        _ptr(seq_lens), seq_lens.numel(), int(window), _ptr(out),
                                        _stream_ptr(stream)), "kv_decode_attn")
         return out
+
+    def prefill_attn(self, q, q_pos, q_offsets, prefix_lens, block_tables, tree_masks=None,
+                     max_q: int | None = None, out=None, stream=None):
+        """Chunked-prefill / tree-verify attention (kv_prefill_attn); returns `out`.
+
+        q [total_q, n_q, d] raw (RoPE applied here at q_pos), q_offsets [n_seqs + 1],
+        prefix_lens [n_seqs] cached tokens before each chunk, tree_masks None (causal
+        chunk) or int64 [total_q] ancestor-or-self bit masks.  max_q bounds the chunk
+        length of every sequence; when None it is read from q_offsets (a device sync).
+        """
+        dt = self.shape.torch_dtype
+        self._check_tensor(q, "q", dt)
+        for t, nm in ((q_pos, "q_pos"), (q_offsets, "q_offsets"), (prefix_lens, "prefix_lens"),
+                      (block_tables, "block_tables")):
+            self._check_tensor(t, nm, torch.int32)
+        if tree_masks is not None:
+            self._check_tensor(tree_masks, "tree_masks", torch.int64)
+        n_seqs = prefix_lens.numel()
+        if q_offsets.numel() != n_seqs + 1:
+            raise ValueError("q_offsets must hold n_seqs + 1 entries")
+        if max_q is None:
+            max_q = int((q_offsets[1:] - q_offsets[:-1]).max().item()) if n_seqs else 0
+        if out is None:
+            out = torch.empty_like(q)
+        self._check_tensor(out, "out", dt)
+        check(self._lib.kv_prefill_attn(self._h, _ptr(q), _ptr(q_pos), _ptr(q_offsets), _ptr(prefix_lens),
+                                        _ptr(tree_masks), _ptr(block_tables), block_tables.shape[-1],
+                                        n_seqs, int(max_q), _ptr(out), _stream_ptr(stream)),
+              "kv_prefill_attn")
+        return out
+
+
+def tree_masks(parents) -> np.ndarray:
+    """Ancestor-or-self bit masks of a parent-index tree (parents[i] < i, root -1),
+    the tree_masks argument of kv_prefill_attn; at most 64 nodes."""
+    n = len(parents)
+    if n > 64:
+        raise ValueError("tree-verify chunks hold at most 64 tokens")
+    m = np.zeros(n, np.uint64)
+    for i, p in enumerate(parents):
+        if not (-1 <= p < i):
+            raise ValueError(f"parent {p} of node {i} does not precede it")
+        m[i] = (m[p] if p >= 0 else np.uint64(0)) | np.uint64(1 << i)
+    return m.view(np.int64)
+

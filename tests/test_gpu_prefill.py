@@ -1,0 +1,201 @@
+"""Parity of chunked-prefill and tree-verify attention (kv_prefill_attn, tcgen05)
+against the CPU oracle.
+
+Each sequence has L cached tokens and a chunk of T new ones, all written with
+kv_append (GPU) and orc_paged_append_token (oracle) from the same bits.  The
+oracle gathers the stored K/V, rotates q at its position and runs
+orc_attention_masked with the explicit mask: every cached key, plus chunk key
+j for query i when j <= i (causal chunk) or j is an ancestor-or-self of i
+(tree).  bf16 tolerance 2e-2, normwise per (token, query head) row.
+"""
+import numpy as np
+import pytest
+
+from llmhost_b200.workloads import PAGE_TOKENS, normal_bits
+from oracle import oracle as O
+from paged_case import PAGE_NONE, assert_close_rows, to_numpy_f32, to_torch
+
+pytestmark = pytest.mark.gpu
+RTOL = 2e-2
+
+
+def _depths(parents):
+    d = []
+    for p in parents:
+        d.append(0 if p < 0 else d[p] + 1)
+    return d
+
+
+class PrefillCase:
+    """seqs: list of (L, T) for a causal chunk or (L, parents) for a tree."""
+
+    def __init__(self, n_q, n_kv, seqs, seed=0, extra_pages=4):
+        from llmhost_b200.kv import tree_masks
+
+        rng = np.random.default_rng(seed)
+        self.n_q, self.n_kv = n_q, n_kv
+        self.L = np.array([s[0] for s in seqs], np.int64)
+        self.parents = [None if isinstance(s[1], int) else list(s[1]) for s in seqs]
+        self.T = np.array([s[1] if isinstance(s[1], int) else len(s[1]) for s in seqs], np.int64)
+        self.tree = any(p is not None for p in self.parents)
+        assert not self.tree or all(p is not None for p in self.parents)
+        n = len(seqs)
+        pages = -(-(self.L + self.T) // PAGE_TOKENS)
+        self.n_pages = int(pages.sum()) + extra_pages
+        perm = rng.permutation(self.n_pages).astype(np.uint32)
+        self.bt = np.full((n, max(int(pages.max()), 1)), PAGE_NONE, np.uint32)
+        cur = 0
+        for s in range(n):
+            self.bt[s, :pages[s]] = perm[cur:cur + pages[s]]
+            cur += pages[s]
+        tot = self.L + self.T
+        # RoPE position of every stored token: cached t at t, chunk i at L + depth(i) (tree) or L + i
+        self.pos = []
+        for s in range(n):
+            chunk = _depths(self.parents[s]) if self.parents[s] is not None else list(range(int(self.T[s])))
+            self.pos.append(np.concatenate([np.arange(self.L[s]), self.L[s] + np.array(chunk, np.int64)]))
+        self.k = [normal_bits(rng, (int(t), n_kv, 64), "bf16") for t in tot]
+        self.v = [normal_bits(rng, (int(t), n_kv, 64), "bf16") for t in tot]
+        self.q = normal_bits(rng, (int(self.T.sum()), n_q, 64), "bf16")
+        self.q_off = np.concatenate([[0], np.cumsum(self.T)]).astype(np.int32)
+        self.q_pos = np.concatenate([p[int(L):] for p, L in zip(self.pos, self.L)]).astype(np.int32)
+        self.masks = None
+        if self.tree:
+            self.masks = np.concatenate([tree_masks(p) for p in self.parents])
+        self.max_pos = int(max((p.max(initial=0) for p in self.pos), default=0)) + 16
+
+    def run_oracle(self):
+        host = O.HostPages(self.n_pages, O.BF16, self.n_q, self.n_kv)
+        outs = []
+        for s in range(len(self.L)):
+            L, T = int(self.L[s]), int(self.T[s])
+            for t in range(L + T):
+                host.append_token(self.bt[s], t, int(self.pos[s][t]), self.k[s][t], self.v[s][t])
+            if T == 0:
+                continue
+            k, v = host.gather(self.bt[s], L + T)
+            q = O.bf16_bits_to_f32(self.q[self.q_off[s]:self.q_off[s + 1]]).copy()  # [T, n_q, d]
+            for i in range(T):
+                c, sn = O.cos_sin(host.inv, int(self.q_pos[self.q_off[s] + i]), 1, 64)
+                O.apply_rope_in_place(q[i], c, sn, self.n_q, 1, 64)
+            mask = np.zeros((T, L + T), np.uint8)
+            mask[:, :L] = 1
+            for i in range(T):
+                if self.parents[s] is None:
+                    mask[i, L:L + i + 1] = 1
+                else:
+                    bits = int(self.masks[self.q_off[s] + i].view(np.uint64))
+                    mask[i, L:] = [(bits >> j) & 1 for j in range(T)]
+            out = O.attention_masked(np.ascontiguousarray(q.transpose(1, 0, 2)), k, v, self.n_q, self.n_kv,
+                                     T, L + T, 64, mask)  # [n_q, T, d]
+            outs.append(out.transpose(1, 0, 2))
+        return host, np.concatenate(outs) if outs else np.zeros((0, self.n_q, 64), np.float32)
+
+    def make_pool(self):
+        from llmhost_b200.kv import KvPool
+
+        return KvPool(dtype="bf16", n_q_heads=self.n_q, n_kv_heads=self.n_kv, n_pages=self.n_pages,
+                      max_positions=self.max_pos, max_seqs=max(len(self.L), 1))
+
+    def run_gpu(self, pool, max_q=None):
+        import torch
+
+        dev = pool.device
+        n = len(self.L)
+        tok_seq = np.concatenate([np.full(int(self.L[s] + self.T[s]), s, np.int32) for s in range(n)])
+        tok_slot = np.concatenate([np.arange(int(self.L[s] + self.T[s]), dtype=np.int32) for s in range(n)])
+        tok_pos = np.concatenate(self.pos).astype(np.int32)
+        k = np.concatenate([a.reshape(-1) for a in self.k])
+        v = np.concatenate([a.reshape(-1) for a in self.v])
+        bt = torch.from_numpy(self.bt.view(np.int32)).to(dev)
+
+        def i32(a):
+            return torch.from_numpy(np.ascontiguousarray(a, np.int32)).to(dev)
+
+        pool.append(to_torch(k, "bf16", dev), to_torch(v, "bf16", dev), i32(tok_seq), i32(tok_slot), i32(tok_pos), bt)
+        masks = None if self.masks is None else torch.from_numpy(self.masks).to(dev)
+        out = pool.prefill_attn(to_torch(self.q, "bf16", dev), i32(self.q_pos), i32(self.q_off), i32(self.L), bt,
+                                tree_masks=masks, max_q=max_q)
+        torch.cuda.synchronize()
+        return to_numpy_f32(out)
+
+
+def check(case: PrefillCase, what: str):
+    host, ref = case.run_oracle()
+    with case.make_pool() as pool:
+        out = case.run_gpu(pool)
+        err = pool.last_error()
+        ids = np.sort(case.bt[case.bt != PAGE_NONE])
+        pages = pool.read_pages(ids)
+    assert err == 0, f"device error word {err}"
+    np.testing.assert_array_equal(pages, host.data[ids], err_msg="stored pages differ from the oracle")
+    return assert_close_rows(out, ref, RTOL, what)
+
+
+def test_prefill_causal_chunks_group3(cuda):
+    # one token, chunks inside and across 42-token query tiles, prefixes that
+    # are and are not multiples of the page size
+    case = PrefillCase(24, 8, [(0, 1), (0, 37), (5, 16), (100, 50), (16, 128), (300, 200)], seed=11)
+    check(case, "causal 24q/8kv")
+
+
+def test_prefill_causal_chunks_group4(cuda):
+    case = PrefillCase(32, 8, [(0, 33), (129, 7), (255, 129), (1000, 96)], seed=12)
+    check(case, "causal 32q/8kv")
+
+
+def test_prefill_from_position_zero_long(cuda):
+    # a whole 1024-token prompt in one chunk (the reference's attn_prefill case)
+    case = PrefillCase(32, 8, [(0, 1024)], seed=13)
+    check(case, "prompt 1024")
+
+
+def test_prefill_single_kv_head(cuda):
+    case = PrefillCase(4, 1, [(3000, 64), (0, 17)], seed=14)
+    check(case, "4q/1kv")
+
+
+@pytest.mark.parametrize("n_q", [24, 32])
+def test_tree_verify(cuda, n_q):
+    rng = np.random.default_rng(n_q)
+
+    def rand_tree(n):
+        return [-1] + [int(rng.integers(0, i)) for i in range(1, n)]
+
+    seqs = [(37, rand_tree(20)), (0, rand_tree(64)), (200, [-1]), (16, list(range(-1, 15))), (513, rand_tree(43))]
+    check(PrefillCase(n_q, 8, seqs, seed=15), f"tree {n_q}q/8kv")
+
+
+def test_prefill_empty_chunk_and_zero_seqs(cuda):
+    case = PrefillCase(24, 8, [(10, 0), (0, 5), (20, 0)], seed=16)
+    check(case, "empty chunks")
+    import torch
+
+    with case.make_pool() as pool:
+        e = torch.empty(0, 24, 64, dtype=torch.bfloat16, device=cuda)
+        z = torch.zeros(1, dtype=torch.int32, device=cuda)
+        pool.prefill_attn(e, z[:0], z, z[:0], torch.zeros(1, 1, dtype=torch.int32, device=cuda), max_q=0)
+        assert pool.last_error() == 0
+
+
+def test_prefill_chunk_longer_than_max_q_is_flagged(cuda):
+    case = PrefillCase(24, 8, [(0, 50)], seed=17)
+    with case.make_pool() as pool:
+        case.run_gpu(pool, max_q=10)
+        assert pool.last_error() == 1  # KV_ERR_INVALID
+        assert pool.last_error() == 0  # the word was cleared
+
+
+def test_prefill_rejects_f32_pool(cuda):
+    import torch
+
+    from llmhost_b200._capi import KvError
+    from llmhost_b200.kv import KvPool
+
+    with KvPool(dtype="f32", n_q_heads=24, n_kv_heads=8, n_pages=8, max_positions=64, max_seqs=2) as pool:
+        q = torch.zeros(1, 24, 64, dtype=torch.float32, device=cuda)
+        z = torch.zeros(2, dtype=torch.int32, device=cuda)
+        with pytest.raises(KvError) as e:
+            pool.prefill_attn(q, z[:1], torch.tensor([0, 1], dtype=torch.int32, device=cuda), z[:1],
+                              torch.zeros(1, 1, dtype=torch.int32, device=cuda), max_q=1)
+        assert e.value.status == 6

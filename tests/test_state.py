@@ -314,3 +314,23 @@ def test_export_tables_pads_with_none():
     assert rows[0].tolist()[:3] == st.table(1, 1) and rows[0, 3] == NONE
     assert rows[1].tolist() == st.table(2, 1) + [NONE] * 3
     assert np.all(rows[1, 1:] == NONE)
+
+
+# ---- tree-verify masks for kv_prefill_attn ----------------------------------------------------
+def test_tree_masks_are_ancestor_or_self_sets():
+    from llmhost_b200.kv import tree_masks
+
+    rng = random.Random(7)
+    for n in (1, 2, 17, 64):
+        tree = _rand_tree(rng, n)
+        m = tree_masks(tree).view(np.uint64)
+        for i in range(n):
+            anc, node = set(), i
+            while node != -1:
+                anc.add(node)
+                node = tree[node]
+            assert {j for j in range(n) if (int(m[i]) >> j) & 1} == anc
+    with pytest.raises(ValueError):
+        tree_masks([-1] * 65)
+    with pytest.raises(ValueError):
+        tree_masks([-1, 1])
