@@ -7,19 +7,27 @@
 // (causal chunk) or, for a speculative tree, when bit j of its
 // ancestor-or-self mask is set.  The chunk's K/V must already be in pages.
 //
-// One CTA per (sequence, kv head, tile of 128 query rows); a row is a
-// (token, query head of the group) pair.  Warps 0-3 own one row per thread
-// (softmax), warp 4 streams K/V head slices page by page with TMA (one
-// {64 x 16} bf16 box per page and per K / V, 128-byte swizzle, no multicast)
-// into a 2-stage ring of 128-key blocks, warp 5 allocates TMEM and issues the
-// tensor-core MMAs from one thread:
-//   S  = Q K^T  : M 128, N 128, K 64, bf16 operands K-major, fp32 in TMEM;
-//   PV = P V    : M 128, N 64,  K 128, P K-major from shared memory, V
-//                 MN-major straight from the page layout, fp32 in TMEM.
-// The softmax threads read their row of S from TMEM, keep the running max
-// and sum in log2 units (q is pre-scaled by log2(e)/sqrt(d)), write P as bf16
-// to shared memory, then fold PV into an fp32 accumulator in registers.
-// Pages past the sequence load as out-of-range boxes (zero fill).
+// One CTA per (sequence, kv head, group of 4 x 128 query rows); a row is a
+// (token, query head of the group) pair.  Keys are consumed in blocks of 64
+// (4 pages).  Roles:
+//   warps 0-15  softmax, one thread per row: warps 4t..4t+3 own tile t
+//   warp 16     TMA producer: per page one {64 x 16} bf16 box of K and one of
+//               V for this kv head (128-byte swizzle, no multicast) into a
+//               4-stage ring
+//   warp 17     TMEM owner; one thread issues the tensor-core MMAs
+//                 S_t  = Q_t K^T : M 128, N 64, K 64, bf16 K-major, fp32 in TMEM
+//                 O_t += P_t V   : M 128, N 64, K 64, P K-major, V MN-major
+//                                  (straight from the page layout), fp32 in TMEM
+// TMEM holds S_t and O_t of all four tiles (4 x 128 columns).  Four tiles keep
+// the tensor core busy while each tile's S -> softmax -> P handoff is in
+// flight, and give every scheduler four softmax warps.
+//
+// Softmax (log2 units: q is pre-scaled by log2(e)/sqrt(d)) keeps a per-row
+// reference maximum m: P = 2^(S - m) is computed in the same pass that finds
+// the block maximum, and only when a block maximum exceeds m by more than
+// kLazyLog2 is m raised, O (in TMEM) and the row sum rescaled and P redone.
+// P therefore stays below 2^kLazyLog2.  Pages past the sequence load as
+// out-of-range boxes (zero fill).
 #include <cmath>
 
 #include "kv_common.cuh"
@@ -28,23 +36,31 @@
 namespace kvb200 {
 namespace {
 
-constexpr int kRows = 128;                                // MMA M
-constexpr int kBlockKeys = 128;                           // keys per block (MMA N of S)
-constexpr int kPagesPerBlock = kBlockKeys / kPageTokens;  // 8
-constexpr int kStages = 2;
-constexpr int kTile = kRows * 128;                        // 16 KiB: 128 rows of 64 bf16
+constexpr int kRows = 128;                                // MMA M: query rows per tile
+constexpr int kTiles = 4;                                 // query tiles per CTA
+constexpr int kBlockKeys = 64;                            // keys per block (MMA N of S, K of PV)
+constexpr int kPagesPerBlock = kBlockKeys / kPageTokens;  // 4
+constexpr int kStages = 4;                                // K/V block ring
+constexpr int kTile = kRows * 128;                        // 16 KiB: 128 rows of 64 bf16 (Q or P tile)
+constexpr int kKvBytes = kBlockKeys * 128;                // 8 KiB: K (or V) of one block
 constexpr int kSliceBytes = kPageTokens * 128;            // one page's K (or V) rows of one head
-constexpr uint32_t kTmemCols = 256;
-constexpr uint32_t kColS = 0, kColPV = 128;
-constexpr int kThreads = 192;
+constexpr uint32_t kTmemCols = 512;                       // tile t: S at 128 t, O at 128 t + 64
+constexpr int kSoftmaxThreads = kTiles * kRows;           // warps 0-15
+constexpr int kProducerWarp = kSoftmaxThreads / 32;       // warp 16: TMA
+constexpr int kMmaWarp = kProducerWarp + 1;               // warp 17: TMEM owner, MMA issue
+constexpr int kThreads = kSoftmaxThreads + 64;
 
 // smem offsets from the 1024-aligned base
-constexpr int kOffQ = 0;
-constexpr int kOffP = kOffQ + kTile;                      // 2 sub-tiles (keys 0-63, 64-127)
-constexpr int kOffStage = kOffP + 2 * kTile;              // stage st: K at +0, V at +kTile
-constexpr int kStageBytes = 2 * kTile;
+constexpr int kOffQ = 0;                                  // Q tile t at + t * kTile
+constexpr int kOffP = kOffQ + kTiles * kTile;             // P tile t at + t * kTile
+constexpr int kOffStage = kOffP + kTiles * kTile;         // stage st: K at +0, V at +kKvBytes
+constexpr int kStageBytes = 2 * kKvBytes;
 constexpr int kOffBar = kOffStage + kStages * kStageBytes;
-constexpr int kSmemBytes = 1024 + kOffBar + 128;
+constexpr int kSmemBytes = 1024 + kOffBar + 256;
+
+// P entries stay below 2^kLazyLog2 times the row's reference maximum; the
+// reference is raised only when a block's maximum exceeds it by more.
+constexpr float kLazyLog2 = 8.f;
 
 struct PrefillArgs {
     const __nv_bfloat16* q;
@@ -54,7 +70,7 @@ struct PrefillArgs {
     const unsigned long long* tree;
     const uint32_t* bt;
     long long bt_stride;
-    int n_q, nkv, group, tile_tokens;
+    int n_q, nkv, group, tile_tokens, max_q;
     const float2* rope;
     int max_pos;
     uint32_t n_pages;
@@ -94,23 +110,36 @@ __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence:
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void proxy_fence() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
-// 32 consecutive fp32 columns of this warp's 32 TMEM lanes.
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
-    uint32_t r[32];
+// 16 consecutive fp32 columns of this warp's 32 TMEM lanes (warp-collective).
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
     asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
         : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
-          "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]),
-          "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]),
-          "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
         : "r"(taddr));
-#pragma unroll
-    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+// Waits for this thread's TMEM loads; the registers are tied to the wait so
+// no use of them can be scheduled before it.
+__device__ __forceinline__ void tmem_wait16(uint32_t (&r)[16]) {
+    asm volatile("tcgen05.wait::ld.sync.aligned;"
+                 : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]),
+                   "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]),
+                   "+r"(r[14]), "+r"(r[15])
+                 :
+                 : "memory");
+}
+
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+            taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+        "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+        : "memory");
+}
+
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 __device__ __forceinline__ float ex2f(float x) {
     float r;
@@ -118,19 +147,131 @@ __device__ __forceinline__ float ex2f(float x) {
     return r;
 }
 
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+    float r;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+    return r;
+}
+
+// max(m, v[0..15])
+__device__ __forceinline__ float max16(float m, const float (&v)[16]) {
+    const float a = max3f(v[0], v[1], v[2]), b = max3f(v[3], v[4], v[5]), c = max3f(v[6], v[7], v[8]);
+    const float d = max3f(v[9], v[10], v[11]), e = max3f(v[12], v[13], v[14]), f = max3f(v[15], m, a);
+    return max3f(max3f(b, c, d), e, f);
+}
+
+// try_wait without a suspend-time hint: the handoffs here are short and on
+// the critical path of every key block.
+__device__ __forceinline__ bool try_wait_nohint(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
 // Bounded wait that gives up (and raises the CTA abort flag) after the time limit.
 __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* err) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (try_wait_nohint(bar, parity)) return true;
     const uint64_t t0 = global_timer_ns();
     for (;;) {
         if (*abort_flag) return false;
-        if (mbar_try_wait(bar, parity)) return true;
+        if (try_wait_nohint(bar, parity)) return true;
         if (global_timer_ns() - t0 > kWaitLimitNs) {
             *abort_flag = 1;
             flag_error(err, kDevErrTimeout);
             return false;
         }
     }
+}
+
+// Row visibility for keys that reach the chunk.
+struct RowMask {
+    int L, T, t_chunk;  // cached keys, chunk length, chunk-relative token of the row
+    unsigned long long bits;
+    bool tree, valid;
+    __device__ __forceinline__ bool visible(int key) const {
+        if (!valid) return false;
+        if (key < L) return true;
+        if (key >= L + T) return false;
+        return tree ? ((bits >> (key - L)) & 1ull) != 0 : (key - L) <= t_chunk;
+    }
+};
+
+// One 16-key group of this thread's S row (keys k0 + 16 g .. k0 + 16 g + 15):
+//   kMax: fold into the block maximum bm
+//   kExp: P = 2^(S - mu) into the P row (two 16-byte chunks) and sum2
+template <bool kMax, bool kExp>
+__device__ __forceinline__ void group16(const uint32_t (&rr)[16], int g, int k0, bool need_mask, const RowMask& rm,
+                                        float mu, uint8_t* prow, int r, float& bm, float2 (&sum2)[2]) {
+    float v[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(rr[i]);
+    if (need_mask) {
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+            if (!rm.visible(k0 + 16 * g + i)) v[i] = -INFINITY;
+    }
+    if (kMax) bm = max16(bm, v);
+    if (kExp) {
+        const float2 nmu = make_float2(-mu, -mu);
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+            uint32_t w[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const float2 d = __fadd2_rn(make_float2(v[8 * hh + 2 * i], v[8 * hh + 2 * i + 1]), nmu);
+                const float2 p = make_float2(ex2f(d.x), ex2f(d.y));
+                sum2[i & 1] = __fadd2_rn(sum2[i & 1], p);
+                w[i] = float2_to_bf16x2(p.x, p.y);
+            }
+            const int c8 = 2 * g + hh;  // 16-byte chunk of the 128-byte P row
+            *reinterpret_cast<uint4*>(prow + ((c8 ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+    }
+}
+
+// One pass over the four 16-key groups of this thread's S row, each TMEM load
+// issued while the previous group is processed.  Warp-collective.
+template <bool kMax, bool kExp>
+__device__ __forceinline__ void sweep_s(uint32_t taddr, int k0, bool need_mask, const RowMask& rm, float mu,
+                                        uint8_t* prow, int r, float& bm, float2 (&sum2)[2]) {
+    uint32_t ra[16], rb[16];
+    tmem_ld16(taddr, ra);
+    tmem_wait16(ra);
+    tmem_ld16(taddr + 16, rb);
+    group16<kMax, kExp>(ra, 0, k0, need_mask, rm, mu, prow, r, bm, sum2);
+    tmem_wait16(rb);
+    tmem_ld16(taddr + 32, ra);
+    group16<kMax, kExp>(rb, 1, k0, need_mask, rm, mu, prow, r, bm, sum2);
+    tmem_wait16(ra);
+    tmem_ld16(taddr + 48, rb);
+    group16<kMax, kExp>(ra, 2, k0, need_mask, rm, mu, prow, r, bm, sum2);
+    tmem_wait16(rb);
+    group16<kMax, kExp>(rb, 3, k0, need_mask, rm, mu, prow, r, bm, sum2);
+}
+
+// O row (64 fp32 columns) scaled in place in TMEM.  Warp-collective.
+__device__ __forceinline__ void scale_o(uint32_t t_o, float f) {
+    const float2 f2 = make_float2(f, f);
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+        uint32_t x[16];
+        tmem_ld16(t_o + 16 * c, x);
+        tmem_wait16(x);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const float2 u = __fmul2_rn(make_float2(__uint_as_float(x[2 * i]), __uint_as_float(x[2 * i + 1])), f2);
+            x[2 * i] = __float_as_uint(u.x);
+            x[2 * i + 1] = __float_as_uint(u.y);
+        }
+        tmem_st16(t_o + 16 * c, x);
+    }
+    tmem_wait_st();
 }
 
 __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_constant__ CUtensorMap hmap,
@@ -140,14 +281,15 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
     const int T = __ldg(a.q_off + s + 1) - q0;
     const int L = __ldg(a.prefix + s);
     const bool tree = a.tree != nullptr;
-    if (T < 0 || L < 0 || T > static_cast<int>(gridDim.x) * a.tile_tokens || (tree && T > 64)) {
+    const int cta_tokens = kTiles * a.tile_tokens;
+    if (T < 0 || L < 0 || T > a.max_q || (tree && T > 64)) {
         if (blockIdx.x == 0 && h == 0 && threadIdx.x == 0) flag_error(a.err, kDevErrBadArg);
         return;
     }
-    const int t_begin = blockIdx.x * a.tile_tokens;
+    const int t_begin = blockIdx.x * cta_tokens;
     if (t_begin >= T) return;
-    const int t_end = min(T, t_begin + a.tile_tokens);
-    const int kmax = tree ? L + T : L + t_end;  // keys [0, kmax) can be visible to this tile
+    const int t_end = min(T, t_begin + cta_tokens);
+    const int kmax = tree ? L + T : L + t_end;  // keys [0, kmax) can be visible to this CTA
     const int nb = (kmax + kBlockKeys - 1) / kBlockKeys;
 
     extern __shared__ uint8_t smem_raw[];
@@ -155,10 +297,10 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
     uint64_t* full = reinterpret_cast<uint64_t*>(base + kOffBar);  // [kStages]
     uint64_t* empty = full + kStages;                               // [kStages]
-    uint64_t* s_full = empty + kStages;
-    uint64_t* p_full = s_full + 1;
-    uint64_t* pv_full = p_full + 1;
-    uint64_t* mma_done = pv_full + 1;
+    uint64_t* s_full = empty + kStages;                             // [kTiles]
+    uint64_t* p_full = s_full + kTiles;                             // [kTiles]
+    uint64_t* pv_full = p_full + kTiles;                            // [kTiles]
+    uint64_t* mma_done = pv_full + kTiles;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -168,68 +310,65 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
             mbar_init(&full[i], 1);
             mbar_init(&empty[i], 1);
         }
-        mbar_init(s_full, 1);
-        mbar_init(p_full, kRows);  // every softmax thread arrives
-        mbar_init(pv_full, 1);
+        for (int t = 0; t < kTiles; ++t) {
+            mbar_init(&s_full[t], 1);
+            mbar_init(&p_full[t], kRows);  // every softmax thread of the tile arrives
+            mbar_init(&pv_full[t], 1);
+        }
         mbar_init(mma_done, 1);
         *abort_flag = 0;
         fence_mbar_init();
     }
-    if (warp == 5) {  // TMEM: S at columns [0, 128), PV at [128, 192)
+    if (warp == kMmaWarp) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(tmem_slot)),
                      "r"(kTmemCols)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
-    if (warp == 4 && lane == 0) prefetch_tmap(&hmap);
+    if (warp == kProducerWarp && lane == 0) prefetch_tmap(&hmap);
 
-    // ---- Q tile (warps 0-3): row r = (token t_begin + r / G, head h*G + r % G),
-    // RoPE at q_pos (rope.rs:76 form), scaled into log2 units, bf16, swizzled.
-    const int r = threadIdx.x;
+    // ---- Q tiles (warps 0-15): thread = (tile tq, row r); row r of tile tq is
+    // (token t_begin + tq * tile_tokens + r / G, head h*G + r % G).  RoPE at
+    // q_pos (rope.rs:76 form), scaled into log2 units, bf16, 128-byte swizzle.
+    const int tq = threadIdx.x / kRows, r = threadIdx.x % kRows;
     const int rt = r / a.group, rg = r % a.group;
-    const int t_row = t_begin + rt;
-    const bool row_valid = (r < kRows) && (rt < a.tile_tokens) && (t_row < t_end);
-    if (r < kRows) {
-        uint4 packed[8];
+    const int t_row = t_begin + tq * a.tile_tokens + rt;
+    const bool row_valid = (threadIdx.x < kSoftmaxThreads) && (rt < a.tile_tokens) && (t_row < t_end);
+    if (threadIdx.x < kSoftmaxThreads) {
+        uint8_t* qrow = base + kOffQ + tq * kTile + r * 128;
         if (row_valid) {
-            const __nv_bfloat16* src = a.q + (static_cast<size_t>(q0 + t_row) * a.n_q + h * a.group + rg) * kHeadDim;
-            float x[kHeadDim];
-#pragma unroll
-            for (int c = 0; c < 8; ++c) {
-                const uint4 u = __ldg(reinterpret_cast<const uint4*>(src) + c);
-                const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const float2 f = bf16x2_to_float2(w[i]);
-                    x[8 * c + 2 * i] = f.x;
-                    x[8 * c + 2 * i + 1] = f.y;
-                }
-            }
+            const uint4* src = reinterpret_cast<const uint4*>(
+                a.q + (static_cast<size_t>(q0 + t_row) * a.n_q + h * a.group + rg) * kHeadDim);
             int pos = __ldg(a.q_pos + q0 + t_row);
             if (pos < 0 || pos >= a.max_pos) {
                 flag_error(a.err, kDevErrBadPos);
                 pos = 0;
             }
             const float2* cs = a.rope + static_cast<size_t>(pos) * (kHeadDim / 2);
-            float y[kHeadDim];
+            // dims 8c .. 8c+7 rotate together with dims 32+8c .. 32+8c+7
 #pragma unroll
-            for (int i = 0; i < kHeadDim / 2; ++i) {
-                const float2 c = __ldg(cs + i);
-                y[i] = __fadd_rn(__fmul_rn(x[i], c.x), __fmul_rn(-x[i + 32], c.y)) * a.qscale;
-                y[i + 32] = __fadd_rn(__fmul_rn(x[i + 32], c.x), __fmul_rn(x[i], c.y)) * a.qscale;
+            for (int c = 0; c < 4; ++c) {
+                const uint4 u0 = __ldg(src + c), u1 = __ldg(src + c + 4);
+                const uint32_t w0[4] = {u0.x, u0.y, u0.z, u0.w}, w1[4] = {u1.x, u1.y, u1.z, u1.w};
+                uint32_t lo[4], hi[4];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const float2 x = bf16x2_to_float2(w0[i]), y = bf16x2_to_float2(w1[i]);
+                    const float2 c0 = __ldg(cs + 8 * c + 2 * i), c1 = __ldg(cs + 8 * c + 2 * i + 1);
+                    const float a0 = __fadd_rn(__fmul_rn(x.x, c0.x), __fmul_rn(-y.x, c0.y)) * a.qscale;
+                    const float a1 = __fadd_rn(__fmul_rn(x.y, c1.x), __fmul_rn(-y.y, c1.y)) * a.qscale;
+                    const float b0 = __fadd_rn(__fmul_rn(y.x, c0.x), __fmul_rn(x.x, c0.y)) * a.qscale;
+                    const float b1 = __fadd_rn(__fmul_rn(y.y, c1.x), __fmul_rn(x.y, c1.y)) * a.qscale;
+                    lo[i] = float2_to_bf16x2(a0, a1);
+                    hi[i] = float2_to_bf16x2(b0, b1);
+                }
+                *reinterpret_cast<uint4*>(qrow + ((c ^ (r & 7)) << 4)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+                *reinterpret_cast<uint4*>(qrow + (((c + 4) ^ (r & 7)) << 4)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
             }
-#pragma unroll
-            for (int c = 0; c < 8; ++c)
-                packed[c] = make_uint4(float2_to_bf16x2(y[8 * c], y[8 * c + 1]), float2_to_bf16x2(y[8 * c + 2], y[8 * c + 3]),
-                                       float2_to_bf16x2(y[8 * c + 4], y[8 * c + 5]),
-                                       float2_to_bf16x2(y[8 * c + 6], y[8 * c + 7]));
         } else {
 #pragma unroll
-            for (int c = 0; c < 8; ++c) packed[c] = make_uint4(0, 0, 0, 0);
+            for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(qrow + (c << 4)) = make_uint4(0, 0, 0, 0);
         }
-#pragma unroll
-        for (int c = 0; c < 8; ++c)
-            *reinterpret_cast<uint4*>(base + kOffQ + r * 128 + ((c ^ (r & 7)) << 4)) = packed[c];
         proxy_fence();  // the tensor core reads Q through the async proxy
     }
     tc_fence_before();
@@ -237,8 +376,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    if (warp == 4) {
-        // ---------------- producer: K/V head slices, 8 pages per block ----------------
+    if (warp == kProducerWarp) {
+        // ---------------- producer: K/V head slices, 4 pages per block ----------------
         if (lane == 0) {
             const int total_rows = static_cast<int>(a.n_pages) * a.page_rows;
             int issued = 0;
@@ -263,7 +402,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
                         }
                     }
                     tma_load_2d(kt + i * kSliceBytes, &hmap, &full[st], 0, rk);
-                    tma_load_2d(kt + kTile + i * kSliceBytes, &hmap, &full[st], 0, rv);
+                    tma_load_2d(kt + kKvBytes + i * kSliceBytes, &hmap, &full[st], 0, rv);
                 }
                 issued = j + 1;
             }
@@ -274,128 +413,141 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
                 }
             }
         }
-    } else if (warp == 5) {
+    } else if (warp == kMmaWarp) {
         // ---------------- MMA issuer (one thread) ----------------
+        // Per block j and tile t: O_t += P_t(j-1) V(j-1) once P_t is written,
+        // then S_t(j) (which overwrites S_t only after the softmax read it).
+        // The K/V stage of block j-1 is released after the last tile's PV.
         if (lane == 0) {
             constexpr uint32_t kIdescS = instr_desc(kBlockKeys, kRows, false);
             constexpr uint32_t kIdescPV = instr_desc(kHeadDim, kRows, true);
             const uint32_t q_addr = smem_addr(base + kOffQ);
             const uint32_t p_addr = smem_addr(base + kOffP);
-            for (int j = 0; j < nb; ++j) {
-                const int st = j % kStages;
-                if (!wait_bar(&full[st], static_cast<uint32_t>(j / kStages) & 1u, abort_flag, a.err)) break;
+            const uint32_t stage_addr = smem_addr(base + kOffStage);
+            for (int j = 0; j <= nb; ++j) {
+                const int st = j % kStages, pst = (j + kStages - 1) % kStages;
+                if (j < nb && !wait_bar(&full[st], static_cast<uint32_t>(j / kStages) & 1u, abort_flag, a.err))
+                    break;
                 tc_fence_after();
-                const uint32_t k_addr = smem_addr(base + kOffStage + st * kStageBytes);
-                const uint32_t v_addr = k_addr + kTile;
+                bool ok = true;
 #pragma unroll
-                for (int kk = 0; kk < kHeadDim / 16; ++kk)
-                    mma_f16(tmem + kColS, smem_desc(q_addr + 32 * kk, 16, 1024), smem_desc(k_addr + 32 * kk, 16, 1024),
-                            kIdescS, kk > 0);
-                mma_commit(s_full);
-                if (!wait_bar(p_full, static_cast<uint32_t>(j) & 1u, abort_flag, a.err)) break;
-                tc_fence_after();
+                for (int t = 0; t < kTiles; ++t) {
+                    if (j > 0) {
+                        if (!wait_bar(&p_full[t], static_cast<uint32_t>(j - 1) & 1u, abort_flag, a.err)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        const uint32_t v_addr = stage_addr + pst * kStageBytes + kKvBytes;
+                        const uint32_t pa = p_addr + t * kTile;
 #pragma unroll
-                for (int kk = 0; kk < kBlockKeys / 16; ++kk)
-                    mma_f16(tmem + kColPV, smem_desc(p_addr + (kk / 4) * kTile + 32 * (kk % 4), 16, 1024),
-                            smem_desc(v_addr + 2048 * kk, kTile, 1024), kIdescPV, kk > 0);
-                mma_commit(pv_full);
-                mma_commit(&empty[st]);
+                        for (int kk = 0; kk < kBlockKeys / 16; ++kk)
+                            mma_f16(tmem + 128 * t + 64, smem_desc(pa + 32 * kk, 16, 1024),
+                                    smem_desc(v_addr + 2048 * kk, kKvBytes, 1024), kIdescPV, j > 1 || kk > 0);
+                        mma_commit(&pv_full[t]);
+                    }
+                    if (j < nb) {
+                        const uint32_t k_addr = stage_addr + st * kStageBytes;
+                        const uint32_t qa = q_addr + t * kTile;
+#pragma unroll
+                        for (int kk = 0; kk < kHeadDim / 16; ++kk)
+                            mma_f16(tmem + 128 * t, smem_desc(qa + 32 * kk, 16, 1024),
+                                    smem_desc(k_addr + 32 * kk, 16, 1024), kIdescS, kk > 0);
+                        mma_commit(&s_full[t]);
+                    }
+                }
+                if (!ok) break;
+                if (j > 0) mma_commit(&empty[pst]);
             }
             // Every MMA issued above has finished before TMEM is released.
             mma_commit(mma_done);
             mbar_wait(mma_done, 0);
         }
     } else {
-        // ---------------- softmax: thread r owns row r ----------------
-        const uint32_t t_lane = tmem + (static_cast<uint32_t>(32 * warp) << 16);
-        const int t_chunk = rt + t_begin;  // chunk-relative token of this row
-        const unsigned long long tmask = (tree && row_valid) ? __ldg(a.tree + q0 + t_row) : 0ull;
-        float o[kHeadDim];
-#pragma unroll
-        for (int i = 0; i < kHeadDim; ++i) o[i] = 0.f;
+        // ---------------- softmax: thread (tq, r) owns row r of tile tq ----------------
+        const uint32_t lane_base = tmem + (static_cast<uint32_t>(32 * (warp & 3)) << 16);
+        const uint32_t t_s = lane_base + 128 * tq;
+        const uint32_t t_o = t_s + 64;
+        RowMask rm;
+        rm.L = L;
+        rm.T = T;
+        rm.t_chunk = t_row;
+        rm.tree = tree;
+        rm.valid = row_valid;
+        rm.bits = (tree && row_valid) ? __ldg(a.tree + q0 + t_row) : 0ull;
+        uint8_t* prow = base + kOffP + tq * kTile + r * 128;
+        // m: the row's reference maximum (log2 units; -inf until a key is seen).
+        // O (in TMEM) and l are sums of 2^(S - m) terms.
         float m = -INFINITY, l = 0.f;
-        for (int j = 0; j < nb; ++j) {
-            if (!wait_bar(s_full, static_cast<uint32_t>(j) & 1u, abort_flag, a.err)) break;
+        // tcgen05.ld / st are warp-collective (.sync.aligned): every branch
+        // around them below is decided by a warp vote, never per row.
+        constexpr unsigned kAll = 0xffffffffu;
+        int j = 0;
+        for (; j < nb; ++j) {
+            if (!__all_sync(kAll, wait_bar(&s_full[tq], static_cast<uint32_t>(j) & 1u, abort_flag, a.err))) break;
+            // PV of the previous block is done: its P buffer is free, O is current
+            if (j > 0 &&
+                !__all_sync(kAll, wait_bar(&pv_full[tq], static_cast<uint32_t>(j - 1) & 1u, abort_flag, a.err)))
+                break;
             tc_fence_after();
-            float sv[kBlockKeys];
-#pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                float part[32];
-                tmem_ld32(t_lane + kColS + 32 * c, part);
-#pragma unroll
-                for (int i = 0; i < 32; ++i) sv[32 * c + i] = part[i];
-            }
-            tmem_wait_ld();
             const int k0 = j * kBlockKeys;
-            if (k0 + kBlockKeys > L) {  // the block reaches the chunk: mask per key
-#pragma unroll
-                for (int c = 0; c < kBlockKeys; ++c) {
-                    const int key = k0 + c;
-                    bool vis;
-                    if (key < L) vis = true;
-                    else if (key >= L + T) vis = false;
-                    else if (tree) vis = (tmask >> (key - L)) & 1ull;
-                    else vis = (key - L) <= t_chunk;
-                    if (!vis || !row_valid) sv[c] = -INFINITY;
-                }
-            }
+            const bool need_mask = !row_valid || k0 + kBlockKeys > L;
+            float2 sum2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
             float bm = -INFINITY;
-#pragma unroll
-            for (int c = 0; c < kBlockKeys; ++c) bm = fmaxf(bm, sv[c]);
-            const float mn = fmaxf(m, bm);
-            const float mu = (mn == -INFINITY) ? 0.f : mn;
-            const float alpha = ex2f(m - mu);
-            float sum = 0.f;
-            uint8_t* prow = base + kOffP + r * 128;
-#pragma unroll
-            for (int c8 = 0; c8 < kBlockKeys / 8; ++c8) {
-                float p[8];
-#pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    p[i] = ex2f(sv[8 * c8 + i] - mu);
-                    sum += p[i];
-                }
-                const uint4 u = make_uint4(float2_to_bf16x2(p[0], p[1]), float2_to_bf16x2(p[2], p[3]),
-                                           float2_to_bf16x2(p[4], p[5]), float2_to_bf16x2(p[6], p[7]));
-                *reinterpret_cast<uint4*>(prow + (c8 / 8) * kTile + (((c8 % 8) ^ (r & 7)) << 4)) = u;
+            const bool first = __any_sync(kAll, m == -INFINITY);  // some row has no reference yet
+            if (!first)  // one pass: block maximum and P against the current reference
+                sweep_s<true, true>(t_s, k0, need_mask, rm, m, prow, r, bm, sum2);
+            else
+                sweep_s<true, false>(t_s, k0, need_mask, rm, 0.f, prow, r, bm, sum2);
+            // raise this row's reference to the block maximum?
+            const bool raise = bm > m + kLazyLog2 || (m == -INFINITY && bm != -INFINITY);
+            if (first || __any_sync(kAll, raise)) {
+                const bool rescale = raise && m != -INFINITY;
+                const float alpha = rescale ? ex2f(m - bm) : 1.f;
+                if (__any_sync(kAll, rescale)) scale_o(t_o, alpha);  // O *= alpha (1 for other rows)
+                l *= alpha;
+                if (raise) m = bm;
+                // redo P for the whole warp; rows with no visible key yet have
+                // S = -inf everywhere, so mu = 0 gives P = 0
+                sum2[0] = sum2[1] = make_float2(0.f, 0.f);
+                sweep_s<false, true>(t_s, k0, need_mask, rm, m == -INFINITY ? 0.f : m, prow, r, bm, sum2);
             }
-            l = l * alpha + sum;
-            m = mn;
             proxy_fence();  // P is read by the tensor core (async proxy)
             tc_fence_before();
-            mbar_arrive(p_full);
-            if (!wait_bar(pv_full, static_cast<uint32_t>(j) & 1u, abort_flag, a.err)) break;
-            tc_fence_after();
-            float pv[kHeadDim];
-#pragma unroll
-            for (int c = 0; c < 2; ++c) {
-                float part[32];
-                tmem_ld32(t_lane + kColPV + 32 * c, part);
-#pragma unroll
-                for (int i = 0; i < 32; ++i) pv[32 * c + i] = part[i];
-            }
-            tmem_wait_ld();
-#pragma unroll
-            for (int i = 0; i < kHeadDim; ++i) o[i] = fmaf(o[i], alpha, pv[i]);
+            mbar_arrive(&p_full[tq]);
+            const float2 s01 = __fadd2_rn(sum2[0], sum2[1]);
+            l += s01.x + s01.y;
         }
-        if (row_valid && !*abort_flag) {
+        if (j == nb &&
+            __all_sync(kAll, wait_bar(&pv_full[tq], static_cast<uint32_t>(nb - 1) & 1u, abort_flag, a.err))) {
+            tc_fence_after();
             const float inv = l > 0.f ? 1.f / l : 0.f;
             __nv_bfloat16* dst = a.out + (static_cast<size_t>(q0 + t_row) * a.n_q + h * a.group + rg) * kHeadDim;
+            const bool write = row_valid && !*abort_flag;
 #pragma unroll
-            for (int c = 0; c < 8; ++c)
-                reinterpret_cast<uint4*>(dst)[c] =
-                    make_uint4(float2_to_bf16x2(o[8 * c] * inv, o[8 * c + 1] * inv),
-                               float2_to_bf16x2(o[8 * c + 2] * inv, o[8 * c + 3] * inv),
-                               float2_to_bf16x2(o[8 * c + 4] * inv, o[8 * c + 5] * inv),
-                               float2_to_bf16x2(o[8 * c + 6] * inv, o[8 * c + 7] * inv));
+            for (int c = 0; c < 4; ++c) {
+                uint32_t x[16];
+                tmem_ld16(t_o + 16 * c, x);
+                tmem_wait16(x);
+                uint32_t w[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i)
+                    w[i] = float2_to_bf16x2(__uint_as_float(x[2 * i]) * inv, __uint_as_float(x[2 * i + 1]) * inv);
+                if (write) {
+                    reinterpret_cast<uint4*>(dst)[2 * c] = make_uint4(w[0], w[1], w[2], w[3]);
+                    reinterpret_cast<uint4*>(dst)[2 * c + 1] = make_uint4(w[4], w[5], w[6], w[7]);
+                }
+            }
         }
     }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    if (warp == 5)
+    if (warp == kMmaWarp) {
+        __syncwarp();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols)
                      : "memory");
+    }
 }
 
 }  // namespace
@@ -427,6 +579,7 @@ int launch_prefill(kv_pool* pool, const void* q, const int32_t* q_pos, const int
     a.nkv = c.n_kv_heads;
     a.group = group;
     a.tile_tokens = kRows / group;
+    a.max_q = max_q;
     a.rope = pool->rope;
     a.max_pos = c.max_positions;
     a.n_pages = c.n_pages;
@@ -434,7 +587,8 @@ int launch_prefill(kv_pool* pool, const void* q, const int32_t* q_pos, const int
     a.out = static_cast<__nv_bfloat16*>(out);
     a.err = pool->dev_error;
     a.qscale = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(c.head_dim)));
-    const dim3 grid((max_q + a.tile_tokens - 1) / a.tile_tokens, c.n_kv_heads, n_seqs);
+    const int cta_tokens = kTiles * a.tile_tokens;
+    const dim3 grid((max_q + cta_tokens - 1) / cta_tokens, c.n_kv_heads, n_seqs);
     void* args[] = {&pool->head_map, &a};
     const cudaError_t e = cudaLaunchKernel(reinterpret_cast<const void*>(&prefill_kernel), grid, dim3(kThreads), args,
                                            kSmemBytes, stream);
