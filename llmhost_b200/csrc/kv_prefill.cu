@@ -7,20 +7,20 @@
 // (causal chunk) or, for a speculative tree, when bit j of its
 // ancestor-or-self mask is set.  The chunk's K/V must already be in pages.
 //
-// One CTA per (sequence, kv head, group of 4 x 128 query rows); a row is a
-// (token, query head of the group) pair.  Keys are consumed in blocks of 64
-// (4 pages).  Roles:
-//   warps 0-15  softmax, one thread per row: warps 4t..4t+3 own tile t
-//   warp 16     TMA producer: per page one {64 x 16} bf16 box of K and one of
+// One CTA per (sequence, kv head, 2 x 128 query rows); a row is a (token,
+// query head of the group) pair.  Keys are consumed in blocks of 128 (8 pages).
+// Roles:
+//   warps 0-7   softmax, one thread per row: warps 4t..4t+3 own tile t
+//   warp 8      TMA producer: per page one {64 x 16} bf16 box of K and one of
 //               V for this kv head (128-byte swizzle, no multicast) into a
 //               4-stage ring
-//   warp 17     TMEM owner; one thread issues the tensor-core MMAs
-//                 S_t  = Q_t K^T : M 128, N 64, K 64, bf16 K-major, fp32 in TMEM
-//                 O_t += P_t V   : M 128, N 64, K 64, P K-major, V MN-major
-//                                  (straight from the page layout), fp32 in TMEM
-// TMEM holds S_t and O_t of all four tiles (4 x 128 columns).  Four tiles keep
-// the tensor core busy while each tile's S -> softmax -> P handoff is in
-// flight, and give every scheduler four softmax warps.
+//   warp 9      TMEM owner; one thread issues the tensor-core MMAs:
+//                 S_t  = Q_t K^T : M 128, N 128, K 64; Q_t and K K-major in
+//                                  shared memory; fp32 S_t in TMEM
+//                 O_t += P_t V   : M 128, N 64, K 128; P_t (bf16) in TMEM, V
+//                                  MN-major straight from the page layout
+// TMEM per tile (256 columns): S_t [0, 128), P_t [128, 192), O_t [192, 256).
+// The softmax writes P_t group by group while it sweeps S_t.
 //
 // Softmax (log2 units: q is pre-scaled by log2(e)/sqrt(d)) keeps a per-row
 // reference maximum m: P = 2^(S - m) is computed in the same pass that finds
@@ -37,24 +37,25 @@ namespace kvb200 {
 namespace {
 
 constexpr int kRows = 128;                                // MMA M: query rows per tile
-constexpr int kTiles = 4;                                 // query tiles per CTA
-constexpr int kBlockKeys = 64;                            // keys per block (MMA N of S, K of PV)
-constexpr int kPagesPerBlock = kBlockKeys / kPageTokens;  // 4
+constexpr int kTiles = 2;                                 // query tiles per CTA
+constexpr int kBlockKeys = 128;                           // keys per block (MMA N of S, K of PV)
+constexpr int kPagesPerBlock = kBlockKeys / kPageTokens;  // 8
 constexpr int kStages = 4;                                // K/V block ring
-constexpr int kTile = kRows * 128;                        // 16 KiB: 128 rows of 64 bf16 (Q or P tile)
-constexpr int kKvBytes = kBlockKeys * 128;                // 8 KiB: K (or V) of one block
+constexpr int kKvBytes = kBlockKeys * 128;                // 16 KiB: K (or V) of one block
 constexpr int kSliceBytes = kPageTokens * 128;            // one page's K (or V) rows of one head
-constexpr uint32_t kTmemCols = 512;                       // tile t: S at 128 t, O at 128 t + 64
-constexpr int kSoftmaxThreads = kTiles * kRows;           // warps 0-15
-constexpr int kProducerWarp = kSoftmaxThreads / 32;       // warp 16: TMA
-constexpr int kMmaWarp = kProducerWarp + 1;               // warp 17: TMEM owner, MMA issue
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kTileCols = 256;                       // TMEM columns per tile
+constexpr uint32_t kColP = 128, kColO = 192;              // within a tile; S at 0
+constexpr int kSoftmaxThreads = kTiles * kRows;           // warps 0-7
+constexpr int kProducerWarp = kSoftmaxThreads / 32;       // warp 8: TMA
+constexpr int kMmaWarp = kProducerWarp + 1;               // warp 9: TMEM owner, MMA issue
 constexpr int kThreads = kSoftmaxThreads + 64;
 
-// smem offsets from the 1024-aligned base
-constexpr int kOffQ = 0;                                  // Q tile t at + t * kTile
-constexpr int kOffP = kOffQ + kTiles * kTile;             // P tile t at + t * kTile
-constexpr int kOffStage = kOffP + kTiles * kTile;         // stage st: K at +0, V at +kKvBytes
+// smem: Q tiles (128 rows x 128 B, 128-byte swizzle), the K/V ring (stage st:
+// K at +0, V at +kKvBytes), then the barriers
+constexpr int kQBytes = kRows * 128;
 constexpr int kStageBytes = 2 * kKvBytes;
+constexpr int kOffStage = kTiles * kQBytes;
 constexpr int kOffBar = kOffStage + kStages * kStageBytes;
 constexpr int kSmemBytes = 1024 + kOffBar + 256;
 
@@ -93,12 +94,24 @@ __host__ __device__ constexpr uint32_t instr_desc(int n, int m, bool b_mn_major)
            (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);
 }
 
-__device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, bool acc) {
+// tcgen05.mma kind::f16 (bf16 in, fp32 accumulate), both operands in shared memory.
+__device__ __forceinline__ void mma_ss(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, bool acc) {
     asm volatile(
         "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
         "l"(a), "l"(b), "r"(idesc), "r"(acc ? 1 : 0));
 }
+
+// tcgen05.mma kind::f16 (bf16 in, fp32 accumulate) with the A operand in
+// TMEM (lane = row, two bf16 per 32-bit column, lower index in the low half).
+__device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b, uint32_t idesc, bool acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b), "r"(idesc), "r"(acc ? 1 : 0));
+}
+
+__device__ __forceinline__ void proxy_fence() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
@@ -108,7 +121,6 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
 
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void proxy_fence() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 // 16 consecutive fp32 columns of this warp's 32 TMEM lanes (warp-collective).
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
@@ -130,6 +142,29 @@ __device__ __forceinline__ void tmem_wait16(uint32_t (&r)[16]) {
                  : "memory");
 }
 
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
+          "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]),
+          "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]),
+          "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+}
+
+__device__ __forceinline__ void tmem_wait32(uint32_t (&r)[32]) {
+    asm volatile("tcgen05.wait::ld.sync.aligned;"
+                 : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]),
+                   "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]),
+                   "+r"(r[14]), "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]),
+                   "+r"(r[21]), "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]),
+                   "+r"(r[28]), "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
+                 :
+                 : "memory");
+}
+
 __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
     asm volatile(
         "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
@@ -137,6 +172,12 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16
         "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
         "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
         : "memory");
+}
+
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&r)[8]) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr), "r"(r[0]),
+                 "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+                 : "memory");
 }
 
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
@@ -202,57 +243,107 @@ struct RowMask {
     }
 };
 
-// One 16-key group of this thread's S row (keys k0 + 16 g .. k0 + 16 g + 15):
-//   kMax: fold into the block maximum bm
-//   kExp: P = 2^(S - mu) into the P row (two 16-byte chunks) and sum2
-template <bool kMax, bool kExp>
-__device__ __forceinline__ void group16(const uint32_t (&rr)[16], int g, int k0, bool need_mask, const RowMask& rm,
-                                        float mu, uint8_t* prow, int r, float& bm, float2 (&sum2)[2]) {
-    float v[16];
+// One 32-key group g of this thread's S row (keys k0 + 32 g .. k0 + 32 g + 31):
+// folds it into the block maximum bm and writes P = 2^(S - mu) as bf16 pairs
+// to TMEM columns t_p + 16 g .. + 15; adds P to sum2.  Masked keys are made
+// -inf in place.
+__device__ __forceinline__ void group32(uint32_t (&rr)[32], int g, int k0, bool need_mask, const RowMask& rm,
+                                        float mu, uint32_t t_p, float& bm, float2 (&sum2)[2]) {
+    if (need_mask) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+            if (!rm.visible(k0 + 32 * g + i)) rr[i] = __float_as_uint(-INFINITY);
+    }
+    float t[11];
+#pragma unroll
+    for (int i = 0; i < 10; ++i)
+        t[i] = max3f(__uint_as_float(rr[3 * i]), __uint_as_float(rr[3 * i + 1]), __uint_as_float(rr[3 * i + 2]));
+    t[10] = max3f(__uint_as_float(rr[30]), __uint_as_float(rr[31]), bm);
+    bm = max3f(max3f(t[0], t[1], t[2]), max3f(t[3], t[4], t[5]), max3f(max3f(t[6], t[7], t[8]), t[9], t[10]));
+    const float2 nmu = make_float2(-mu, -mu);
+    uint32_t w[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+        const float2 d = __fadd2_rn(make_float2(__uint_as_float(rr[2 * i]), __uint_as_float(rr[2 * i + 1])), nmu);
+        const float2 p = make_float2(ex2f(d.x), ex2f(d.y));
+        sum2[i & 1] = __fadd2_rn(sum2[i & 1], p);
+        w[i] = float2_to_bf16x2(p.x, p.y);
+    }
+    tmem_st16(t_p + 16 * g, w);
+}
+
+// One pass over the four 32-key groups of this thread's S row (block maximum
+// and P against the reference mu), each TMEM load issued while the previous
+// group is processed.  Warp-collective.
+__device__ __forceinline__ void sweep_s(uint32_t t_s, uint32_t t_p, int k0, bool need_mask, const RowMask& rm,
+                                        float mu, float& bm, float2 (&sum2)[2]) {
+    uint32_t ra[32], rb[32];
+    tmem_ld32(t_s, ra);
+    tmem_wait32(ra);
+    tmem_ld32(t_s + 32, rb);
+    group32(ra, 0, k0, need_mask, rm, mu, t_p, bm, sum2);
+    tmem_wait32(rb);
+    tmem_ld32(t_s + 64, ra);
+    group32(rb, 1, k0, need_mask, rm, mu, t_p, bm, sum2);
+    tmem_wait32(ra);
+    tmem_ld32(t_s + 96, rb);
+    group32(ra, 2, k0, need_mask, rm, mu, t_p, bm, sum2);
+    tmem_wait32(rb);
+    group32(rb, 3, k0, need_mask, rm, mu, t_p, bm, sum2);
+}
+
+// S values of a 16-key group as floats, masked keys at -inf.
+__device__ __forceinline__ void s_group(const uint32_t (&rr)[16], int key0, bool need_mask, const RowMask& rm,
+                                        float (&v)[16]) {
 #pragma unroll
     for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(rr[i]);
     if (need_mask) {
 #pragma unroll
         for (int i = 0; i < 16; ++i)
-            if (!rm.visible(k0 + 16 * g + i)) v[i] = -INFINITY;
-    }
-    if (kMax) bm = max16(bm, v);
-    if (kExp) {
-        const float2 nmu = make_float2(-mu, -mu);
-#pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-            uint32_t w[4];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const float2 d = __fadd2_rn(make_float2(v[8 * hh + 2 * i], v[8 * hh + 2 * i + 1]), nmu);
-                const float2 p = make_float2(ex2f(d.x), ex2f(d.y));
-                sum2[i & 1] = __fadd2_rn(sum2[i & 1], p);
-                w[i] = float2_to_bf16x2(p.x, p.y);
-            }
-            const int c8 = 2 * g + hh;  // 16-byte chunk of the 128-byte P row
-            *reinterpret_cast<uint4*>(prow + ((c8 ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
-        }
+            if (!rm.visible(key0 + i)) v[i] = -INFINITY;
     }
 }
 
-// One pass over the four 16-key groups of this thread's S row, each TMEM load
-// issued while the previous group is processed.  Warp-collective.
-template <bool kMax, bool kExp>
-__device__ __forceinline__ void sweep_s(uint32_t taddr, int k0, bool need_mask, const RowMask& rm, float mu,
-                                        uint8_t* prow, int r, float& bm, float2 (&sum2)[2]) {
-    uint32_t ra[16], rb[16];
-    tmem_ld16(taddr, ra);
-    tmem_wait16(ra);
-    tmem_ld16(taddr + 16, rb);
-    group16<kMax, kExp>(ra, 0, k0, need_mask, rm, mu, prow, r, bm, sum2);
-    tmem_wait16(rb);
-    tmem_ld16(taddr + 32, ra);
-    group16<kMax, kExp>(rb, 1, k0, need_mask, rm, mu, prow, r, bm, sum2);
-    tmem_wait16(ra);
-    tmem_ld16(taddr + 48, rb);
-    group16<kMax, kExp>(ra, 2, k0, need_mask, rm, mu, prow, r, bm, sum2);
-    tmem_wait16(rb);
-    group16<kMax, kExp>(rb, 3, k0, need_mask, rm, mu, prow, r, bm, sum2);
+// Block maximum of this thread's S row (rarely needed: first block only).
+// A rolled loop, to keep the instruction footprint of the softmax small.
+__device__ __forceinline__ float row_max(uint32_t taddr, int k0, bool need_mask, const RowMask& rm) {
+    float bm = -INFINITY;
+#pragma unroll 1
+    for (int g = 0; g < 8; ++g) {
+        uint32_t rr[16];
+        tmem_ld16(taddr + 16 * g, rr);
+        tmem_wait16(rr);
+        float v[16];
+        s_group(rr, k0 + 16 * g, need_mask, rm, v);
+        bm = max16(bm, v);
+    }
+    return bm;
+}
+
+// P = 2^(S - mu) straight into the P columns of TMEM (rarely needed: a block
+// that raised a row's reference), plus the row sum.  Rolled loop.
+__device__ __forceinline__ float2 row_exp_to_tmem(uint32_t t_s, uint32_t t_p, int k0, bool need_mask,
+                                                  const RowMask& rm, float mu) {
+    const float2 nmu = make_float2(-mu, -mu);
+    float2 sum2 = make_float2(0.f, 0.f);
+#pragma unroll 1
+    for (int g = 0; g < 8; ++g) {
+        uint32_t rr[16];
+        tmem_ld16(t_s + 16 * g, rr);
+        tmem_wait16(rr);
+        float v[16];
+        s_group(rr, k0 + 16 * g, need_mask, rm, v);
+        uint32_t w[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const float2 d = __fadd2_rn(make_float2(v[2 * i], v[2 * i + 1]), nmu);
+            const float2 p = make_float2(ex2f(d.x), ex2f(d.y));
+            sum2 = __fadd2_rn(sum2, p);
+            w[i] = float2_to_bf16x2(p.x, p.y);
+        }
+        tmem_st8(t_p + 8 * g, w);
+    }
+    return sum2;
 }
 
 // O row (64 fp32 columns) scaled in place in TMEM.  Warp-collective.
@@ -327,15 +418,21 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
     }
     if (warp == kProducerWarp && lane == 0) prefetch_tmap(&hmap);
 
-    // ---- Q tiles (warps 0-15): thread = (tile tq, row r); row r of tile tq is
+    // ---- Q tiles (warps 0-7): thread = (tile tq, row r); row r of tile tq is
     // (token t_begin + tq * tile_tokens + r / G, head h*G + r % G).  RoPE at
-    // q_pos (rope.rs:76 form), scaled into log2 units, bf16, 128-byte swizzle.
+    // q_pos (rope.rs:76 form), scaled into log2 units, bf16, into TMEM.
     const int tq = threadIdx.x / kRows, r = threadIdx.x % kRows;
     const int rt = r / a.group, rg = r % a.group;
     const int t_row = t_begin + tq * a.tile_tokens + rt;
     const bool row_valid = (threadIdx.x < kSoftmaxThreads) && (rt < a.tile_tokens) && (t_row < t_end);
+    tc_fence_before();
+    __syncthreads();  // the TMEM address is published
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(32 * (warp & 3)) << 16);
+    const uint32_t t_tile = lane_base + kTileCols * tq;  // this thread's row of its tile
     if (threadIdx.x < kSoftmaxThreads) {
-        uint8_t* qrow = base + kOffQ + tq * kTile + r * 128;
+        uint8_t* qrow = base + tq * kQBytes + r * 128;
         if (row_valid) {
             const uint4* src = reinterpret_cast<const uint4*>(
                 a.q + (static_cast<size_t>(q0 + t_row) * a.n_q + h * a.group + rg) * kHeadDim);
@@ -374,10 +471,9 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    const uint32_t tmem = *tmem_slot;
 
     if (warp == kProducerWarp) {
-        // ---------------- producer: K/V head slices, 4 pages per block ----------------
+        // ---------------- producer: K/V head slices, 8 pages per block ----------------
         if (lane == 0) {
             const int total_rows = static_cast<int>(a.n_pages) * a.page_rows;
             int issued = 0;
@@ -415,14 +511,15 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
         }
     } else if (warp == kMmaWarp) {
         // ---------------- MMA issuer (one thread) ----------------
-        // Per block j and tile t: O_t += P_t(j-1) V(j-1) once P_t is written,
-        // then S_t(j) (which overwrites S_t only after the softmax read it).
-        // The K/V stage of block j-1 is released after the last tile's PV.
+        // Per block j and tile t: O_t += P_t(j-1) V(j-1) once P_t(j-1) is
+        // written, then S_t(j).  tcgen05.mma executes in issue order, so when
+        // S_t(j) completes P_t(j-1) V(j-1) has too: the softmax may then
+        // overwrite P_t and rescale O_t.  The K/V stage of block j-1 is
+        // released after the last tile's PV.
         if (lane == 0) {
             constexpr uint32_t kIdescS = instr_desc(kBlockKeys, kRows, false);
             constexpr uint32_t kIdescPV = instr_desc(kHeadDim, kRows, true);
-            const uint32_t q_addr = smem_addr(base + kOffQ);
-            const uint32_t p_addr = smem_addr(base + kOffP);
+            const uint32_t q_addr = smem_addr(base);
             const uint32_t stage_addr = smem_addr(base + kOffStage);
             for (int j = 0; j <= nb; ++j) {
                 const int st = j % kStages, pst = (j + kStages - 1) % kStages;
@@ -432,6 +529,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
                 bool ok = true;
 #pragma unroll
                 for (int t = 0; t < kTiles; ++t) {
+                    const uint32_t tt = tmem + kTileCols * t;
                     if (j > 0) {
                         if (!wait_bar(&p_full[t], static_cast<uint32_t>(j - 1) & 1u, abort_flag, a.err)) {
                             ok = false;
@@ -439,20 +537,19 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
                         }
                         tc_fence_after();
                         const uint32_t v_addr = stage_addr + pst * kStageBytes + kKvBytes;
-                        const uint32_t pa = p_addr + t * kTile;
 #pragma unroll
                         for (int kk = 0; kk < kBlockKeys / 16; ++kk)
-                            mma_f16(tmem + 128 * t + 64, smem_desc(pa + 32 * kk, 16, 1024),
-                                    smem_desc(v_addr + 2048 * kk, kKvBytes, 1024), kIdescPV, j > 1 || kk > 0);
+                            mma_ts(tt + kColO, tt + kColP + 8 * kk, smem_desc(v_addr + 2048 * kk, kKvBytes, 1024),
+                                   kIdescPV, j > 1 || kk > 0);
                         mma_commit(&pv_full[t]);
                     }
                     if (j < nb) {
                         const uint32_t k_addr = stage_addr + st * kStageBytes;
-                        const uint32_t qa = q_addr + t * kTile;
+                        const uint32_t qa = q_addr + t * kQBytes;
 #pragma unroll
                         for (int kk = 0; kk < kHeadDim / 16; ++kk)
-                            mma_f16(tmem + 128 * t, smem_desc(qa + 32 * kk, 16, 1024),
-                                    smem_desc(k_addr + 32 * kk, 16, 1024), kIdescS, kk > 0);
+                            mma_ss(tt, smem_desc(qa + 32 * kk, 16, 1024), smem_desc(k_addr + 32 * kk, 16, 1024), kIdescS,
+                                   kk > 0);
                         mma_commit(&s_full[t]);
                     }
                 }
@@ -465,9 +562,6 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
         }
     } else {
         // ---------------- softmax: thread (tq, r) owns row r of tile tq ----------------
-        const uint32_t lane_base = tmem + (static_cast<uint32_t>(32 * (warp & 3)) << 16);
-        const uint32_t t_s = lane_base + 128 * tq;
-        const uint32_t t_o = t_s + 64;
         RowMask rm;
         rm.L = L;
         rm.T = T;
@@ -475,7 +569,6 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
         rm.tree = tree;
         rm.valid = row_valid;
         rm.bits = (tree && row_valid) ? __ldg(a.tree + q0 + t_row) : 0ull;
-        uint8_t* prow = base + kOffP + tq * kTile + r * 128;
         // m: the row's reference maximum (log2 units; -inf until a key is seen).
         // O (in TMEM) and l are sums of 2^(S - m) terms.
         float m = -INFINITY, l = 0.f;
@@ -485,10 +578,6 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
         int j = 0;
         for (; j < nb; ++j) {
             if (!__all_sync(kAll, wait_bar(&s_full[tq], static_cast<uint32_t>(j) & 1u, abort_flag, a.err))) break;
-            // PV of the previous block is done: its P buffer is free, O is current
-            if (j > 0 &&
-                !__all_sync(kAll, wait_bar(&pv_full[tq], static_cast<uint32_t>(j - 1) & 1u, abort_flag, a.err)))
-                break;
             tc_fence_after();
             const int k0 = j * kBlockKeys;
             const bool need_mask = !row_valid || k0 + kBlockKeys > L;
@@ -496,23 +585,24 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
             float bm = -INFINITY;
             const bool first = __any_sync(kAll, m == -INFINITY);  // some row has no reference yet
             if (!first)  // one pass: block maximum and P against the current reference
-                sweep_s<true, true>(t_s, k0, need_mask, rm, m, prow, r, bm, sum2);
+                sweep_s(t_tile, t_tile + kColP, k0, need_mask, rm, m, bm, sum2);
             else
-                sweep_s<true, false>(t_s, k0, need_mask, rm, 0.f, prow, r, bm, sum2);
+                bm = row_max(t_tile, k0, need_mask, rm);
             // raise this row's reference to the block maximum?
             const bool raise = bm > m + kLazyLog2 || (m == -INFINITY && bm != -INFINITY);
             if (first || __any_sync(kAll, raise)) {
                 const bool rescale = raise && m != -INFINITY;
                 const float alpha = rescale ? ex2f(m - bm) : 1.f;
-                if (__any_sync(kAll, rescale)) scale_o(t_o, alpha);  // O *= alpha (1 for other rows)
+                if (__any_sync(kAll, rescale)) scale_o(t_tile + kColO, alpha);  // O *= alpha (1 for other rows)
                 l *= alpha;
                 if (raise) m = bm;
-                // redo P for the whole warp; rows with no visible key yet have
-                // S = -inf everywhere, so mu = 0 gives P = 0
-                sum2[0] = sum2[1] = make_float2(0.f, 0.f);
-                sweep_s<false, true>(t_s, k0, need_mask, rm, m == -INFINITY ? 0.f : m, prow, r, bm, sum2);
+                // P again for the whole warp; rows with no visible key yet
+                // have S = -inf everywhere, so mu = 0 gives P = 0
+                tmem_wait_st();
+                sum2[0] = row_exp_to_tmem(t_tile, t_tile + kColP, k0, need_mask, rm, m == -INFINITY ? 0.f : m);
+                sum2[1] = make_float2(0.f, 0.f);
             }
-            proxy_fence();  // P is read by the tensor core (async proxy)
+            tmem_wait_st();
             tc_fence_before();
             mbar_arrive(&p_full[tq]);
             const float2 s01 = __fadd2_rn(sum2[0], sum2[1]);
@@ -527,7 +617,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
 #pragma unroll
             for (int c = 0; c < 4; ++c) {
                 uint32_t x[16];
-                tmem_ld16(t_o + 16 * c, x);
+                tmem_ld16(t_tile + kColO + 16 * c, x);
                 tmem_wait16(x);
                 uint32_t w[8];
 #pragma unroll
