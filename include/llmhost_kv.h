@@ -136,8 +136,8 @@ int kv_decode_attn(kv_pool *pool, const void *q, const uint32_t *block_tables, i
  * launch covers that many tokens per sequence; a larger T_s, or T_s > 64 with
  * tree masks, is flagged in the error word as an invalid argument).  Slots
  * past L_s + T_s in the sequence's last page must hold finite values (as a
- * fresh pool and kv_append leave them).  bf16 pools only (tcgen05 tensor
- * cores); KV_ERR_UNSUPPORTED for f32. */
+ * fresh pool and kv_append leave them).  bf16 pools run on the tcgen05
+ * tensor cores, fp32 pools on the CUDA cores in fp32. */
 int kv_prefill_attn(kv_pool *pool, const void *q, const int32_t *q_pos, const int32_t *q_offsets,
                     const int32_t *prefix_lens, const uint64_t *tree_masks,
                     const uint32_t *block_tables, int32_t bt_stride, int32_t n_seqs,

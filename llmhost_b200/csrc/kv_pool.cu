@@ -306,7 +306,6 @@ int kv_prefill_attn(kv_pool* pool, const void* q, const int32_t* q_pos, const in
                     const int32_t* prefix_lens, const uint64_t* tree_masks, const uint32_t* block_tables,
                     int32_t bt_stride, int32_t n_seqs, int32_t max_q_per_seq, void* out, void* stream) {
     if (!pool || n_seqs < 0 || max_q_per_seq < 0) return KV_ERR_INVALID;
-    if (pool->cfg.dtype != KV_DTYPE_BF16) return KV_ERR_UNSUPPORTED;
     if (n_seqs == 0 || max_q_per_seq == 0) return KV_OK;
     if (!q || !q_pos || !q_offsets || !prefix_lens || !block_tables || !out || bt_stride <= 0 ||
         n_seqs > 65535 || (tree_masks && max_q_per_seq > 64))

@@ -41,11 +41,15 @@ int launch_decode(kv_pool* pool, const void* q, const uint32_t* bt, int32_t bt_s
                   const int32_t* seq_lens, int32_t n_seqs, int32_t window, void* out,
                   cudaStream_t stream);
 
-// Prefill / tree-verify attention on tcgen05 (kv_prefill.cu); bf16 pools.
+// Prefill / tree-verify attention: tcgen05 for bf16 pools (kv_prefill.cu).
 int prefill_setup(kv_pool* pool);
 int launch_prefill(kv_pool* pool, const void* q, const int32_t* q_pos, const int32_t* q_off,
                    const int32_t* prefix, const unsigned long long* tree, int32_t n_seqs, int32_t max_q,
                    const uint32_t* bt, int32_t bt_stride, void* out, cudaStream_t stream);
+// fp32 pools: CUDA-core kernel (kv_prefill_f32.cu), same arguments.
+int launch_prefill_f32(kv_pool* pool, const void* q, const int32_t* q_pos, const int32_t* q_off,
+                       const int32_t* prefix, const unsigned long long* tree, int32_t n_seqs, int32_t max_q,
+                       const uint32_t* bt, int32_t bt_stride, void* out, cudaStream_t stream);
 
 // Decode launch on explicit workspace pointers and an explicit tensor map,
 // for the entry point that owns no pool (kv_noalloc.cu).

@@ -654,7 +654,8 @@ int launch_prefill(kv_pool* pool, const void* q, const int32_t* q_pos, const int
                    const int32_t* prefix, const unsigned long long* tree, int32_t n_seqs, int32_t max_q,
                    const uint32_t* bt, int32_t bt_stride, void* out, cudaStream_t stream) {
     const auto& c = pool->cfg;
-    if (c.dtype != KV_DTYPE_BF16) return KV_ERR_UNSUPPORTED;
+    if (c.dtype == KV_DTYPE_F32)
+        return launch_prefill_f32(pool, q, q_pos, q_off, prefix, tree, n_seqs, max_q, bt, bt_stride, out, stream);
     const int group = c.n_q_heads / c.n_kv_heads;
     if (group < 1 || group > kRows) return KV_ERR_UNSUPPORTED;
     PrefillArgs a;

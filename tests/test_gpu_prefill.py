@@ -1,12 +1,13 @@
-"""Parity of chunked-prefill and tree-verify attention (kv_prefill_attn, tcgen05)
-against the CPU oracle.
+"""Parity of chunked-prefill and tree-verify attention (kv_prefill_attn) against
+the CPU oracle.
 
 Each sequence has L cached tokens and a chunk of T new ones, all written with
 kv_append (GPU) and orc_paged_append_token (oracle) from the same bits.  The
 oracle gathers the stored K/V, rotates q at its position and runs
 orc_attention_masked with the explicit mask: every cached key, plus chunk key
 j for query i when j <= i (causal chunk) or j is an ancestor-or-self of i
-(tree).  bf16 tolerance 2e-2, normwise per (token, query head) row.
+(tree).  Tolerances normwise per (token, query head) row: 2e-2 for bf16 pools
+(tcgen05 kernel), 1e-5 for fp32 pools (CUDA-core kernel).
 """
 import numpy as np
 import pytest
@@ -16,7 +17,7 @@ from oracle import oracle as O
 from paged_case import PAGE_NONE, assert_close_rows, to_numpy_f32, to_torch
 
 pytestmark = pytest.mark.gpu
-RTOL = 2e-2
+RTOL = {"bf16": 2e-2, "f32": 1e-5}
 
 
 def _depths(parents):
@@ -29,11 +30,11 @@ def _depths(parents):
 class PrefillCase:
     """seqs: list of (L, T) for a causal chunk or (L, parents) for a tree."""
 
-    def __init__(self, n_q, n_kv, seqs, seed=0, extra_pages=4):
+    def __init__(self, n_q, n_kv, seqs, seed=0, extra_pages=4, dtype="bf16"):
         from llmhost_b200.kv import tree_masks
 
         rng = np.random.default_rng(seed)
-        self.n_q, self.n_kv = n_q, n_kv
+        self.n_q, self.n_kv, self.dtype = n_q, n_kv, dtype
         self.L = np.array([s[0] for s in seqs], np.int64)
         self.parents = [None if isinstance(s[1], int) else list(s[1]) for s in seqs]
         self.T = np.array([s[1] if isinstance(s[1], int) else len(s[1]) for s in seqs], np.int64)
@@ -54,9 +55,9 @@ class PrefillCase:
         for s in range(n):
             chunk = _depths(self.parents[s]) if self.parents[s] is not None else list(range(int(self.T[s])))
             self.pos.append(np.concatenate([np.arange(self.L[s]), self.L[s] + np.array(chunk, np.int64)]))
-        self.k = [normal_bits(rng, (int(t), n_kv, 64), "bf16") for t in tot]
-        self.v = [normal_bits(rng, (int(t), n_kv, 64), "bf16") for t in tot]
-        self.q = normal_bits(rng, (int(self.T.sum()), n_q, 64), "bf16")
+        self.k = [normal_bits(rng, (int(t), n_kv, 64), dtype) for t in tot]
+        self.v = [normal_bits(rng, (int(t), n_kv, 64), dtype) for t in tot]
+        self.q = normal_bits(rng, (int(self.T.sum()), n_q, 64), dtype)
         self.q_off = np.concatenate([[0], np.cumsum(self.T)]).astype(np.int32)
         self.q_pos = np.concatenate([p[int(L):] for p, L in zip(self.pos, self.L)]).astype(np.int32)
         self.masks = None
@@ -65,7 +66,7 @@ class PrefillCase:
         self.max_pos = int(max((p.max(initial=0) for p in self.pos), default=0)) + 16
 
     def run_oracle(self):
-        host = O.HostPages(self.n_pages, O.BF16, self.n_q, self.n_kv)
+        host = O.HostPages(self.n_pages, O.BF16 if self.dtype == "bf16" else O.F32, self.n_q, self.n_kv)
         outs = []
         for s in range(len(self.L)):
             L, T = int(self.L[s]), int(self.T[s])
@@ -74,7 +75,8 @@ class PrefillCase:
             if T == 0:
                 continue
             k, v = host.gather(self.bt[s], L + T)
-            q = O.bf16_bits_to_f32(self.q[self.q_off[s]:self.q_off[s + 1]]).copy()  # [T, n_q, d]
+            qr = self.q[self.q_off[s]:self.q_off[s + 1]]
+            q = (O.bf16_bits_to_f32(qr) if self.dtype == "bf16" else np.asarray(qr, np.float32)).copy()  # [T, n_q, d]
             for i in range(T):
                 c, sn = O.cos_sin(host.inv, int(self.q_pos[self.q_off[s] + i]), 1, 64)
                 O.apply_rope_in_place(q[i], c, sn, self.n_q, 1, 64)
@@ -94,7 +96,7 @@ class PrefillCase:
     def make_pool(self):
         from llmhost_b200.kv import KvPool
 
-        return KvPool(dtype="bf16", n_q_heads=self.n_q, n_kv_heads=self.n_kv, n_pages=self.n_pages,
+        return KvPool(dtype=self.dtype, n_q_heads=self.n_q, n_kv_heads=self.n_kv, n_pages=self.n_pages,
                       max_positions=self.max_pos, max_seqs=max(len(self.L), 1))
 
     def run_gpu(self, pool, max_q=None):
@@ -112,9 +114,10 @@ class PrefillCase:
         def i32(a):
             return torch.from_numpy(np.ascontiguousarray(a, np.int32)).to(dev)
 
-        pool.append(to_torch(k, "bf16", dev), to_torch(v, "bf16", dev), i32(tok_seq), i32(tok_slot), i32(tok_pos), bt)
+        pool.append(to_torch(k, self.dtype, dev), to_torch(v, self.dtype, dev), i32(tok_seq), i32(tok_slot),
+                    i32(tok_pos), bt)
         masks = None if self.masks is None else torch.from_numpy(self.masks).to(dev)
-        out = pool.prefill_attn(to_torch(self.q, "bf16", dev), i32(self.q_pos), i32(self.q_off), i32(self.L), bt,
+        out = pool.prefill_attn(to_torch(self.q, self.dtype, dev), i32(self.q_pos), i32(self.q_off), i32(self.L), bt,
                                 tree_masks=masks, max_q=max_q)
         torch.cuda.synchronize()
         return to_numpy_f32(out)
@@ -129,73 +132,70 @@ def check(case: PrefillCase, what: str):
         pages = pool.read_pages(ids)
     assert err == 0, f"device error word {err}"
     np.testing.assert_array_equal(pages, host.data[ids], err_msg="stored pages differ from the oracle")
-    return assert_close_rows(out, ref, RTOL, what)
+    return assert_close_rows(out, ref, RTOL[case.dtype], what)
 
 
-def test_prefill_causal_chunks_group3(cuda):
-    # one token, chunks inside and across 42-token query tiles, prefixes that
-    # are and are not multiples of the page size
-    case = PrefillCase(24, 8, [(0, 1), (0, 37), (5, 16), (100, 50), (16, 128), (300, 200)], seed=11)
-    check(case, "causal 24q/8kv")
+DTYPES = ["bf16", "f32"]
 
 
-def test_prefill_causal_chunks_group4(cuda):
-    case = PrefillCase(32, 8, [(0, 33), (129, 7), (255, 129), (1000, 96)], seed=12)
-    check(case, "causal 32q/8kv")
+@pytest.mark.parametrize("dtype", DTYPES)
+def test_prefill_causal_chunks_group3(cuda, dtype):
+    # one token, chunks inside and across query tiles, prefixes that are and
+    # are not multiples of the page size
+    case = PrefillCase(24, 8, [(0, 1), (0, 37), (5, 16), (100, 50), (16, 128), (300, 200)], seed=11, dtype=dtype)
+    check(case, f"{dtype} causal 24q/8kv")
 
 
-def test_prefill_from_position_zero_long(cuda):
-    # a whole 1024-token prompt in one chunk (the reference's attn_prefill case)
-    case = PrefillCase(32, 8, [(0, 1024)], seed=13)
-    check(case, "prompt 1024")
+@pytest.mark.parametrize("dtype", DTYPES)
+def test_prefill_causal_chunks_group4(cuda, dtype):
+    case = PrefillCase(32, 8, [(0, 33), (129, 7), (255, 129), (1000, 96)], seed=12, dtype=dtype)
+    check(case, f"{dtype} causal 32q/8kv")
 
 
-def test_prefill_single_kv_head(cuda):
-    case = PrefillCase(4, 1, [(3000, 64), (0, 17)], seed=14)
-    check(case, "4q/1kv")
+@pytest.mark.parametrize("dtype", DTYPES)
+def test_prefill_from_position_zero_long(cuda, dtype):
+    # a whole prompt in one chunk (the reference's attn_prefill case; the fp32
+    # single-session workload prefills 2048 tokens of 24q/8kv)
+    n_q, n = (32, 1024) if dtype == "bf16" else (24, 2048)
+    case = PrefillCase(n_q, 8, [(0, n)], seed=13, dtype=dtype)
+    check(case, f"{dtype} prompt {n}")
 
 
+@pytest.mark.parametrize("dtype", DTYPES)
+def test_prefill_single_kv_head(cuda, dtype):
+    case = PrefillCase(4, 1, [(3000, 64), (0, 17)], seed=14, dtype=dtype)
+    check(case, f"{dtype} 4q/1kv")
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
 @pytest.mark.parametrize("n_q", [24, 32])
-def test_tree_verify(cuda, n_q):
+def test_tree_verify(cuda, n_q, dtype):
     rng = np.random.default_rng(n_q)
 
     def rand_tree(n):
         return [-1] + [int(rng.integers(0, i)) for i in range(1, n)]
 
     seqs = [(37, rand_tree(20)), (0, rand_tree(64)), (200, [-1]), (16, list(range(-1, 15))), (513, rand_tree(43))]
-    check(PrefillCase(n_q, 8, seqs, seed=15), f"tree {n_q}q/8kv")
+    check(PrefillCase(n_q, 8, seqs, seed=15, dtype=dtype), f"{dtype} tree {n_q}q/8kv")
 
 
-def test_prefill_empty_chunk_and_zero_seqs(cuda):
-    case = PrefillCase(24, 8, [(10, 0), (0, 5), (20, 0)], seed=16)
-    check(case, "empty chunks")
+@pytest.mark.parametrize("dtype", DTYPES)
+def test_prefill_empty_chunk_and_zero_seqs(cuda, dtype):
+    case = PrefillCase(24, 8, [(10, 0), (0, 5), (20, 0)], seed=16, dtype=dtype)
+    check(case, f"{dtype} empty chunks")
     import torch
 
     with case.make_pool() as pool:
-        e = torch.empty(0, 24, 64, dtype=torch.bfloat16, device=cuda)
+        e = torch.empty(0, 24, 64, dtype=torch.bfloat16 if dtype == "bf16" else torch.float32, device=cuda)
         z = torch.zeros(1, dtype=torch.int32, device=cuda)
         pool.prefill_attn(e, z[:0], z, z[:0], torch.zeros(1, 1, dtype=torch.int32, device=cuda), max_q=0)
         assert pool.last_error() == 0
 
 
-def test_prefill_chunk_longer_than_max_q_is_flagged(cuda):
-    case = PrefillCase(24, 8, [(0, 50)], seed=17)
+@pytest.mark.parametrize("dtype", DTYPES)
+def test_prefill_chunk_longer_than_max_q_is_flagged(cuda, dtype):
+    case = PrefillCase(24, 8, [(0, 50)], seed=17, dtype=dtype)
     with case.make_pool() as pool:
         case.run_gpu(pool, max_q=10)
         assert pool.last_error() == 1  # KV_ERR_INVALID
         assert pool.last_error() == 0  # the word was cleared
-
-
-def test_prefill_rejects_f32_pool(cuda):
-    import torch
-
-    from llmhost_b200._capi import KvError
-    from llmhost_b200.kv import KvPool
-
-    with KvPool(dtype="f32", n_q_heads=24, n_kv_heads=8, n_pages=8, max_positions=64, max_seqs=2) as pool:
-        q = torch.zeros(1, 24, 64, dtype=torch.float32, device=cuda)
-        z = torch.zeros(2, dtype=torch.int32, device=cuda)
-        with pytest.raises(KvError) as e:
-            pool.prefill_attn(q, z[:1], torch.tensor([0, 1], dtype=torch.int32, device=cuda), z[:1],
-                              torch.zeros(1, 1, dtype=torch.int32, device=cuda), max_q=1)
-        assert e.value.status == 6
