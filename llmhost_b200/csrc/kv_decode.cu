@@ -665,9 +665,13 @@ const DecodeVariant* find_variant(int dtype, int nkv, int group) {
         make_variant<__nv_bfloat16, 8, 3, 6>(KV_DTYPE_BF16),
         make_variant<__nv_bfloat16, 8, 4, 6>(KV_DTYPE_BF16),
         make_variant<__nv_bfloat16, 1, 4, 8>(KV_DTYPE_BF16),
+        make_variant<__nv_bfloat16, 2, 4, 8>(KV_DTYPE_BF16),  // 32q/8kv split over 4 GPUs by KV head
+        make_variant<__nv_bfloat16, 4, 4, 6>(KV_DTYPE_BF16),  // ... over 2 GPUs
         make_variant<float, 8, 3, 2>(KV_DTYPE_F32),
         make_variant<float, 8, 4, 2>(KV_DTYPE_F32),
         make_variant<float, 1, 4, 8>(KV_DTYPE_F32),
+        make_variant<float, 2, 4, 4>(KV_DTYPE_F32),
+        make_variant<float, 4, 4, 2>(KV_DTYPE_F32),
     };
     for (const auto& v : table)
         if (v.dtype == dtype && v.nkv == nkv && v.group == group) return &v;

@@ -14,6 +14,7 @@ import torch
 
 from . import _capi
 from ._capi import KV_DTYPE_BF16, KV_DTYPE_F32, KvPoolConfig, check
+from .plans import tree_masks  # noqa: F401  (ancestor-or-self masks for prefill_attn)
 
 _TORCH_DTYPE = {KV_DTYPE_F32: torch.float32, KV_DTYPE_BF16: torch.bfloat16}
 
@@ -209,18 +210,4 @@ class KvPool:
                                         n_seqs, int(max_q), _ptr(out), _stream_ptr(stream)),
               "kv_prefill_attn")
         return out
-
-
-def tree_masks(parents) -> np.ndarray:
-    """Ancestor-or-self bit masks of a parent-index tree (parents[i] < i, root -1),
-    the tree_masks argument of kv_prefill_attn; at most 64 nodes."""
-    n = len(parents)
-    if n > 64:
-        raise ValueError("tree-verify chunks hold at most 64 tokens")
-    m = np.zeros(n, np.uint64)
-    for i, p in enumerate(parents):
-        if not (-1 <= p < i):
-            raise ValueError(f"parent {p} of node {i} does not precede it")
-        m[i] = (m[p] if p >= 0 else np.uint64(0)) | np.uint64(1 << i)
-    return m.view(np.int64)
 

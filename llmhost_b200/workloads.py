@@ -8,6 +8,12 @@ Decode configuration ("bf16 batched decode"): 64 sessions with cached lengths
 uniform in [128, 8192], page size 16, physical pages consumed in order from a
 seeded permutation of a 2^20-page pool, 24 query / 8 KV heads, head_dim 64,
 6 attention layers, one append plus one paged attention per layer per step.
+
+The other configurations (one generator each below): an fp32 single session
+(prefill 2048, then 256 decode steps), bf16 chunked prefill (16 sessions x 32
+chunks of 512 tokens), a speculative tree step (32 sessions sharing a
+4096-token prefix, 64-node trees of depth <= 6), and long context with a
+sliding window (256 sessions, log-uniform lengths, LPT-partitioned over GPUs).
 """
 from __future__ import annotations
 
@@ -119,3 +125,213 @@ def normal_bits(rng: np.random.Generator, shape, dtype: str) -> np.ndarray:
         return x
     u = x.view(np.uint32).astype(np.uint64)
     return ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+
+
+# ---- fp32 single session --------------------------------------------------------------
+@dataclass
+class SingleSessionWorkload:
+    """One fp32 session: prefill `prefill` tokens, then `steps` decode steps.
+    Block table of layer l is contiguous: page l * pages_per_layer + i."""
+    name: str = "fp32 single session"
+    dtype: str = "f32"
+    n_q: int = 24
+    n_kv: int = 8
+    n_layers: int = 6
+    prefill: int = 2048
+    steps: int = 256
+    rope_theta: float = 1e6
+
+    @property
+    def pages_per_layer(self) -> int:
+        return int(ceil_div(self.prefill + self.steps, PAGE_TOKENS))
+
+    @property
+    def pool_pages(self) -> int:
+        return self.n_layers * self.pages_per_layer
+
+    def block_table(self, layer: int) -> np.ndarray:
+        n = self.pages_per_layer
+        return (layer * n + np.arange(n)).astype(np.uint32)
+
+    def prefill_flops(self) -> float:
+        """4 d per visible (query row, key) pair, causal, all layers."""
+        t = self.prefill
+        return 4.0 * 64 * self.n_q * (t * (t + 1) / 2) * self.n_layers
+
+
+# ---- bf16 chunked prefill ---------------------------------------------------------------
+@dataclass
+class ChunkedPrefillWorkload:
+    """Sessions append `chunk`-token chunks up to `total` tokens; chunk c of
+    every session sees the c * chunk cached tokens plus a causal chunk."""
+    name: str
+    n_seqs: int
+    chunk: int
+    total: int
+    n_q: int
+    n_kv: int
+    n_layers: int
+    pool_pages: int
+    block_tables: np.ndarray  # [n_layers, n_seqs, total / 16] uint32
+    dtype: str = "bf16"
+    rope_theta: float = 1e6
+
+    @property
+    def n_chunks(self) -> int:
+        return self.total // self.chunk
+
+    def chunk_flops(self, c: int) -> float:
+        """Algorithmic FLOPs of chunk c for one layer and all sessions: 4 d per
+        visible (query row, key) pair."""
+        C = self.chunk
+        pairs = C * (C * c) + C * (C + 1) / 2
+        return 4.0 * 64 * self.n_q * pairs * self.n_seqs
+
+    def total_flops(self) -> float:
+        return sum(self.chunk_flops(c) for c in range(self.n_chunks)) * self.n_layers
+
+
+def chunked_prefill_config(seed: int = 3, n_seqs: int = 16, chunk: int = 512, total: int = 16384,
+                           n_q: int = 32, n_kv: int = 8, n_layers: int = 6,
+                           pool_pages: int = 1 << 17) -> ChunkedPrefillWorkload:
+    rng = np.random.default_rng(seed)
+    order = rng.permutation(pool_pages).astype(np.uint32)
+    per = total // PAGE_TOKENS
+    need = n_layers * n_seqs * per
+    if need > pool_pages:
+        raise ValueError("pool too small for the chunked-prefill workload")
+    bt = order[:need].reshape(n_layers, n_seqs, per)
+    return ChunkedPrefillWorkload("bf16 chunked prefill", n_seqs, chunk, total, n_q, n_kv, n_layers,
+                                  pool_pages, bt)
+
+
+# ---- speculative tree --------------------------------------------------------------------
+def draft_tree(rng: np.random.Generator, nodes: int = 64, depth: int = 6, fanout: int = 4):
+    """A candidate tree built best-first by cumulative probability: every
+    expanded node offers `fanout` children with Dirichlet(1) probabilities;
+    the most probable open candidate is added next, until `nodes` nodes, no
+    node deeper than `depth` (root at depth 0).  Returns (parents, children)
+    where children[u] is the list of (probability, node index or -1 when the
+    candidate was not added)."""
+    import heapq
+
+    parents = [-1]
+    depth_of = [0]
+    children: list[list[list]] = [[]]
+    heap = []  # (-cumulative probability, tiebreak, parent, slot)
+    tie = 0
+
+    def expand(u, cum):
+        nonlocal tie
+        if depth_of[u] >= depth:
+            return
+        probs = rng.dirichlet(np.ones(fanout))
+        for slot, p in enumerate(probs):
+            children[u].append([float(p), -1])
+            heapq.heappush(heap, (-cum * float(p), tie, u, slot))
+            tie += 1
+
+    expand(0, 1.0)
+    while len(parents) < nodes and heap:
+        negcum, _, u, slot = heapq.heappop(heap)
+        v = len(parents)
+        parents.append(u)
+        depth_of.append(depth_of[u] + 1)
+        children.append([])
+        children[u][slot][1] = v
+        expand(v, -negcum)
+    return parents, children
+
+
+def accept_path(rng: np.random.Generator, children) -> list[int]:
+    """Walk from the root, sampling a child by its probability; stop at a
+    candidate that is not in the tree.  The root is always accepted."""
+    path = [0]
+    u = 0
+    while children[u]:
+        probs = np.array([c[0] for c in children[u]])
+        pick = int(rng.choice(len(probs), p=probs / probs.sum()))
+        v = children[u][pick][1]
+        if v < 0:
+            break
+        path.append(v)
+        u = v
+    return path
+
+
+@dataclass
+class SpecTreeWorkload:
+    name: str = "bf16 speculative tree"
+    n_seqs: int = 32
+    prefix: int = 4096
+    nodes: int = 64
+    depth: int = 6
+    steps: int = 64
+    n_q: int = 24
+    n_kv: int = 8
+    n_layers: int = 6
+    dtype: str = "bf16"
+    pool_pages: int = 1 << 16
+    seed: int = 4
+    rope_theta: float = 1e6
+
+    def plan(self):
+        """Per step and session: (parents, accepted indices)."""
+        rng = np.random.default_rng(self.seed)
+        out = []
+        for _ in range(self.steps):
+            row = []
+            for _ in range(self.n_seqs):
+                parents, children = draft_tree(rng, self.nodes, self.depth)
+                row.append((parents, accept_path(rng, children)))
+            out.append(row)
+        return out
+
+
+# ---- long context with a sliding window ---------------------------------------------------
+def lpt_partition(weights, bins: int) -> list[list[int]]:
+    """Longest-processing-time-first: items in decreasing weight, each to the
+    currently lightest bin (ties to the lowest bin index).  Deterministic."""
+    order = sorted(range(len(weights)), key=lambda i: (-weights[i], i))
+    load = [0] * bins
+    out: list[list[int]] = [[] for _ in range(bins)]
+    for i in order:
+        b = min(range(bins), key=lambda k: (load[k], k))
+        out[b].append(i)
+        load[b] += weights[i]
+    return [sorted(x) for x in out]
+
+
+@dataclass
+class LongContextWorkload:
+    name: str
+    lengths: np.ndarray      # [n_total] tokens cached before step 0, all sessions
+    shard: list              # session indices of this GPU's share
+    window: int
+    steps: int
+    compact_every: int
+    n_q: int
+    n_kv: int
+    n_layers: int
+    dtype: str = "bf16"
+    rope_theta: float = 1e6
+    long_session: int = 1 << 20
+
+    @property
+    def l0(self) -> np.ndarray:
+        return self.lengths[self.shard]
+
+
+def long_context_config(rank: int = 0, bins: int = 8, seed: int = 5, n_total: int = 256,
+                        lo: int = 1024, hi: int = 131072, window: int = 32768, steps: int = 256,
+                        compact_every: int = 64, n_q: int = 32, n_kv: int = 8,
+                        n_layers: int = 6) -> LongContextWorkload:
+    """256 sessions with lengths log-uniform in [lo, hi]; GPU `rank` of `bins`
+    takes the LPT share by resident length min(L, window)."""
+    rng = np.random.default_rng(seed)
+    lengths = np.exp(rng.uniform(np.log(lo), np.log(hi), size=n_total)).astype(np.int64)
+    resident = np.minimum(lengths, window)
+    parts = lpt_partition(resident.tolist(), bins)
+    return LongContextWorkload("bf16 long context, sliding window", lengths, parts[rank % bins], window, steps,
+                               compact_every, n_q, n_kv, n_layers)
+

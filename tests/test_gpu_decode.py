@@ -146,3 +146,12 @@ def test_bad_page_id_sets_error_word(cuda):
         assert pool.last_error() == 2
         # the context stays usable
         assert pool.last_error() == 0
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "f32"])
+@pytest.mark.parametrize("n_kv", [2, 4])
+def test_decode_kv_head_shards(cuda, dtype, n_kv):
+    # the shapes one GPU holds when a 32q/8kv session is split by KV head over 4 or 2 GPUs
+    case = DecodeCase(dtype, 4 * n_kv, n_kv, [3, 900, 5000, 17], seed=6 + n_kv)
+    out, ref = run_case(case)
+    assert_close_rows(out, ref, RTOL[dtype], f"{dtype} {4 * n_kv}q/{n_kv}kv")
