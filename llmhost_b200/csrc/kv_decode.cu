@@ -28,6 +28,8 @@
 // Every wait is bounded by %globaltimer; a timeout sets the pool's error word
 // and an abort flag so the CTA drains and exits instead of hanging.
 #include <cmath>
+#include <map>
+#include <mutex>
 
 #include "kv_common.cuh"
 #include "kv_pool_impl.h"
@@ -81,6 +83,9 @@ __device__ __forceinline__ int find_seq(const int* pstart, int n, int g) {
     }
     return lo;
 }
+
+// Fewest pages a CTA's slice holds (unless the batch has fewer in total).
+constexpr int kMinSlicePages = 8;
 
 // CTA whose slice [floor(c*T/G), floor((c+1)*T/G)) holds global page x.
 __device__ __forceinline__ int cta_of(int x, int grid, int total) {
@@ -399,13 +404,18 @@ decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeArgs a) {
     __syncthreads();
 
     const int total = pstart[n];
-    const int grid = gridDim.x, cta = blockIdx.x;
-    for (int s = cta; s < n; s += grid) {  // sequences with no tokens: zeros
+    const int cta = blockIdx.x;
+    // Slices of at least kMinSlicePages pages: a short batch uses fewer CTAs
+    // rather than splitting each sequence over many (whose partials one CTA
+    // would then merge).
+    const int grid = max(1, min(static_cast<int>(gridDim.x), total / kMinSlicePages));
+    for (int s = cta; s < n; s += gridDim.x) {  // sequences with no tokens: zeros
         if (__ldg(a.seq_lens + s) <= 0) {
             T* o = static_cast<T*>(a.out) + static_cast<size_t>(s) * NQ * kHeadDim;
             for (int i = threadIdx.x; i < NQ * kHeadDim; i += NCONS) o[i] = to_elem<T>(0.f);
         }
     }
+    if (cta >= grid) return;
     const int gb = static_cast<int>((static_cast<long long>(cta) * total) / grid);
     const int ge = static_cast<int>((static_cast<long long>(cta + 1) * total) / grid);
     if (gb >= ge) return;
@@ -607,26 +617,55 @@ decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeArgs a) {
             const int n_contrib = dense ? cta_of(s_end - 1, grid, total) - c_first + 1 : s_end - s_begin;
             if (misc[0] == n_contrib - 1) {  // last contributor merges the splits
                 __threadfence();
+                auto slot_of = [&](int i) {
+                    const int c = dense ? c_first + i : cta_of(s_begin + i, grid, total);
+                    return (c == c_first) ? 2 * c + 1 : 2 * c;
+                };
+                // per q head: the largest split maximum and the weighted sum
+                // of the split sums, one warp per head (xbuf is free here)
+                for (int qh = warp; qh < NQ; qh += NCW) {
+                    float mx = -INFINITY;
+                    for (int i = lane; i < n_contrib; i += 32)
+                        mx = fmaxf(mx, __ldcg(a.part_ml + (static_cast<size_t>(slot_of(i)) * NQ + qh) * 2));
+#pragma unroll
+                    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+                    const float mu = (mx == -INFINITY) ? 0.f : mx;
+                    float L = 0.f;
+                    for (int i = lane; i < n_contrib; i += 32) {
+                        const float2 ml = __ldcg(reinterpret_cast<const float2*>(
+                            a.part_ml + (static_cast<size_t>(slot_of(i)) * NQ + qh) * 2));
+                        L = fmaf(ml.y, ex2(ml.x - mu), L);
+                    }
+#pragma unroll
+                    for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+                    if (lane == 0) {
+                        xbuf[2 * qh] = mu;
+                        xbuf[2 * qh + 1] = L;
+                    }
+                }
+                named_bar_sync(1, NCONS);
+                // outputs: dims contiguous across a warp (coalesced partial rows),
+                // four splits in flight per thread
                 for (int idx = threadIdx.x; idx < NQ * kHeadDim; idx += NCONS) {
                     const int qh = idx / kHeadDim, dd = idx % kHeadDim;
-                    float mx = -INFINITY;
-                    for (int i = 0; i < n_contrib; ++i) {
-                        const int c = dense ? c_first + i : cta_of(s_begin + i, grid, total);
-                        const int sl = (c == c_first) ? 2 * c + 1 : 2 * c;
-                        mx = fmaxf(mx, __ldcg(a.part_ml + (static_cast<size_t>(sl) * NQ + qh) * 2));
+                    const float mu = xbuf[2 * qh], L = xbuf[2 * qh + 1];
+                    float O[4] = {0.f, 0.f, 0.f, 0.f};
+                    int i = 0;
+                    for (; i + 4 <= n_contrib; i += 4) {
+#pragma unroll
+                        for (int u = 0; u < 4; ++u) {
+                            const size_t row = static_cast<size_t>(slot_of(i + u)) * NQ + qh;
+                            O[u] = fmaf(__ldcg(a.part_o + row * kHeadDim + dd), ex2(__ldcg(a.part_ml + row * 2) - mu),
+                                        O[u]);
+                        }
                     }
-                    const float mu = (mx == -INFINITY) ? 0.f : mx;
-                    float L = 0.f, O = 0.f;
-                    for (int i = 0; i < n_contrib; ++i) {
-                        const int c = dense ? c_first + i : cta_of(s_begin + i, grid, total);
-                        const int sl = (c == c_first) ? 2 * c + 1 : 2 * c;
-                        const size_t row = static_cast<size_t>(sl) * NQ + qh;
-                        const float w = ex2(__ldcg(a.part_ml + row * 2) - mu);
-                        L = fmaf(__ldcg(a.part_ml + row * 2 + 1), w, L);
-                        O = fmaf(__ldcg(a.part_o + row * kHeadDim + dd), w, O);
+                    for (; i < n_contrib; ++i) {
+                        const size_t row = static_cast<size_t>(slot_of(i)) * NQ + qh;
+                        O[0] = fmaf(__ldcg(a.part_o + row * kHeadDim + dd), ex2(__ldcg(a.part_ml + row * 2) - mu), O[0]);
                     }
+                    const float o = (O[0] + O[1]) + (O[2] + O[3]);
                     static_cast<T*>(a.out)[(static_cast<size_t>(s) * NQ + qh) * kHeadDim + dd] =
-                        to_elem<T>(L > 0.f ? O / L : 0.f);
+                        to_elem<T>(L > 0.f ? o / L : 0.f);
                 }
                 if (threadIdx.x == 0) a.counters[s] = 0;
             }
@@ -678,6 +717,23 @@ const DecodeVariant* find_variant(int dtype, int nkv, int group) {
     return nullptr;
 }
 
+// A kernel's dynamic shared-memory limit is one attribute per device, shared
+// by every pool and caller that launches it.  It only ever grows here, to the
+// largest size any of them needs, so setting up a pool with a smaller
+// workspace never breaks the launches of one created earlier.
+int raise_smem_limit(const void* fn, int device, size_t bytes) {
+    static std::mutex mu;
+    static std::map<std::pair<const void*, int>, size_t> current;
+    std::lock_guard<std::mutex> lock(mu);
+    size_t& cur = current[{fn, device}];
+    if (bytes <= cur) return KV_OK;
+    if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes)) !=
+        cudaSuccess)
+        return KV_ERR_CUDA;
+    cur = bytes;
+    return KV_OK;
+}
+
 }  // namespace
 
 int decode_setup(kv_pool* pool) {
@@ -689,9 +745,7 @@ int decode_setup(kv_pool* pool) {
     if (cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, c.device) != cudaSuccess)
         return KV_ERR_CUDA;
     if (smem > static_cast<size_t>(optin)) return KV_ERR_INVALID;  // max_seqs too large
-    if (cudaFuncSetAttribute(v->fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(smem)) != cudaSuccess)
-        return KV_ERR_CUDA;
+    if (raise_smem_limit(v->fn, c.device, smem) != KV_OK) return KV_ERR_CUDA;
     int per_sm = 0;
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, v->fn, v->threads, smem) !=
             cudaSuccess ||
@@ -742,9 +796,7 @@ int decode_configure_raw(int dtype, int nkv, int group, int max_seqs, int device
     if (cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device) != cudaSuccess)
         return KV_ERR_CUDA;
     if (bytes > static_cast<size_t>(optin)) return KV_ERR_INVALID;
-    if (cudaFuncSetAttribute(v->fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(bytes)) != cudaSuccess)
-        return KV_ERR_CUDA;
+    if (raise_smem_limit(v->fn, device, bytes) != KV_OK) return KV_ERR_CUDA;
     int per_sm = 0;
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, v->fn, v->threads, bytes) != cudaSuccess ||
         per_sm < 1)
@@ -773,11 +825,6 @@ int launch_decode_raw(const DecodeRaw& r, cudaStream_t stream) {
     a.counters = r.counters;
     a.err = r.err;
     a.qscale = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(kHeadDim)));
-    // A pool created since the last call may have lowered the kernel's
-    // shared-memory limit to its own size: restore the size this launch needs.
-    if (cudaFuncSetAttribute(v->fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(r.smem)) != cudaSuccess)
-        return KV_ERR_CUDA;
     CUtensorMap map = *r.map;
     void* args[] = {&map, &a};
     const cudaError_t e = cudaLaunchKernel(v->fn, dim3(r.grid), dim3(v->threads), args, r.smem, stream);

@@ -155,3 +155,19 @@ def test_decode_kv_head_shards(cuda, dtype, n_kv):
     case = DecodeCase(dtype, 4 * n_kv, n_kv, [3, 900, 5000, 17], seed=6 + n_kv)
     out, ref = run_case(case)
     assert_close_rows(out, ref, RTOL[dtype], f"{dtype} {4 * n_kv}q/{n_kv}kv")
+
+
+def test_pools_of_one_shape_with_different_workspaces(cuda):
+    # The decode kernel's shared-memory limit is per device: creating a pool
+    # with a smaller workspace must not break launches of an earlier pool.
+    big = DecodeCase("bf16", 32, 8, [100, 2000] * 16, seed=21)
+    host, ref = big.run_oracle()
+    with big.make_pool(max_seqs=64) as p1:
+        big.prefill_gpu(p1)
+        from llmhost_b200.kv import KvPool
+
+        with KvPool(dtype="bf16", n_q_heads=32, n_kv_heads=8, n_pages=16, max_positions=64, max_seqs=1):
+            pass
+        out = big.decode_gpu(p1)
+        assert p1.last_error() == 0
+    assert_close_rows(to_numpy_f32(out), ref, RTOL["bf16"], "first pool after a smaller one")
