@@ -153,7 +153,7 @@ typedef struct {
 
 /* Page copies (copy-on-write, compaction): page src[i] -> dst[i], i < n, src and
  * dst device arrays.  The copies of one call must be independent (no page is
- * both a source and a destination). */
+ * both a source and a destination).  Any n >= 0 (one launch per 65535). */
 int kv_copy_pages(kv_pool *pool, const uint32_t *src, const uint32_t *dst, int32_t n, void *stream);
 /* Token moves (commit of accepted draft tokens): moves is a device array of
  * n_moves; group g is moves[group_offsets[g] .. group_offsets[g+1]) (device

@@ -90,15 +90,21 @@ int kv_copy_pages(kv_pool* pool, const uint32_t* src, const uint32_t* dst, int32
     using namespace kvb200;
     if (!pool || n < 0) return KV_ERR_INVALID;
     if (n == 0) return KV_OK;
-    if (!src || !dst || n > 65535) return KV_ERR_INVALID;
+    if (!src || !dst) return KV_ERR_INVALID;
     int prev = -1;
     cudaGetDevice(&prev);
     if (prev != pool->cfg.device) cudaSetDevice(pool->cfg.device);
     const int page_vecs = static_cast<int>(pool->page_bytes / 16);
     const unsigned gx = static_cast<unsigned>(std::min(8, (page_vecs + 255) / 256));
-    copy_pages_kernel<<<dim3(gx, n), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-        static_cast<uint4*>(pool->pages), src, dst, n, pool->cfg.n_pages, page_vecs, pool->dev_error);
-    const cudaError_t e = cudaGetLastError();
+    constexpr int kMaxGridY = 65535;  // one launch per 65535 copies (grid.y limit)
+    cudaError_t e = cudaSuccess;
+    for (int32_t off = 0; off < n && e == cudaSuccess; off += kMaxGridY) {
+        const int m = std::min<int32_t>(kMaxGridY, n - off);
+        copy_pages_kernel<<<dim3(gx, m), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+            static_cast<uint4*>(pool->pages), src + off, dst + off, m, pool->cfg.n_pages, page_vecs,
+            pool->dev_error);
+        e = cudaGetLastError();
+    }
     if (prev >= 0 && prev != pool->cfg.device) cudaSetDevice(prev);
     return e == cudaSuccess ? KV_OK : KV_ERR_CUDA;
 }

@@ -136,3 +136,21 @@ def test_speculative_round_matches_oracle(cuda, seed):
         assert_close_rows(to_numpy_f32(out), ref, 2e-2, f"decode after commit, layer {layer}")
     assert pool.last_error() == 0
     pool.close()
+
+
+def test_copy_pages_more_than_one_launch(cuda):
+    # a compaction can move more pages than one launch's grid holds (65535)
+    import torch
+    from llmhost_b200.kv import KvPool
+
+    n = 70000
+    with KvPool(dtype="bf16", n_q_heads=4, n_kv_heads=1, n_pages=2 * n, max_positions=64, max_seqs=1) as pool:
+        src_ids = np.arange(n, 2 * n)
+        data = np.random.default_rng(3).integers(0, 1 << 16, size=(n, pool.shape.page_elems), dtype=np.uint16)
+        pool.write_pages(src_ids, data)
+        pool.copy_pages(torch.arange(n, 2 * n, dtype=torch.int32, device=cuda),
+                        torch.arange(0, n, dtype=torch.int32, device=cuda))
+        torch.cuda.synchronize()
+        assert pool.last_error() == 0
+        got = pool.read_pages(np.array([0, 65534, 65535, 65536, n - 1]))
+    np.testing.assert_array_equal(got, data[[0, 65534, 65535, 65536, n - 1]])
