@@ -54,6 +54,8 @@ def parse_args():
     ap.add_argument("--cpu-budget", type=float, default=12.0, help="seconds of CPU-baseline work")
     ap.add_argument("--schedule", type=int, default=512, help="decode steps in the workload")
     ap.add_argument("--layers", type=int, default=6, help="attention layers (6 in the workload)")
+    ap.add_argument("--prefill-start-chunk", type=int, default=0,
+                    help="prefill workload: chunk of the first warm-up step (profiling a long-prefix chunk)")
     ap.add_argument("--pool-pages", type=int, default=1 << 20,
                     help="pool size in pages (2^20 in the workload; smaller only for profiling)")
     args = ap.parse_args()
@@ -731,11 +733,12 @@ def run_prefill(args, ctx):
                 e[1].record(st)
                 rec.append((e, c))
 
+    c0 = args.prefill_start_chunk
     for w in range(args.warmup):
-        step(w)
+        step(c0 + w)
     torch.cuda.synchronize()
     pool.check_device_error()
-    ms, clocks = ctx.timed(lambda i: step(i, record=True), args.warmup, args.steps)
+    ms, clocks = ctx.timed(lambda i: step(i, record=True), c0 + args.warmup, args.steps)
     pool.check_device_error()
     launch = [(a.elapsed_time(b), c) for (a, b), c in rec]
     flops = sum(wl.chunk_flops(c) for _, c in launch)
@@ -781,7 +784,7 @@ def run_prefill(args, ctx):
         cpu = {"value": v_cpu, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample,
                "host": host_info()}
     if ctx.rank == 0:
-        covered = sorted({(args.warmup + i) % wl.n_chunks for i in range(args.steps)})
+        covered = sorted({(c0 + args.warmup + i) % wl.n_chunks for i in range(args.steps)})
         cfg = {"workload": wl.name, "sessions_per_gpu": n, "chunk": C, "total_tokens": wl.total, "layers": L,
                "q_heads": wl.n_q, "kv_heads": wl.n_kv, "head_dim": 64, "page_tokens": 16,
                "chunks_timed": f"{len(covered)} of {wl.n_chunks}",
@@ -789,7 +792,7 @@ def run_prefill(args, ctx):
                "parallelism": f"batch-sharded x{ctx.world}"}
         print(json.dumps(_line(args, ctx, METRIC_PREFILL, value, "tokens/s", ms / args.steps, "bf16", cfg, roofline,
                                cpu, e2e, args.steps * L * 2, clocks, attention_tflops=achieved,
-                               step_tflops=sum(wl.chunk_flops((args.warmup + i) % wl.n_chunks)
+                               step_tflops=sum(wl.chunk_flops((c0 + args.warmup + i) % wl.n_chunks)
                                                for i in range(args.steps)) * L * ctx.world / (ms / 1e3) / 1e12)),
               flush=True)
     pool.close()
