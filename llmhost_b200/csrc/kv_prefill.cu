@@ -570,8 +570,11 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
         rm.valid = row_valid;
         rm.bits = (tree && row_valid) ? __ldg(a.tree + q0 + t_row) : 0ull;
         // m: the row's reference maximum (log2 units; -inf until a key is seen).
-        // O (in TMEM) and l are sums of 2^(S - m) terms.
-        float m = -INFINITY, l = 0.f;
+        // O (in TMEM) and l are sums of 2^(S - m) terms.  Padding rows (past
+        // the chunk, or the last rows of a tile when G does not divide 128)
+        // have Q = 0, so S = 0 on unmasked keys: they start at m = 0 and never
+        // ask for a first pass or a redo; their results are not written.
+        float m = row_valid ? -INFINITY : 0.f, l = 0.f;
         // tcgen05.ld / st are warp-collective (.sync.aligned): every branch
         // around them below is decided by a warp vote, never per row.
         constexpr unsigned kAll = 0xffffffffu;
@@ -580,7 +583,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
             if (!__all_sync(kAll, wait_bar(&s_full[tq], static_cast<uint32_t>(j) & 1u, abort_flag, a.err))) break;
             tc_fence_after();
             const int k0 = j * kBlockKeys;
-            const bool need_mask = !row_valid || k0 + kBlockKeys > L;
+            const bool need_mask = k0 + kBlockKeys > L;  // block-level, so warp-uniform
             float2 sum2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
             float bm = -INFINITY;
             const bool first = __any_sync(kAll, m == -INFINITY);  // some row has no reference yet
