@@ -86,6 +86,8 @@ __device__ __forceinline__ int find_seq(const int* pstart, int n, int g) {
 
 // Fewest pages a CTA's slice holds (unless the batch has fewer in total).
 constexpr int kMinSlicePages = 8;
+// Split partials a merging thread has in flight at once.
+constexpr int kMergeUnroll = 8;
 
 // CTA whose slice [floor(c*T/G), floor((c+1)*T/G)) holds global page x.
 __device__ __forceinline__ int cta_of(int x, int grid, int total) {
@@ -333,22 +335,27 @@ __device__ __forceinline__ void page_step(const uint8_t* buf, const LaneOffsets<
     __syncwarp();  // pb is rewritten by this warp's next page
 }
 
-// Two warps per kv head, taking alternate pages; warp 0 also issues the loads.
+// Sixteen warps: W = 16 / NKV per kv head, warp (h, sub) taking the slice
+// pages k with k % W == sub; warp 0 also issues the loads.  Few kv heads
+// (one GPU's share of a head-sharded session) thus still fill an SM with one
+// CTA, and a long sequence splits into at most one partial per SM.
 template <typename T, int NKV, int G, int STAGES>
 struct DecodeShape {
-    // Warps alternate pages by parity, and a stage's successive pages must
-    // have the same parity: the warps that wait on a stage's next phase then
-    // have seen its previous one, so a parity wait can never pass on a stale
-    // phase.  Hence an even number of stages.
-    static_assert(STAGES % 2 == 0, "the page ring must have an even number of stages");
+    static constexpr int W = 16 / NKV;
+    static_assert(16 % NKV == 0, "kv heads must divide 16");
+    // A stage's successive pages (k, k + STAGES) go to the same warp: the warp
+    // that waits on a stage's next phase has seen its previous one, so a
+    // parity wait can never pass on a stale phase.  And STAGES >= W keeps every
+    // warp's next page within the issued window.
+    static_assert(STAGES % W == 0, "the page ring must hold a multiple of W stages");
     using Geo = Geom<T, NKV>;
-    static constexpr int kConsumers = 2 * NKV;
+    static constexpr int kConsumers = 16;
     static constexpr int kThreads = kConsumers * 32;
     static size_t smem_bytes(int max_seqs) {
         return 1024 + static_cast<size_t>(STAGES) * Geo::kPageBytes   // page ring
                + 2 * STAGES * 8                                         // full/empty barriers
                + static_cast<size_t>(kConsumers) * G * 16 * 8           // (p, p) buffers
-               + static_cast<size_t>(NKV) * G * (kHeadDim + 4) * 4      // half-merge buffers
+               + static_cast<size_t>(NKV) * (W - 1) * G * (kHeadDim + 4) * 4  // per-head merge buffers
                + 16 + (static_cast<size_t>(max_seqs) + 1) * 4;          // misc + page scan
     }
 };
@@ -358,7 +365,8 @@ __global__ void __launch_bounds__(DecodeShape<T, NKV, G, STAGES>::kThreads, 1)
 decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeArgs a) {
     using Geo = Geom<T, NKV>;
     constexpr int NQ = NKV * G;
-    constexpr int NCW = 2 * NKV;  // warps
+    constexpr int W = DecodeShape<T, NKV, G, STAGES>::W;  // warps per kv head
+    constexpr int NCW = 16;                               // warps
     constexpr int NCONS = NCW * 32;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* stage = reinterpret_cast<uint8_t*>(
@@ -366,8 +374,8 @@ decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeArgs a) {
     uint64_t* full = reinterpret_cast<uint64_t*>(stage + STAGES * Geo::kPageBytes);
     uint64_t* empty = full + STAGES;
     float2* pbuf = reinterpret_cast<float2*>(empty + STAGES);  // [NCW][G][16]
-    float* xbuf = reinterpret_cast<float*>(pbuf + NCW * G * 16);  // [NKV][G][64 + 4]
-    int* misc = reinterpret_cast<int*>(xbuf + NKV * G * (kHeadDim + 4));  // [0] counter, [1] abort
+    float* xbuf = reinterpret_cast<float*>(pbuf + NCW * G * 16);  // [NKV][W - 1][G][64 + 4]
+    int* misc = reinterpret_cast<int*>(xbuf + NKV * (W - 1) * G * (kHeadDim + 4));  // [0] counter, [1] abort
     int* pstart = misc + 4;                                               // [n_seqs + 1]
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -475,11 +483,11 @@ decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeArgs a) {
     if (warp == 0) issue_upto(STAGES);
 
     // ---- consumers: warp w owns kv head w/2 and the slice pages of parity w%2 ----
-    const int h = warp >> 1, half = warp & 1;
+    const int h = warp / W, sub = warp % W;
     const int qd = lane & 3;
     const LaneOffsets<T> lofs(h, lane, NKV);
     float2* my_pb = pbuf + warp * (G * 16);
-    float* my_x = xbuf + h * G * (kHeadDim + 4);
+    float* head_x = xbuf + h * (W - 1) * G * (kHeadDim + 4);  // slots of warps sub = 1 .. W - 1
     float2 q2[G][8];
     float2 o2[G][2];
     float lp[G], M[G];
@@ -503,8 +511,8 @@ decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeArgs a) {
             lp[gg] = 0.f;
             M[gg] = -INFINITY;
         }
-        // This warp's pages of the segment: slice page k = g - gb with k % 2 == half.
-        for (int gw = g + (((g - gb) & 1) ^ half); gw < seg_end; gw += 2) {
+        // This warp's pages of the segment: slice page k = g - gb with k % W == sub.
+        for (int gw = g + ((sub - (g - gb)) % W + W) % W; gw < seg_end; gw += W) {
             const int k = gw - gb;
             // Up to page k + STAGES - 1: it reuses the stage of page k - 1,
             // never the stage of page k that this warp is about to read.
@@ -546,7 +554,8 @@ decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeArgs a) {
             }
         }
         const int dg = lane & 15;
-        if (half == 1 && lane < 16) {
+        if (sub != 0 && lane < 16) {
+            float* my_x = head_x + (sub - 1) * G * (kHeadDim + 4);
 #pragma unroll
             for (int gg = 0; gg < G; ++gg) {
                 *reinterpret_cast<float4*>(my_x + gg * (kHeadDim + 4) + 4 * dg) =
@@ -557,25 +566,28 @@ decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeArgs a) {
                 }
             }
         }
-        named_bar_sync(2 + h, 64);
-        if (half == 0) {
+        named_bar_sync(2 + h, W * 32);
+        if (sub == 0) {
+            for (int j = 0; j < W - 1; ++j) {
+                const float* ox_base = head_x + j * G * (kHeadDim + 4);
 #pragma unroll
-            for (int gg = 0; gg < G; ++gg) {
-                const float4 ox = *reinterpret_cast<const float4*>(my_x + gg * (kHeadDim + 4) + 4 * dg);
-                const float mx = my_x[gg * (kHeadDim + 4) + kHeadDim];
-                const float lx = my_x[gg * (kHeadDim + 4) + kHeadDim + 1];
-                const float mn = fmaxf(M[gg], mx);
-                const float mu = (mn == -INFINITY) ? 0.f : mn;
-                const float wa = ex2(M[gg] - mu), wb = ex2(mx - mu);
-                lp[gg] = lp[gg] * wa + lx * wb;
-                o2[gg][0] = make_float2(fmaf(ox.x, wb, o2[gg][0].x * wa), fmaf(ox.y, wb, o2[gg][0].y * wa));
-                o2[gg][1] = make_float2(fmaf(ox.z, wb, o2[gg][1].x * wa), fmaf(ox.w, wb, o2[gg][1].y * wa));
-                M[gg] = mn;
+                for (int gg = 0; gg < G; ++gg) {
+                    const float4 ox = *reinterpret_cast<const float4*>(ox_base + gg * (kHeadDim + 4) + 4 * dg);
+                    const float mx = ox_base[gg * (kHeadDim + 4) + kHeadDim];
+                    const float lx = ox_base[gg * (kHeadDim + 4) + kHeadDim + 1];
+                    const float mn = fmaxf(M[gg], mx);
+                    const float mu = (mn == -INFINITY) ? 0.f : mn;
+                    const float wa = ex2(M[gg] - mu), wb = ex2(mx - mu);
+                    lp[gg] = lp[gg] * wa + lx * wb;
+                    o2[gg][0] = make_float2(fmaf(ox.x, wb, o2[gg][0].x * wa), fmaf(ox.y, wb, o2[gg][0].y * wa));
+                    o2[gg][1] = make_float2(fmaf(ox.z, wb, o2[gg][1].x * wa), fmaf(ox.w, wb, o2[gg][1].y * wa));
+                    M[gg] = mn;
+                }
             }
         }
-        named_bar_sync(2 + h, 64);  // xbuf is free again
+        named_bar_sync(2 + h, W * 32);  // xbuf is free again
         const bool whole = (s_begin >= gb) && (s_end <= ge);
-        const bool writer = (half == 0 && lane < 16);
+        const bool writer = (sub == 0 && lane < 16);
         if (whole) {
             if (writer) {
 #pragma unroll
@@ -645,15 +657,15 @@ decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeArgs a) {
                 }
                 named_bar_sync(1, NCONS);
                 // outputs: dims contiguous across a warp (coalesced partial rows),
-                // four splits in flight per thread
+                // kMergeUnroll splits in flight per thread
                 for (int idx = threadIdx.x; idx < NQ * kHeadDim; idx += NCONS) {
                     const int qh = idx / kHeadDim, dd = idx % kHeadDim;
                     const float mu = xbuf[2 * qh], L = xbuf[2 * qh + 1];
-                    float O[4] = {0.f, 0.f, 0.f, 0.f};
+                    float O[kMergeUnroll] = {};
                     int i = 0;
-                    for (; i + 4 <= n_contrib; i += 4) {
+                    for (; i + kMergeUnroll <= n_contrib; i += kMergeUnroll) {
 #pragma unroll
-                        for (int u = 0; u < 4; ++u) {
+                        for (int u = 0; u < kMergeUnroll; ++u) {
                             const size_t row = static_cast<size_t>(slot_of(i + u)) * NQ + qh;
                             O[u] = fmaf(__ldcg(a.part_o + row * kHeadDim + dd), ex2(__ldcg(a.part_ml + row * 2) - mu),
                                         O[u]);
@@ -663,7 +675,9 @@ decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeArgs a) {
                         const size_t row = static_cast<size_t>(slot_of(i)) * NQ + qh;
                         O[0] = fmaf(__ldcg(a.part_o + row * kHeadDim + dd), ex2(__ldcg(a.part_ml + row * 2) - mu), O[0]);
                     }
-                    const float o = (O[0] + O[1]) + (O[2] + O[3]);
+                    float o = 0.f;
+#pragma unroll
+                    for (int u = 0; u < kMergeUnroll; ++u) o += O[u];
                     static_cast<T*>(a.out)[(static_cast<size_t>(s) * NQ + qh) * kHeadDim + dd] =
                         to_elem<T>(L > 0.f ? o / L : 0.f);
                 }
@@ -703,14 +717,14 @@ const DecodeVariant* find_variant(int dtype, int nkv, int group) {
     static const DecodeVariant table[] = {
         make_variant<__nv_bfloat16, 8, 3, 6>(KV_DTYPE_BF16),
         make_variant<__nv_bfloat16, 8, 4, 6>(KV_DTYPE_BF16),
-        make_variant<__nv_bfloat16, 1, 4, 8>(KV_DTYPE_BF16),
-        make_variant<__nv_bfloat16, 2, 4, 8>(KV_DTYPE_BF16),  // 32q/8kv split over 4 GPUs by KV head
-        make_variant<__nv_bfloat16, 4, 4, 6>(KV_DTYPE_BF16),  // ... over 2 GPUs
+        make_variant<__nv_bfloat16, 1, 4, 32>(KV_DTYPE_BF16),  // 32q/8kv split over 8 GPUs by KV head
+        make_variant<__nv_bfloat16, 2, 4, 16>(KV_DTYPE_BF16),  // ... over 4 GPUs
+        make_variant<__nv_bfloat16, 4, 4, 8>(KV_DTYPE_BF16),   // ... over 2 GPUs
         make_variant<float, 8, 3, 2>(KV_DTYPE_F32),
         make_variant<float, 8, 4, 2>(KV_DTYPE_F32),
-        make_variant<float, 1, 4, 8>(KV_DTYPE_F32),
-        make_variant<float, 2, 4, 4>(KV_DTYPE_F32),
-        make_variant<float, 4, 4, 2>(KV_DTYPE_F32),
+        make_variant<float, 1, 4, 16>(KV_DTYPE_F32),
+        make_variant<float, 2, 4, 8>(KV_DTYPE_F32),
+        make_variant<float, 4, 4, 4>(KV_DTYPE_F32),
     };
     for (const auto& v : table)
         if (v.dtype == dtype && v.nkv == nkv && v.group == group) return &v;
