@@ -86,8 +86,8 @@ __device__ __forceinline__ int find_seq(const int* pstart, int n, int g) {
 
 // Fewest pages a CTA's slice holds (unless the batch has fewer in total).
 constexpr int kMinSlicePages = 8;
-// Split partials a merging thread has in flight at once.
-constexpr int kMergeUnroll = 8;
+// Partial rows a merging warp has in flight at once.
+constexpr int kMergeBatch = 16;
 
 // CTA whose slice [floor(c*T/G), floor((c+1)*T/G)) holds global page x.
 __device__ __forceinline__ int cta_of(int x, int grid, int total) {
@@ -633,53 +633,89 @@ decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeArgs a) {
                     const int c = dense ? c_first + i : cta_of(s_begin + i, grid, total);
                     return (c == c_first) ? 2 * c + 1 : 2 * c;
                 };
-                // per q head: the largest split maximum and the weighted sum
-                // of the split sums, one warp per head (xbuf is free here)
-                for (int qh = warp; qh < NQ; qh += NCW) {
-                    float mx = -INFINITY;
-                    for (int i = lane; i < n_contrib; i += 32)
-                        mx = fmaxf(mx, __ldcg(a.part_ml + (static_cast<size_t>(slot_of(i)) * NQ + qh) * 2));
+                // One warp folds a head's partial rows (256 bytes each, lane l
+                // takes dims 2l, 2l+1) with an online max, kMergeBatch rows in
+                // flight.  With fewer heads than warps, kWpq warps share a head
+                // (strided over the splits) and combine through xbuf.
+                constexpr int kWpq = NQ >= NCW ? 1 : NCW / NQ;
+                auto fold = [&](int qh, int first, int step, float& Mr, float& Lr, float2& Or) {
+                    Mr = -INFINITY;
+                    Lr = 0.f;
+                    Or = make_float2(0.f, 0.f);
+                    for (int i0 = first; i0 < n_contrib; i0 += step * kMergeBatch) {
+                        float2 ml[kMergeBatch], ov[kMergeBatch];
 #pragma unroll
-                    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-                    const float mu = (mx == -INFINITY) ? 0.f : mx;
-                    float L = 0.f;
-                    for (int i = lane; i < n_contrib; i += 32) {
-                        const float2 ml = __ldcg(reinterpret_cast<const float2*>(
-                            a.part_ml + (static_cast<size_t>(slot_of(i)) * NQ + qh) * 2));
-                        L = fmaf(ml.y, ex2(ml.x - mu), L);
+                        for (int u = 0; u < kMergeBatch; ++u) {
+                            const int i = i0 + u * step;
+                            if (i < n_contrib) {
+                                const size_t row = static_cast<size_t>(slot_of(i)) * NQ + qh;
+                                ml[u] = __ldcg(reinterpret_cast<const float2*>(a.part_ml + row * 2));
+                                ov[u] = __ldcg(reinterpret_cast<const float2*>(a.part_o + row * kHeadDim) + lane);
+                            } else {
+                                ml[u] = make_float2(-INFINITY, 0.f);
+                                ov[u] = make_float2(0.f, 0.f);
+                            }
+                        }
+                        float bm = Mr;
+#pragma unroll
+                        for (int u = 0; u < kMergeBatch; ++u) bm = fmaxf(bm, ml[u].x);
+                        const float mu = (bm == -INFINITY) ? 0.f : bm;
+                        const float sc = ex2(Mr - mu);
+                        Lr *= sc;
+                        Or = make_float2(Or.x * sc, Or.y * sc);
+#pragma unroll
+                        for (int u = 0; u < kMergeBatch; ++u) {
+                            const float w = ex2(ml[u].x - mu);
+                            Lr = fmaf(ml[u].y, w, Lr);
+                            Or = make_float2(fmaf(ov[u].x, w, Or.x), fmaf(ov[u].y, w, Or.y));
+                        }
+                        Mr = bm;
                     }
-#pragma unroll
-                    for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
-                    if (lane == 0) {
-                        xbuf[2 * qh] = mu;
-                        xbuf[2 * qh + 1] = L;
+                };
+                auto write_out = [&](int qh, float Lr, float2 Or) {
+                    const float inv = Lr > 0.f ? 1.f / Lr : 0.f;
+                    T* orow = static_cast<T*>(a.out) + (static_cast<size_t>(s) * NQ + qh) * kHeadDim + 2 * lane;
+                    if constexpr (sizeof(T) == 2)
+                        *reinterpret_cast<uint32_t*>(orow) = float2_to_bf16x2(Or.x * inv, Or.y * inv);
+                    else
+                        *reinterpret_cast<float2*>(orow) = make_float2(Or.x * inv, Or.y * inv);
+                };
+                if constexpr (kWpq == 1) {
+                    for (int qh = warp; qh < NQ; qh += NCW) {
+                        float Mr, Lr;
+                        float2 Or;
+                        fold(qh, 0, 1, Mr, Lr, Or);
+                        write_out(qh, Lr, Or);
                     }
-                }
-                named_bar_sync(1, NCONS);
-                // outputs: dims contiguous across a warp (coalesced partial rows),
-                // kMergeUnroll splits in flight per thread
-                for (int idx = threadIdx.x; idx < NQ * kHeadDim; idx += NCONS) {
-                    const int qh = idx / kHeadDim, dd = idx % kHeadDim;
-                    const float mu = xbuf[2 * qh], L = xbuf[2 * qh + 1];
-                    float O[kMergeUnroll] = {};
-                    int i = 0;
-                    for (; i + kMergeUnroll <= n_contrib; i += kMergeUnroll) {
-#pragma unroll
-                        for (int u = 0; u < kMergeUnroll; ++u) {
-                            const size_t row = static_cast<size_t>(slot_of(i + u)) * NQ + qh;
-                            O[u] = fmaf(__ldcg(a.part_o + row * kHeadDim + dd), ex2(__ldcg(a.part_ml + row * 2) - mu),
-                                        O[u]);
+                } else {
+                    const int qh = warp / kWpq, part = warp % kWpq;
+                    float* st = xbuf + warp * (kHeadDim + 2);  // [NCW][64 + 2]
+                    if (qh < NQ) {
+                        float Mr, Lr;
+                        float2 Or;
+                        fold(qh, part, kWpq, Mr, Lr, Or);
+                        *reinterpret_cast<float2*>(st + 2 * lane) = Or;
+                        if (lane == 0) {
+                            st[kHeadDim] = Mr;
+                            st[kHeadDim + 1] = Lr;
                         }
                     }
-                    for (; i < n_contrib; ++i) {
-                        const size_t row = static_cast<size_t>(slot_of(i)) * NQ + qh;
-                        O[0] = fmaf(__ldcg(a.part_o + row * kHeadDim + dd), ex2(__ldcg(a.part_ml + row * 2) - mu), O[0]);
+                    named_bar_sync(1, NCONS);
+                    if (warp < NQ) {
+                        float Mr = -INFINITY;
+                        for (int p = 0; p < kWpq; ++p) Mr = fmaxf(Mr, xbuf[(warp * kWpq + p) * (kHeadDim + 2) + kHeadDim]);
+                        const float mu = (Mr == -INFINITY) ? 0.f : Mr;
+                        float Lr = 0.f;
+                        float2 Or = make_float2(0.f, 0.f);
+                        for (int p = 0; p < kWpq; ++p) {
+                            const float* sp = xbuf + (warp * kWpq + p) * (kHeadDim + 2);
+                            const float w = ex2(sp[kHeadDim] - mu);
+                            Lr = fmaf(sp[kHeadDim + 1], w, Lr);
+                            const float2 o = *reinterpret_cast<const float2*>(sp + 2 * lane);
+                            Or = make_float2(fmaf(o.x, w, Or.x), fmaf(o.y, w, Or.y));
+                        }
+                        write_out(warp, Lr, Or);
                     }
-                    float o = 0.f;
-#pragma unroll
-                    for (int u = 0; u < kMergeUnroll; ++u) o += O[u];
-                    static_cast<T*>(a.out)[(static_cast<size_t>(s) * NQ + qh) * kHeadDim + dd] =
-                        to_elem<T>(L > 0.f ? o / L : 0.f);
                 }
                 if (threadIdx.x == 0) a.counters[s] = 0;
             }
