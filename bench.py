@@ -7,8 +7,10 @@ independent batches -- weak scaling, no collective on the data path):
 64 sessions, cached lengths uniform in [128, 8192] (seed 1 + 1000*rank), bf16,
 24 query / 8 KV heads, head_dim 64, page 16, pages drawn in order from a seeded
 permutation of a 2^20-page pool, 6 attention layers.  A step is one token per
-session through all 6 layers: per layer one kv_append_decode plus one
-kv_decode_attn.  The 512-step schedule is replayed cyclically when K + W > 512.
+session through all 6 layers: per layer one kv_append_decode_attn (the
+token's K/V append and the attention in one launch; --unfused runs
+kv_append_decode then kv_decode_attn).  The 512-step schedule is replayed
+cyclically when K + W > 512.
 
 Reported: tokens/s over all ranks (value), the device-timed step, the
 decode-attention kernel's achieved HBM GB/s against MEASURED_PEAKS.json
@@ -50,6 +52,8 @@ def parse_args():
     ap.add_argument("--warmup", type=int, default=None, help="untimed warm-up steps (default per workload)")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--unfused", action="store_true",
+                    help="decode workloads: kv_append_decode + kv_decode_attn as two launches per layer")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=12.0, help="seconds of CPU-baseline work")
     ap.add_argument("--schedule", type=int, default=512, help="decode steps in the workload")
@@ -74,12 +78,14 @@ def peaks():
     return FALLBACK_HBM_GBS, "fallback"
 
 
-def load_traffic_ratio():
-    """DRAM bytes / algorithmic bytes of the decode kernel from the committed ncu summary."""
+def load_traffic_ratio(fused: bool = True):
+    """DRAM bytes / algorithmic bytes of the decode kernel (the fused launch,
+    or the attention-only launch) from the committed ncu summary."""
     p = ROOT / "profiles" / "decode_attn_traffic.json"
     if p.exists():
         d = json.loads(p.read_text())
-        return float(d["dram_bytes_per_launch"]) / float(d["algorithmic_bytes_per_launch"]), d
+        r = d if fused else d.get("unfused_attention_launch", d)
+        return float(r["dram_bytes_per_launch"]) / float(r["algorithmic_bytes_per_launch"]), d
     return None, None
 
 
@@ -280,14 +286,22 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     out = [torch.empty((n, wl.n_q, 64), device=dev, dtype=tdt) for _ in range(L)]
     stream = torch.cuda.current_stream()
 
+    fused = not args.unfused
+
     def step(t, ev=None):
         i = t % n_sets
         lens = lens_dev[t % S]
         for l in range(L):
-            pool.append_decode(k_c[i][l], v_c[i][l], bt_dev[l], lens, stream=stream)
-            if ev is not None:
-                ev[l][0].record(stream)
-            pool.decode_attn(q_c[i][l], bt_dev[l], lens, out=out[l], stream=stream)
+            if fused:
+                if ev is not None:
+                    ev[l][0].record(stream)
+                pool.append_decode_attn(k_c[i][l], v_c[i][l], q_c[i][l], bt_dev[l], lens, out=out[l],
+                                        stream=stream)
+            else:
+                pool.append_decode(k_c[i][l], v_c[i][l], bt_dev[l], lens, stream=stream)
+                if ev is not None:
+                    ev[l][0].record(stream)
+                pool.decode_attn(q_c[i][l], bt_dev[l], lens, out=out[l], stream=stream)
             if ev is not None:
                 ev[l][1].record(stream)
 
@@ -329,8 +343,11 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     ms_local = t_start.elapsed_time(t_end)
     ms = max_over_ranks(ms_local)
     kernel_ms = [kev[i][l][0].elapsed_time(kev[i][l][1]) for i in range(K) for l in range(L)]
-    attn_bytes = [wl.attn_bytes((args.warmup + i) % S) for i in range(K) for _ in range(L)]
+    # The fused launch moves the whole layer's algorithmic bytes (append
+    # included); the plain decode launch only the attention's.
     step_bytes = [wl.step_bytes((args.warmup + i) % S) for i in range(K)]
+    attn_bytes = [(step_bytes[i] // L if fused else wl.attn_bytes((args.warmup + i) % S))
+                  for i in range(K) for _ in range(L)]
     tokens = n * K * world
     value = tokens / (ms / 1e3)
     ms_per_step = ms / K
@@ -339,10 +356,11 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     mean_kernel_s = float(np.mean(kernel_ms)) / 1e3
     mean_attn_bytes = float(np.mean(attn_bytes))
     achieved = mean_attn_bytes / mean_kernel_s / 1e9
-    ratio, prof = load_traffic_ratio()
+    ratio, prof = load_traffic_ratio(fused)
     roofline = {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
                 "traffic": (ratio * mean_attn_bytes) if ratio else None,
-                "kernel": "decode_kernel (kv_decode_attn)",
+                "kernel": "decode_kernel (kv_append_decode_attn: append + attention, one launch per layer)"
+                if fused else "decode_kernel (kv_decode_attn)",
                 "algorithmic_bytes_per_launch": mean_attn_bytes,
                 "mean_launch_us": mean_kernel_s * 1e6,
                 "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
@@ -370,8 +388,11 @@ def run_ours(args, rank: int, world: int, local_rank: int):
                 dq[l].copy_(pin_q[i][l], non_blocking=True)
                 dk[l].copy_(pin_k[i][l], non_blocking=True)
                 dv[l].copy_(pin_v[i][l], non_blocking=True)
-                pool.append_decode(dk[l], dv[l], bt_dev[l], dlens, stream=stream)
-                pool.decode_attn(dq[l], bt_dev[l], dlens, out=out[l], stream=stream)
+                if fused:
+                    pool.append_decode_attn(dk[l], dv[l], dq[l], bt_dev[l], dlens, out=out[l], stream=stream)
+                else:
+                    pool.append_decode(dk[l], dv[l], bt_dev[l], dlens, stream=stream)
+                    pool.decode_attn(dq[l], bt_dev[l], dlens, out=out[l], stream=stream)
                 pin_out[l].copy_(out[l], non_blocking=True)
 
         for t in range(3):
@@ -392,7 +413,8 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         d2h = L * n * wl.n_q * 64 * esz
         e2e = {"value": n * Ke * world / (e_ms / 1e3), "unit": UNIT, "h2d_bytes_per_step": h2d,
                "d2h_bytes_per_step": d2h, "steps": Ke,
-               "path": "pinned host q/k/v -> KvPool.append_decode + decode_attn (C ABI) -> pinned host out"}
+               "path": "pinned host q/k/v -> KvPool.append_decode_attn (C ABI) -> pinned host out" if fused
+               else "pinned host q/k/v -> KvPool.append_decode + decode_attn (C ABI) -> pinned host out"}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -415,7 +437,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
                        "parallelism": f"batch-sharded x{world} (independent sessions per GPU)"},
             "step_gbs": step_gbs, "step_frac_of_peak": step_gbs / hbm,
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
-            "gpu_launches": K * L * 2, "clocks": clocks,
+            "gpu_launches": K * L * (1 if fused else 2), "clocks": clocks,
         }
         print(json.dumps(line), flush=True)
     pool.close()
@@ -580,11 +602,10 @@ def run_single(args, ctx):
                 rec["pre"].append(e)
         for t in range(D):
             for l in range(L):
-                pool.append_decode(k_d[l, t], v_d[l, t], bt[l], lens[t], stream=st)
                 e = ctx.events() if record and t % 8 == 0 else None
                 if e:
                     e[0].record(st)
-                pool.decode_attn(q_d[l, t], bt[l], lens[t], out=outd, stream=st)
+                pool.append_decode_attn(k_d[l, t], v_d[l, t], q_d[l, t], bt[l], lens[t], out=outd, stream=st)
                 if e:
                     e[1].record(st)
                     rec["dec"].append((e, T + t + 1))
@@ -626,8 +647,8 @@ def run_single(args, ctx):
                 host_pre[l].copy_(outp, non_blocking=True)
             for t in range(D):
                 for l in range(L):
-                    pool.append_decode(k_d[l, t], v_d[l, t], bt[l], lens[t], stream=st)
-                    pool.decode_attn(q_d[l, t], bt[l], lens[t], out=outd, stream=st)
+                    pool.append_decode_attn(k_d[l, t], v_d[l, t], q_d[l, t], bt[l], lens[t], out=outd,
+                                            stream=st)
                     host_out[l, t].copy_(outd, non_blocking=True)
 
         e2e_job(0)
@@ -1120,11 +1141,10 @@ def run_longctx(args, ctx):
         lens.add_(1)
         j = i % 4
         for l in range(L):
-            pool.append_decode(ks[j, l], vs[j, l], dtables[l], lens, stream=stm)
             e = ctx.events() if record else None
             if e:
                 e[0].record(stm)
-            pool.decode_attn(qs[j, l], dtables[l], lens, window=W, out=out, stream=stm)
+            pool.append_decode_attn(ks[j, l], vs[j, l], qs[j, l], dtables[l], lens, window=W, out=out, stream=stm)
             if e:
                 e[1].record(stm)
                 rec.append(e)
@@ -1133,8 +1153,7 @@ def run_longctx(args, ctx):
         if eb:
             eb[0].record(stm)
         for l in range(L):
-            big.append_decode(bk[j, l], bk[j, l], big_bt[l], big_len_dev, stream=stm)
-            big.decode_attn(bq[j, l], big_bt[l], big_len_dev, out=bout[l], stream=stm)
+            big.append_decode_attn(bk[j, l], bk[j, l], bq[j, l], big_bt[l], big_len_dev, out=bout[l], stream=stm)
         if eb:
             eb[1].record(stm)
             brec.append(eb)

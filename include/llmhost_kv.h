@@ -19,6 +19,8 @@
  *                       prefill K/V store (lfm2.rs:751-761)
  *   kv_decode_attn      attention_decode_cached (lfm2.rs:1006-1056) with RoPE
  *                       on q (lfm2.rs:816-822) and the key mask (lfm2.rs:1032-1035)
+ *   kv_append_decode_attn  the decode K/V store (lfm2.rs:828-832) and
+ *                       attention_decode_cached in one launch
  *   kv_tree_*           validate_tree_for_tokens, validate_accept_path (tree.rs:48-123)
  *   kv_state_*          Engine::{open, forward, accept, rollback, committed,
  *                       session_kv} (batch.rs:128-297) and PagedKv (cache.rs:12-51),
@@ -95,7 +97,8 @@ int kv_pool_write_pages(kv_pool *pool, const uint32_t *page_ids, int32_t n, cons
  * (KV_OK if clear).  Synchronises the pool's device. */
 int kv_last_error(kv_pool *pool);
 
-/* Append tokens.  k, v: [n_tokens, n_kv_heads, head_dim] in the pool dtype.
+/* Append tokens.  k, v: [n_tokens, n_kv_heads, head_dim] in the pool dtype,
+ * 16-byte aligned (KV_ERR_INVALID otherwise).
  * Token i goes to sequence tok_seq[i] (row of block_tables, [n_seqs, bt_stride]
  * u32 page ids), storage slot tok_slot[i] (page bt[slot / P], slot % P), and
  * K is rotated at RoPE position tok_pos[i].  All arrays are device memory.
@@ -107,7 +110,8 @@ int kv_append(kv_pool *pool, const void *k, const void *v, const int32_t *tok_se
               const uint32_t *block_tables, int32_t n_seqs, int32_t bt_stride, void *stream);
 
 /* Decode append: one token per sequence s at position seq_lens[s] - 1, where
- * seq_lens already counts the new token.  k, v: [n_seqs, n_kv_heads, head_dim]. */
+ * seq_lens already counts the new token.  k, v: [n_seqs, n_kv_heads, head_dim],
+ * 16-byte aligned (as for kv_append). */
 int kv_append_decode(kv_pool *pool, const void *k, const void *v, const uint32_t *block_tables,
                      int32_t bt_stride, const int32_t *seq_lens, int32_t n_seqs, void *stream);
 
@@ -119,6 +123,18 @@ int kv_append_decode(kv_pool *pool, const void *k, const void *v, const uint32_t
 int kv_decode_attn(kv_pool *pool, const void *q, const uint32_t *block_tables, int32_t bt_stride,
                    const int32_t *seq_lens, int32_t n_seqs, int32_t window, void *out,
                    void *stream);
+
+/* One decode step of an attention layer in one launch: kv_append_decode(k, v,
+ * ...) followed by kv_decode_attn(q, ...) on the same block tables and
+ * seq_lens, with the same results bit for bit (pages and out).  It replaces
+ * the pair the reference runs per layer: the K/V store (lfm2.rs:828-832)
+ * and attention_decode_cached (lfm2.rs:1006-1056).  The page holding each
+ * sequence's new slot must belong to that sequence alone (copy-on-write
+ * first), as it must for kv_append_decode: the new row is written into the
+ * copy of the page this launch reads, not re-read from HBM. */
+int kv_append_decode_attn(kv_pool *pool, const void *k, const void *v, const void *q,
+                          const uint32_t *block_tables, int32_t bt_stride, const int32_t *seq_lens,
+                          int32_t n_seqs, int32_t window, void *out, void *stream);
 
 /* Chunked-prefill and tree-verify attention: attention_forward
  * (lfm2.rs:1058-1111) for T_s new query tokens of sequence s that follow

@@ -75,6 +75,9 @@ SIGNATURES = [
      [c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_void_p, c_int32, c_void_p]),
     ("kv_decode_attn", c_int32,
      [c_void_p, c_void_p, c_void_p, c_int32, c_void_p, c_int32, c_int32, c_void_p, c_void_p]),
+    ("kv_append_decode_attn", c_int32,
+     [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_void_p, c_int32, c_int32, c_void_p,
+      c_void_p]),
     ("kv_prefill_attn", c_int32,
      [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32,
       c_void_p, c_void_p]),

@@ -63,6 +63,12 @@ struct DecodeArgs {
     int* counters;
     int* err;
     float qscale;  // log2(e) / sqrt(d): scores come out in log2 units
+    // Fused append (kv_append_decode_attn): the new token's K and V,
+    // [n_seqs, NKV, 64] each, stored at slot seq_lens[s] - 1 before it is
+    // attended.  Null: plain decode.
+    const void* new_k;
+    const void* new_v;
+    void* pages;
 };
 
 __device__ __forceinline__ int seq_lo(int n_tok, int window) {
@@ -225,6 +231,102 @@ __device__ __forceinline__ void load_v(const uint8_t* buf, const LaneOffsets<flo
     v1 = make_float2(f.z, f.w);
 }
 
+// Byte offset in a staged page of byte b of token row r (the 128-byte
+// swizzle of the TMA copy: chunk c of 128-byte row R sits at chunk c ^ (R & 7)).
+template <typename T>
+__device__ __forceinline__ uint32_t staged_offset(int r, int b) {
+    constexpr int kRpt = kHeadDim * static_cast<int>(sizeof(T)) / 128;
+    const int R = r * kRpt + (b >> 7);
+    return static_cast<uint32_t>(R * 128 + ((((b & 127) >> 4) ^ (R & 7)) << 4) + (b & 15));
+}
+
+// Bytes a warp stages for a fused append: the new token's K and V rows of
+// its kv head and the (cos, sin) row of its position.
+template <typename T>
+constexpr int patch_bytes() { return 2 * kHeadDim * static_cast<int>(sizeof(T)) + kHeadDim / 2 * 8; }
+
+// Fused append, part 1 (when the warp starts the sequence): cp.async the
+// inputs into the warp's staging area, so part 2 never waits on HBM while it
+// holds a stage of the page ring.
+template <typename T>
+__device__ __forceinline__ void stage_patch_inputs(uint8_t* dst, const T* ks, const T* vs, const float2* cs,
+                                                   int lane) {
+    constexpr int nk = kHeadDim * static_cast<int>(sizeof(T)) / 16;  // 16-byte pieces of a row
+    for (int c = lane; c < 2 * nk + 16; c += 32) {
+        const void* src = c < nk       ? static_cast<const void*>(reinterpret_cast<const uint8_t*>(ks) + 16 * c)
+                          : c < 2 * nk ? static_cast<const void*>(reinterpret_cast<const uint8_t*>(vs) + 16 * (c - nk))
+                                       : static_cast<const void*>(reinterpret_cast<const uint8_t*>(cs) + 16 * (c - 2 * nk));
+        cp_async16(dst + 16 * c, src);
+    }
+    cp_async_commit();
+}
+
+// Fused append, part 2: kv head h's new token (slot j of its page) written by
+// the one warp that reads this head of the staged page, into the staged copy
+// before the warp's first read of it and into the page in HBM (`gpage`).  K
+// is rotated exactly as append_kernel does (two rounded products and a
+// rounded sum per output, then rounding to the pool type), V copied as
+// stored bits, so pages and attention are bit-identical to kv_append_decode
+// followed by kv_decode_attn.  Lanes 0-15: K dims 2i, 2i+1 and their
+// partners 32 + 2i, 33 + 2i; lanes 16-31: V dims [4i, 4i + 4).  Out of line:
+// it runs once per sequence and head, and must not take registers from the
+// page loop.
+template <typename T, int NKV>
+__device__ __noinline__ void patch_new_token(uint8_t* buf, uint8_t* gpage, const uint8_t* in, int h, int j,
+                                             int lane) {
+    constexpr int kE = static_cast<int>(sizeof(T));
+    cp_async_wait<0>();
+    __syncwarp();
+    const int i = lane & 15;
+    if (lane < 16) {
+        const int kr = h * kPageTokens + j;
+        float2 x, y;
+        if constexpr (kE == 2) {
+            x = bf16x2_to_float2(*reinterpret_cast<const uint32_t*>(in + 4 * i));
+            y = bf16x2_to_float2(*reinterpret_cast<const uint32_t*>(in + 64 + 4 * i));
+        } else {
+            x = *reinterpret_cast<const float2*>(in + 8 * i);
+            y = *reinterpret_cast<const float2*>(in + 128 + 8 * i);
+        }
+        const float4 c = *reinterpret_cast<const float4*>(in + 2 * kHeadDim * kE + 16 * i);
+        const float x0 = __fadd_rn(__fmul_rn(x.x, c.x), __fmul_rn(-y.x, c.y));
+        const float x1 = __fadd_rn(__fmul_rn(x.y, c.z), __fmul_rn(-y.y, c.w));
+        const float y0 = __fadd_rn(__fmul_rn(y.x, c.x), __fmul_rn(x.x, c.y));
+        const float y1 = __fadd_rn(__fmul_rn(y.y, c.z), __fmul_rn(x.y, c.w));
+        const int bx = 2 * i * kE, by = (32 + 2 * i) * kE;
+        uint8_t* grow = gpage + kr * kHeadDim * kE;
+        if constexpr (kE == 2) {
+            const uint32_t wx = float2_to_bf16x2(x0, x1), wy = float2_to_bf16x2(y0, y1);
+            *reinterpret_cast<uint32_t*>(buf + staged_offset<T>(kr, bx)) = wx;
+            *reinterpret_cast<uint32_t*>(buf + staged_offset<T>(kr, by)) = wy;
+            *reinterpret_cast<uint32_t*>(grow + bx) = wx;
+            *reinterpret_cast<uint32_t*>(grow + by) = wy;
+        } else {
+            *reinterpret_cast<float2*>(buf + staged_offset<T>(kr, bx)) = make_float2(x0, x1);
+            *reinterpret_cast<float2*>(buf + staged_offset<T>(kr, by)) = make_float2(y0, y1);
+            *reinterpret_cast<float2*>(grow + bx) = make_float2(x0, x1);
+            *reinterpret_cast<float2*>(grow + by) = make_float2(y0, y1);
+        }
+    } else {
+        const int vr = (NKV + h) * kPageTokens + j;
+        const int b = 4 * i * kE;
+        const uint8_t* vin = in + kHeadDim * kE + b;
+        uint8_t* grow = gpage + vr * kHeadDim * kE;
+        if constexpr (kE == 2) {
+            const uint2 w = *reinterpret_cast<const uint2*>(vin);
+            *reinterpret_cast<uint2*>(buf + staged_offset<T>(vr, b)) = w;
+            *reinterpret_cast<uint2*>(grow + b) = w;
+        } else {
+            const float4 w = *reinterpret_cast<const float4*>(vin);
+            *reinterpret_cast<float4*>(buf + staged_offset<T>(vr, b)) = w;
+            *reinterpret_cast<float4*>(grow + b) = w;
+        }
+    }
+    // The stage is refilled by the TMA (async proxy) once it is handed back.
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    __syncwarp();
+}
+
 // Warp-wide max in one instruction (sm_100a redux.sync on f32).
 __device__ __forceinline__ float warp_max(float x) {
     float r;
@@ -356,6 +458,7 @@ struct DecodeShape {
                + 2 * STAGES * 8                                         // full/empty barriers
                + static_cast<size_t>(kConsumers) * G * 16 * 8           // (p, p) buffers
                + static_cast<size_t>(NKV) * (W - 1) * G * (kHeadDim + 4) * 4  // per-head merge buffers
+               + static_cast<size_t>(kConsumers) * patch_bytes<T>()    // fused-append staging
                + 16 + (static_cast<size_t>(max_seqs) + 1) * 4;          // misc + page scan
     }
 };
@@ -375,7 +478,8 @@ decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeArgs a) {
     uint64_t* empty = full + STAGES;
     float2* pbuf = reinterpret_cast<float2*>(empty + STAGES);  // [NCW][G][16]
     float* xbuf = reinterpret_cast<float*>(pbuf + NCW * G * 16);  // [NKV][W - 1][G][64 + 4]
-    int* misc = reinterpret_cast<int*>(xbuf + NKV * (W - 1) * G * (kHeadDim + 4));  // [0] counter, [1] abort
+    uint8_t* patch_in = reinterpret_cast<uint8_t*>(xbuf + NKV * (W - 1) * G * (kHeadDim + 4));  // [NCW][patch_bytes]
+    int* misc = reinterpret_cast<int*>(patch_in + NCW * patch_bytes<T>());  // [0] counter, [1] abort
     int* pstart = misc + 4;                                               // [n_seqs + 1]
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -500,9 +604,22 @@ decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeArgs a) {
         const int s_begin = pstart[s], s_end = pstart[s + 1];
         const int seg_end = min(ge, s_end);
         int pos = nt - 1;
+        // The new token is appended by the warp of each head that reads the
+        // sequence's last page, when this slice holds it.
+        bool patch = a.new_k != nullptr && s_end <= ge;
         if (pos >= a.max_pos) {
             if (lane == 0) flag_error(a.err, kDevErrBadPos);
             pos = 0;
+            patch = false;  // as kv_append_decode: nothing stored
+        }
+        // Of the warps of a head, the one that reads the last page appends.
+        patch = patch && ((s_end - 1 - gb) % W == sub);
+        uint8_t* my_patch_in = patch_in + warp * patch_bytes<T>();
+        if (patch) {
+            const size_t src = (static_cast<size_t>(s) * NKV + h) * kHeadDim;
+            stage_patch_inputs<T>(my_patch_in, static_cast<const T*>(a.new_k) + src,
+                                  static_cast<const T*>(a.new_v) + src,
+                                  a.rope + static_cast<size_t>(pos) * (kHeadDim / 2), lane);
         }
         load_q<T, G>(a, s, NQ, h, qd, pos, q2);
 #pragma unroll
@@ -522,8 +639,17 @@ decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeArgs a) {
             // A failed wait (timeout or abort) keeps the stage: it is never
             // handed back, so no copy can be issued over one still landing.
             if (!wait_or_abort(&full[st], par, abort_flag, a.err)) continue;
-            const uint8_t* buf = stage + st * Geo::kPageBytes;
+            uint8_t* buf = stage + st * Geo::kPageBytes;
             const int pg = plo + (gw - s_begin);
+            if (patch && gw == s_end - 1) {
+                // The loader flagged a bad entry already; store nothing then.
+                const uint32_t page = pg < a.bt_stride
+                                          ? __ldg(a.bt + static_cast<size_t>(s) * a.bt_stride + pg)
+                                          : kPageNone;
+                if (page < a.n_pages)
+                    patch_new_token<T, NKV>(buf, static_cast<uint8_t*>(a.pages) + static_cast<size_t>(page) * Geo::kPageBytes,
+                                            my_patch_in, h, pos % kPageTokens, lane);
+            }
             const int t0 = max(lo - pg * kPageTokens, 0);
             const int t1 = min(nt - pg * kPageTokens, kPageTokens);
             if (t0 == 0 && t1 == kPageTokens)
@@ -723,6 +849,7 @@ decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeArgs a) {
         }
         if (g < ge) s = find_seq(pstart, n, g);
     }
+    cp_async_wait<0>();  // a staged append skipped after a failed wait
     // Warp 0: do not leave while a copy issued here may still be landing.  A
     // stage is reused only after its previous page was handed back, so the
     // last page issued into each stage covers every copy in flight.
@@ -810,7 +937,7 @@ size_t decode_workspace_slots(const kv_pool* pool) { return 2 * static_cast<size
 
 int launch_decode(kv_pool* pool, const void* q, const uint32_t* bt, int32_t bt_stride,
                   const int32_t* seq_lens, int32_t n_seqs, int32_t window, void* out,
-                  cudaStream_t stream) {
+                  cudaStream_t stream, const void* new_k, const void* new_v) {
     const auto& c = pool->cfg;
     const DecodeVariant* v = find_variant(c.dtype, c.n_kv_heads, c.n_q_heads / c.n_kv_heads);
     if (!v) return KV_ERR_UNSUPPORTED;
@@ -830,6 +957,9 @@ int launch_decode(kv_pool* pool, const void* q, const uint32_t* bt, int32_t bt_s
     a.counters = pool->counters;
     a.err = pool->dev_error;
     a.qscale = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(c.head_dim)));
+    a.new_k = new_k;
+    a.new_v = new_v;
+    a.pages = pool->pages;
     void* args[] = {&pool->page_map, &a};
     const cudaError_t e = cudaLaunchKernel(v->fn, dim3(pool->decode_grid), dim3(v->threads), args,
                                            pool->decode_smem, stream);
@@ -875,6 +1005,9 @@ int launch_decode_raw(const DecodeRaw& r, cudaStream_t stream) {
     a.counters = r.counters;
     a.err = r.err;
     a.qscale = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(kHeadDim)));
+    a.new_k = nullptr;
+    a.new_v = nullptr;
+    a.pages = nullptr;
     CUtensorMap map = *r.map;
     void* args[] = {&map, &a};
     const cudaError_t e = cudaLaunchKernel(v->fn, dim3(r.grid), dim3(v->threads), args, r.smem, stream);

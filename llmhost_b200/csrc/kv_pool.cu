@@ -32,6 +32,9 @@ struct DeviceScope {
     }
 };
 
+// The append kernels read k and v rows as 16-byte vectors.
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
 bool valid_config(const kv_pool_config& c) {
     if (c.dtype != KV_DTYPE_F32 && c.dtype != KV_DTYPE_BF16) return false;
     if (c.head_dim != kvb200::kHeadDim || c.page_tokens != kvb200::kPageTokens) return false;
@@ -273,7 +276,7 @@ int kv_append(kv_pool* pool, const void* k, const void* v, const int32_t* tok_se
     if (!pool || n_tokens < 0 || n_seqs < 0) return KV_ERR_INVALID;
     if (n_tokens == 0) return KV_OK;
     if (!k || !v || !tok_seq || !tok_slot || !tok_pos || !block_tables || bt_stride <= 0 ||
-        n_seqs == 0)
+        n_seqs == 0 || !aligned16(k) || !aligned16(v))
         return KV_ERR_INVALID;
     DeviceScope dev(pool->cfg.device);
     return kvb200::launch_append(pool, k, v, tok_seq, tok_slot, tok_pos, nullptr, n_tokens, n_seqs,
@@ -284,7 +287,8 @@ int kv_append_decode(kv_pool* pool, const void* k, const void* v, const uint32_t
                      int32_t bt_stride, const int32_t* seq_lens, int32_t n_seqs, void* stream) {
     if (!pool || n_seqs < 0) return KV_ERR_INVALID;
     if (n_seqs == 0) return KV_OK;
-    if (!k || !v || !block_tables || !seq_lens || bt_stride <= 0) return KV_ERR_INVALID;
+    if (!k || !v || !block_tables || !seq_lens || bt_stride <= 0 || !aligned16(k) || !aligned16(v))
+        return KV_ERR_INVALID;
     DeviceScope dev(pool->cfg.device);
     return kvb200::launch_append(pool, k, v, nullptr, nullptr, nullptr, seq_lens, n_seqs, n_seqs,
                                  block_tables, bt_stride, static_cast<cudaStream_t>(stream));
@@ -300,6 +304,20 @@ int kv_decode_attn(kv_pool* pool, const void* q, const uint32_t* block_tables, i
     DeviceScope dev(pool->cfg.device);
     return kvb200::launch_decode(pool, q, block_tables, bt_stride, seq_lens, n_seqs, window, out,
                                  static_cast<cudaStream_t>(stream));
+}
+
+int kv_append_decode_attn(kv_pool* pool, const void* k, const void* v, const void* q,
+                          const uint32_t* block_tables, int32_t bt_stride, const int32_t* seq_lens,
+                          int32_t n_seqs, int32_t window, void* out, void* stream) {
+    if (!pool || n_seqs < 0 || window < 0) return KV_ERR_INVALID;
+    if (n_seqs == 0) return KV_OK;
+    if (n_seqs > pool->cfg.max_seqs) return KV_ERR_INVALID;
+    if (!k || !v || !q || !block_tables || !seq_lens || !out || bt_stride <= 0 || !aligned16(k) ||
+        !aligned16(v))
+        return KV_ERR_INVALID;
+    DeviceScope dev(pool->cfg.device);
+    return kvb200::launch_decode(pool, q, block_tables, bt_stride, seq_lens, n_seqs, window, out,
+                                 static_cast<cudaStream_t>(stream), k, v);
 }
 
 int kv_prefill_attn(kv_pool* pool, const void* q, const int32_t* q_pos, const int32_t* q_offsets,

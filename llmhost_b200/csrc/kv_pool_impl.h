@@ -37,9 +37,11 @@ int launch_append(kv_pool* pool, const void* k, const void* v, const int32_t* to
 // at pool creation.  Returns KV_ERR_UNSUPPORTED for shapes not compiled.
 int decode_setup(kv_pool* pool);
 size_t decode_workspace_slots(const kv_pool* pool);
+// new_k / new_v non-null: append each sequence's new token first (fused
+// kv_append_decode; the last page of every sequence must be its own).
 int launch_decode(kv_pool* pool, const void* q, const uint32_t* bt, int32_t bt_stride,
                   const int32_t* seq_lens, int32_t n_seqs, int32_t window, void* out,
-                  cudaStream_t stream);
+                  cudaStream_t stream, const void* new_k = nullptr, const void* new_v = nullptr);
 
 // Prefill / tree-verify attention: tcgen05 for bf16 pools (kv_prefill.cu).
 int prefill_setup(kv_pool* pool);

@@ -52,13 +52,6 @@ __device__ __forceinline__ float ex2f(float x) {
     return r;
 }
 
-__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(smem)), "l"(gmem) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
-
 struct Stage {
     float k[kPageTokens * kKRow];   // key kk: dims [0,32) at kk*66, [32,64) at kk*66 + 33
     float v[kPageTokens * kHeadDim];

@@ -181,6 +181,24 @@ class KvPool:
                                        _stream_ptr(stream)), "kv_decode_attn")
         return out
 
+    def append_decode_attn(self, k, v, q, block_tables, seq_lens, window: int = 0, out=None, stream=None):
+        """append_decode then decode_attn in one launch (kv_append_decode_attn),
+        bit-identical to the two calls; returns `out`."""
+        dt = self.shape.torch_dtype
+        self._check_tensor(k, "k", dt)
+        self._check_tensor(v, "v", dt)
+        self._check_tensor(q, "q", dt)
+        self._check_tensor(block_tables, "block_tables", torch.int32)
+        self._check_tensor(seq_lens, "seq_lens", torch.int32)
+        if out is None:
+            out = torch.empty_like(q)
+        self._check_tensor(out, "out", dt)
+        check(self._lib.kv_append_decode_attn(self._h, _ptr(k), _ptr(v), _ptr(q), _ptr(block_tables),
+                                              block_tables.shape[-1], _ptr(seq_lens), seq_lens.numel(),
+                                              int(window), _ptr(out), _stream_ptr(stream)),
+              "kv_append_decode_attn")
+        return out
+
     def prefill_attn(self, q, q_pos, q_offsets, prefix_lens, block_tables, tree_masks=None,
                      max_q: int | None = None, out=None, stream=None):
         """Chunked-prefill / tree-verify attention (kv_prefill_attn); returns `out`.

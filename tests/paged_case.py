@@ -95,17 +95,24 @@ class DecodeCase:
         tl = torch.from_numpy(tok_slot).to(dev)
         pool.append(to_torch(k, self.dtype, dev), to_torch(v, self.dtype, dev), ts, tl, tl, bt)
 
-    def decode_gpu(self, pool, repeat: int = 1):
+    def decode_gpu(self, pool, repeat: int = 1, fused: bool = False):
+        """Append the new token and attend; `fused` does both in one
+        kv_append_decode_attn launch (on the attention's block tables: the
+        new token's page is never below the window)."""
         import torch
 
         dev = pool.device
         bt = torch.from_numpy(self.bt.view(np.int32)).to(dev)
         bt_attn = torch.from_numpy(self.bt_attn.view(np.int32)).to(dev)
         lens = torch.from_numpy(self.seq_lens).to(dev)
-        pool.append_decode(to_torch(self.k_new, self.dtype, dev), to_torch(self.v_new, self.dtype, dev),
-                           bt, lens)
+        k = to_torch(self.k_new, self.dtype, dev)
+        v = to_torch(self.v_new, self.dtype, dev)
         q = to_torch(self.q, self.dtype, dev)
-        out = None
+        if fused:
+            out = pool.append_decode_attn(k, v, q, bt_attn, lens, window=self.window)
+            repeat -= 1
+        else:
+            pool.append_decode(k, v, bt, lens)
         for _ in range(repeat):
             out = pool.decode_attn(q, bt_attn, lens, window=self.window)
         torch.cuda.synchronize()

@@ -14,11 +14,11 @@ pytestmark = pytest.mark.gpu
 RTOL = {"f32": 1e-5, "bf16": 2e-2}
 
 
-def run_case(case: DecodeCase, repeat: int = 1):
+def run_case(case: DecodeCase, repeat: int = 1, fused: bool = False):
     host, ref = case.run_oracle()
     with case.make_pool() as pool:
         case.prefill_gpu(pool)
-        out = case.decode_gpu(pool, repeat=repeat)
+        out = case.decode_gpu(pool, repeat=repeat, fused=fused)
         err = pool.last_error()
         ids = case.used_pages()
         gpu_pages = pool.read_pages(ids)
@@ -171,3 +171,95 @@ def test_pools_of_one_shape_with_different_workspaces(cuda):
         out = big.decode_gpu(p1)
         assert p1.last_error() == 0
     assert_close_rows(to_numpy_f32(out), ref, RTOL["bf16"], "first pool after a smaller one")
+
+
+# ---- fused append + attention (kv_append_decode_attn) -----------------------
+
+FUSED_CASES = {
+    "ragged": dict(n_q=24, n_kv=8, lens=[0, 1, 14, 15, 16, 17, 31, 100, 1000, 2999], seed=21),
+    "group4": dict(n_q=32, n_kv=8, lens=[5, 700, 4097, 63, 16, 33], seed=22),
+    "one kv head, long": dict(n_q=4, n_kv=1, lens=[20001], seed=23),
+    "two kv heads": dict(n_q=8, n_kv=2, lens=[1, 900, 3000], seed=24),
+    "sparse": dict(n_q=24, n_kv=8, lens=[0, 3, 9, 200], seed=25),
+    "window, evicted": dict(n_q=24, n_kv=8, lens=[5000, 40, 1030, 2047], seed=26, window=1024,
+                            evict_below_window=True),
+}
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "f32"])
+@pytest.mark.parametrize("name", list(FUSED_CASES))
+def test_fused_append_decode_against_oracle(cuda, dtype, name):
+    c = dict(FUSED_CASES[name])
+    case = DecodeCase(dtype, c.pop("n_q"), c.pop("n_kv"), c.pop("lens"), **c)
+    out, ref = run_case(case, repeat=2, fused=True)  # then a plain decode over the appended pages
+    assert_close_rows(out, ref, RTOL[dtype], f"{dtype} fused {name}")
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "f32"])
+def test_fused_is_bit_identical_to_two_launches(cuda, dtype):
+    # Same pages and the same output bits as kv_append_decode + kv_decode_attn,
+    # including a sequence split over many CTAs and one-token sequences.
+    import torch
+
+    rng = np.random.default_rng(27)
+    lens = np.concatenate([[1, 16, 17, 30000], rng.integers(1, 3000, size=60)])
+    case = DecodeCase(dtype, 24, 8, lens, seed=27)
+    outs, pages = [], []
+    for fused in (False, True):
+        with case.make_pool() as pool:
+            case.prefill_gpu(pool)
+            out = case.decode_gpu(pool, fused=fused)
+            assert pool.last_error() == 0
+            outs.append(out.view(torch.int16 if dtype == "bf16" else torch.int32).cpu().numpy())
+            pages.append(pool.read_pages(case.used_pages()))
+    np.testing.assert_array_equal(pages[1], pages[0])
+    np.testing.assert_array_equal(outs[1], outs[0])
+
+
+def test_fused_bad_position_stores_nothing(cuda):
+    # A position past the RoPE table: flagged, and (as kv_append_decode) the
+    # token is not stored; the other sequence is appended normally.
+    import torch
+    from paged_case import to_torch
+
+    case = DecodeCase("bf16", 24, 8, [64, 40], seed=28)  # new tokens at positions 64 and 40
+    with case.make_pool(max_positions=64) as pool:
+        case.prefill_gpu(pool)
+        torch.cuda.synchronize()
+        assert pool.last_error() == 0
+        ids = list(case.used_pages())
+        before = pool.read_pages(ids)
+        dev = pool.device
+        pool.append_decode_attn(to_torch(case.k_new, "bf16", dev), to_torch(case.v_new, "bf16", dev),
+                                to_torch(case.q, "bf16", dev), torch.from_numpy(case.bt.view(np.int32)).to(dev),
+                                torch.from_numpy(case.seq_lens).to(dev))
+        torch.cuda.synchronize()
+        assert pool.last_error() == 7  # KV_ERR_BAD_POS
+        after = pool.read_pages(ids)
+    a_page = ids.index(int(case.bt[0, 64 // 16]))
+    b_page = ids.index(int(case.bt[1, 40 // 16]))
+    np.testing.assert_array_equal(after[a_page], before[a_page])  # position 64: nothing stored
+    assert not np.array_equal(after[b_page], before[b_page])      # position 40: stored
+
+
+def test_misaligned_k_is_rejected_before_launch(cuda):
+    # k / v rows are read as 16-byte vectors: an unaligned pointer is refused
+    # with KV_ERR_INVALID by every append entry point, with no launch.
+    import torch
+    from llmhost_b200._capi import KvError
+
+    case = DecodeCase("bf16", 24, 8, [10, 20], seed=29)
+    with case.make_pool() as pool:
+        dev = pool.device
+        buf = torch.zeros(2 * 8 * 64 + 1, dtype=torch.bfloat16, device=dev)
+        k_bad = buf[1:].view(2, 8, 64)  # 2 bytes past an aligned base
+        v = torch.zeros(2, 8, 64, dtype=torch.bfloat16, device=dev)
+        q = torch.zeros(2, 24, 64, dtype=torch.bfloat16, device=dev)
+        bt = torch.from_numpy(case.bt.view(np.int32)).to(dev)
+        lens = torch.from_numpy(case.seq_lens).to(dev)
+        for call in (lambda: pool.append_decode(k_bad, v, bt, lens),
+                     lambda: pool.append_decode_attn(k_bad, v, q, bt, lens)):
+            with pytest.raises(KvError) as e:
+                call()
+            assert e.value.status == 1  # KV_ERR_INVALID
+        assert pool.last_error() == 0
