@@ -32,6 +32,7 @@
 #include <mutex>
 
 #include "kv_common.cuh"
+#include "kv_decode_sched.cuh"
 #include "kv_pool_impl.h"
 
 namespace kvb200 {
@@ -70,35 +71,6 @@ struct DecodeArgs {
     const void* new_v;
     void* pages;
 };
-
-__device__ __forceinline__ int seq_lo(int n_tok, int window) {
-    return (window > 0 && n_tok > window) ? n_tok - window : 0;
-}
-
-__device__ __forceinline__ int seq_pages(int n_tok, int window) {
-    if (n_tok <= 0) return 0;
-    return (n_tok + kPageTokens - 1) / kPageTokens - seq_lo(n_tok, window) / kPageTokens;
-}
-
-// Largest s in [0, n) with pstart[s] <= g (pstart is nondecreasing, pstart[0] = 0).
-__device__ __forceinline__ int find_seq(const int* pstart, int n, int g) {
-    int lo = 0, hi = n;
-    while (hi - lo > 1) {
-        const int mid = (lo + hi) >> 1;
-        if (pstart[mid] <= g) lo = mid; else hi = mid;
-    }
-    return lo;
-}
-
-// Fewest pages a CTA's slice holds (unless the batch has fewer in total).
-constexpr int kMinSlicePages = 8;
-// Partial rows a merging warp has in flight at once.
-constexpr int kMergeBatch = 16;
-
-// CTA whose slice [floor(c*T/G), floor((c+1)*T/G)) holds global page x.
-__device__ __forceinline__ int cta_of(int x, int grid, int total) {
-    return static_cast<int>(((static_cast<long long>(x) + 1) * grid - 1) / total);
-}
 
 __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity,
                                               volatile int* abort_flag, int* err) {
@@ -495,24 +467,7 @@ decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeArgs a) {
         misc[0] = 0;
         misc[1] = 0;
     }
-    if (warp == 0) {  // exclusive scan of per-sequence page counts
-        const int per = (n + 31) >> 5;
-        const int b = min(n, lane * per), e = min(n, b + per);
-        int local = 0;
-        for (int s = b; s < e; ++s) local += seq_pages(__ldg(a.seq_lens + s), a.window);
-        int incl = local;
-#pragma unroll
-        for (int off = 1; off < 32; off <<= 1) {
-            const int y = __shfl_up_sync(~0u, incl, off);
-            if (lane >= off) incl += y;
-        }
-        int run = incl - local;
-        for (int s = b; s < e; ++s) {
-            pstart[s] = run;
-            run += seq_pages(__ldg(a.seq_lens + s), a.window);
-        }
-        if (lane == 31) pstart[n] = incl;
-    }
+    if (warp == 0) scan_pages(a.seq_lens, n, a.window, pstart, lane);  // exclusive scan of page counts
     __syncthreads();
 
     const int total = pstart[n];
@@ -894,6 +849,9 @@ const DecodeVariant* find_variant(int dtype, int nkv, int group) {
     return nullptr;
 }
 
+
+}  // namespace
+
 // A kernel's dynamic shared-memory limit is one attribute per device, shared
 // by every pool and caller that launches it.  It only ever grows here, to the
 // largest size any of them needs, so setting up a pool with a smaller
@@ -911,10 +869,9 @@ int raise_smem_limit(const void* fn, int device, size_t bytes) {
     return KV_OK;
 }
 
-}  // namespace
-
 int decode_setup(kv_pool* pool) {
     const auto& c = pool->cfg;
+    if (c.dtype == KV_DTYPE_BF16) return decode_tc_setup(pool);
     const DecodeVariant* v = find_variant(c.dtype, c.n_kv_heads, c.n_q_heads / c.n_kv_heads);
     if (!v) return KV_ERR_UNSUPPORTED;
     const size_t smem = v->smem(c.max_seqs);
@@ -939,6 +896,8 @@ int launch_decode(kv_pool* pool, const void* q, const uint32_t* bt, int32_t bt_s
                   const int32_t* seq_lens, int32_t n_seqs, int32_t window, void* out,
                   cudaStream_t stream, const void* new_k, const void* new_v) {
     const auto& c = pool->cfg;
+    if (c.dtype == KV_DTYPE_BF16)
+        return launch_decode_tc(pool, q, bt, bt_stride, seq_lens, n_seqs, window, out, stream, new_k, new_v);
     const DecodeVariant* v = find_variant(c.dtype, c.n_kv_heads, c.n_q_heads / c.n_kv_heads);
     if (!v) return KV_ERR_UNSUPPORTED;
     DecodeArgs a;

@@ -1,0 +1,930 @@
+// kv_decode_tc.cu -- paged decode attention on tcgen05, for bf16 pools.
+//
+// Same contract as decode_kernel (kv_decode.cu): attention_decode_cached
+// (crates/llm-engine/src/lfm2.rs:1006-1056) for one new token per sequence,
+// q rotated at seq_lens[s] - 1 (crates/llm-cpu/src/rope.rs:56-81 form), the
+// key range [lo, seq_lens[s]) of lfm2.rs:1032-1035 with the sliding window,
+// split-K over pages with a last-arriving-contributor merge, and the fused
+// append of kv_append_decode_attn.  The dot products run on the tensor cores:
+//
+//   unit    one kv head over a block of up to 8 pages (128 keys) of one
+//           sequence.  A stage of the ring holds two units: K_0, K_1, V_0,
+//           V_1, each a [128 keys x 64] bf16 tile of TMA boxes {64 x 16} (one
+//           per page and head, 128-byte swizzle, no multicast).  Pages past
+//           the block's end load as out-of-range boxes, which fill zeros.
+//   S_u^T  = K_u Q_u^T        M 128 keys, N 16 (the unit's query heads, padded), K 64
+//   O^T   += [V_0; V_1]^T P   M 128 (the 64 dims of each unit), N 16 (8 query
+//                             columns per unit), K 128 keys
+// With keys on the M axis each softmax thread owns one key of the block.
+// The PV product of the two stacked V tiles yields two useful 64 x 8 blocks
+// (unit u's dims x unit u's query heads) and two unused ones.  Units pair the
+// kv heads (2p, 2p+1) of a block; with a single kv head they pair
+// consecutive blocks of it.
+//
+// Roles (320 threads, one CTA per SM):
+//   warps 0-3  Q tiles, softmax, epilogue and split merge; thread t is key t
+//              of the block and TMEM lane t
+//   warp 4     TMA producer (one box per lane per stage), and the fused
+//              append: the new token's K/V rows are stored to the page in HBM
+//              before the box that covers them is loaded
+//   warp 5     TMEM owner; lane 0 issues the MMAs
+//   warps 6-9  epilogue: a finished sequence segment's O (one of two TMEM
+//              buffers), its normalisation or partial row, and the split
+//              merge, while warps 0-3 go on with the next segment
+//
+// Softmax in log2 units (q is pre-scaled by log2(e)/sqrt(d)) against a
+// reference maximum per query head, shared by the CTA: P = 2^(S - m), and m
+// is raised (O and the row sums rescaled) only when a block's maximum passes
+// it by more than kLazyLog2.  P is stored as bf16 and the row sums add the
+// same rounded values.  Every wait is bounded; a timeout sets the error word
+// and an abort flag, and the CTA runs its schedule out without work.
+#include <cmath>
+
+#include "kv_common.cuh"
+#include "kv_decode_sched.cuh"
+#include "kv_pool_impl.h"
+#include "kv_tc.cuh"
+
+namespace kvb200 {
+namespace {
+
+constexpr int kUnitKeys = 128;                        // keys per unit (MMA M of S, K of PV)
+constexpr int kUnitPages = kUnitKeys / kPageTokens;   // 8
+constexpr int kUnitBytes = kUnitKeys * 128;           // 16 KiB: K (or V) of one unit
+constexpr int kStageBytes = 4 * kUnitBytes;           // K_0 K_1 V_0 V_1
+constexpr int kStages = 3;
+constexpr int kSoftThreads = 128;                     // warps 0-3
+constexpr int kProducerWarp = 4;
+constexpr int kMmaWarp = 5;
+constexpr int kEpiWarp0 = 6;                          // warps 6-9
+constexpr int kEpiThreads = 128;
+constexpr int kThreads = 320;
+constexpr uint32_t kTmemCols = 256;
+constexpr uint32_t kColS = 0;   // S of buffer sb, unit u: columns kColS + 32 sb + 16 u ..
+constexpr uint32_t kColO = 64;  // O of segment buffer e, accumulator c: kColO + 64 e + 16 c; unit u's queries at + 8 u
+constexpr int kPBytes = 2 * 16 * 128;  // P: 16 rows x 128 keys as two 64-key atoms
+constexpr float kLazyLog2 = 8.f;
+constexpr int kSoftBar = 1;     // named barrier of the softmax warps
+constexpr int kEpiBar = 2;      // named barrier of the epilogue warps
+constexpr unsigned kAll = 0xffffffffu;
+
+struct TcArgs {
+    const __nv_bfloat16* q;
+    __nv_bfloat16* out;
+    const uint32_t* bt;
+    long long bt_stride;
+    const int32_t* seq_lens;
+    int n_seqs;
+    int window;
+    const float2* rope;
+    int max_pos;
+    uint32_t n_pages;
+    int page_rows;
+    float* part_o;
+    float* part_ml;
+    int* counters;
+    int* err;
+    float qscale;
+    const __nv_bfloat16* new_k;  // fused append (null: none)
+    const __nv_bfloat16* new_v;
+    uint8_t* pages;
+};
+
+template <int NKV, int G>
+struct TcShape {
+    static_assert(G >= 1 && G <= 4, "query heads per kv head");
+    static_assert(NKV == 1 || NKV == 2 || NKV == 4 || NKV == 8, "kv heads");
+    static constexpr int NQ = NKV * G;
+    static constexpr int kPairs = NKV >= 2 ? NKV / 2 : 1;  // stages per block round = O accumulators
+    // shared memory, from a 1024-aligned base
+    static constexpr int kOffQ = kStages * kStageBytes;             // Q tiles: head h at + 1024 h (8 rows)
+    static constexpr int kOffP = kOffQ + (NKV + 1) * 1024;          // P, two buffers
+    static constexpr int kOffStg = kOffP + 2 * kPBytes;             // fused append inputs
+    static constexpr int kStgBytes = NKV * 256 + 256;               // per head K row, V row; RoPE row
+    static constexpr int kOffMax = kOffStg + kStgBytes;             // float [2][4 warps][2 units][4]
+    static constexpr int kOffM = kOffMax + 2 * 4 * 8 * 4;           // float [2 buffers][NQ]: reference maxima
+    static constexpr int kOffL = kOffM + 2 * NQ * 4;                // float [2 buffers][4 warps][NQ]: row sums
+    static constexpr int kOffOb = kOffL + 2 * 4 * NQ * 4;           // float [64][4]
+    static constexpr int kOffBar = (kOffOb + 64 * 4 * 4 + 7) & ~7;  // 24 mbarriers
+    static constexpr int kOffInt = kOffBar + 24 * 8;                // int [16]
+    static constexpr int kOffScan = kOffInt + 16 * 4;               // int [n_seqs + 1]
+    static size_t smem_bytes(int max_seqs) { return 1024 + kOffScan + (static_cast<size_t>(max_seqs) + 1) * 4; }
+};
+
+// Work is sliced in chunks of one stage round: a block of 8 pages (all kv
+// heads) or, with a single kv head, two blocks.  Every sequence's pages are
+// cut into chunks from its first page (the last chunk may be partial), the
+// chunks of all sequences laid end to end, and each CTA takes an equal run
+// of whole chunks, so a cut between CTAs never leaves two partial blocks.
+template <int NKV>
+struct Chunk {
+    static constexpr int kPages = NKV >= 2 ? kUnitPages : 2 * kUnitPages;
+};
+
+// One sequence's chunks [g, min(ge, s_end)) inside this CTA's slice [gb, ge)
+// (chunk indices): s_begin / s_end are the sequence's first and end chunk.
+struct Seg {
+    int s, nt, lo, pg0, np, s_begin, s_end, nst;
+};
+
+template <int NKV>
+__device__ __forceinline__ Seg make_seg(const TcArgs& a, const int* cstart, int s, int g, int ge) {
+    constexpr int kCp = Chunk<NKV>::kPages;
+    Seg q;
+    q.s = s;
+    q.nt = __ldg(a.seq_lens + s);
+    q.lo = seq_lo(q.nt, a.window);
+    q.s_begin = cstart[s];
+    q.s_end = cstart[s + 1];
+    const int p0 = kCp * (g - q.s_begin);
+    const int p1 = min(seq_pages(q.nt, a.window), kCp * (min(ge, q.s_end) - q.s_begin));
+    q.np = p1 - p0;
+    q.pg0 = q.lo / kPageTokens + p0;  // block-table index of the segment's first page
+    const int nblk = (q.np + kUnitPages - 1) / kUnitPages;
+    q.nst = NKV >= 2 ? nblk * (NKV / 2) : (nblk + 1) / 2;
+    return q;
+}
+
+// Stage j of a segment: each unit's block and its page count, and the pair p.
+template <int NKV>
+__device__ __forceinline__ void stage_units(const Seg& q, int j, int& b0, int& b1, int& n0, int& n1, int& p) {
+    constexpr int kPairs = NKV >= 2 ? NKV / 2 : 1;
+    if (NKV >= 2) {
+        b0 = b1 = j / kPairs;
+        p = j % kPairs;
+    } else {
+        b0 = 2 * j;
+        b1 = 2 * j + 1;
+        p = 0;
+    }
+    n0 = max(0, min(kUnitPages, q.np - kUnitPages * b0));
+    n1 = max(0, min(kUnitPages, q.np - kUnitPages * b1));
+}
+
+// Walks a CTA's stages in schedule order: stage i, stage j of segment q.
+template <int NKV>
+struct StageCursor {
+    int i, j, g, s, seg_no, ge, n;
+    bool done;
+    Seg q;
+    __device__ __forceinline__ void start(const TcArgs& a, const int* pstart, int n_, int gb, int ge_) {
+        i = j = seg_no = 0;
+        n = n_;
+        ge = ge_;
+        g = gb;
+        s = find_seq(pstart, n, gb);
+        q = make_seg<NKV>(a, pstart, s, g, ge);
+        done = false;
+    }
+    __device__ __forceinline__ void next(const TcArgs& a, const int* pstart) {
+        ++i;
+        if (++j < q.nst) return;
+        j = 0;
+        g = min(ge, q.s_end);
+        if (g >= ge) {
+            done = true;
+            return;
+        }
+        s = find_seq(pstart, n, g);
+        q = make_seg<NKV>(a, pstart, s, g, ge);
+        ++seg_no;
+    }
+};
+
+__device__ __forceinline__ float warp_maxf(float x) {
+    float r;
+    asm volatile("redux.sync.max.f32 %0, %1, 0xffffffff;" : "=f"(r) : "f"(x));
+    return r;
+}
+
+__device__ __forceinline__ float warp_sumf(float x) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(kAll, x, o);
+    return x;
+}
+
+__device__ __forceinline__ float2 ld_pair(const __nv_bfloat16* p) {
+    return bf16x2_to_float2(__ldg(reinterpret_cast<const unsigned int*>(p)));
+}
+
+template <int NKV, int G>
+__global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(const __grid_constant__ CUtensorMap hmap,
+                                                                const TcArgs a) {
+    using Sh = TcShape<NKV, G>;
+    constexpr int NQ = Sh::NQ;
+    constexpr int kPairs = Sh::kPairs;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* bars = reinterpret_cast<uint64_t*>(base + Sh::kOffBar);
+    uint64_t* full = bars;            // [kStages]  TMA landed
+    uint64_t* empty = bars + 3;       // [kStages]  PV done with the stage
+    uint64_t* s_full = bars + 6;      // [2]        S MMAs done
+    uint64_t* s_free = bars + 8;      // [2]        S read by the softmax
+    uint64_t* p_full = bars + 10;     // [2]        P (and zeroed V rows) written
+    uint64_t* pv_done = bars + 12;    // [2]        PV MMAs done
+    uint64_t* q_full = bars + 14;     //            Q tiles of the next segment written
+    uint64_t* mma_done = bars + 15;
+    uint64_t* o_full = bars + 16;     // [2]        a segment's last PV done (O buffer e)
+    uint64_t* seg_done = bars + 18;   // [2]        its reference maxima and row sums written
+    uint64_t* o_free = bars + 20;     // [2]        the epilogue is done with O buffer e and its sums
+    int* ints = reinterpret_cast<int*>(base + Sh::kOffInt);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ints);
+    volatile int* abort_flag = ints + 1;
+    int* contrib = ints + 2;
+    int* vote = ints + 8;             // [2][4]
+    int* pstart = reinterpret_cast<int*>(base + Sh::kOffScan);  // chunk starts, [n_seqs + 1]
+    float* fmax = reinterpret_cast<float*>(base + Sh::kOffMax);
+    float* fm = reinterpret_cast<float*>(base + Sh::kOffM);
+    float* fl = reinterpret_cast<float*>(base + Sh::kOffL);
+    float* fob = reinterpret_cast<float*>(base + Sh::kOffOb);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n = a.n_seqs;
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < kStages; ++i) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&s_full[i], 1);
+            mbar_init(&s_free[i], kSoftThreads);
+            mbar_init(&p_full[i], kSoftThreads);
+            mbar_init(&pv_done[i], 1);
+        }
+        mbar_init(q_full, kSoftThreads);
+        mbar_init(mma_done, 1);
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&o_full[i], 1);
+            mbar_init(&seg_done[i], kSoftThreads);
+            mbar_init(&o_free[i], kEpiThreads);
+        }
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 0) scan_units(a.seq_lens, n, a.window, Chunk<NKV>::kPages, pstart, lane);  // chunk starts
+    if (threadIdx.x < kSoftThreads) {  // Q padding rows and P rows never written stay zero
+        uint4* z = reinterpret_cast<uint4*>(base + Sh::kOffQ);
+        for (int i = threadIdx.x; i < ((NKV + 1) * 1024 + 2 * kPBytes) / 16; i += kSoftThreads)
+            z[i] = make_uint4(0, 0, 0, 0);
+        proxy_fence();
+    }
+    __syncthreads();
+
+    const int total = pstart[n];
+    const int cta = blockIdx.x;
+    const int grid = max(1, min(static_cast<int>(gridDim.x), total));  // at least one chunk per CTA
+    for (int s = cta; s < n; s += gridDim.x) {  // sequences with no tokens: zeros
+        if (__ldg(a.seq_lens + s) <= 0) {
+            __nv_bfloat16* o = a.out + static_cast<size_t>(s) * NQ * kHeadDim;
+            for (int i = threadIdx.x; i < NQ * kHeadDim; i += kThreads) o[i] = __float2bfloat16_rn(0.f);
+        }
+    }
+    if (cta >= grid) return;
+    const int gb = static_cast<int>((static_cast<long long>(cta) * total) / grid);
+    const int ge = static_cast<int>((static_cast<long long>(cta + 1) * total) / grid);
+    if (gb >= ge) return;
+
+    if (warp == kMmaWarp) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(tmem_slot)),
+                     "r"(kTmemCols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    if (warp == kProducerWarp && lane == 0) prefetch_tmap(&hmap);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == kProducerWarp) {
+        // ---------------- producer ----------------
+        const int total_rows = static_cast<int>(a.n_pages) * a.page_rows;
+        uint8_t* stg = base + Sh::kOffStg;
+        int i = 0, issued = 0;
+        bool issuing = true;
+        int g = gb, s = find_seq(pstart, n, gb);
+        while (g < ge) {
+            const Seg q = make_seg<NKV>(a, pstart, s, g, ge);
+            // Fused append: the new token (slot nt - 1, on the sequence's last
+            // page) when that page is in this slice and its position is valid.
+            bool app = a.new_k != nullptr && q.s_end <= ge && q.nt - 1 < a.max_pos;
+            const int blast = (q.np - 1) / kUnitPages;
+            if (app) {
+                const __nv_bfloat16* kr = a.new_k + static_cast<size_t>(q.s) * NKV * kHeadDim;
+                const __nv_bfloat16* vr = a.new_v + static_cast<size_t>(q.s) * NKV * kHeadDim;
+                const uint8_t* cr = reinterpret_cast<const uint8_t*>(a.rope + static_cast<size_t>(q.nt - 1) * (kHeadDim / 2));
+                for (int c = lane; c < NKV * 16 + 16; c += 32) {
+                    if (c < NKV * 16) {
+                        const int h = c >> 4, r = c & 15;
+                        const __nv_bfloat16* src = (r < 8 ? kr : vr) + h * kHeadDim + (r & 7) * 8;
+                        cp_async16(stg + h * 256 + (r >> 3) * 128 + (r & 7) * 16, src);
+                    } else {
+                        cp_async16(stg + NKV * 256 + (c - NKV * 16) * 16, cr + (c - NKV * 16) * 16);
+                    }
+                }
+                cp_async_commit();
+            }
+            for (int j = 0; j < q.nst; ++j, ++i) {
+                int b0, b1, n0, n1, p;
+                stage_units<NKV>(q, j, b0, b1, n0, n1, p);
+                const int st = i % kStages;
+                if (issuing) {
+                    bool ok = true;
+                    if (lane == 0 && i >= kStages)
+                        ok = wait_bar(&empty[st], static_cast<uint32_t>(i / kStages - 1) & 1u, abort_flag, a.err);
+                    issuing = __shfl_sync(kAll, ok, 0);
+                }
+                if (!issuing) continue;
+                if (app && (b0 == blast || b1 == blast)) {
+                    // Store the rotated K and the V rows of every head to the
+                    // page, then let the async proxy (TMA) see them.
+                    cp_async_wait<0>();
+                    __syncwarp();
+                    const int pgl = q.pg0 + q.np - 1;
+                    const uint32_t page = pgl < a.bt_stride ? __ldg(a.bt + static_cast<size_t>(q.s) * a.bt_stride + pgl)
+                                                            : kPageNone;
+                    if (page < a.n_pages) {
+                        const int jslot = (q.nt - 1) % kPageTokens;
+                        uint8_t* gpage = a.pages + static_cast<size_t>(page) * a.page_rows * 128;
+                        const float4 c = *reinterpret_cast<const float4*>(stg + NKV * 256 + 16 * (lane & 15));
+                        const int ii = lane & 15;
+#pragma unroll
+                        for (int h = 0; h < NKV; ++h) {
+                            const uint8_t* in = stg + h * 256;
+                            if (lane < 16) {
+                                const float2 x = bf16x2_to_float2(*reinterpret_cast<const uint32_t*>(in + 4 * ii));
+                                const float2 y = bf16x2_to_float2(*reinterpret_cast<const uint32_t*>(in + 64 + 4 * ii));
+                                const float x0 = __fadd_rn(__fmul_rn(x.x, c.x), __fmul_rn(-y.x, c.y));
+                                const float x1 = __fadd_rn(__fmul_rn(x.y, c.z), __fmul_rn(-y.y, c.w));
+                                const float y0 = __fadd_rn(__fmul_rn(y.x, c.x), __fmul_rn(x.x, c.y));
+                                const float y1 = __fadd_rn(__fmul_rn(y.y, c.z), __fmul_rn(x.y, c.w));
+                                uint8_t* row = gpage + (h * kPageTokens + jslot) * 128;
+                                *reinterpret_cast<uint32_t*>(row + 4 * ii) = float2_to_bf16x2(x0, x1);
+                                *reinterpret_cast<uint32_t*>(row + 64 + 4 * ii) = float2_to_bf16x2(y0, y1);
+                            } else {
+                                uint8_t* row = gpage + ((NKV + h) * kPageTokens + jslot) * 128;
+                                *reinterpret_cast<uint2*>(row + 8 * ii) = *reinterpret_cast<const uint2*>(in + 128 + 8 * ii);
+                            }
+                        }
+                        asm volatile("fence.proxy.async.global;" ::: "memory");
+                    }
+                    __syncwarp();
+                    app = false;
+                }
+                if (lane == 0) mbar_arrive_expect_tx(&full[st], kStageBytes);
+                __syncwarp();
+                // lane: page k of the unit's block, K or V, unit u.  Lanes 4k ..
+                // 4k+3 read page k's K rows of both units' heads (adjacent in
+                // the page when the units are heads 2p, 2p+1) and their V rows.
+                const int k = lane >> 2, kv = (lane >> 1) & 1, u = lane & 1;
+                const int bu = u ? b1 : b0, nu = u ? n1 : n0;
+                const int hu = NKV >= 2 ? 2 * p + u : 0;
+                int row = total_rows;  // out of range: zero fill
+                if (k < nu) {
+                    const int pg = q.pg0 + kUnitPages * bu + k;
+                    const uint32_t phys = pg < a.bt_stride ? __ldg(a.bt + static_cast<size_t>(q.s) * a.bt_stride + pg)
+                                                           : kPageNone;
+                    if (phys < a.n_pages)
+                        row = static_cast<int>(phys) * a.page_rows + (kv ? NKV + hu : hu) * kPageTokens;
+                    else
+                        flag_error(a.err, kDevErrBadPage);
+                }
+                tma_load_2d(base + st * kStageBytes + kv * 2 * kUnitBytes + u * kUnitBytes + k * 2048, &hmap, &full[st],
+                            0, row);
+                issued = i + 1;
+            }
+            if (app) cp_async_wait<0>();  // staged, not stored (the issue stopped)
+            g = min(ge, q.s_end);
+            if (g < ge) s = find_seq(pstart, n, g);
+        }
+        // Do not leave while a copy may still be landing: the newest copy
+        // issued into each stage covers every older one.
+        if (lane == 0) {
+            for (int st = 0; st < kStages && st < issued; ++st) {
+                const int last = st + ((issued - 1 - st) / kStages) * kStages;
+                mbar_wait(&full[st], static_cast<uint32_t>(last / kStages) & 1u);
+            }
+        }
+    } else if (warp == kMmaWarp) {
+        // ---------------- MMA issuer ----------------
+        // Two cursors over the schedule: S(si) once its K tiles have landed,
+        // its S buffer is free and its segment's Q is written; PV(pi) once
+        // P(pi) is written.  Neither waits on the other: a PV (which hands
+        // its stage back to the producer) never queues behind the next
+        // stage's copy.  PV(pi) is issued only after S(pi).
+        if (lane == 0) {
+            constexpr uint32_t kIdS = instr_desc(16, 128, false, false);
+            constexpr uint32_t kIdPV = instr_desc(16, 128, false, true);
+            const uint32_t st_addr = smem_addr(base), q_addr = smem_addr(base + Sh::kOffQ);
+            const uint32_t p_addr = smem_addr(base + Sh::kOffP);
+            StageCursor<NKV> sc, pc;
+            sc.start(a, pstart, n, gb, ge);
+            pc.start(a, pstart, n, gb, ge);
+            bool q_ready = false;
+            uint64_t t_last = global_timer_ns();
+            while (!pc.done) {
+                if (*abort_flag) break;
+                bool progress = false;
+                const bool first = pc.j < kPairs;  // first PV into its accumulator in this segment
+                const int eb = pc.seg_no & 1;      // O buffer of the segment
+                if (pc.i < sc.i && mbar_test(&p_full[pc.i & 1], static_cast<uint32_t>(pc.i >> 1) & 1u) &&
+                    (!first || pc.seg_no < 2 ||
+                     mbar_test(&o_free[eb], static_cast<uint32_t>((pc.seg_no - 2) >> 1) & 1u))) {
+                    tc_fence_after();
+                    const int pcc = NKV >= 2 ? pc.j % kPairs : 0;
+                    const uint32_t va = st_addr + (pc.i % kStages) * kStageBytes + 2 * kUnitBytes;
+                    const uint32_t pa = p_addr + (pc.i & 1) * kPBytes;
+#pragma unroll
+                    for (int kk = 0; kk < kUnitKeys / 16; ++kk)
+                        mma_ss(tmem + kColO + 64 * eb + 16 * pcc, smem_desc(va + 2048 * kk, kUnitBytes, 1024),
+                               smem_desc(pa + (kk >> 2) * 2048 + (kk & 3) * 32, 16, 1024), kIdPV, !first || kk > 0);
+                    mma_commit(&pv_done[pc.i & 1]);
+                    mma_commit(&empty[pc.i % kStages]);
+                    if (pc.j == pc.q.nst - 1) mma_commit(&o_full[eb]);
+                    pc.next(a, pstart);
+                    progress = true;
+                }
+                if (!sc.done) {
+                    const int st = sc.i % kStages, sb = sc.i & 1;
+                    if (!q_ready) q_ready = mbar_test(q_full, static_cast<uint32_t>(sc.seg_no) & 1u);
+                    if (q_ready && mbar_test(&full[st], static_cast<uint32_t>(sc.i / kStages) & 1u) &&
+                        (sc.i < 2 || mbar_test(&s_free[sb], static_cast<uint32_t>((sc.i - 2) >> 1) & 1u))) {
+                        tc_fence_after();
+                        int b0, b1, n0, n1, p;
+                        stage_units<NKV>(sc.q, sc.j, b0, b1, n0, n1, p);
+                        const uint32_t ka = st_addr + st * kStageBytes;
+#pragma unroll
+                        for (int u = 0; u < 2; ++u) {
+                            if ((u ? n1 : n0) == 0) continue;
+                            const int hu = NKV >= 2 ? 2 * p + u : 0;
+#pragma unroll
+                            for (int kk = 0; kk < kHeadDim / 16; ++kk)
+                                mma_ss(tmem + kColS + 32 * sb + 16 * u,
+                                       smem_desc(ka + u * kUnitBytes + 32 * kk, 16, 1024),
+                                       smem_desc(q_addr + hu * 1024 + 32 * kk, 16, 1024), kIdS, kk > 0);
+                        }
+                        mma_commit(&s_full[sb]);
+                        const int seg = sc.seg_no;
+                        sc.next(a, pstart);
+                        if (sc.seg_no != seg) q_ready = false;
+                        progress = true;
+                    }
+                }
+                if (progress) {
+                    t_last = global_timer_ns();
+                } else if (global_timer_ns() - t_last > kWaitLimitNs) {
+                    *abort_flag = 1;
+                    flag_error(a.err, kDevErrTimeout);
+                    break;
+                }
+            }
+            // Every MMA issued above has finished before TMEM is released.
+            mma_commit(mma_done);
+            mbar_wait(mma_done, 0);
+        }
+    } else if (warp < kProducerWarp) {
+        // ---------------- softmax and Q tiles (warps 0-3) ----------------
+        const int t = threadIdx.x;
+        const uint32_t lane_base = tmem + (static_cast<uint32_t>(32 * warp) << 16);
+        const int kp = t >> 4, slot = t & 15;  // page of the block and slot of this thread's key
+        const int ut = t >> 6;                 // O rows of this thread's TMEM lane: unit ut
+        // Q tiles of a segment: item (h, n, c) rotates dims [8c, 8c+8) with
+        // [32+8c, 32+8c+8) of query head h*G + n (rope.rs:76 form), scales them
+        // into log2 units and stores bf16 row n of head h's 8-row group.
+        auto build_q = [&](const Seg& q) {
+            int pos = q.nt - 1;
+            if (pos >= a.max_pos) {
+                if (t == 0) flag_error(a.err, kDevErrBadPos);
+                pos = 0;
+            }
+            if (t < NQ * 4) {
+                const int h = t / (G * 4), n_ = (t >> 2) % G, c = t & 3;
+                const __nv_bfloat16* src = a.q + (static_cast<size_t>(q.s) * NQ + h * G + n_) * kHeadDim;
+                const float2* cs = a.rope + static_cast<size_t>(pos) * (kHeadDim / 2) + 8 * c;
+                uint32_t lo[4], hi[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const float2 x = ld_pair(src + 8 * c + 2 * e), y = ld_pair(src + 32 + 8 * c + 2 * e);
+                    const float2 c0 = __ldg(cs + 2 * e), c1 = __ldg(cs + 2 * e + 1);
+                    const float a0 = __fadd_rn(__fmul_rn(x.x, c0.x), __fmul_rn(-y.x, c0.y)) * a.qscale;
+                    const float a1 = __fadd_rn(__fmul_rn(x.y, c1.x), __fmul_rn(-y.y, c1.y)) * a.qscale;
+                    const float b0 = __fadd_rn(__fmul_rn(y.x, c0.x), __fmul_rn(x.x, c0.y)) * a.qscale;
+                    const float b1 = __fadd_rn(__fmul_rn(y.y, c1.x), __fmul_rn(x.y, c1.y)) * a.qscale;
+                    lo[e] = float2_to_bf16x2(a0, a1);
+                    hi[e] = float2_to_bf16x2(b0, b1);
+                }
+                uint8_t* row = base + Sh::kOffQ + h * 1024 + n_ * 128;
+                *reinterpret_cast<uint4*>(row + ((c ^ n_) << 4)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+                *reinterpret_cast<uint4*>(row + (((c + 4) ^ n_) << 4)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+            }
+            proxy_fence();  // the tensor core reads Q through the async proxy
+            mbar_arrive(q_full);
+        };
+
+        float m[NKV][G], l[NKV][G];
+        int i = 0, segk = 0;
+        int g = gb, s = find_seq(pstart, n, gb);
+        Seg q = make_seg<NKV>(a, pstart, s, g, ge);
+        build_q(q);
+        for (;;) {
+#pragma unroll
+            for (int h = 0; h < NKV; ++h)
+#pragma unroll
+                for (int c = 0; c < G; ++c) {
+                    m[h][c] = -INFINITY;
+                    l[h][c] = 0.f;
+                }
+            const int rounds = q.nst / kPairs;
+            for (int r = 0; r < rounds; ++r) {
+#pragma unroll
+                for (int p = 0; p < kPairs; ++p, ++i) {
+                    const int j = r * kPairs + p;
+                    int b0, b1, n0, n1, pp;
+                    stage_units<NKV>(q, j, b0, b1, n0, n1, pp);
+                    constexpr int kH1 = NKV >= 2 ? 1 : 0;
+                    const int h0 = NKV >= 2 ? 2 * p : 0;
+                    const int h1 = h0 + kH1;
+                    const int sb = i & 1, st = i % kStages;
+                    uint8_t* stage = base + st * kStageBytes;
+                    // ---- S of this stage: key t's scores for each unit's query heads
+                    const bool okS =
+                        __all_sync(kAll, wait_bar(&s_full[sb], static_cast<uint32_t>(i >> 1) & 1u, abort_flag, a.err));
+                    uint32_t r0[4] = {0, 0, 0, 0}, r1[4] = {0, 0, 0, 0};
+                    if (okS) {
+                        tc_fence_after();
+                        tmem_ld4(lane_base + kColS + 32 * sb, r0);
+                        tmem_ld4(lane_base + kColS + 32 * sb + 16, r1);
+                        tmem_wait4x2(r0, r1);
+                    }
+                    tc_fence_before();
+                    mbar_arrive(&s_free[sb]);
+                    const int tok0 = (q.pg0 + kUnitPages * b0 + kp) * kPageTokens + slot;
+                    const int tok1 = (q.pg0 + kUnitPages * b1 + kp) * kPageTokens + slot;
+                    const bool v0 = okS && kp < n0 && tok0 >= q.lo && tok0 < q.nt;
+                    const bool v1 = okS && kp < n1 && tok1 >= q.lo && tok1 < q.nt;
+                    float s0[G], s1[G];
+                    bool exceed = false;
+#pragma unroll
+                    for (int c = 0; c < G; ++c) {
+                        s0[c] = v0 ? __uint_as_float(r0[c]) : -INFINITY;
+                        s1[c] = v1 ? __uint_as_float(r1[c]) : -INFINITY;
+                        exceed |= s0[c] > m[h0][c] + kLazyLog2;
+                        exceed |= s1[c] > m[h1][c] + kLazyLog2;
+                    }
+                    // ---- raise references?  (decided for the whole CTA: every
+                    // key of the block is multiplied into the same O)
+                    int* vt = vote + 4 * (i & 1);
+                    const unsigned bal = __ballot_sync(kAll, exceed);
+                    if (lane == 0) vt[warp] = bal != 0u;
+                    named_bar_sync(kSoftBar, kSoftThreads);
+                    if (vt[0] | vt[1] | vt[2] | vt[3]) {
+                        float* mx = fmax + 32 * (i & 1);  // [warp][unit][4]
+#pragma unroll
+                        for (int c = 0; c < G; ++c) {
+                            const float x0 = warp_maxf(s0[c]), x1 = warp_maxf(s1[c]);
+                            if (lane == 0) {
+                                mx[warp * 8 + c] = x0;
+                                mx[warp * 8 + 4 + c] = x1;
+                            }
+                        }
+                        named_bar_sync(kSoftBar, kSoftThreads);
+                        float f0[G], f1[G];
+                        bool resc = false;
+#pragma unroll
+                        for (int c = 0; c < G; ++c) {
+                            float bm0 = fmaxf(fmaxf(mx[c], mx[8 + c]), fmaxf(mx[16 + c], mx[24 + c]));
+                            float bm1 = fmaxf(fmaxf(mx[4 + c], mx[12 + c]), fmaxf(mx[20 + c], mx[28 + c]));
+                            if (NKV == 1) bm0 = bm1 = fmaxf(bm0, bm1);
+                            {
+                                const float mo = m[h0][c];
+                                const float mn = bm0 > mo + kLazyLog2 ? bm0 : mo;
+                                f0[c] = (mn == mo || mo == -INFINITY) ? 1.f : ex2f(mo - mn);
+                                resc |= mn != mo && mo != -INFINITY;
+                                l[h0][c] *= f0[c];
+                                m[h0][c] = mn;
+                            }
+                            if (NKV == 1) {
+                                f1[c] = f0[c];
+                            } else {
+                                const float mo = m[h1][c];
+                                const float mn = bm1 > mo + kLazyLog2 ? bm1 : mo;
+                                f1[c] = (mn == mo || mo == -INFINITY) ? 1.f : ex2f(mo - mn);
+                                resc |= mn != mo && mo != -INFINITY;
+                                l[h1][c] *= f1[c];
+                                m[h1][c] = mn;
+                            }
+                        }
+                        if (resc) {
+                            // O of accumulator p holds this segment's earlier
+                            // blocks; the PV issued last (stage i - 1) covers them.
+                            const bool okP = __all_sync(
+                                kAll, wait_bar(&pv_done[(i - 1) & 1], static_cast<uint32_t>((i - 1) >> 1) & 1u,
+                                               abort_flag, a.err));
+                            if (okP) {
+                                tc_fence_after();
+                                const uint32_t to = lane_base + kColO + 64 * (segk & 1) + 16 * p + 8 * ut;
+                                uint32_t o[4];
+                                tmem_ld4(to, o);
+                                tmem_wait4(o);
+#pragma unroll
+                                for (int c = 0; c < G; ++c)
+                                    o[c] = __float_as_uint(__uint_as_float(o[c]) * (ut ? f1[c] : f0[c]));
+                                tmem_st4(to, o);
+                                tmem_wait_st();
+                            }
+                        }
+                    }
+                    // ---- P = 2^(S - m) as bf16 into P[i & 1]; zero the V rows
+                    // of keys outside the range on loaded pages (stale slots)
+                    if (i >= 2) wait_bar(&pv_done[sb], static_cast<uint32_t>((i - 2) >> 1) & 1u, abort_flag, a.err);
+                    uint8_t* prow = base + Sh::kOffP + sb * kPBytes + (t >> 6) * 2048;
+                    const int chunk = (t & 63) >> 3, within = (t & 7) * 2;
+#pragma unroll
+                    for (int c = 0; c < G; ++c) {
+                        const __nv_bfloat16 p0 = __float2bfloat16_rn(v0 ? ex2f(s0[c] - m[h0][c]) : 0.f);
+                        const __nv_bfloat16 p1 = __float2bfloat16_rn(v1 ? ex2f(s1[c] - m[h1][c]) : 0.f);
+                        l[h0][c] += __bfloat162float(p0);
+                        l[h1][c] += __bfloat162float(p1);
+                        *reinterpret_cast<__nv_bfloat16*>(prow + c * 128 + ((chunk ^ c) << 4) + within) = p0;
+                        *reinterpret_cast<__nv_bfloat16*>(prow + (8 + c) * 128 + ((chunk ^ c) << 4) + within) = p1;
+                    }
+                    if (okS && !v0 && kp < n0) {
+                        uint4* vrow = reinterpret_cast<uint4*>(stage + 2 * kUnitBytes + t * 128);
+#pragma unroll
+                        for (int c = 0; c < 8; ++c) vrow[c] = make_uint4(0, 0, 0, 0);
+                    }
+                    if (okS && !v1 && kp < n1) {
+                        uint4* vrow = reinterpret_cast<uint4*>(stage + 3 * kUnitBytes + t * 128);
+#pragma unroll
+                        for (int c = 0; c < 8; ++c) vrow[c] = make_uint4(0, 0, 0, 0);
+                    }
+                    proxy_fence();
+                    tc_fence_before();
+                    mbar_arrive(&p_full[sb]);
+                }
+            }
+            // ---- segment done: Q of the next segment first (every S of this
+            // one has completed), then hand its reference maxima and row sums
+            // to the epilogue warps (O buffer segk & 1), once the epilogue of
+            // segment segk - 2 is done with that buffer.
+            const Seg cur = q;
+            g = min(ge, cur.s_end);
+            const bool more = g < ge;
+            if (more) {
+                s = find_seq(pstart, n, g);
+                q = make_seg<NKV>(a, pstart, s, g, ge);
+                build_q(q);
+            }
+            const int eb = segk & 1;
+            if (segk >= 2) wait_bar(&o_free[eb], static_cast<uint32_t>((segk - 2) >> 1) & 1u, abort_flag, a.err);
+            float* lw = fl + (eb * 4 + warp) * NQ;
+#pragma unroll
+            for (int h = 0; h < NKV; ++h)
+#pragma unroll
+                for (int c = 0; c < G; ++c) {
+                    const float x = warp_sumf(l[h][c]);
+                    if (lane == 0) lw[h * G + c] = x;
+                    if (t == 0) fm[eb * NQ + h * G + c] = m[h][c];
+                }
+            mbar_arrive(&seg_done[eb]);
+            ++segk;
+            if (!more) break;
+        }
+    } else if (warp >= kEpiWarp0) {
+        // ---------------- epilogue (warps 6-9) ----------------
+        // Segment k: O buffer k & 1 once its last PV is done (o_full) and its
+        // maxima and row sums are written (seg_done).  TMEM lane r holds head
+        // dim r & 63 of unit r >> 6 (the pair's second kv head, or for a
+        // single kv head the odd blocks' share of the same head).
+        const int e = threadIdx.x - kEpiWarp0 * 32;
+        const int row = 32 * (warp & 3) + lane;
+        const uint32_t lane_base = tmem + (static_cast<uint32_t>(32 * (warp & 3)) << 16);
+        const int ut = row >> 6, d = row & 63;
+        const int ew = warp - kEpiWarp0;  // 0-3
+        int k = 0;
+        int g = gb, s = find_seq(pstart, n, gb);
+        while (g < ge) {
+            const Seg cur = make_seg<NKV>(a, pstart, s, g, ge);
+            const int eb = k & 1;
+            const uint32_t ph = static_cast<uint32_t>(k >> 1) & 1u;
+            const bool okE = __all_sync(kAll, wait_bar(&o_full[eb], ph, abort_flag, a.err)) &&
+                             __all_sync(kAll, wait_bar(&seg_done[eb], ph, abort_flag, a.err));
+            float ov[kPairs][G], Lv[kPairs][G], Mv[kPairs][G];
+#pragma unroll
+            for (int p = 0; p < kPairs; ++p) {
+                uint32_t o[4] = {0, 0, 0, 0};
+                if (okE) {
+                    tc_fence_after();
+                    tmem_ld4(lane_base + kColO + 64 * eb + 16 * p + 8 * ut, o);
+                    tmem_wait4(o);
+                }
+                const int h = NKV >= 2 ? 2 * p + ut : 0;
+#pragma unroll
+                for (int c = 0; c < G; ++c) {
+                    const int qh = h * G + c;
+                    const float* lb = fl + eb * 4 * NQ;
+                    ov[p][c] = __uint_as_float(o[c]);
+                    Lv[p][c] = lb[qh] + lb[NQ + qh] + lb[2 * NQ + qh] + lb[3 * NQ + qh];
+                    Mv[p][c] = fm[eb * NQ + qh];
+                }
+            }
+            if (NKV == 1) {  // the odd blocks accumulate in lanes 64-127: add them in
+                if (ut == 1)
+#pragma unroll
+                    for (int c = 0; c < G; ++c) fob[d * 4 + c] = ov[0][c];
+                named_bar_sync(kEpiBar, kEpiThreads);
+                if (ut == 0)
+#pragma unroll
+                    for (int c = 0; c < G; ++c) ov[0][c] += fob[d * 4 + c];
+                named_bar_sync(kEpiBar, kEpiThreads);  // fob is free again
+            }
+            tc_fence_before();
+            mbar_arrive(&o_free[eb]);  // O buffer eb and its sums may be reused
+            const bool whole = cur.s_begin >= gb && cur.s_end <= ge;
+            const int pslot = (cur.s_begin < gb) ? 2 * cta : 2 * cta + 1;
+            if (NKV >= 2 || ut == 0) {
+#pragma unroll
+                for (int p = 0; p < kPairs; ++p) {
+                    const int h = NKV >= 2 ? 2 * p + ut : 0;
+#pragma unroll
+                    for (int c = 0; c < G; ++c) {
+                        const int qh = h * G + c;
+                        if (whole) {
+                            const float inv = Lv[p][c] > 0.f ? 1.f / Lv[p][c] : 0.f;
+                            a.out[(static_cast<size_t>(cur.s) * NQ + qh) * kHeadDim + d] =
+                                __float2bfloat16_rn(ov[p][c] * inv);
+                        } else {
+                            const size_t prow = static_cast<size_t>(pslot) * NQ + qh;
+                            a.part_o[prow * kHeadDim + d] = ov[p][c];
+                            if (d == 0) *reinterpret_cast<float2*>(a.part_ml + prow * 2) = make_float2(Mv[p][c], Lv[p][c]);
+                        }
+                    }
+                }
+            }
+            if (!whole) {
+                __threadfence();
+                named_bar_sync(kEpiBar, kEpiThreads);
+                if (e == 0) *contrib = atomicAdd(a.counters + cur.s, 1);
+                named_bar_sync(kEpiBar, kEpiThreads);
+                // Contributors: the CTAs whose slice holds a chunk of s; every
+                // CTA holds at least one chunk, so they are consecutive.  The
+                // last to arrive merges the partials.
+                const int c_first = cta_of(cur.s_begin, grid, total);
+                const int n_contrib = cta_of(cur.s_end - 1, grid, total) - c_first + 1;
+                if (*contrib == n_contrib - 1) {
+                    __threadfence();
+                    // Warp w folds query heads w, w + 4, ..., kMH of them at a
+                    // time, each row a partial (256 bytes, lane takes dims
+                    // 2 lane, 2 lane + 1) into an online maximum, kMB rows of
+                    // each head in flight.
+                    constexpr int kMH = 3, kMB = 8;
+                    for (int qb = ew; qb < NQ; qb += 4 * kMH) {
+                        float Mr[kMH], Lr[kMH];
+                        float2 Or[kMH];
+#pragma unroll
+                        for (int hh = 0; hh < kMH; ++hh) {
+                            Mr[hh] = -INFINITY;
+                            Lr[hh] = 0.f;
+                            Or[hh] = make_float2(0.f, 0.f);
+                        }
+                        for (int i0 = 0; i0 < n_contrib; i0 += kMB) {
+                            float2 ml[kMH][kMB], pv[kMH][kMB];
+#pragma unroll
+                            for (int u = 0; u < kMB; ++u) {
+                                const int ic = i0 + u;
+                                const int cc = ic < n_contrib ? c_first + ic : c_first;
+                                const int sl = (cc == c_first) ? 2 * cc + 1 : 2 * cc;
+#pragma unroll
+                                for (int hh = 0; hh < kMH; ++hh) {
+                                    const int qh = qb + 4 * hh;
+                                    if (ic < n_contrib && qh < NQ) {
+                                        const size_t prow = static_cast<size_t>(sl) * NQ + qh;
+                                        ml[hh][u] = __ldcg(reinterpret_cast<const float2*>(a.part_ml + prow * 2));
+                                        pv[hh][u] = __ldcg(reinterpret_cast<const float2*>(a.part_o + prow * kHeadDim) + lane);
+                                    } else {
+                                        ml[hh][u] = make_float2(-INFINITY, 0.f);
+                                        pv[hh][u] = make_float2(0.f, 0.f);
+                                    }
+                                }
+                            }
+#pragma unroll
+                            for (int hh = 0; hh < kMH; ++hh) {
+                                float bm = Mr[hh];
+#pragma unroll
+                                for (int u = 0; u < kMB; ++u) bm = fmaxf(bm, ml[hh][u].x);
+                                const float mu = (bm == -INFINITY) ? 0.f : bm;
+                                const float sc = ex2f(Mr[hh] - mu);
+                                Lr[hh] *= sc;
+                                Or[hh] = make_float2(Or[hh].x * sc, Or[hh].y * sc);
+#pragma unroll
+                                for (int u = 0; u < kMB; ++u) {
+                                    const float w = ex2f(ml[hh][u].x - mu);
+                                    Lr[hh] = fmaf(ml[hh][u].y, w, Lr[hh]);
+                                    Or[hh] = make_float2(fmaf(pv[hh][u].x, w, Or[hh].x), fmaf(pv[hh][u].y, w, Or[hh].y));
+                                }
+                                Mr[hh] = bm;
+                            }
+                        }
+#pragma unroll
+                        for (int hh = 0; hh < kMH; ++hh) {
+                            const int qh = qb + 4 * hh;
+                            if (qh < NQ) {
+                                const float inv = Lr[hh] > 0.f ? 1.f / Lr[hh] : 0.f;
+                                *reinterpret_cast<uint32_t*>(a.out + (static_cast<size_t>(cur.s) * NQ + qh) * kHeadDim +
+                                                             2 * lane) = float2_to_bf16x2(Or[hh].x * inv, Or[hh].y * inv);
+                            }
+                        }
+                    }
+                    if (e == 0) a.counters[cur.s] = 0;
+                }
+                named_bar_sync(kEpiBar, kEpiThreads);  // contrib is read by all before the next segment
+            }
+            ++k;
+            g = min(ge, cur.s_end);
+            if (g < ge) s = find_seq(pstart, n, g);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == kMmaWarp) {
+        __syncwarp();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+    }
+}
+
+// ---------------------------------------------------------------------------
+struct TcVariant {
+    int nkv, group;
+    const void* fn;
+    size_t (*smem)(int);
+};
+
+template <int NKV, int G>
+TcVariant make_tc_variant() {
+    return TcVariant{NKV, G, reinterpret_cast<const void*>(&decode_tc_kernel<NKV, G>), &TcShape<NKV, G>::smem_bytes};
+}
+
+const TcVariant* find_tc_variant(int nkv, int group) {
+    static const TcVariant table[] = {
+        make_tc_variant<8, 3>(), make_tc_variant<8, 4>(), make_tc_variant<1, 4>(),
+        make_tc_variant<2, 4>(), make_tc_variant<4, 4>(),
+    };
+    for (const auto& v : table)
+        if (v.nkv == nkv && v.group == group) return &v;
+    return nullptr;
+}
+
+}  // namespace
+
+int decode_tc_setup(kv_pool* pool) {
+    const auto& c = pool->cfg;
+    const TcVariant* v = find_tc_variant(c.n_kv_heads, c.n_q_heads / c.n_kv_heads);
+    if (!v) return KV_ERR_UNSUPPORTED;
+    const size_t smem = v->smem(c.max_seqs);
+    int optin = 0;
+    if (cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, c.device) != cudaSuccess)
+        return KV_ERR_CUDA;
+    if (smem > static_cast<size_t>(optin)) return KV_ERR_INVALID;  // max_seqs too large
+    if (raise_smem_limit(v->fn, c.device, smem) != KV_OK) return KV_ERR_CUDA;
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, v->fn, kThreads, smem) != cudaSuccess || per_sm < 1)
+        return KV_ERR_CUDA;
+    pool->decode_grid = pool->sm_count * per_sm;
+    pool->decode_smem = smem;
+    return KV_OK;
+}
+
+int launch_decode_tc(kv_pool* pool, const void* q, const uint32_t* bt, int32_t bt_stride, const int32_t* seq_lens,
+                     int32_t n_seqs, int32_t window, void* out, cudaStream_t stream, const void* new_k,
+                     const void* new_v) {
+    const auto& c = pool->cfg;
+    const TcVariant* v = find_tc_variant(c.n_kv_heads, c.n_q_heads / c.n_kv_heads);
+    if (!v) return KV_ERR_UNSUPPORTED;
+    TcArgs a;
+    a.q = static_cast<const __nv_bfloat16*>(q);
+    a.out = static_cast<__nv_bfloat16*>(out);
+    a.bt = bt;
+    a.bt_stride = bt_stride;
+    a.seq_lens = seq_lens;
+    a.n_seqs = n_seqs;
+    a.window = window;
+    a.rope = pool->rope;
+    a.max_pos = c.max_positions;
+    a.n_pages = c.n_pages;
+    a.page_rows = static_cast<int>(pool->page_bytes / 128);
+    a.part_o = pool->part_o;
+    a.part_ml = pool->part_ml;
+    a.counters = pool->counters;
+    a.err = pool->dev_error;
+    a.qscale = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(c.head_dim)));
+    a.new_k = static_cast<const __nv_bfloat16*>(new_k);
+    a.new_v = static_cast<const __nv_bfloat16*>(new_v);
+    a.pages = static_cast<uint8_t*>(pool->pages);
+    void* args[] = {&pool->head_map, &a};
+    const cudaError_t e =
+        cudaLaunchKernel(v->fn, dim3(pool->decode_grid), dim3(kThreads), args, pool->decode_smem, stream);
+    return e == cudaSuccess ? KV_OK : KV_ERR_CUDA;
+}
+
+}  // namespace kvb200

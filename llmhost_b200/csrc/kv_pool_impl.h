@@ -33,6 +33,10 @@ int launch_append(kv_pool* pool, const void* k, const void* v, const int32_t* to
                   int32_t n_tokens, int32_t n_seqs, const uint32_t* bt, int32_t bt_stride,
                   cudaStream_t stream);
 
+// Raises a kernel's dynamic shared-memory limit on `device` to at least
+// `bytes` (never lowers it: the attribute is shared by every pool).
+int raise_smem_limit(const void* fn, int device, size_t bytes);
+
 // Sets up the decode kernel for the pool (smem attribute, grid); called once
 // at pool creation.  Returns KV_ERR_UNSUPPORTED for shapes not compiled.
 int decode_setup(kv_pool* pool);
@@ -42,6 +46,13 @@ size_t decode_workspace_slots(const kv_pool* pool);
 int launch_decode(kv_pool* pool, const void* q, const uint32_t* bt, int32_t bt_stride,
                   const int32_t* seq_lens, int32_t n_seqs, int32_t window, void* out,
                   cudaStream_t stream, const void* new_k = nullptr, const void* new_v = nullptr);
+
+// Decode attention on tcgen05 for bf16 pools (kv_decode_tc.cu); decode_setup
+// and launch_decode route bf16 pools here.
+int decode_tc_setup(kv_pool* pool);
+int launch_decode_tc(kv_pool* pool, const void* q, const uint32_t* bt, int32_t bt_stride, const int32_t* seq_lens,
+                     int32_t n_seqs, int32_t window, void* out, cudaStream_t stream, const void* new_k,
+                     const void* new_v);
 
 // Prefill / tree-verify attention: tcgen05 for bf16 pools (kv_prefill.cu).
 int prefill_setup(kv_pool* pool);
