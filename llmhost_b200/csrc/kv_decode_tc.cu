@@ -111,51 +111,63 @@ struct TcShape {
     static size_t smem_bytes(int max_seqs) { return 1024 + kOffScan + (static_cast<size_t>(max_seqs) + 1) * 4; }
 };
 
-// Work is sliced in chunks of one stage round: a block of 8 pages (all kv
-// heads) or, with a single kv head, two blocks.  Every sequence's pages are
-// cut into chunks from its first page (the last chunk may be partial), the
-// chunks of all sequences laid end to end, and each CTA takes an equal run
-// of whole chunks, so a cut between CTAs never leaves two partial blocks.
+// Work is sliced in stages.  Every sequence's pages are cut into chunks from
+// its first page (8 pages; 16 with a single kv head; the last chunk may be
+// partial), each chunk into kStages stages (one per kv head pair), the
+// stages of all sequences laid end to end, and each CTA takes an equal run
+// of them.  A cut between CTAs never splits a block, only the head pairs of
+// one chunk.
 template <int NKV>
 struct Chunk {
     static constexpr int kPages = NKV >= 2 ? kUnitPages : 2 * kUnitPages;
+    static constexpr int kStages = NKV >= 2 ? NKV / 2 : 1;
 };
 
-// One sequence's chunks [g, min(ge, s_end)) inside this CTA's slice [gb, ge)
-// (chunk indices): s_begin / s_end are the sequence's first and end chunk.
+// One sequence's stages [g, min(ge, s_end)) inside this CTA's slice [gb, ge)
+// (global stage indices; s_begin / s_end are the sequence's first and end
+// stage).  j0, j1: the same range counted from the sequence's first stage;
+// c0: the chunk of stage j0; pg0, np: block-table index of chunk c0's first
+// page, and the pages from there to the end of the segment's last chunk;
+// last_chunk: the chunk holding the sequence's last page.
 struct Seg {
-    int s, nt, lo, pg0, np, s_begin, s_end, nst;
+    int s, nt, lo, pg0, np, s_begin, s_end, j0, j1, c0, nst, last_chunk;
 };
 
 template <int NKV>
-__device__ __forceinline__ Seg make_seg(const TcArgs& a, const int* cstart, int s, int g, int ge) {
-    constexpr int kCp = Chunk<NKV>::kPages;
+__device__ __forceinline__ Seg make_seg(const TcArgs& a, const int* sstart, int s, int g, int ge) {
+    constexpr int kCp = Chunk<NKV>::kPages, kSt = Chunk<NKV>::kStages;
     Seg q;
     q.s = s;
     q.nt = __ldg(a.seq_lens + s);
     q.lo = seq_lo(q.nt, a.window);
-    q.s_begin = cstart[s];
-    q.s_end = cstart[s + 1];
-    const int p0 = kCp * (g - q.s_begin);
-    const int p1 = min(seq_pages(q.nt, a.window), kCp * (min(ge, q.s_end) - q.s_begin));
+    q.s_begin = sstart[s];
+    q.s_end = sstart[s + 1];
+    q.j0 = g - q.s_begin;
+    q.j1 = min(ge, q.s_end) - q.s_begin;
+    q.c0 = q.j0 / kSt;
+    const int pages = seq_pages(q.nt, a.window);
+    const int p0 = kCp * q.c0;
+    const int p1 = min(pages, kCp * ((q.j1 - 1) / kSt + 1));
     q.np = p1 - p0;
-    q.pg0 = q.lo / kPageTokens + p0;  // block-table index of the segment's first page
-    const int nblk = (q.np + kUnitPages - 1) / kUnitPages;
-    q.nst = NKV >= 2 ? nblk * (NKV / 2) : (nblk + 1) / 2;
+    q.pg0 = q.lo / kPageTokens + p0;
+    q.nst = q.j1 - q.j0;
+    q.last_chunk = (pages - 1) / kCp;
     return q;
 }
 
-// Stage j of a segment: each unit's block and its page count, and the pair p.
+// Stage jj of a segment: each unit's block (counted from chunk c0) and its
+// page count, and the pair p.
 template <int NKV>
-__device__ __forceinline__ void stage_units(const Seg& q, int j, int& b0, int& b1, int& n0, int& n1, int& p) {
-    constexpr int kPairs = NKV >= 2 ? NKV / 2 : 1;
+__device__ __forceinline__ void stage_units(const Seg& q, int jj, int& b0, int& b1, int& n0, int& n1, int& p) {
+    constexpr int kSt = Chunk<NKV>::kStages;
+    const int j = q.j0 + jj;
+    const int c = j / kSt - q.c0;
+    p = j % kSt;
     if (NKV >= 2) {
-        b0 = b1 = j / kPairs;
-        p = j % kPairs;
+        b0 = b1 = c;
     } else {
-        b0 = 2 * j;
-        b1 = 2 * j + 1;
-        p = 0;
+        b0 = 2 * c;
+        b1 = 2 * c + 1;
     }
     n0 = max(0, min(kUnitPages, q.np - kUnitPages * b0));
     n1 = max(0, min(kUnitPages, q.np - kUnitPages * b1));
@@ -197,10 +209,50 @@ __device__ __forceinline__ float warp_maxf(float x) {
     return r;
 }
 
-__device__ __forceinline__ float warp_sumf(float x) {
+// Warp reduce-scatter of N per-lane values: level LV (partner lane ^ (16 >>
+// LV)) halves the vector while it splits evenly and did so at the level
+// before, else adds the partner's whole vector.  Afterwards the lanes whose
+// full-exchange bits are clear hold the warp sums of values [base, base +
+// len) in v[0 .. len).
+template <int N, int LEN, int LV, bool HALVING>
+struct ReduceScatter {
+    static constexpr bool kHalve = HALVING && LEN % 2 == 0;
+    static constexpr int kNext = kHalve ? LEN / 2 : LEN;
+    static constexpr int kFinal = ReduceScatter<N, kNext, LV + 1, kHalve>::kFinal;
+    __device__ __forceinline__ static void run(float (&v)[N], int lane, int& base, int& full_mask) {
+        constexpr int o = 16 >> LV;
+        if constexpr (kHalve) {
+            const bool upper = (lane & o) != 0;
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(kAll, x, o);
-    return x;
+            for (int j = 0; j < kNext; ++j) {
+                const float send = upper ? v[j] : v[j + kNext];
+                const float keep = upper ? v[j + kNext] : v[j];
+                v[j] = keep + __shfl_xor_sync(kAll, send, o);
+            }
+            if (upper) base += kNext;
+        } else {
+#pragma unroll
+            for (int j = 0; j < LEN; ++j) v[j] += __shfl_xor_sync(kAll, v[j], o);
+            full_mask |= o;
+        }
+        ReduceScatter<N, kNext, LV + 1, kHalve>::run(v, lane, base, full_mask);
+    }
+};
+template <int N, int LEN, bool HALVING>
+struct ReduceScatter<N, LEN, 5, HALVING> {
+    static constexpr int kFinal = LEN;
+    __device__ __forceinline__ static void run(float (&)[N], int, int&, int&) {}
+};
+
+// Warp sums of v[0 .. N) stored to dst[0 .. N).
+template <int N>
+__device__ __forceinline__ void warp_reduce_scatter_store(float (&v)[N], float* dst, int lane) {
+    int base = 0, full_mask = 0;
+    ReduceScatter<N, N, 0, true>::run(v, lane, base, full_mask);
+    if ((lane & full_mask) == 0) {
+#pragma unroll
+        for (int j = 0; j < ReduceScatter<N, N, 0, true>::kFinal; ++j) dst[base + j] = v[j];
+    }
 }
 
 __device__ __forceinline__ float2 ld_pair(const __nv_bfloat16* p) {
@@ -232,7 +284,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(const __grid_con
     volatile int* abort_flag = ints + 1;
     int* contrib = ints + 2;
     int* vote = ints + 8;             // [2][4]
-    int* pstart = reinterpret_cast<int*>(base + Sh::kOffScan);  // chunk starts, [n_seqs + 1]
+    int* pstart = reinterpret_cast<int*>(base + Sh::kOffScan);  // stage starts, [n_seqs + 1]
     float* fmax = reinterpret_cast<float*>(base + Sh::kOffMax);
     float* fm = reinterpret_cast<float*>(base + Sh::kOffM);
     float* fl = reinterpret_cast<float*>(base + Sh::kOffL);
@@ -261,7 +313,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(const __grid_con
         *abort_flag = 0;
         fence_mbar_init();
     }
-    if (warp == 0) scan_units(a.seq_lens, n, a.window, Chunk<NKV>::kPages, pstart, lane);  // chunk starts
+    if (warp == 0) scan_units(a.seq_lens, n, a.window, Chunk<NKV>::kPages, pstart, lane, Chunk<NKV>::kStages);
     if (threadIdx.x < kSoftThreads) {  // Q padding rows and P rows never written stay zero
         uint4* z = reinterpret_cast<uint4*>(base + Sh::kOffQ);
         for (int i = threadIdx.x; i < ((NKV + 1) * 1024 + 2 * kPBytes) / 16; i += kSoftThreads)
@@ -272,7 +324,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(const __grid_con
 
     const int total = pstart[n];
     const int cta = blockIdx.x;
-    const int grid = max(1, min(static_cast<int>(gridDim.x), total));  // at least one chunk per CTA
+    const int grid = max(1, min(static_cast<int>(gridDim.x), total));  // at least one stage per CTA
     for (int s = cta; s < n; s += gridDim.x) {  // sequences with no tokens: zeros
         if (__ldg(a.seq_lens + s) <= 0) {
             __nv_bfloat16* o = a.out + static_cast<size_t>(s) * NQ * kHeadDim;
@@ -306,9 +358,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(const __grid_con
         while (g < ge) {
             const Seg q = make_seg<NKV>(a, pstart, s, g, ge);
             // Fused append: the new token (slot nt - 1, on the sequence's last
-            // page) when that page is in this slice and its position is valid.
-            bool app = a.new_k != nullptr && q.s_end <= ge && q.nt - 1 < a.max_pos;
-            const int blast = (q.np - 1) / kUnitPages;
+            // page) for the heads of this slice's stages of the last chunk,
+            // when its position is valid.
+            const bool app = a.new_k != nullptr && (q.j1 - 1) / Chunk<NKV>::kStages == q.last_chunk &&
+                             q.nt - 1 < a.max_pos;
             if (app) {
                 const __nv_bfloat16* kr = a.new_k + static_cast<size_t>(q.s) * NKV * kHeadDim;
                 const __nv_bfloat16* vr = a.new_v + static_cast<size_t>(q.s) * NKV * kHeadDim;
@@ -335,9 +388,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(const __grid_con
                     issuing = __shfl_sync(kAll, ok, 0);
                 }
                 if (!issuing) continue;
-                if (app && (b0 == blast || b1 == blast)) {
-                    // Store the rotated K and the V rows of every head to the
-                    // page, then let the async proxy (TMA) see them.
+                if (app && (q.j0 + j) / Chunk<NKV>::kStages == q.last_chunk) {
+                    // Store the rotated K and the V rows of this stage's heads
+                    // to the page, then let the async proxy (TMA) see them.
                     cp_async_wait<0>();
                     __syncwarp();
                     const int pgl = q.pg0 + q.np - 1;
@@ -349,7 +402,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(const __grid_con
                         const float4 c = *reinterpret_cast<const float4*>(stg + NKV * 256 + 16 * (lane & 15));
                         const int ii = lane & 15;
 #pragma unroll
-                        for (int h = 0; h < NKV; ++h) {
+                        for (int hh = 0; hh < (NKV >= 2 ? 2 : 1); ++hh) {
+                            const int h = NKV >= 2 ? 2 * p + hh : 0;
                             const uint8_t* in = stg + h * 256;
                             if (lane < 16) {
                                 const float2 x = bf16x2_to_float2(*reinterpret_cast<const uint32_t*>(in + 4 * ii));
@@ -369,7 +423,6 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(const __grid_con
                         asm volatile("fence.proxy.async.global;" ::: "memory");
                     }
                     __syncwarp();
-                    app = false;
                 }
                 if (lane == 0) mbar_arrive_expect_tx(&full[st], kStageBytes);
                 __syncwarp();
@@ -393,7 +446,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(const __grid_con
                             0, row);
                 issued = i + 1;
             }
-            if (app) cp_async_wait<0>();  // staged, not stored (the issue stopped)
+            if (app) cp_async_wait<0>();  // nothing left in flight into the staging area
             g = min(ge, q.s_end);
             if (g < ge) s = find_seq(pstart, n, g);
         }
@@ -425,13 +478,15 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(const __grid_con
             while (!pc.done) {
                 if (*abort_flag) break;
                 bool progress = false;
-                const bool first = pc.j < kPairs;  // first PV into its accumulator in this segment
+                // first PV into its accumulator in this segment: every pair
+                // occurs once in any kPairs consecutive stages
+                const bool first = pc.j < kPairs;
                 const int eb = pc.seg_no & 1;      // O buffer of the segment
                 if (pc.i < sc.i && mbar_test(&p_full[pc.i & 1], static_cast<uint32_t>(pc.i >> 1) & 1u) &&
                     (!first || pc.seg_no < 2 ||
                      mbar_test(&o_free[eb], static_cast<uint32_t>((pc.seg_no - 2) >> 1) & 1u))) {
                     tc_fence_after();
-                    const int pcc = NKV >= 2 ? pc.j % kPairs : 0;
+                    const int pcc = NKV >= 2 ? (pc.q.j0 + pc.j) % kPairs : 0;
                     const uint32_t va = st_addr + (pc.i % kStages) * kStageBytes + 2 * kUnitBytes;
                     const uint32_t pa = p_addr + (pc.i & 1) * kPBytes;
 #pragma unroll
@@ -534,11 +589,14 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(const __grid_con
                     m[h][c] = -INFINITY;
                     l[h][c] = 0.f;
                 }
-            const int rounds = q.nst / kPairs;
-            for (int r = 0; r < rounds; ++r) {
+            // chunks of the segment; a head pair outside [j0, j1) is another CTA's
+            const int c_end = (q.j1 - 1) / kPairs;
+            for (int cc = q.c0; cc <= c_end; ++cc) {
 #pragma unroll
-                for (int p = 0; p < kPairs; ++p, ++i) {
-                    const int j = r * kPairs + p;
+                for (int p = 0; p < kPairs; ++p) {
+                    const int jseq = cc * kPairs + p;
+                    if (jseq < q.j0 || jseq >= q.j1) continue;
+                    const int j = jseq - q.j0;
                     int b0, b1, n0, n1, pp;
                     stage_units<NKV>(q, j, b0, b1, n0, n1, pp);
                     constexpr int kH1 = NKV >= 2 ? 1 : 0;
@@ -661,6 +719,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(const __grid_con
                     proxy_fence();
                     tc_fence_before();
                     mbar_arrive(&p_full[sb]);
+                    ++i;
                 }
             }
             // ---- segment done: Q of the next segment first (every S of this
@@ -677,15 +736,15 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(const __grid_con
             }
             const int eb = segk & 1;
             if (segk >= 2) wait_bar(&o_free[eb], static_cast<uint32_t>((segk - 2) >> 1) & 1u, abort_flag, a.err);
-            float* lw = fl + (eb * 4 + warp) * NQ;
+            float lv[NQ];
 #pragma unroll
             for (int h = 0; h < NKV; ++h)
 #pragma unroll
                 for (int c = 0; c < G; ++c) {
-                    const float x = warp_sumf(l[h][c]);
-                    if (lane == 0) lw[h * G + c] = x;
+                    lv[h * G + c] = l[h][c];
                     if (t == 0) fm[eb * NQ + h * G + c] = m[h][c];
                 }
+            warp_reduce_scatter_store<NQ>(lv, fl + (eb * 4 + warp) * NQ, lane);
             mbar_arrive(&seg_done[eb]);
             ++segk;
             if (!more) break;
@@ -710,22 +769,30 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(const __grid_con
             const bool okE = __all_sync(kAll, wait_bar(&o_full[eb], ph, abort_flag, a.err)) &&
                              __all_sync(kAll, wait_bar(&seg_done[eb], ph, abort_flag, a.err));
             float ov[kPairs][G], Lv[kPairs][G], Mv[kPairs][G];
+            uint32_t oa[kPairs][4];
+            if (okE) {
+                tc_fence_after();
+#pragma unroll
+                for (int p = 0; p < kPairs; ++p) tmem_ld4(lane_base + kColO + 64 * eb + 16 * p + 8 * ut, oa[p]);
+#pragma unroll
+                for (int p = 0; p < kPairs; ++p) tmem_wait4(oa[p]);  // one wait; the rest tie the registers
+            } else {
+#pragma unroll
+                for (int p = 0; p < kPairs; ++p) oa[p][0] = oa[p][1] = oa[p][2] = oa[p][3] = 0u;
+            }
 #pragma unroll
             for (int p = 0; p < kPairs; ++p) {
-                uint32_t o[4] = {0, 0, 0, 0};
-                if (okE) {
-                    tc_fence_after();
-                    tmem_ld4(lane_base + kColO + 64 * eb + 16 * p + 8 * ut, o);
-                    tmem_wait4(o);
-                }
+                uint32_t o[4] = {oa[p][0], oa[p][1], oa[p][2], oa[p][3]};
                 const int h = NKV >= 2 ? 2 * p + ut : 0;
 #pragma unroll
                 for (int c = 0; c < G; ++c) {
                     const int qh = h * G + c;
                     const float* lb = fl + eb * 4 * NQ;
-                    ov[p][c] = __uint_as_float(o[c]);
                     Lv[p][c] = lb[qh] + lb[NQ + qh] + lb[2 * NQ + qh] + lb[3 * NQ + qh];
                     Mv[p][c] = fm[eb * NQ + qh];
+                    // a head pair with no stage in this segment (another CTA
+                    // took its part of the chunk): its O columns are stale
+                    ov[p][c] = Lv[p][c] > 0.f ? __uint_as_float(o[c]) : 0.f;
                 }
             }
             if (NKV == 1) {  // the odd blocks accumulate in lanes 64-127: add them in
