@@ -78,14 +78,12 @@ def peaks():
     return FALLBACK_HBM_GBS, "fallback"
 
 
-def load_traffic_ratio(fused: bool = True):
-    """DRAM bytes / algorithmic bytes of the decode kernel (the fused launch,
-    or the attention-only launch) from the committed ncu summary."""
+def load_traffic_ratio():
+    """DRAM bytes / algorithmic bytes of the decode kernel from the committed ncu summary."""
     p = ROOT / "profiles" / "decode_attn_traffic.json"
     if p.exists():
         d = json.loads(p.read_text())
-        r = d if fused else d.get("unfused_attention_launch", d)
-        return float(r["dram_bytes_per_launch"]) / float(r["algorithmic_bytes_per_launch"]), d
+        return float(d["dram_bytes_per_launch"]) / float(d["algorithmic_bytes_per_launch"]), d
     return None, None
 
 
@@ -356,11 +354,11 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     mean_kernel_s = float(np.mean(kernel_ms)) / 1e3
     mean_attn_bytes = float(np.mean(attn_bytes))
     achieved = mean_attn_bytes / mean_kernel_s / 1e9
-    ratio, prof = load_traffic_ratio(fused)
+    ratio, prof = load_traffic_ratio()
     roofline = {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
                 "traffic": (ratio * mean_attn_bytes) if ratio else None,
-                "kernel": "decode_kernel (kv_append_decode_attn: append + attention, one launch per layer)"
-                if fused else "decode_kernel (kv_decode_attn)",
+                "kernel": "decode_tc_kernel (kv_append_decode_attn: append + attention, one launch per layer)"
+                if fused else "decode_tc_kernel (kv_decode_attn)",
                 "algorithmic_bytes_per_launch": mean_attn_bytes,
                 "mean_launch_us": mean_kernel_s * 1e6,
                 "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
@@ -623,7 +621,7 @@ def run_single(args, ctx):
     achieved = float(np.mean(dec_bytes)) / (dec_us * 1e-6) / 1e9
     hbm, kind = peaks()
     roofline = {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
-                "traffic": None, "kernel": "decode_kernel (kv_decode_attn, fp32, 1 session)",
+                "traffic": None, "kernel": "decode_kernel (kv_append_decode_attn, fp32 CUDA cores, 1 session)",
                 "algorithmic_bytes_per_launch": float(np.mean(dec_bytes)), "mean_launch_us": dec_us,
                 "peak_kind": kind,
                 "note": "one session: a launch moves ~4.5 MB, so the kernel is latency-bound, not HBM-bound"}
@@ -1187,7 +1185,7 @@ def run_longctx(args, ctx):
     hbm, kind = peaks()
     achieved = abytes / (kt / 1e3) / 1e9
     roofline = {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
-                "traffic": None, "kernel": "decode_kernel (kv_decode_attn, window 32768)",
+                "traffic": None, "kernel": "decode_tc_kernel (kv_append_decode_attn, window 32768)",
                 "algorithmic_bytes_per_launch": abytes, "mean_launch_us": kt * 1e3, "peak_kind": kind}
     big_ms = float(np.mean([a.elapsed_time(b) for a, b in brec]))
     big_bytes = L * (2 * hpr * 64 * 2 * big_len)
