@@ -890,7 +890,16 @@ int decode_setup(kv_pool* pool) {
     return KV_OK;
 }
 
-size_t decode_workspace_slots(const kv_pool* pool) { return 2 * static_cast<size_t>(pool->decode_grid); }
+// Partial rows: two per CTA; the tensor-core kernel (bf16 pools) keeps two
+// more per CTA for the run partials of a long sequence's two-level merge.
+size_t decode_workspace_slots(const kv_pool* pool) {
+    return (pool->cfg.dtype == KV_DTYPE_BF16 ? 4 : 2) * static_cast<size_t>(pool->decode_grid);
+}
+
+// Merge counters: one per sequence, then two per CTA for the runs.
+size_t decode_counter_count(const kv_pool* pool) {
+    return static_cast<size_t>(pool->cfg.max_seqs) + 2 * static_cast<size_t>(pool->decode_grid);
+}
 
 int launch_decode(kv_pool* pool, const void* q, const uint32_t* bt, int32_t bt_stride,
                   const int32_t* seq_lens, int32_t n_seqs, int32_t window, void* out,

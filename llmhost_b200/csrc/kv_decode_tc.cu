@@ -82,7 +82,8 @@ struct TcArgs {
     int page_rows;
     float* part_o;
     float* part_ml;
-    int* counters;
+    int* counters;   // [n_seqs]: contributors (or runs) merged per sequence
+    int* gcounters;  // [2 * gridDim.x]: contributors merged per run of a long sequence
     int* err;
     float qscale;
     const __nv_bfloat16* new_k;  // fused append (null: none)
@@ -829,21 +830,26 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(const __grid_con
                 }
             }
             if (!whole) {
-                __threadfence();
-                named_bar_sync(kEpiBar, kEpiThreads);
-                if (e == 0) *contrib = atomicAdd(a.counters + cur.s, 1);
-                named_bar_sync(kEpiBar, kEpiThreads);
-                // Contributors: the CTAs whose slice holds a chunk of s; every
-                // CTA holds at least one chunk, so they are consecutive.  The
-                // last to arrive merges the partials.
+                // Contributors: the CTAs whose slice holds a stage of s; every
+                // CTA holds at least one stage, so they are consecutive.  CTA c
+                // wrote its partial to slot 2c + (c == c_first).  Up to kGroup
+                // contributors: the last to arrive merges them all.  More: the
+                // last of each run of kGroup contributors merges its run into
+                // the run's slot in the second half of the workspace, and the
+                // last run to finish merges the run partials.
                 const int c_first = cta_of(cur.s_begin, grid, total);
                 const int n_contrib = cta_of(cur.s_end - 1, grid, total) - c_first + 1;
-                if (*contrib == n_contrib - 1) {
-                    __threadfence();
-                    // Warp w folds query heads w, w + 4, ..., kMH of them at a
-                    // time, each row a partial (256 bytes, lane takes dims
-                    // 2 lane, 2 lane + 1) into an online maximum, kMB rows of
-                    // each head in flight.
+                auto slot_of = [&](int c) { return static_cast<size_t>((c == c_first) ? 2 * c + 1 : 2 * c); };
+                constexpr int kGroup = 16;
+                const int n_groups = (n_contrib + kGroup - 1) / kGroup;
+                const int g_first = c_first + ((cta - c_first) / kGroup) * kGroup;
+                const int g_size = min(kGroup, c_first + n_contrib - g_first);
+                const size_t run_base = 2 * static_cast<size_t>(gridDim.x);
+                // Warp w folds query heads w, w + 4, ..., kMH of them at a time,
+                // each row a partial (256 bytes, lane takes dims 2 lane, 2 lane
+                // + 1) into an online maximum, kMB rows of each head in flight;
+                // the result goes to the output (normalised) or to a partial slot.
+                auto merge = [&](int n_rows, auto row_slot, bool to_out, size_t dst_slot) {
                     constexpr int kMH = 3, kMB = 8;
                     for (int qb = ew; qb < NQ; qb += 4 * kMH) {
                         float Mr[kMH], Lr[kMH];
@@ -854,18 +860,17 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(const __grid_con
                             Lr[hh] = 0.f;
                             Or[hh] = make_float2(0.f, 0.f);
                         }
-                        for (int i0 = 0; i0 < n_contrib; i0 += kMB) {
+                        for (int i0 = 0; i0 < n_rows; i0 += kMB) {
                             float2 ml[kMH][kMB], pv[kMH][kMB];
 #pragma unroll
                             for (int u = 0; u < kMB; ++u) {
                                 const int ic = i0 + u;
-                                const int cc = ic < n_contrib ? c_first + ic : c_first;
-                                const int sl = (cc == c_first) ? 2 * cc + 1 : 2 * cc;
+                                const size_t sl = row_slot(ic < n_rows ? ic : 0);
 #pragma unroll
                                 for (int hh = 0; hh < kMH; ++hh) {
                                     const int qh = qb + 4 * hh;
-                                    if (ic < n_contrib && qh < NQ) {
-                                        const size_t prow = static_cast<size_t>(sl) * NQ + qh;
+                                    if (ic < n_rows && qh < NQ) {
+                                        const size_t prow = sl * NQ + qh;
                                         ml[hh][u] = __ldcg(reinterpret_cast<const float2*>(a.part_ml + prow * 2));
                                         pv[hh][u] = __ldcg(reinterpret_cast<const float2*>(a.part_o + prow * kHeadDim) + lane);
                                     } else {
@@ -895,14 +900,44 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(const __grid_con
 #pragma unroll
                         for (int hh = 0; hh < kMH; ++hh) {
                             const int qh = qb + 4 * hh;
-                            if (qh < NQ) {
+                            if (qh >= NQ) continue;
+                            if (to_out) {
                                 const float inv = Lr[hh] > 0.f ? 1.f / Lr[hh] : 0.f;
                                 *reinterpret_cast<uint32_t*>(a.out + (static_cast<size_t>(cur.s) * NQ + qh) * kHeadDim +
                                                              2 * lane) = float2_to_bf16x2(Or[hh].x * inv, Or[hh].y * inv);
+                            } else {
+                                const size_t prow = dst_slot * NQ + qh;
+                                *(reinterpret_cast<float2*>(a.part_o + prow * kHeadDim) + lane) = Or[hh];
+                                if (lane == 0)
+                                    *reinterpret_cast<float2*>(a.part_ml + prow * 2) = make_float2(Mr[hh], Lr[hh]);
                             }
                         }
                     }
-                    if (e == 0) a.counters[cur.s] = 0;
+                };
+                __threadfence();
+                named_bar_sync(kEpiBar, kEpiThreads);
+                if (e == 0)
+                    *contrib = atomicAdd(n_groups == 1 ? a.counters + cur.s : a.gcounters + slot_of(g_first), 1);
+                named_bar_sync(kEpiBar, kEpiThreads);
+                if (n_groups == 1) {
+                    if (*contrib == n_contrib - 1) {
+                        __threadfence();
+                        merge(n_contrib, [&](int r) { return slot_of(c_first + r); }, true, 0);
+                        if (e == 0) a.counters[cur.s] = 0;
+                    }
+                } else if (*contrib == g_size - 1) {
+                    __threadfence();
+                    merge(g_size, [&](int r) { return slot_of(g_first + r); }, false, run_base + slot_of(g_first));
+                    if (e == 0) a.gcounters[slot_of(g_first)] = 0;
+                    __threadfence();
+                    named_bar_sync(kEpiBar, kEpiThreads);  // every thread has read contrib
+                    if (e == 0) *contrib = atomicAdd(a.counters + cur.s, 1);
+                    named_bar_sync(kEpiBar, kEpiThreads);
+                    if (*contrib == n_groups - 1) {
+                        __threadfence();
+                        merge(n_groups, [&](int r) { return run_base + slot_of(c_first + r * kGroup); }, true, 0);
+                        if (e == 0) a.counters[cur.s] = 0;
+                    }
                 }
                 named_bar_sync(kEpiBar, kEpiThreads);  // contrib is read by all before the next segment
             }
@@ -983,6 +1018,7 @@ int launch_decode_tc(kv_pool* pool, const void* q, const uint32_t* bt, int32_t b
     a.part_o = pool->part_o;
     a.part_ml = pool->part_ml;
     a.counters = pool->counters;
+    a.gcounters = pool->counters + c.max_seqs;
     a.err = pool->dev_error;
     a.qscale = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(c.head_dim)));
     a.new_k = static_cast<const __nv_bfloat16*>(new_k);

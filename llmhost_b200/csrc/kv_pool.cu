@@ -187,7 +187,7 @@ int kv_pool_create(const kv_pool_config* cfg, kv_pool** out) {
         (rc = alloc_dev(reinterpret_cast<void**>(&p->part_o),
                         slots * cfg->n_q_heads * cfg->head_dim * sizeof(float))) ||
         (rc = alloc_dev(reinterpret_cast<void**>(&p->part_ml), slots * cfg->n_q_heads * 2 * sizeof(float))) ||
-        (rc = alloc_dev(reinterpret_cast<void**>(&p->counters), cfg->max_seqs * sizeof(int)))) {
+        (rc = alloc_dev(reinterpret_cast<void**>(&p->counters), kvb200::decode_counter_count(p) * sizeof(int)))) {
         free_pool(p);
         return rc;
     }
@@ -195,7 +195,7 @@ int kv_pool_create(const kv_pool_config* cfg, kv_pool** out) {
     build_rope_table(cfg->max_positions, cfg->head_dim, cfg->rope_theta, table);
     if (cudaMemset(p->pages, 0, pool_bytes) != cudaSuccess ||
         cudaMemset(p->dev_error, 0, sizeof(kvb200::DeviceWs)) != cudaSuccess ||
-        cudaMemset(p->counters, 0, cfg->max_seqs * sizeof(int)) != cudaSuccess ||
+        cudaMemset(p->counters, 0, kvb200::decode_counter_count(p) * sizeof(int)) != cudaSuccess ||
         cudaMemcpy(p->rope, table.data(), rope_elems * sizeof(float2), cudaMemcpyHostToDevice) !=
             cudaSuccess ||
         cudaDeviceSynchronize() != cudaSuccess) {
@@ -261,7 +261,7 @@ int kv_last_error(kv_pool* pool) {
     if (word == 0) return KV_OK;
     cudaMemset(pool->dev_error, 0, sizeof(int));
     // A wait that gave up may have left a split counter half counted.
-    cudaMemset(pool->counters, 0, pool->cfg.max_seqs * sizeof(int));
+    cudaMemset(pool->counters, 0, kvb200::decode_counter_count(pool) * sizeof(int));
     cudaDeviceSynchronize();
     if (word & kvb200::kDevErrTimeout) return KV_ERR_TIMEOUT;
     if (word & kvb200::kDevErrBadPage) return KV_ERR_BAD_PAGE;

@@ -16,9 +16,9 @@ struct kv_pool {
     float2* rope = nullptr;       // [max_positions][head_dim / 2] (cos, sin), device
     int* dev_error = nullptr;     // device error word
     // decode split workspace
-    float* part_o = nullptr;      // [2 * decode_grid][n_q][head_dim]
-    float* part_ml = nullptr;     // [2 * decode_grid][n_q][2]
-    int* counters = nullptr;      // [max_seqs]
+    float* part_o = nullptr;      // [decode_workspace_slots][n_q][head_dim]
+    float* part_ml = nullptr;     // [decode_workspace_slots][n_q][2]
+    int* counters = nullptr;      // [decode_counter_count]: per sequence, then per CTA run
     int decode_grid = 0;
     size_t decode_smem = 0;
     CUtensorMap page_map;         // TMA view of the pool as 128-byte rows
@@ -41,6 +41,7 @@ int raise_smem_limit(const void* fn, int device, size_t bytes);
 // at pool creation.  Returns KV_ERR_UNSUPPORTED for shapes not compiled.
 int decode_setup(kv_pool* pool);
 size_t decode_workspace_slots(const kv_pool* pool);
+size_t decode_counter_count(const kv_pool* pool);
 // new_k / new_v non-null: append each sequence's new token first (fused
 // kv_append_decode; the last page of every sequence must be its own).
 int launch_decode(kv_pool* pool, const void* q, const uint32_t* bt, int32_t bt_stride,
