@@ -126,6 +126,11 @@ __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
+// Arrive at a named barrier without waiting for it.
+__device__ __forceinline__ void named_bar_arrive(int id, int nthreads) {
+    asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
 // ---- element helpers -------------------------------------------------------
 // Two bf16 packed in a 32-bit word -> float2 (exact widening).
 __device__ __forceinline__ float2 bf16x2_to_float2(uint32_t w) {

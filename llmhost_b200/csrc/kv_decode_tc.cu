@@ -66,6 +66,7 @@ constexpr int kPBytes = 2 * 16 * 128;  // P: 16 rows x 128 keys as two 64-key at
 constexpr float kLazyLog2 = 8.f;
 constexpr int kSoftBar = 1;     // named barrier of the softmax warps
 constexpr int kEpiBar = 2;      // named barrier of the epilogue warps
+constexpr int kSetupBar = 3;    // the producer's scan is done (it arrives, the others wait)
 constexpr unsigned kAll = 0xffffffffu;
 
 struct TcArgs {
@@ -293,61 +294,78 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(const __grid_con
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n = a.n_seqs;
-    if (threadIdx.x == 0) {
-        for (int i = 0; i < kStages; ++i) {
-            mbar_init(&full[i], 1);
-            mbar_init(&empty[i], 1);
+    // Set-up.  The producer warp initialises the barriers, scans the stage
+    // counts and goes straight on to its first copies; the other warps clear
+    // the Q padding and P buffers, allocate TMEM and wait for the scan.
+    if (warp == kProducerWarp) {
+        if (lane == 0) {
+            for (int i = 0; i < kStages; ++i) {
+                mbar_init(&full[i], 1);
+                mbar_init(&empty[i], 1);
+            }
+            for (int i = 0; i < 2; ++i) {
+                mbar_init(&s_full[i], 1);
+                mbar_init(&s_free[i], kSoftThreads);
+                mbar_init(&p_full[i], kSoftThreads);
+                mbar_init(&pv_done[i], 1);
+            }
+            mbar_init(q_full, kSoftThreads);
+            mbar_init(mma_done, 1);
+            for (int i = 0; i < 2; ++i) {
+                mbar_init(&o_full[i], 1);
+                mbar_init(&seg_done[i], kSoftThreads);
+                mbar_init(&o_free[i], kEpiThreads);
+            }
+            *abort_flag = 0;
+            fence_mbar_init();
+            prefetch_tmap(&hmap);
         }
-        for (int i = 0; i < 2; ++i) {
-            mbar_init(&s_full[i], 1);
-            mbar_init(&s_free[i], kSoftThreads);
-            mbar_init(&p_full[i], kSoftThreads);
-            mbar_init(&pv_done[i], 1);
+        __syncwarp();
+        scan_units(a.seq_lens, n, a.window, Chunk<NKV>::kPages, pstart, lane, Chunk<NKV>::kStages);
+        __syncwarp();
+        named_bar_arrive(kSetupBar, kThreads);
+    } else {
+        if (threadIdx.x < kSoftThreads) {  // Q padding rows and P rows never written stay zero
+            uint4* z = reinterpret_cast<uint4*>(base + Sh::kOffQ);
+            for (int i = threadIdx.x; i < ((NKV + 1) * 1024 + 2 * kPBytes) / 16; i += kSoftThreads)
+                z[i] = make_uint4(0, 0, 0, 0);
+            proxy_fence();
         }
-        mbar_init(q_full, kSoftThreads);
-        mbar_init(mma_done, 1);
-        for (int i = 0; i < 2; ++i) {
-            mbar_init(&o_full[i], 1);
-            mbar_init(&seg_done[i], kSoftThreads);
-            mbar_init(&o_free[i], kEpiThreads);
+        if (warp == kMmaWarp) {
+            asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                             smem_addr(tmem_slot)),
+                         "r"(kTmemCols)
+                         : "memory");
+            asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
         }
-        *abort_flag = 0;
-        fence_mbar_init();
+        tc_fence_before();
+        named_bar_sync(kSetupBar, kThreads);
+        tc_fence_after();
     }
-    if (warp == 0) scan_units(a.seq_lens, n, a.window, Chunk<NKV>::kPages, pstart, lane, Chunk<NKV>::kStages);
-    if (threadIdx.x < kSoftThreads) {  // Q padding rows and P rows never written stay zero
-        uint4* z = reinterpret_cast<uint4*>(base + Sh::kOffQ);
-        for (int i = threadIdx.x; i < ((NKV + 1) * 1024 + 2 * kPBytes) / 16; i += kSoftThreads)
-            z[i] = make_uint4(0, 0, 0, 0);
-        proxy_fence();
-    }
-    __syncthreads();
 
     const int total = pstart[n];
     const int cta = blockIdx.x;
     const int grid = max(1, min(static_cast<int>(gridDim.x), total));  // at least one stage per CTA
-    for (int s = cta; s < n; s += gridDim.x) {  // sequences with no tokens: zeros
-        if (__ldg(a.seq_lens + s) <= 0) {
-            __nv_bfloat16* o = a.out + static_cast<size_t>(s) * NQ * kHeadDim;
-            for (int i = threadIdx.x; i < NQ * kHeadDim; i += kThreads) o[i] = __float2bfloat16_rn(0.f);
-        }
-    }
-    if (cta >= grid) return;
     const int gb = static_cast<int>((static_cast<long long>(cta) * total) / grid);
     const int ge = static_cast<int>((static_cast<long long>(cta + 1) * total) / grid);
-    if (gb >= ge) return;
-
-    if (warp == kMmaWarp) {
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(tmem_slot)),
-                     "r"(kTmemCols)
-                     : "memory");
-        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    if (warp >= kEpiWarp0) {  // sequences with no tokens: zeros (every CTA, idle ones too)
+        for (int s = cta; s < n; s += gridDim.x) {
+            if (__ldg(a.seq_lens + s) <= 0) {
+                __nv_bfloat16* o = a.out + static_cast<size_t>(s) * NQ * kHeadDim;
+                for (int i = threadIdx.x - kEpiWarp0 * 32; i < NQ * kHeadDim; i += kEpiThreads)
+                    o[i] = __float2bfloat16_rn(0.f);
+            }
+        }
     }
-    if (warp == kProducerWarp && lane == 0) prefetch_tmap(&hmap);
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    const uint32_t tmem = *tmem_slot;
+    if (cta >= grid || gb >= ge) {  // no work: hand TMEM back and leave
+        if (warp == kMmaWarp) {
+            const uint32_t tm = *tmem_slot;
+            asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tm), "r"(kTmemCols)
+                         : "memory");
+        }
+        return;
+    }
+    const uint32_t tmem = *tmem_slot;  // read by the warps that waited on the set-up barrier
 
     if (warp == kProducerWarp) {
         // ---------------- producer ----------------
