@@ -116,7 +116,7 @@ int kv_append_decode(kv_pool *pool, const void *k, const void *v, const uint32_t
                      int32_t bt_stride, const int32_t *seq_lens, int32_t n_seqs, void *stream);
 
 /* Paged decode attention.  q: [n_seqs, n_q_heads, head_dim] (pool dtype,
- * before RoPE; rotated here at seq_lens[s] - 1).  Sequence s attends keys
+ * before RoPE; rotated here at seq_lens[s] - 1), 16-byte aligned.  Sequence s attends keys
  * [lo, seq_lens[s]) with lo = window > 0 ? max(0, seq_lens[s] - window) : 0.
  * out: [n_seqs, n_q_heads, head_dim] in the pool dtype.  A sequence with
  * seq_lens[s] == 0 gets zeros. */

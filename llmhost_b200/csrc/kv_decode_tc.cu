@@ -103,7 +103,9 @@ struct TcShape {
     static constexpr int kOffP = kOffQ + (NKV + 1) * 1024;          // P, two buffers
     static constexpr int kOffStg = kOffP + 2 * kPBytes;             // fused append inputs
     static constexpr int kStgBytes = NKV * 256 + 256;               // per head K row, V row; RoPE row
-    static constexpr int kOffMax = kOffStg + kStgBytes;             // float [2][4 warps][2 units][4]
+    static constexpr int kOffQstg = kOffStg + kStgBytes;            // next segment's q rows and RoPE row
+    static constexpr int kQstgBytes = NQ * 128 + 256;
+    static constexpr int kOffMax = kOffQstg + kQstgBytes;           // float [2][4 warps][2 units][4]
     static constexpr int kOffM = kOffMax + 2 * 4 * 8 * 4;           // float [2 buffers][NQ]: reference maxima
     static constexpr int kOffL = kOffM + 2 * NQ * 4;                // float [2 buffers][4 warps][NQ]: row sums
     static constexpr int kOffOb = kOffL + 2 * 4 * NQ * 4;           // float [64][4]
@@ -257,9 +259,6 @@ __device__ __forceinline__ void warp_reduce_scatter_store(float (&v)[N], float* 
     }
 }
 
-__device__ __forceinline__ float2 ld_pair(const __nv_bfloat16* p) {
-    return bf16x2_to_float2(__ldg(reinterpret_cast<const unsigned int*>(p)));
-}
 
 template <int NKV, int G>
 __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(const __grid_constant__ CUtensorMap hmap,
@@ -369,45 +368,72 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(const __grid_con
 
     if (warp == kProducerWarp) {
         // ---------------- producer ----------------
+        // Software-pipelined: stage i + 1's block-table entries are loaded
+        // (and, at a sequence boundary, its segment worked out) before stage
+        // i waits for its ring slot, so the copies go out as the slot frees.
+        // Lane: page k of the unit's block, K or V, unit u.  Lanes 4k .. 4k+3
+        // read page k's K rows of both units' heads (adjacent in the page when
+        // the units are heads 2p, 2p+1) and their V rows.
         const int total_rows = static_cast<int>(a.n_pages) * a.page_rows;
         uint8_t* stg = base + Sh::kOffStg;
-        int i = 0, issued = 0;
-        bool issuing = true;
-        int g = gb, s = find_seq(pstart, n, gb);
-        while (g < ge) {
-            const Seg q = make_seg<NKV>(a, pstart, s, g, ge);
-            // Fused append: the new token (slot nt - 1, on the sequence's last
-            // page) for the heads of this slice's stages of the last chunk,
-            // when its position is valid.
-            const bool app = a.new_k != nullptr && (q.j1 - 1) / Chunk<NKV>::kStages == q.last_chunk &&
-                             q.nt - 1 < a.max_pos;
-            if (app) {
-                const __nv_bfloat16* kr = a.new_k + static_cast<size_t>(q.s) * NKV * kHeadDim;
-                const __nv_bfloat16* vr = a.new_v + static_cast<size_t>(q.s) * NKV * kHeadDim;
-                const uint8_t* cr = reinterpret_cast<const uint8_t*>(a.rope + static_cast<size_t>(q.nt - 1) * (kHeadDim / 2));
-                for (int c = lane; c < NKV * 16 + 16; c += 32) {
-                    if (c < NKV * 16) {
-                        const int h = c >> 4, r = c & 15;
-                        const __nv_bfloat16* src = (r < 8 ? kr : vr) + h * kHeadDim + (r & 7) * 8;
-                        cp_async16(stg + h * 256 + (r >> 3) * 128 + (r & 7) * 16, src);
-                    } else {
-                        cp_async16(stg + NKV * 256 + (c - NKV * 16) * 16, cr + (c - NKV * 16) * 16);
+        const int k = lane >> 2, kv = (lane >> 1) & 1, u = lane & 1;
+        struct Fetch {
+            uint32_t phys;
+            bool load;  // false: past the block's pages (zero fill)
+        };
+        auto fetch = [&](const StageCursor<NKV>& c) -> Fetch {
+            int b0, b1, n0, n1, p;
+            stage_units<NKV>(c.q, c.j, b0, b1, n0, n1, p);
+            if (k >= (u ? n1 : n0)) return Fetch{0u, false};
+            const int pg = c.q.pg0 + kUnitPages * (u ? b1 : b0) + k;
+            return Fetch{pg < a.bt_stride ? __ldg(a.bt + static_cast<size_t>(c.q.s) * a.bt_stride + pg) : kPageNone,
+                         true};
+        };
+        StageCursor<NKV> cur;
+        cur.start(a, pstart, n, gb, ge);
+        Fetch fc = fetch(cur);
+        int issued = 0;
+        bool issuing = true, app = false;
+        while (!cur.done) {
+            const Seg& q = cur.q;
+            if (cur.j == 0) {
+                // Fused append: the new token (slot nt - 1, on the sequence's
+                // last page) for the heads of this slice's stages of the last
+                // chunk, when its position is valid.  Its inputs are staged now.
+                if (app) cp_async_wait<0>();
+                app = a.new_k != nullptr && (q.j1 - 1) / Chunk<NKV>::kStages == q.last_chunk &&
+                      q.nt - 1 < a.max_pos;
+                if (app) {
+                    const __nv_bfloat16* kr = a.new_k + static_cast<size_t>(q.s) * NKV * kHeadDim;
+                    const __nv_bfloat16* vr = a.new_v + static_cast<size_t>(q.s) * NKV * kHeadDim;
+                    const uint8_t* cr =
+                        reinterpret_cast<const uint8_t*>(a.rope + static_cast<size_t>(q.nt - 1) * (kHeadDim / 2));
+                    for (int c = lane; c < NKV * 16 + 16; c += 32) {
+                        if (c < NKV * 16) {
+                            const int h = c >> 4, r = c & 15;
+                            const __nv_bfloat16* src = (r < 8 ? kr : vr) + h * kHeadDim + (r & 7) * 8;
+                            cp_async16(stg + h * 256 + (r >> 3) * 128 + (r & 7) * 16, src);
+                        } else {
+                            cp_async16(stg + NKV * 256 + (c - NKV * 16) * 16, cr + (c - NKV * 16) * 16);
+                        }
                     }
+                    cp_async_commit();
                 }
-                cp_async_commit();
             }
-            for (int j = 0; j < q.nst; ++j, ++i) {
+            StageCursor<NKV> nxt = cur;
+            nxt.next(a, pstart);
+            const Fetch fn = nxt.done ? Fetch{0u, false} : fetch(nxt);  // in flight during the wait below
+            const int i = cur.i, st = i % kStages;
+            if (issuing) {
+                bool ok = true;
+                if (lane == 0 && i >= kStages)
+                    ok = wait_bar(&empty[st], static_cast<uint32_t>(i / kStages - 1) & 1u, abort_flag, a.err);
+                issuing = __shfl_sync(kAll, ok, 0);
+            }
+            if (issuing) {
                 int b0, b1, n0, n1, p;
-                stage_units<NKV>(q, j, b0, b1, n0, n1, p);
-                const int st = i % kStages;
-                if (issuing) {
-                    bool ok = true;
-                    if (lane == 0 && i >= kStages)
-                        ok = wait_bar(&empty[st], static_cast<uint32_t>(i / kStages - 1) & 1u, abort_flag, a.err);
-                    issuing = __shfl_sync(kAll, ok, 0);
-                }
-                if (!issuing) continue;
-                if (app && (q.j0 + j) / Chunk<NKV>::kStages == q.last_chunk) {
+                stage_units<NKV>(q, cur.j, b0, b1, n0, n1, p);
+                if (app && (q.j0 + cur.j) / Chunk<NKV>::kStages == q.last_chunk) {
                     // Store the rotated K and the V rows of this stage's heads
                     // to the page, then let the async proxy (TMA) see them.
                     cp_async_wait<0>();
@@ -445,19 +471,11 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(const __grid_con
                 }
                 if (lane == 0) mbar_arrive_expect_tx(&full[st], kStageBytes);
                 __syncwarp();
-                // lane: page k of the unit's block, K or V, unit u.  Lanes 4k ..
-                // 4k+3 read page k's K rows of both units' heads (adjacent in
-                // the page when the units are heads 2p, 2p+1) and their V rows.
-                const int k = lane >> 2, kv = (lane >> 1) & 1, u = lane & 1;
-                const int bu = u ? b1 : b0, nu = u ? n1 : n0;
                 const int hu = NKV >= 2 ? 2 * p + u : 0;
                 int row = total_rows;  // out of range: zero fill
-                if (k < nu) {
-                    const int pg = q.pg0 + kUnitPages * bu + k;
-                    const uint32_t phys = pg < a.bt_stride ? __ldg(a.bt + static_cast<size_t>(q.s) * a.bt_stride + pg)
-                                                           : kPageNone;
-                    if (phys < a.n_pages)
-                        row = static_cast<int>(phys) * a.page_rows + (kv ? NKV + hu : hu) * kPageTokens;
+                if (fc.load) {
+                    if (fc.phys < a.n_pages)
+                        row = static_cast<int>(fc.phys) * a.page_rows + (kv ? NKV + hu : hu) * kPageTokens;
                     else
                         flag_error(a.err, kDevErrBadPage);
                 }
@@ -465,10 +483,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(const __grid_con
                             0, row);
                 issued = i + 1;
             }
-            if (app) cp_async_wait<0>();  // nothing left in flight into the staging area
-            g = min(ge, q.s_end);
-            if (g < ge) s = find_seq(pstart, n, g);
+            cur = nxt;
+            fc = fn;
         }
+        if (app) cp_async_wait<0>();  // nothing left in flight into the staging area
         // Do not leave while a copy may still be landing: the newest copy
         // issued into each stage covers every older one.
         if (lane == 0) {
@@ -565,21 +583,35 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(const __grid_con
         // Q tiles of a segment: item (h, n, c) rotates dims [8c, 8c+8) with
         // [32+8c, 32+8c+8) of query head h*G + n (rope.rs:76 form), scales them
         // into log2 units and stores bf16 row n of head h's 8-row group.
+        // A segment's q rows and RoPE row are fetched into shared memory
+        // (cp.async) while the segment before it streams, so that building its
+        // Q tiles at the boundary waits on no global load.
+        uint8_t* qstg = base + Sh::kOffQstg;
+        auto seg_pos = [&](const Seg& q) { return q.nt - 1 < a.max_pos ? q.nt - 1 : 0; };
+        auto prefetch_q = [&](const Seg& q) {
+            const uint8_t* src = reinterpret_cast<const uint8_t*>(a.q + static_cast<size_t>(q.s) * NQ * kHeadDim);
+            const uint8_t* cr = reinterpret_cast<const uint8_t*>(a.rope + static_cast<size_t>(seg_pos(q)) * (kHeadDim / 2));
+            for (int c = t; c < NQ * 8 + 16; c += kSoftThreads)
+                cp_async16(qstg + 16 * c, c < NQ * 8 ? src + 16 * c : cr + 16 * (c - NQ * 8));
+            cp_async_commit();
+        };
+        // Q tiles: item (h, n, c) rotates dims [8c, 8c+8) with [32+8c, 32+8c+8)
+        // of query head h*G + n (rope.rs:76 form), scales them into log2 units
+        // and stores bf16 row n of head h's 8-row group.
         auto build_q = [&](const Seg& q) {
-            int pos = q.nt - 1;
-            if (pos >= a.max_pos) {
-                if (t == 0) flag_error(a.err, kDevErrBadPos);
-                pos = 0;
-            }
+            if (q.nt - 1 >= a.max_pos && t == 0) flag_error(a.err, kDevErrBadPos);
+            cp_async_wait<0>();
+            named_bar_sync(kSoftBar, kSoftThreads);  // every thread's pieces have landed
             if (t < NQ * 4) {
                 const int h = t / (G * 4), n_ = (t >> 2) % G, c = t & 3;
-                const __nv_bfloat16* src = a.q + (static_cast<size_t>(q.s) * NQ + h * G + n_) * kHeadDim;
-                const float2* cs = a.rope + static_cast<size_t>(pos) * (kHeadDim / 2) + 8 * c;
+                const uint8_t* row_in = qstg + (h * G + n_) * 128;
+                const float2* cs = reinterpret_cast<const float2*>(qstg + NQ * 128) + 8 * c;
                 uint32_t lo[4], hi[4];
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
-                    const float2 x = ld_pair(src + 8 * c + 2 * e), y = ld_pair(src + 32 + 8 * c + 2 * e);
-                    const float2 c0 = __ldg(cs + 2 * e), c1 = __ldg(cs + 2 * e + 1);
+                    const float2 x = bf16x2_to_float2(*reinterpret_cast<const uint32_t*>(row_in + 16 * c + 4 * e));
+                    const float2 y = bf16x2_to_float2(*reinterpret_cast<const uint32_t*>(row_in + 64 + 16 * c + 4 * e));
+                    const float2 c0 = cs[2 * e], c1 = cs[2 * e + 1];
                     const float a0 = __fadd_rn(__fmul_rn(x.x, c0.x), __fmul_rn(-y.x, c0.y)) * a.qscale;
                     const float a1 = __fadd_rn(__fmul_rn(x.y, c1.x), __fmul_rn(-y.y, c1.y)) * a.qscale;
                     const float b0 = __fadd_rn(__fmul_rn(y.x, c0.x), __fmul_rn(x.x, c0.y)) * a.qscale;
@@ -593,14 +625,23 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(const __grid_con
             }
             proxy_fence();  // the tensor core reads Q through the async proxy
             mbar_arrive(q_full);
+            named_bar_sync(kSoftBar, kSoftThreads);  // the staging area is free again
         };
 
         float m[NKV][G], l[NKV][G];
         int i = 0, segk = 0;
-        int g = gb, s = find_seq(pstart, n, gb);
-        Seg q = make_seg<NKV>(a, pstart, s, g, ge);
+        Seg q = make_seg<NKV>(a, pstart, find_seq(pstart, n, gb), gb, ge);
+        prefetch_q(q);
         build_q(q);
         for (;;) {
+            // the next segment of this slice, its q fetched while this one streams
+            const int g_next = min(ge, q.s_end);
+            const bool more = g_next < ge;
+            Seg nq = q;
+            if (more) {
+                nq = make_seg<NKV>(a, pstart, find_seq(pstart, n, g_next), g_next, ge);
+                prefetch_q(nq);
+            }
 #pragma unroll
             for (int h = 0; h < NKV; ++h)
 #pragma unroll
@@ -745,12 +786,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(const __grid_con
             // one has completed), then hand its reference maxima and row sums
             // to the epilogue warps (O buffer segk & 1), once the epilogue of
             // segment segk - 2 is done with that buffer.
-            const Seg cur = q;
-            g = min(ge, cur.s_end);
-            const bool more = g < ge;
             if (more) {
-                s = find_seq(pstart, n, g);
-                q = make_seg<NKV>(a, pstart, s, g, ge);
+                q = nq;
                 build_q(q);
             }
             const int eb = segk & 1;

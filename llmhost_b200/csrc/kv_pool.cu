@@ -32,7 +32,7 @@ struct DeviceScope {
     }
 };
 
-// The append kernels read k and v rows as 16-byte vectors.
+// k, v and q rows are read as 16-byte vectors (appends, the decode kernels' staging).
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 bool valid_config(const kv_pool_config& c) {
@@ -300,7 +300,7 @@ int kv_decode_attn(kv_pool* pool, const void* q, const uint32_t* block_tables, i
     if (!pool || n_seqs < 0 || window < 0) return KV_ERR_INVALID;
     if (n_seqs == 0) return KV_OK;
     if (n_seqs > pool->cfg.max_seqs) return KV_ERR_INVALID;
-    if (!q || !block_tables || !seq_lens || !out || bt_stride <= 0) return KV_ERR_INVALID;
+    if (!q || !block_tables || !seq_lens || !out || bt_stride <= 0 || !aligned16(q)) return KV_ERR_INVALID;
     DeviceScope dev(pool->cfg.device);
     return kvb200::launch_decode(pool, q, block_tables, bt_stride, seq_lens, n_seqs, window, out,
                                  static_cast<cudaStream_t>(stream));
@@ -313,7 +313,7 @@ int kv_append_decode_attn(kv_pool* pool, const void* k, const void* v, const voi
     if (n_seqs == 0) return KV_OK;
     if (n_seqs > pool->cfg.max_seqs) return KV_ERR_INVALID;
     if (!k || !v || !q || !block_tables || !seq_lens || !out || bt_stride <= 0 || !aligned16(k) ||
-        !aligned16(v))
+        !aligned16(v) || !aligned16(q))
         return KV_ERR_INVALID;
     DeviceScope dev(pool->cfg.device);
     return kvb200::launch_decode(pool, q, block_tables, bt_stride, seq_lens, n_seqs, window, out,
