@@ -7,7 +7,7 @@ stored pages bit-exact (RoPE'd K uses the same libm cos/sin as the reference).
 import numpy as np
 import pytest
 
-from paged_case import DecodeCase, assert_close_rows, to_numpy_f32
+from paged_case import DecodeCase, assert_close_rows, to_numpy_f32, to_torch
 
 pytestmark = pytest.mark.gpu
 
@@ -263,3 +263,41 @@ def test_misaligned_k_is_rejected_before_launch(cuda):
                 call()
             assert e.value.status == 1  # KV_ERR_INVALID
         assert pool.last_error() == 0
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "f32"])
+def test_empty_sequences_get_zeros(cuda, dtype):
+    # seq_lens[s] == 0 (no token at all): the row of out is zeros, whatever it
+    # held, and the other sequences are unaffected.
+    import torch
+
+    case = DecodeCase(dtype, 24, 8, [300, 40, 2000, 5], seed=32)
+    host, ref = case.run_oracle()
+    with case.make_pool() as pool:
+        case.prefill_gpu(pool)
+        case.decode_gpu(pool)  # appends the new tokens (ref covers them)
+        dev = pool.device
+        lens = case.seq_lens.copy()
+        lens[[1, 3]] = 0
+        q = to_torch(case.q, dtype, dev)
+        out = torch.full_like(q, 7.0)
+        pool.decode_attn(q, torch.from_numpy(case.bt_attn.view(np.int32)).to(dev),
+                         torch.from_numpy(lens).to(dev), out=out)
+        torch.cuda.synchronize()
+        assert pool.last_error() == 0
+        got = to_numpy_f32(out)
+    assert np.all(got[[1, 3]] == 0)
+    assert_close_rows(got[[0, 2]], ref[[0, 2]], RTOL[dtype], f"{dtype} rows beside empty ones")
+
+
+@pytest.mark.parametrize("seed", range(6))
+def test_fused_random_batches(cuda, seed):
+    # Random batch shapes: sequence ends, CTA cuts and head-pair splits land
+    # in different places for every seed.
+    rng = np.random.default_rng(100 + seed)
+    n = int(rng.integers(1, 90))
+    lens = rng.integers(0, int(rng.choice([64, 700, 5000])), size=n)
+    n_q, n_kv = [(24, 8), (32, 8), (8, 2), (16, 4), (4, 1)][seed % 5]
+    case = DecodeCase("bf16", n_q, n_kv, lens, seed=200 + seed)
+    out, ref = run_case(case, fused=True)
+    assert_close_rows(out, ref, RTOL["bf16"], f"random batch {seed}")
