@@ -21,6 +21,7 @@
  *                       on q (lfm2.rs:816-822) and the key mask (lfm2.rs:1032-1035)
  *   kv_append_decode_attn  the decode K/V store (lfm2.rs:828-832) and
  *                       attention_decode_cached in one launch
+ *   kv_norm_append_decode_attn  the same with the q/k RMSNorm (lfm2.rs:797-812)
  *   kv_tree_*           validate_tree_for_tokens, validate_accept_path (tree.rs:48-123)
  *   kv_state_*          Engine::{open, forward, accept, rollback, committed,
  *                       session_kv} (batch.rs:128-297) and PagedKv (cache.rs:12-51),
@@ -135,6 +136,16 @@ int kv_decode_attn(kv_pool *pool, const void *q, const uint32_t *block_tables, i
 int kv_append_decode_attn(kv_pool *pool, const void *k, const void *v, const void *q,
                           const uint32_t *block_tables, int32_t bt_stride, const int32_t *seq_lens,
                           int32_t n_seqs, int32_t window, void *out, void *stream);
+
+/* kv_append_decode_attn with the attention layer's per-head RMSNorm of q and
+ * of the new k folded in, before RoPE (lfm2.rs:797-812, the norm of
+ * crates/llm-cpu/src/ops.rs:8-23): x' = w * (x * s) with
+ * s = 1 / sqrt(sum(x^2) / head_dim + eps), the sum in double.  q_norm and
+ * k_norm are [head_dim] fp32 device weights, 16-byte aligned; eps >= 0.  The
+ * stored K is the normalised, rotated k. */
+int kv_norm_append_decode_attn(kv_pool *pool, const void *k, const void *v, const void *q, const float *q_norm,
+                               const float *k_norm, float eps, const uint32_t *block_tables, int32_t bt_stride,
+                               const int32_t *seq_lens, int32_t n_seqs, int32_t window, void *out, void *stream);
 
 /* Chunked-prefill and tree-verify attention: attention_forward
  * (lfm2.rs:1058-1111) for T_s new query tokens of sequence s that follow

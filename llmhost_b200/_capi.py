@@ -78,6 +78,9 @@ SIGNATURES = [
     ("kv_append_decode_attn", c_int32,
      [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_void_p, c_int32, c_int32, c_void_p,
       c_void_p]),
+    ("kv_norm_append_decode_attn", c_int32,
+     [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, ctypes.c_float, c_void_p, c_int32, c_void_p,
+      c_int32, c_int32, c_void_p, c_void_p]),
     ("kv_prefill_attn", c_int32,
      [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32,
       c_void_p, c_void_p]),

@@ -151,4 +151,33 @@ __device__ __forceinline__ uint32_t swz128(uint32_t lin) {
     return (row << 7) | (((chunk ^ (row & 7u)) << 4)) | (lin & 15u);
 }
 
+
+// RMSNorm scale of one head row of 64 values (crates/llm-cpu/src/ops.rs:12-18):
+// the sum of squares in double, in dimension order, as separate rounded
+// products and sums (Rust does not contract), then
+// (float)(1 / sqrt(sumsq / 64 + eps)) with IEEE square root and reciprocal.
+__device__ __forceinline__ float rms_scale_row(const __nv_bfloat16* row, float eps) {
+    double s = 0.0;
+#pragma unroll 8
+    for (int i = 0; i < 64; ++i) {
+        const double v = static_cast<double>(__bfloat162float(row[i]));
+        s = __dadd_rn(s, __dmul_rn(v, v));
+    }
+    const double m = __dadd_rn(__dmul_rn(s, 1.0 / 64.0), static_cast<double>(eps));
+    return __double2float_rn(__drcp_rn(__dsqrt_rn(m)));
+}
+__device__ __forceinline__ float rms_scale_row(const float* row, float eps) {
+    double s = 0.0;
+#pragma unroll 8
+    for (int i = 0; i < 64; ++i) {
+        const double v = static_cast<double>(row[i]);
+        s = __dadd_rn(s, __dmul_rn(v, v));
+    }
+    const double m = __dadd_rn(__dmul_rn(s, 1.0 / 64.0), static_cast<double>(eps));
+    return __double2float_rn(__drcp_rn(__dsqrt_rn(m)));
+}
+
+// x' = w * (x * scale): RMSNorm's two rounded products (ops.rs:19-21).
+__device__ __forceinline__ float rms_apply(float x, float scale, float w) { return __fmul_rn(w, __fmul_rn(x, scale)); }
+
 }  // namespace kvb200

@@ -70,6 +70,11 @@ struct DecodeArgs {
     const void* new_k;
     const void* new_v;
     void* pages;
+    // kv_norm_append_decode_attn: the attention layer's per-head RMSNorm of q
+    // and of the new k before RoPE ([64] weights each; null: none).
+    const float* q_norm;
+    const float* k_norm;
+    float eps;
 };
 
 __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity,
@@ -103,20 +108,39 @@ __device__ __forceinline__ float2 load_pair(const float* p) {
     return __ldg(reinterpret_cast<const float2*>(p));
 }
 
+// With a.q_norm, each head row is first RMS-normalised (lfm2.rs:797-804):
+// lanes 0..G-1 work out the scales of the G heads, one row each.
 template <typename T, int G>
 __device__ __forceinline__ void load_q(const DecodeArgs& a, int s, int nq, int h, int qd, int pos,
-                                       float2 (&q2)[G][8]) {
+                                       float2 (&q2)[G][8], int lane) {
     const float4* cs = reinterpret_cast<const float4*>(a.rope + static_cast<size_t>(pos) * (kHeadDim / 2) +
                                                        ((16 * qd) & 31));
     const float sgn = qd < 2 ? -1.f : 1.f;
+    const T* rows = static_cast<const T*>(a.q) + (static_cast<size_t>(s) * nq + h * G) * kHeadDim;
+    float sc[G];
+    if (a.q_norm != nullptr) {
+        const float mine = lane < G ? rms_scale_row(rows + (lane < G ? lane : 0) * kHeadDim, a.eps) : 0.f;
+#pragma unroll
+        for (int g = 0; g < G; ++g) sc[g] = __shfl_sync(~0u, mine, g);
+    }
+    const int dx = 16 * qd, dy = (16 * qd + 32) & 63;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
         const float4 c = __ldg(cs + i);  // (cos, sin) of dims 16qd+2i and 16qd+2i+1
+        float2 wx = make_float2(1.f, 1.f), wy = make_float2(1.f, 1.f);
+        if (a.q_norm != nullptr) {
+            wx = __ldg(reinterpret_cast<const float2*>(a.q_norm + dx + 2 * i));
+            wy = __ldg(reinterpret_cast<const float2*>(a.q_norm + dy + 2 * i));
+        }
 #pragma unroll
         for (int g = 0; g < G; ++g) {
-            const T* row = static_cast<const T*>(a.q) + (static_cast<size_t>(s) * nq + h * G + g) * kHeadDim;
-            const float2 x = load_pair(row + 16 * qd + 2 * i);
-            const float2 y = load_pair(row + ((16 * qd + 32) & 63) + 2 * i);
+            const T* row = rows + g * kHeadDim;
+            float2 x = load_pair(row + dx + 2 * i);
+            float2 y = load_pair(row + dy + 2 * i);
+            if (a.q_norm != nullptr) {
+                x = make_float2(rms_apply(x.x, sc[g], wx.x), rms_apply(x.y, sc[g], wx.y));
+                y = make_float2(rms_apply(y.x, sc[g], wy.x), rms_apply(y.y, sc[g], wy.y));
+            }
             const float r0 = __fadd_rn(__fmul_rn(x.x, c.x), __fmul_rn(sgn * y.x, c.y));
             const float r1 = __fadd_rn(__fmul_rn(x.y, c.z), __fmul_rn(sgn * y.y, c.w));
             q2[g][i] = make_float2(r0 * a.qscale, r1 * a.qscale);
@@ -245,10 +269,13 @@ __device__ __forceinline__ void stage_patch_inputs(uint8_t* dst, const T* ks, co
 // page loop.
 template <typename T, int NKV>
 __device__ __noinline__ void patch_new_token(uint8_t* buf, uint8_t* gpage, const uint8_t* in, int h, int j,
-                                             int lane) {
+                                             int lane, const float* k_norm, float eps) {
     constexpr int kE = static_cast<int>(sizeof(T));
     cp_async_wait<0>();
     __syncwarp();
+    // With k_norm, the row is first RMS-normalised (lfm2.rs:805-812).
+    float sc = 0.f;
+    if (k_norm != nullptr) sc = __shfl_sync(~0u, lane == 0 ? rms_scale_row(reinterpret_cast<const T*>(in), eps) : 0.f, 0);
     const int i = lane & 15;
     if (lane < 16) {
         const int kr = h * kPageTokens + j;
@@ -259,6 +286,12 @@ __device__ __noinline__ void patch_new_token(uint8_t* buf, uint8_t* gpage, const
         } else {
             x = *reinterpret_cast<const float2*>(in + 8 * i);
             y = *reinterpret_cast<const float2*>(in + 128 + 8 * i);
+        }
+        if (k_norm != nullptr) {
+            const float2 wx = __ldg(reinterpret_cast<const float2*>(k_norm + 2 * i));
+            const float2 wy = __ldg(reinterpret_cast<const float2*>(k_norm + 32 + 2 * i));
+            x = make_float2(rms_apply(x.x, sc, wx.x), rms_apply(x.y, sc, wx.y));
+            y = make_float2(rms_apply(y.x, sc, wy.x), rms_apply(y.y, sc, wy.y));
         }
         const float4 c = *reinterpret_cast<const float4*>(in + 2 * kHeadDim * kE + 16 * i);
         const float x0 = __fadd_rn(__fmul_rn(x.x, c.x), __fmul_rn(-y.x, c.y));
@@ -576,7 +609,7 @@ decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeArgs a) {
                                   static_cast<const T*>(a.new_v) + src,
                                   a.rope + static_cast<size_t>(pos) * (kHeadDim / 2), lane);
         }
-        load_q<T, G>(a, s, NQ, h, qd, pos, q2);
+        load_q<T, G>(a, s, NQ, h, qd, pos, q2, lane);
 #pragma unroll
         for (int gg = 0; gg < G; ++gg) {
             o2[gg][0] = o2[gg][1] = make_float2(0.f, 0.f);
@@ -603,7 +636,7 @@ decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeArgs a) {
                                           : kPageNone;
                 if (page < a.n_pages)
                     patch_new_token<T, NKV>(buf, static_cast<uint8_t*>(a.pages) + static_cast<size_t>(page) * Geo::kPageBytes,
-                                            my_patch_in, h, pos % kPageTokens, lane);
+                                            my_patch_in, h, pos % kPageTokens, lane, a.k_norm, a.eps);
             }
             const int t0 = max(lo - pg * kPageTokens, 0);
             const int t1 = min(nt - pg * kPageTokens, kPageTokens);
@@ -903,10 +936,12 @@ size_t decode_counter_count(const kv_pool* pool) {
 
 int launch_decode(kv_pool* pool, const void* q, const uint32_t* bt, int32_t bt_stride,
                   const int32_t* seq_lens, int32_t n_seqs, int32_t window, void* out,
-                  cudaStream_t stream, const void* new_k, const void* new_v) {
+                  cudaStream_t stream, const void* new_k, const void* new_v, const float* q_norm,
+                  const float* k_norm, float eps) {
     const auto& c = pool->cfg;
     if (c.dtype == KV_DTYPE_BF16)
-        return launch_decode_tc(pool, q, bt, bt_stride, seq_lens, n_seqs, window, out, stream, new_k, new_v);
+        return launch_decode_tc(pool, q, bt, bt_stride, seq_lens, n_seqs, window, out, stream, new_k, new_v, q_norm,
+                                k_norm, eps);
     const DecodeVariant* v = find_variant(c.dtype, c.n_kv_heads, c.n_q_heads / c.n_kv_heads);
     if (!v) return KV_ERR_UNSUPPORTED;
     DecodeArgs a;
@@ -928,6 +963,9 @@ int launch_decode(kv_pool* pool, const void* q, const uint32_t* bt, int32_t bt_s
     a.new_k = new_k;
     a.new_v = new_v;
     a.pages = pool->pages;
+    a.q_norm = q_norm;
+    a.k_norm = k_norm;
+    a.eps = eps;
     void* args[] = {&pool->page_map, &a};
     const cudaError_t e = cudaLaunchKernel(v->fn, dim3(pool->decode_grid), dim3(v->threads), args,
                                            pool->decode_smem, stream);
@@ -976,6 +1014,9 @@ int launch_decode_raw(const DecodeRaw& r, cudaStream_t stream) {
     a.new_k = nullptr;
     a.new_v = nullptr;
     a.pages = nullptr;
+    a.q_norm = nullptr;
+    a.k_norm = nullptr;
+    a.eps = 0.f;
     CUtensorMap map = *r.map;
     void* args[] = {&map, &a};
     const cudaError_t e = cudaLaunchKernel(v->fn, dim3(r.grid), dim3(v->threads), args, r.smem, stream);

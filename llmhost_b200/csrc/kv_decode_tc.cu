@@ -90,6 +90,9 @@ struct TcArgs {
     const __nv_bfloat16* new_k;  // fused append (null: none)
     const __nv_bfloat16* new_v;
     uint8_t* pages;
+    const float* q_norm;  // per-head RMSNorm weights of q and the new k (null: none)
+    const float* k_norm;
+    float eps;
 };
 
 template <int NKV, int G>
@@ -105,7 +108,8 @@ struct TcShape {
     static constexpr int kStgBytes = NKV * 256 + 256;               // per head K row, V row; RoPE row
     static constexpr int kOffQstg = kOffStg + kStgBytes;            // next segment's q rows and RoPE row
     static constexpr int kQstgBytes = NQ * 128 + 256;
-    static constexpr int kOffMax = kOffQstg + kQstgBytes;           // float [2][4 warps][2 units][4]
+    static constexpr int kOffQsc = kOffQstg + kQstgBytes;           // float [NQ]: q RMSNorm scales
+    static constexpr int kOffMax = kOffQsc + ((NQ * 4 + 15) & ~15); // float [2][4 warps][2 units][4]
     static constexpr int kOffM = kOffMax + 2 * 4 * 8 * 4;           // float [2 buffers][NQ]: reference maxima
     static constexpr int kOffL = kOffM + 2 * NQ * 4;                // float [2 buffers][4 warps][NQ]: row sums
     static constexpr int kOffOb = kOffL + 2 * 4 * NQ * 4;           // float [64][4]
@@ -446,13 +450,26 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(const __grid_con
                         uint8_t* gpage = a.pages + static_cast<size_t>(page) * a.page_rows * 128;
                         const float4 c = *reinterpret_cast<const float4*>(stg + NKV * 256 + 16 * (lane & 15));
                         const int ii = lane & 15;
+                        // With k_norm, each head row is RMS-normalised first
+                        // (lfm2.rs:805-812): lane hh works out head hh's scale.
+                        float scl = 0.f;
+                        if (a.k_norm != nullptr && lane < (NKV >= 2 ? 2 : 1))
+                            scl = rms_scale_row(reinterpret_cast<const __nv_bfloat16*>(stg + (NKV >= 2 ? 2 * p + lane : 0) * 256),
+                                                a.eps);
 #pragma unroll
                         for (int hh = 0; hh < (NKV >= 2 ? 2 : 1); ++hh) {
                             const int h = NKV >= 2 ? 2 * p + hh : 0;
                             const uint8_t* in = stg + h * 256;
+                            const float sc = __shfl_sync(kAll, scl, hh);
                             if (lane < 16) {
-                                const float2 x = bf16x2_to_float2(*reinterpret_cast<const uint32_t*>(in + 4 * ii));
-                                const float2 y = bf16x2_to_float2(*reinterpret_cast<const uint32_t*>(in + 64 + 4 * ii));
+                                float2 x = bf16x2_to_float2(*reinterpret_cast<const uint32_t*>(in + 4 * ii));
+                                float2 y = bf16x2_to_float2(*reinterpret_cast<const uint32_t*>(in + 64 + 4 * ii));
+                                if (a.k_norm != nullptr) {
+                                    const float2 wx = __ldg(reinterpret_cast<const float2*>(a.k_norm + 2 * ii));
+                                    const float2 wy = __ldg(reinterpret_cast<const float2*>(a.k_norm + 32 + 2 * ii));
+                                    x = make_float2(rms_apply(x.x, sc, wx.x), rms_apply(x.y, sc, wx.y));
+                                    y = make_float2(rms_apply(y.x, sc, wy.x), rms_apply(y.y, sc, wy.y));
+                                }
                                 const float x0 = __fadd_rn(__fmul_rn(x.x, c.x), __fmul_rn(-y.x, c.y));
                                 const float x1 = __fadd_rn(__fmul_rn(x.y, c.z), __fmul_rn(-y.y, c.w));
                                 const float y0 = __fadd_rn(__fmul_rn(y.x, c.x), __fmul_rn(x.x, c.y));
@@ -602,15 +619,28 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(const __grid_con
             if (q.nt - 1 >= a.max_pos && t == 0) flag_error(a.err, kDevErrBadPos);
             cp_async_wait<0>();
             named_bar_sync(kSoftBar, kSoftThreads);  // every thread's pieces have landed
+            float* qsc = reinterpret_cast<float*>(base + Sh::kOffQsc);
+            const bool norm = a.q_norm != nullptr;
+            if (norm) {  // RMSNorm scale of each q head (lfm2.rs:797-804), one thread per row
+                if (t < NQ) qsc[t] = rms_scale_row(reinterpret_cast<const __nv_bfloat16*>(qstg + t * 128), a.eps);
+                named_bar_sync(kSoftBar, kSoftThreads);
+            }
             if (t < NQ * 4) {
                 const int h = t / (G * 4), n_ = (t >> 2) % G, c = t & 3;
                 const uint8_t* row_in = qstg + (h * G + n_) * 128;
                 const float2* cs = reinterpret_cast<const float2*>(qstg + NQ * 128) + 8 * c;
+                const float sc = norm ? qsc[h * G + n_] : 1.f;
                 uint32_t lo[4], hi[4];
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
-                    const float2 x = bf16x2_to_float2(*reinterpret_cast<const uint32_t*>(row_in + 16 * c + 4 * e));
-                    const float2 y = bf16x2_to_float2(*reinterpret_cast<const uint32_t*>(row_in + 64 + 16 * c + 4 * e));
+                    float2 x = bf16x2_to_float2(*reinterpret_cast<const uint32_t*>(row_in + 16 * c + 4 * e));
+                    float2 y = bf16x2_to_float2(*reinterpret_cast<const uint32_t*>(row_in + 64 + 16 * c + 4 * e));
+                    if (norm) {
+                        const float2 wx = __ldg(reinterpret_cast<const float2*>(a.q_norm + 8 * c + 2 * e));
+                        const float2 wy = __ldg(reinterpret_cast<const float2*>(a.q_norm + 32 + 8 * c + 2 * e));
+                        x = make_float2(rms_apply(x.x, sc, wx.x), rms_apply(x.y, sc, wx.y));
+                        y = make_float2(rms_apply(y.x, sc, wy.x), rms_apply(y.y, sc, wy.y));
+                    }
                     const float2 c0 = cs[2 * e], c1 = cs[2 * e + 1];
                     const float a0 = __fadd_rn(__fmul_rn(x.x, c0.x), __fmul_rn(-y.x, c0.y)) * a.qscale;
                     const float a1 = __fadd_rn(__fmul_rn(x.y, c1.x), __fmul_rn(-y.y, c1.y)) * a.qscale;
@@ -1054,7 +1084,7 @@ int decode_tc_setup(kv_pool* pool) {
 
 int launch_decode_tc(kv_pool* pool, const void* q, const uint32_t* bt, int32_t bt_stride, const int32_t* seq_lens,
                      int32_t n_seqs, int32_t window, void* out, cudaStream_t stream, const void* new_k,
-                     const void* new_v) {
+                     const void* new_v, const float* q_norm, const float* k_norm, float eps) {
     const auto& c = pool->cfg;
     const TcVariant* v = find_tc_variant(c.n_kv_heads, c.n_q_heads / c.n_kv_heads);
     if (!v) return KV_ERR_UNSUPPORTED;
@@ -1079,6 +1109,9 @@ int launch_decode_tc(kv_pool* pool, const void* q, const uint32_t* bt, int32_t b
     a.new_k = static_cast<const __nv_bfloat16*>(new_k);
     a.new_v = static_cast<const __nv_bfloat16*>(new_v);
     a.pages = static_cast<uint8_t*>(pool->pages);
+    a.q_norm = q_norm;
+    a.k_norm = k_norm;
+    a.eps = eps;
     void* args[] = {&pool->head_map, &a};
     const cudaError_t e =
         cudaLaunchKernel(v->fn, dim3(pool->decode_grid), dim3(kThreads), args, pool->decode_smem, stream);

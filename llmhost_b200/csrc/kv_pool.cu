@@ -320,6 +320,20 @@ int kv_append_decode_attn(kv_pool* pool, const void* k, const void* v, const voi
                                  static_cast<cudaStream_t>(stream), k, v);
 }
 
+int kv_norm_append_decode_attn(kv_pool* pool, const void* k, const void* v, const void* q, const float* q_norm,
+                               const float* k_norm, float eps, const uint32_t* block_tables, int32_t bt_stride,
+                               const int32_t* seq_lens, int32_t n_seqs, int32_t window, void* out, void* stream) {
+    if (!pool || n_seqs < 0 || window < 0 || !(eps >= 0.f)) return KV_ERR_INVALID;
+    if (n_seqs == 0) return KV_OK;
+    if (n_seqs > pool->cfg.max_seqs) return KV_ERR_INVALID;
+    if (!k || !v || !q || !q_norm || !k_norm || !block_tables || !seq_lens || !out || bt_stride <= 0 ||
+        !aligned16(k) || !aligned16(v) || !aligned16(q) || !aligned16(q_norm) || !aligned16(k_norm))
+        return KV_ERR_INVALID;
+    DeviceScope dev(pool->cfg.device);
+    return kvb200::launch_decode(pool, q, block_tables, bt_stride, seq_lens, n_seqs, window, out,
+                                 static_cast<cudaStream_t>(stream), k, v, q_norm, k_norm, eps);
+}
+
 int kv_prefill_attn(kv_pool* pool, const void* q, const int32_t* q_pos, const int32_t* q_offsets,
                     const int32_t* prefix_lens, const uint64_t* tree_masks, const uint32_t* block_tables,
                     int32_t bt_stride, int32_t n_seqs, int32_t max_q_per_seq, void* out, void* stream) {

@@ -44,16 +44,19 @@ size_t decode_workspace_slots(const kv_pool* pool);
 size_t decode_counter_count(const kv_pool* pool);
 // new_k / new_v non-null: append each sequence's new token first (fused
 // kv_append_decode; the last page of every sequence must be its own).
+// q_norm / k_norm non-null: RMS-normalise each q head and the new k heads
+// first (kv_norm_append_decode_attn).
 int launch_decode(kv_pool* pool, const void* q, const uint32_t* bt, int32_t bt_stride,
                   const int32_t* seq_lens, int32_t n_seqs, int32_t window, void* out,
-                  cudaStream_t stream, const void* new_k = nullptr, const void* new_v = nullptr);
+                  cudaStream_t stream, const void* new_k = nullptr, const void* new_v = nullptr,
+                  const float* q_norm = nullptr, const float* k_norm = nullptr, float eps = 0.f);
 
 // Decode attention on tcgen05 for bf16 pools (kv_decode_tc.cu); decode_setup
 // and launch_decode route bf16 pools here.
 int decode_tc_setup(kv_pool* pool);
 int launch_decode_tc(kv_pool* pool, const void* q, const uint32_t* bt, int32_t bt_stride, const int32_t* seq_lens,
                      int32_t n_seqs, int32_t window, void* out, cudaStream_t stream, const void* new_k,
-                     const void* new_v);
+                     const void* new_v, const float* q_norm, const float* k_norm, float eps);
 
 // Prefill / tree-verify attention: tcgen05 for bf16 pools (kv_prefill.cu).
 int prefill_setup(kv_pool* pool);

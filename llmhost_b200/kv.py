@@ -199,6 +199,27 @@ class KvPool:
               "kv_append_decode_attn")
         return out
 
+    def norm_append_decode_attn(self, k, v, q, q_norm, k_norm, eps: float, block_tables, seq_lens,
+                                window: int = 0, out=None, stream=None):
+        """append_decode_attn with the per-head RMSNorm of q and k before RoPE
+        (kv_norm_append_decode_attn); q_norm, k_norm: fp32 [head_dim] device
+        tensors.  Returns `out`."""
+        dt = self.shape.torch_dtype
+        for t, name in ((k, "k"), (v, "v"), (q, "q")):
+            self._check_tensor(t, name, dt)
+        self._check_tensor(q_norm, "q_norm", torch.float32)
+        self._check_tensor(k_norm, "k_norm", torch.float32)
+        self._check_tensor(block_tables, "block_tables", torch.int32)
+        self._check_tensor(seq_lens, "seq_lens", torch.int32)
+        if out is None:
+            out = torch.empty_like(q)
+        self._check_tensor(out, "out", dt)
+        check(self._lib.kv_norm_append_decode_attn(self._h, _ptr(k), _ptr(v), _ptr(q), _ptr(q_norm), _ptr(k_norm),
+                                                   float(eps), _ptr(block_tables), block_tables.shape[-1],
+                                                   _ptr(seq_lens), seq_lens.numel(), int(window), _ptr(out),
+                                                   _stream_ptr(stream)), "kv_norm_append_decode_attn")
+        return out
+
     def prefill_attn(self, q, q_pos, q_offsets, prefix_lens, block_tables, tree_masks=None,
                      max_q: int | None = None, out=None, stream=None):
         """Chunked-prefill / tree-verify attention (kv_prefill_attn); returns `out`.

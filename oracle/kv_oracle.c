@@ -212,14 +212,35 @@ static inline void store_elem(void *base, int dtype, size_t i, float x) {
         ((float *)base)[i] = x;
 }
 
-void orc_paged_append_token(void *pages, int dtype, size_t n_kv, size_t P, size_t d,
-                            const uint32_t *bt, size_t slot, const void *k_raw,
-                            const void *v, const float *cos_row, const float *sin_row) {
+/* ops.rs:8-23
+ *   let inv_dim = 1.0 / dim as f64;
+ *   for row: let mut sumsq = 0.0f64; for &v in row { sumsq += f64::from(v) * f64::from(v); }
+ *            let scale = ((sumsq * inv_dim + f64::from(eps)).sqrt().recip()) as f32;
+ *            *d = w * (v * scale); */
+void orc_rms_norm(const float *x, const float *weight, float eps, size_t dim, size_t rows, float *out) {
+    double inv_dim = 1.0 / (double)dim;
+    for (size_t r = 0; r < rows; r++) {
+        const float *row = x + r * dim;
+        double sumsq = 0.0;
+        for (size_t i = 0; i < dim; i++) sumsq += (double)row[i] * (double)row[i];
+        float scale = (float)(1.0 / sqrt(sumsq * inv_dim + (double)eps));
+        for (size_t i = 0; i < dim; i++) {
+            float t = row[i] * scale;
+            out[r * dim + i] = weight[i] * t;
+        }
+    }
+}
+
+/* k_norm non-NULL: lfm2.rs:805-812 rms_norm_heads on k (heads = n_kv) first. */
+static void append_token_impl(void *pages, int dtype, size_t n_kv, size_t P, size_t d, const uint32_t *bt,
+                              size_t slot, const void *k_raw, const void *v, const float *cos_row,
+                              const float *sin_row, const float *k_norm, float eps) {
     size_t page_elems = 2 * n_kv * P * d;
     uint32_t page = bt[slot / P];
     size_t j = slot % P;
     float *kr = (float *)malloc(n_kv * d * sizeof(float));
     for (size_t i = 0; i < n_kv * d; i++) kr[i] = load_elem(k_raw, dtype, i);
+    if (k_norm) orc_rms_norm(kr, k_norm, eps, d, n_kv, kr);
     /* lfm2.rs:816-825: RoPE on k (heads = n_kv, tokens = 1) before the store
      * at lfm2.rs:828-832. */
     orc_apply_rope_in_place(kr, cos_row, sin_row, n_kv, 1, d);
@@ -232,6 +253,12 @@ void orc_paged_append_token(void *pages, int dtype, size_t n_kv, size_t P, size_
         }
     }
     free(kr);
+}
+
+void orc_paged_append_token(void *pages, int dtype, size_t n_kv, size_t P, size_t d,
+                            const uint32_t *bt, size_t slot, const void *k_raw,
+                            const void *v, const float *cos_row, const float *sin_row) {
+    append_token_impl(pages, dtype, n_kv, P, d, bt, slot, k_raw, v, cos_row, sin_row, NULL, 0.f);
 }
 
 void orc_paged_gather(const void *pages, int dtype, size_t n_kv, size_t P, size_t d,
@@ -258,9 +285,10 @@ void orc_paged_gather(const void *pages, int dtype, size_t n_kv, size_t P, size_
     }
 }
 
-void orc_paged_decode(const void *pages, int dtype, size_t n_q, size_t n_kv, size_t P,
-                      size_t d, const uint32_t *bt, size_t seq_len, size_t window,
-                      const void *q_raw, const float *inv_freq, float *out) {
+/* q_norm non-NULL: lfm2.rs:797-804 rms_norm_heads on q (heads = n_q) first. */
+static void paged_decode_impl(const void *pages, int dtype, size_t n_q, size_t n_kv, size_t P, size_t d,
+                              const uint32_t *bt, size_t seq_len, size_t window, const void *q_raw,
+                              const float *inv_freq, float *out, const float *q_norm, float eps) {
     if (seq_len == 0) { /* build-defined: an empty sequence attends to nothing */
         memset(out, 0, n_q * d * sizeof(float));
         return;
@@ -273,6 +301,7 @@ void orc_paged_decode(const void *pages, int dtype, size_t n_q, size_t n_kv, siz
     uint8_t *valid = NULL;
     orc_paged_gather(pages, dtype, n_kv, P, d, bt, seq_len, k, v);
     for (size_t i = 0; i < n_q * d; i++) q[i] = load_elem(q_raw, dtype, i);
+    if (q_norm) orc_rms_norm(q, q_norm, eps, d, n_q, q);
     /* lfm2.rs:816-822: cos_sin at pos, RoPE on q with heads = n_q, tokens = 1 */
     orc_cos_sin(inv_freq, seq_len - 1, 1, d, cs, cs + d);
     orc_apply_rope_in_place(q, cs, cs + d, n_q, 1, d);
@@ -290,6 +319,12 @@ void orc_paged_decode(const void *pages, int dtype, size_t n_q, size_t n_kv, siz
     free(k);
 }
 
+void orc_paged_decode(const void *pages, int dtype, size_t n_q, size_t n_kv, size_t P,
+                      size_t d, const uint32_t *bt, size_t seq_len, size_t window,
+                      const void *q_raw, const float *inv_freq, float *out) {
+    paged_decode_impl(pages, dtype, n_q, n_kv, P, d, bt, seq_len, window, q_raw, inv_freq, out, NULL, 0.f);
+}
+
 /* One sequence of orc_decode_step. */
 typedef struct {
     void *pages;
@@ -301,6 +336,8 @@ typedef struct {
     const float *inv_freq;
     float *out;
     atomic_long next;
+    const float *q_norm, *k_norm;  /* NULL: no RMSNorm */
+    float eps;
 } step_job;
 
 static void step_one(step_job *j, size_t s) {
@@ -310,13 +347,13 @@ static void step_one(step_job *j, size_t s) {
     if (len > 0) {
         float cs[2 * 256];
         orc_cos_sin(j->inv_freq, len - 1, 1, j->d, cs, cs + j->d);
-        orc_paged_append_token(j->pages, j->dtype, j->n_kv, j->P, j->d, row, len - 1,
-                               (const char *)j->k_raw + s * j->n_kv * j->d * esz,
-                               (const char *)j->v + s * j->n_kv * j->d * esz, cs, cs + j->d);
+        append_token_impl(j->pages, j->dtype, j->n_kv, j->P, j->d, row, len - 1,
+                          (const char *)j->k_raw + s * j->n_kv * j->d * esz,
+                          (const char *)j->v + s * j->n_kv * j->d * esz, cs, cs + j->d, j->k_norm, j->eps);
     }
-    orc_paged_decode(j->pages, j->dtype, j->n_q, j->n_kv, j->P, j->d, row, len, j->window,
-                     (const char *)j->q_raw + s * j->n_q * j->d * esz, j->inv_freq,
-                     j->out + s * j->n_q * j->d);
+    paged_decode_impl(j->pages, j->dtype, j->n_q, j->n_kv, j->P, j->d, row, len, j->window,
+                      (const char *)j->q_raw + s * j->n_q * j->d * esz, j->inv_freq,
+                      j->out + s * j->n_q * j->d, j->q_norm, j->eps);
 }
 
 static void *step_worker(void *arg) {
@@ -329,20 +366,37 @@ static void *step_worker(void *arg) {
     return NULL;
 }
 
+static void run_steps(step_job *j, int n_threads);
+
 void orc_decode_step(void *pages, int dtype, size_t n_q, size_t n_kv, size_t P, size_t d,
                      const uint32_t *bt, size_t bt_stride, const int32_t *seq_lens,
                      size_t n_seqs, size_t window, const void *q_raw, const void *k_raw,
                      const void *v, const float *inv_freq, float *out, int n_threads) {
     step_job j = {pages, dtype, n_q, n_kv, P, d, bt_stride, n_seqs, window, bt, seq_lens,
-                  q_raw, k_raw, v, inv_freq, out, 0};
+                  q_raw, k_raw, v, inv_freq, out, 0, NULL, NULL, 0.f};
+    run_steps(&j, n_threads);
+}
+
+void orc_decode_step_norm(void *pages, int dtype, size_t n_q, size_t n_kv, size_t P, size_t d,
+                          const uint32_t *bt, size_t bt_stride, const int32_t *seq_lens,
+                          size_t n_seqs, size_t window, const void *q_raw, const void *k_raw,
+                          const void *v, const float *inv_freq, const float *q_norm,
+                          const float *k_norm, float eps, float *out, int n_threads) {
+    step_job j = {pages, dtype, n_q, n_kv, P, d, bt_stride, n_seqs, window, bt, seq_lens,
+                  q_raw, k_raw, v, inv_freq, out, 0, q_norm, k_norm, eps};
+    run_steps(&j, n_threads);
+}
+
+static void run_steps(step_job *j, int n_threads) {
+    size_t n_seqs = j->n_seqs;
     int nt = n_threads > 0 ? n_threads : orc_max_threads();
     if (nt > (int)n_seqs) nt = (int)n_seqs;
     if (nt <= 1) {
-        for (size_t s = 0; s < n_seqs; s++) step_one(&j, s);
+        for (size_t s = 0; s < n_seqs; s++) step_one(j, s);
         return;
     }
     pthread_t *th = (pthread_t *)malloc((size_t)nt * sizeof(pthread_t));
-    for (int i = 0; i < nt; i++) pthread_create(&th[i], NULL, step_worker, &j);
+    for (int i = 0; i < nt; i++) pthread_create(&th[i], NULL, step_worker, j);
     for (int i = 0; i < nt; i++) pthread_join(th[i], NULL);
     free(th);
 }

@@ -110,6 +110,19 @@ void orc_decode_step(void *pages, int dtype, size_t n_q, size_t n_kv, size_t P, 
 /* Threads orc_decode_step uses with n_threads = 0 (online CPUs). */
 int orc_max_threads(void);
 
+/* RMSNorm over rows of `dim` values (crates/llm-cpu/src/ops.rs:8-23): the sum
+ * of squares in double, scale = (float)(1 / sqrt(sumsq / dim + eps)),
+ * out = w * (x * scale) as two float products.  out may alias x. */
+void orc_rms_norm(const float *x, const float *weight, float eps, size_t dim, size_t rows, float *out);
+
+/* orc_decode_step with the attention layer's per-head RMSNorm of q and k
+ * before RoPE (lfm2.rs:797-812): q_norm, k_norm are [d] weights. */
+void orc_decode_step_norm(void *pages, int dtype, size_t n_q, size_t n_kv, size_t P, size_t d,
+                          const uint32_t *bt, size_t bt_stride, const int32_t *seq_lens,
+                          size_t n_seqs, size_t window, const void *q_raw, const void *k_raw,
+                          const void *v, const float *inv_freq, const float *q_norm,
+                          const float *k_norm, float eps, float *out, int n_threads);
+
 #ifdef __cplusplus
 }
 #endif

@@ -62,6 +62,10 @@ def lib() -> ctypes.CDLL:
         h.orc_decode_step.argtypes = [c_void_p, c_int, c_size_t, c_size_t, c_size_t, c_size_t,
                                       c_void_p, c_size_t, c_void_p, c_size_t, c_size_t, c_void_p,
                                       c_void_p, c_void_p, fp, fp, c_int]
+        h.orc_decode_step_norm.argtypes = [c_void_p, c_int, c_size_t, c_size_t, c_size_t, c_size_t,
+                                           c_void_p, c_size_t, c_void_p, c_size_t, c_size_t, c_void_p,
+                                           c_void_p, c_void_p, fp, fp, fp, c_float, fp, c_int]
+        h.orc_rms_norm.argtypes = [fp, fp, c_float, c_size_t, c_size_t, fp]
         h.orc_max_threads.restype = c_int
         _lib = h
     return _lib
@@ -197,6 +201,32 @@ class HostPages:
                               q_raw.ctypes.data, k_raw.ctypes.data, v.ctypes.data, _f(self.inv),
                               _f(out), n_threads)
         return out
+
+    def decode_step_norm(self, bt2d, seq_lens, window: int, q_raw, k_raw, v, q_norm, k_norm, eps: float,
+                         n_threads: int = 0):
+        """decode_step with the per-head RMSNorm of q and k before RoPE
+        (orc_decode_step_norm, lfm2.rs:797-812)."""
+        bt2d = np.ascontiguousarray(bt2d, np.uint32)
+        seq_lens = np.ascontiguousarray(seq_lens, np.int32)
+        q_raw, k_raw, v = self._raw(q_raw), self._raw(k_raw), self._raw(v)
+        qn = np.ascontiguousarray(q_norm, np.float32)
+        kn = np.ascontiguousarray(k_norm, np.float32)
+        n = len(seq_lens)
+        out = np.empty((n, self.n_q, self.d), np.float32)
+        lib().orc_decode_step_norm(self.data.ctypes.data, self.dtype, self.n_q, self.n_kv, self.P, self.d,
+                                   bt2d.ctypes.data, bt2d.shape[1], seq_lens.ctypes.data, n, window,
+                                   q_raw.ctypes.data, k_raw.ctypes.data, v.ctypes.data, _f(self.inv),
+                                   _f(qn), _f(kn), ctypes.c_float(eps), _f(out), n_threads)
+        return out
+
+
+def rms_norm(x, weight, eps: float) -> np.ndarray:
+    """RMSNorm over the last axis (orc_rms_norm, ops.rs:8-23); float32 in and out."""
+    x = np.ascontiguousarray(x, np.float32)
+    w = np.ascontiguousarray(weight, np.float32)
+    out = np.empty_like(x)
+    lib().orc_rms_norm(_f(x), _f(w), ctypes.c_float(eps), w.size, x.size // w.size, _f(out))
+    return out
 
 
 def max_threads() -> int:

@@ -63,12 +63,18 @@ class DecodeCase:
                 self.bt_attn[s, :lo // PAGE_TOKENS] = PAGE_NONE
 
     # ---- oracle -------------------------------------------------------------
-    def run_oracle(self):
+    def run_oracle(self, norm=None):
+        """norm = (q_norm, k_norm, eps): the decode step RMS-normalises q and
+        the new k before RoPE (orc_decode_step_norm)."""
         host = O.HostPages(self.n_pages, O.BF16 if self.dtype == "bf16" else O.F32, self.n_q, self.n_kv)
         for s in range(len(self.lens)):
             for t in range(int(self.lens[s])):
                 host.append_token(self.bt[s], t, t, self.k_pre[s][t], self.v_pre[s][t])
-        out = host.decode_step(self.bt_attn, self.seq_lens, self.window, self.q, self.k_new, self.v_new)
+        if norm is None:
+            out = host.decode_step(self.bt_attn, self.seq_lens, self.window, self.q, self.k_new, self.v_new)
+        else:
+            out = host.decode_step_norm(self.bt_attn, self.seq_lens, self.window, self.q, self.k_new, self.v_new,
+                                        *norm)
         return host, out
 
     # ---- CUDA library ----------------------------------------------------------
@@ -94,6 +100,20 @@ class DecodeCase:
         ts = torch.from_numpy(tok_seq).to(dev)
         tl = torch.from_numpy(tok_slot).to(dev)
         pool.append(to_torch(k, self.dtype, dev), to_torch(v, self.dtype, dev), ts, tl, tl, bt)
+
+    def decode_norm_gpu(self, pool, norm):
+        """kv_norm_append_decode_attn on the attention's block tables."""
+        import torch
+
+        dev = pool.device
+        qw, kw, eps = norm
+        out = pool.norm_append_decode_attn(
+            to_torch(self.k_new, self.dtype, dev), to_torch(self.v_new, self.dtype, dev),
+            to_torch(self.q, self.dtype, dev), torch.from_numpy(qw).to(dev), torch.from_numpy(kw).to(dev), eps,
+            torch.from_numpy(self.bt_attn.view(np.int32)).to(dev), torch.from_numpy(self.seq_lens).to(dev),
+            window=self.window)
+        torch.cuda.synchronize()
+        return out
 
     def decode_gpu(self, pool, repeat: int = 1, fused: bool = False):
         """Append the new token and attend; `fused` does both in one

@@ -301,3 +301,34 @@ def test_fused_random_batches(cuda, seed):
     case = DecodeCase("bf16", n_q, n_kv, lens, seed=200 + seed)
     out, ref = run_case(case, fused=True)
     assert_close_rows(out, ref, RTOL["bf16"], f"random batch {seed}")
+
+
+# ---- q/k RMSNorm folded in (kv_norm_append_decode_attn) ----------------------
+
+NORM_CASES = {
+    "ragged": dict(n_q=24, n_kv=8, lens=[0, 1, 17, 300, 2999], seed=41),
+    "group4": dict(n_q=32, n_kv=8, lens=[5, 700, 4097, 63], seed=42),
+    "one kv head, long": dict(n_q=4, n_kv=1, lens=[20001], seed=43),
+    "two kv heads": dict(n_q=8, n_kv=2, lens=[1, 900], seed=44),
+    "window, evicted": dict(n_q=24, n_kv=8, lens=[5000, 40, 1030], seed=45, window=1024, evict_below_window=True),
+}
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "f32"])
+@pytest.mark.parametrize("name", list(NORM_CASES))
+def test_norm_fused_decode_against_oracle(cuda, dtype, name):
+    # Stored pages hold the normalised, rotated k bit for bit (the scale's sum
+    # of squares is in double, as ops.rs:14-18); outputs within tolerance.
+    c = dict(NORM_CASES[name])
+    case = DecodeCase(dtype, c.pop("n_q"), c.pop("n_kv"), c.pop("lens"), **c)
+    rng = np.random.default_rng(7)
+    norm = (rng.uniform(0.5, 1.5, 64).astype(np.float32), rng.uniform(0.5, 1.5, 64).astype(np.float32), 1e-5)
+    host, ref = case.run_oracle(norm=norm)
+    with case.make_pool() as pool:
+        case.prefill_gpu(pool)
+        out = to_numpy_f32(case.decode_norm_gpu(pool, norm))
+        assert pool.last_error() == 0
+        ids = case.used_pages()
+        pages = pool.read_pages(ids)
+    np.testing.assert_array_equal(pages, host.data[ids], err_msg="stored pages differ from the oracle")
+    assert_close_rows(out, ref, RTOL[dtype], f"{dtype} norm-fused {name}")

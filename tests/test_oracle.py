@@ -186,3 +186,29 @@ def test_decode_step_threads_agree():
     b = host2.decode_step(bt, lens, 0, q, k, v, n_threads=4)
     np.testing.assert_array_equal(a, b)
     np.testing.assert_array_equal(host1.data, host2.data)
+
+
+def test_rms_norm_known_answer():
+    # ops.rs:108-117: x = [3, 4], unit weight, eps 0 -> x / sqrt(12.5)
+    y = O.rms_norm(np.array([3.0, 4.0], np.float32), np.array([1.0, 1.0], np.float32), 0.0)
+    rms = np.sqrt(np.float32(12.5))
+    assert abs(y[0] - 3.0 / rms) < 1e-6 and abs(y[1] - 4.0 / rms) < 1e-6
+
+
+def test_rms_norm_matches_sequential_double_restatement():
+    # The same operations in plain Python (floats are doubles, the loop is
+    # sequential like ops.rs:14-17): bit-exact.
+    import math
+
+    rng = np.random.default_rng(5)
+    x = rng.standard_normal((6, 64)).astype(np.float32) * np.float32(3.0)
+    w = rng.standard_normal(64).astype(np.float32)
+    eps = 1e-5
+    got = O.rms_norm(x, w, eps)
+    for r in range(x.shape[0]):
+        s = 0.0
+        for v in x[r]:
+            s += float(v) * float(v)
+        scale = np.float32(1.0 / math.sqrt(s * (1.0 / 64) + float(np.float32(eps))))
+        want = w * (x[r] * scale)
+        np.testing.assert_array_equal(got[r], want)
