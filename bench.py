@@ -54,6 +54,8 @@ def parse_args():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--unfused", action="store_true",
                     help="decode workloads: kv_append_decode + kv_decode_attn as two launches per layer")
+    ap.add_argument("--qk-norm", action="store_true",
+                    help="decode workload: kv_norm_append_decode_attn (the layer's q/k RMSNorm folded in)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=12.0, help="seconds of CPU-baseline work")
     ap.add_argument("--schedule", type=int, default=512, help="decode steps in the workload")
@@ -285,6 +287,10 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     stream = torch.cuda.current_stream()
 
     fused = not args.unfused
+    qk_norm = args.qk_norm and fused
+    if qk_norm:  # per-layer RMSNorm weights, as the attention layer's q_norm / k_norm
+        qn_w = [torch.empty(64, device=dev).uniform_(0.5, 1.5, generator=gen) for _ in range(L)]
+        kn_w = [torch.empty(64, device=dev).uniform_(0.5, 1.5, generator=gen) for _ in range(L)]
 
     def step(t, ev=None):
         i = t % n_sets
@@ -293,8 +299,12 @@ def run_ours(args, rank: int, world: int, local_rank: int):
             if fused:
                 if ev is not None:
                     ev[l][0].record(stream)
-                pool.append_decode_attn(k_c[i][l], v_c[i][l], q_c[i][l], bt_dev[l], lens, out=out[l],
-                                        stream=stream)
+                if qk_norm:
+                    pool.norm_append_decode_attn(k_c[i][l], v_c[i][l], q_c[i][l], qn_w[l], kn_w[l], 1e-5, bt_dev[l],
+                                                 lens, out=out[l], stream=stream)
+                else:
+                    pool.append_decode_attn(k_c[i][l], v_c[i][l], q_c[i][l], bt_dev[l], lens, out=out[l],
+                                            stream=stream)
             else:
                 pool.append_decode(k_c[i][l], v_c[i][l], bt_dev[l], lens, stream=stream)
                 if ev is not None:
@@ -361,7 +371,9 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     ratio, prof = load_traffic_ratio()
     roofline = {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
                 "traffic": (ratio * mean_attn_bytes) if ratio else None,
-                "kernel": "decode_tc_kernel (kv_append_decode_attn: append + attention, one launch per layer)"
+                "kernel": ("decode_tc_kernel (kv_norm_append_decode_attn: q/k RMSNorm + append + attention, "
+                           "one launch per layer)") if qk_norm
+                else "decode_tc_kernel (kv_append_decode_attn: append + attention, one launch per layer)"
                 if fused else "decode_tc_kernel (kv_decode_attn)",
                 "algorithmic_bytes_per_launch": mean_attn_bytes,
                 "mean_launch_us": mean_kernel_s * 1e6,

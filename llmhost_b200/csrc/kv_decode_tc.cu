@@ -397,7 +397,16 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(const __grid_con
         cur.start(a, pstart, n, gb, ge);
         Fetch fc = fetch(cur);
         int issued = 0;
-        bool issuing = true, app = false;
+        bool issuing = true, app = false, have_ksc = false;
+        float ksc = 0.f;  // lane h < NKV: RMSNorm scale of the new k of head h
+        // With k_norm: every head's scale, one lane per head, once the staged
+        // rows have landed (kept off the stage that stores them).
+        auto k_scales = [&]() {
+            cp_async_wait<0>();
+            __syncwarp();
+            if (lane < NKV) ksc = rms_scale_row(reinterpret_cast<const __nv_bfloat16*>(stg + lane * 256), a.eps);
+            have_ksc = true;
+        };
         while (!cur.done) {
             const Seg& q = cur.q;
             if (cur.j == 0) {
@@ -405,6 +414,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(const __grid_con
                 // last page) for the heads of this slice's stages of the last
                 // chunk, when its position is valid.  Its inputs are staged now.
                 if (app) cp_async_wait<0>();
+                have_ksc = false;
                 app = a.new_k != nullptr && (q.j1 - 1) / Chunk<NKV>::kStages == q.last_chunk &&
                       q.nt - 1 < a.max_pos;
                 if (app) {
@@ -424,6 +434,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(const __grid_con
                     cp_async_commit();
                 }
             }
+            if (app && a.k_norm != nullptr && !have_ksc && cur.j == 1) k_scales();
             StageCursor<NKV> nxt = cur;
             nxt.next(a, pstart);
             const Fetch fn = nxt.done ? Fetch{0u, false} : fetch(nxt);  // in flight during the wait below
@@ -451,16 +462,13 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(const __grid_con
                         const float4 c = *reinterpret_cast<const float4*>(stg + NKV * 256 + 16 * (lane & 15));
                         const int ii = lane & 15;
                         // With k_norm, each head row is RMS-normalised first
-                        // (lfm2.rs:805-812): lane hh works out head hh's scale.
-                        float scl = 0.f;
-                        if (a.k_norm != nullptr && lane < (NKV >= 2 ? 2 : 1))
-                            scl = rms_scale_row(reinterpret_cast<const __nv_bfloat16*>(stg + (NKV >= 2 ? 2 * p + lane : 0) * 256),
-                                                a.eps);
+                        // (lfm2.rs:805-812) with the scale lane h holds.
+                        if (a.k_norm != nullptr && !have_ksc) k_scales();
 #pragma unroll
                         for (int hh = 0; hh < (NKV >= 2 ? 2 : 1); ++hh) {
                             const int h = NKV >= 2 ? 2 * p + hh : 0;
                             const uint8_t* in = stg + h * 256;
-                            const float sc = __shfl_sync(kAll, scl, hh);
+                            const float sc = __shfl_sync(kAll, ksc, h);
                             if (lane < 16) {
                                 float2 x = bf16x2_to_float2(*reinterpret_cast<const uint32_t*>(in + 4 * ii));
                                 float2 y = bf16x2_to_float2(*reinterpret_cast<const uint32_t*>(in + 64 + 4 * ii));
@@ -615,16 +623,24 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(const __grid_con
         // Q tiles: item (h, n, c) rotates dims [8c, 8c+8) with [32+8c, 32+8c+8)
         // of query head h*G + n (rope.rs:76 form), scales them into log2 units
         // and stores bf16 row n of head h's 8-row group.
-        auto build_q = [&](const Seg& q) {
-            if (q.nt - 1 >= a.max_pos && t == 0) flag_error(a.err, kDevErrBadPos);
+        // With q_norm: the RMSNorm scale of each staged q row (lfm2.rs:797-804),
+        // one thread per row; worked out during the segment before when it
+        // has a second stage, where the softmax warps have slack.
+        float* qsc = reinterpret_cast<float*>(base + Sh::kOffQsc);
+        bool qsc_ready = false;
+        auto q_scales = [&]() {
             cp_async_wait<0>();
             named_bar_sync(kSoftBar, kSoftThreads);  // every thread's pieces have landed
-            float* qsc = reinterpret_cast<float*>(base + Sh::kOffQsc);
+            if (t < NQ) qsc[t] = rms_scale_row(reinterpret_cast<const __nv_bfloat16*>(qstg + t * 128), a.eps);
+            qsc_ready = true;
+        };
+        auto build_q = [&](const Seg& q) {
+            if (q.nt - 1 >= a.max_pos && t == 0) flag_error(a.err, kDevErrBadPos);
             const bool norm = a.q_norm != nullptr;
-            if (norm) {  // RMSNorm scale of each q head (lfm2.rs:797-804), one thread per row
-                if (t < NQ) qsc[t] = rms_scale_row(reinterpret_cast<const __nv_bfloat16*>(qstg + t * 128), a.eps);
-                named_bar_sync(kSoftBar, kSoftThreads);
-            }
+            if (norm && !qsc_ready) q_scales();
+            cp_async_wait<0>();
+            named_bar_sync(kSoftBar, kSoftThreads);  // the staged rows (and scales) are visible
+            qsc_ready = false;
             if (t < NQ * 4) {
                 const int h = t / (G * 4), n_ = (t >> 2) % G, c = t & 3;
                 const uint8_t* row_in = qstg + (h * G + n_) * 128;
@@ -810,6 +826,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(const __grid_con
                     tc_fence_before();
                     mbar_arrive(&p_full[sb]);
                     ++i;
+                    if (a.q_norm != nullptr && more && j == 1) q_scales();  // the next segment's
                 }
             }
             // ---- segment done: Q of the next segment first (every S of this
