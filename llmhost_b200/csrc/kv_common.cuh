@@ -156,9 +156,10 @@ __device__ __forceinline__ uint32_t swz128(uint32_t lin) {
 // the sum of squares in double, in dimension order, as separate rounded
 // products and sums (Rust does not contract), then
 // (float)(1 / sqrt(sumsq / 64 + eps)) with IEEE square root and reciprocal.
-__device__ __forceinline__ float rms_scale_row(const __nv_bfloat16* row, float eps) {
+// Out of line: called once per row, it must not grow the kernels' hot code.
+static __device__ __noinline__ float rms_scale_row(const __nv_bfloat16* row, float eps) {
     double s = 0.0;
-#pragma unroll 8
+#pragma unroll 4
     for (int i = 0; i < 64; ++i) {
         const double v = static_cast<double>(__bfloat162float(row[i]));
         s = __dadd_rn(s, __dmul_rn(v, v));
@@ -166,9 +167,9 @@ __device__ __forceinline__ float rms_scale_row(const __nv_bfloat16* row, float e
     const double m = __dadd_rn(__dmul_rn(s, 1.0 / 64.0), static_cast<double>(eps));
     return __double2float_rn(__drcp_rn(__dsqrt_rn(m)));
 }
-__device__ __forceinline__ float rms_scale_row(const float* row, float eps) {
+static __device__ __noinline__ float rms_scale_row(const float* row, float eps) {
     double s = 0.0;
-#pragma unroll 8
+#pragma unroll 4
     for (int i = 0; i < 64; ++i) {
         const double v = static_cast<double>(row[i]);
         s = __dadd_rn(s, __dmul_rn(v, v));

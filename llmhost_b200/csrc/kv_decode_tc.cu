@@ -264,7 +264,9 @@ __device__ __forceinline__ void warp_reduce_scatter_store(float (&v)[N], float* 
 }
 
 
-template <int NKV, int G>
+// kNorm: the q/k RMSNorm of kv_norm_append_decode_attn is compiled in (a
+// separate instantiation, so that the plain kernel's hot loops stay as they are).
+template <int NKV, int G, bool kNorm>
 __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(const __grid_constant__ CUtensorMap hmap,
                                                                 const TcArgs a) {
     using Sh = TcShape<NKV, G>;
@@ -434,7 +436,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(const __grid_con
                     cp_async_commit();
                 }
             }
-            if (app && a.k_norm != nullptr && !have_ksc && cur.j == 1) k_scales();
+            if constexpr (kNorm)
+                if (app && !have_ksc && cur.j == 1) k_scales();
             StageCursor<NKV> nxt = cur;
             nxt.next(a, pstart);
             const Fetch fn = nxt.done ? Fetch{0u, false} : fetch(nxt);  // in flight during the wait below
@@ -463,16 +466,18 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(const __grid_con
                         const int ii = lane & 15;
                         // With k_norm, each head row is RMS-normalised first
                         // (lfm2.rs:805-812) with the scale lane h holds.
-                        if (a.k_norm != nullptr && !have_ksc) k_scales();
+                        if constexpr (kNorm)
+                            if (!have_ksc) k_scales();
 #pragma unroll
                         for (int hh = 0; hh < (NKV >= 2 ? 2 : 1); ++hh) {
                             const int h = NKV >= 2 ? 2 * p + hh : 0;
                             const uint8_t* in = stg + h * 256;
-                            const float sc = __shfl_sync(kAll, ksc, h);
+                            float sc = 1.f;
+                            if constexpr (kNorm) sc = __shfl_sync(kAll, ksc, h);
                             if (lane < 16) {
                                 float2 x = bf16x2_to_float2(*reinterpret_cast<const uint32_t*>(in + 4 * ii));
                                 float2 y = bf16x2_to_float2(*reinterpret_cast<const uint32_t*>(in + 64 + 4 * ii));
-                                if (a.k_norm != nullptr) {
+                                if constexpr (kNorm) {
                                     const float2 wx = __ldg(reinterpret_cast<const float2*>(a.k_norm + 2 * ii));
                                     const float2 wy = __ldg(reinterpret_cast<const float2*>(a.k_norm + 32 + 2 * ii));
                                     x = make_float2(rms_apply(x.x, sc, wx.x), rms_apply(x.y, sc, wx.y));
@@ -636,8 +641,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(const __grid_con
         };
         auto build_q = [&](const Seg& q) {
             if (q.nt - 1 >= a.max_pos && t == 0) flag_error(a.err, kDevErrBadPos);
-            const bool norm = a.q_norm != nullptr;
-            if (norm && !qsc_ready) q_scales();
+            constexpr bool norm = kNorm;
+            if constexpr (kNorm)
+                if (!qsc_ready) q_scales();
             cp_async_wait<0>();
             named_bar_sync(kSoftBar, kSoftThreads);  // the staged rows (and scales) are visible
             qsc_ready = false;
@@ -651,7 +657,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(const __grid_con
                 for (int e = 0; e < 4; ++e) {
                     float2 x = bf16x2_to_float2(*reinterpret_cast<const uint32_t*>(row_in + 16 * c + 4 * e));
                     float2 y = bf16x2_to_float2(*reinterpret_cast<const uint32_t*>(row_in + 64 + 16 * c + 4 * e));
-                    if (norm) {
+                    if constexpr (kNorm) {
                         const float2 wx = __ldg(reinterpret_cast<const float2*>(a.q_norm + 8 * c + 2 * e));
                         const float2 wy = __ldg(reinterpret_cast<const float2*>(a.q_norm + 32 + 8 * c + 2 * e));
                         x = make_float2(rms_apply(x.x, sc, wx.x), rms_apply(x.y, sc, wx.y));
@@ -826,7 +832,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(const __grid_con
                     tc_fence_before();
                     mbar_arrive(&p_full[sb]);
                     ++i;
-                    if (a.q_norm != nullptr && more && j == 1) q_scales();  // the next segment's
+                    if constexpr (kNorm)
+                        if (more && j == 1) q_scales();  // the next segment's
                 }
             }
             // ---- segment done: Q of the next segment first (every S of this
@@ -1060,13 +1067,15 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(const __grid_con
 // ---------------------------------------------------------------------------
 struct TcVariant {
     int nkv, group;
-    const void* fn;
+    const void* fn;       // plain
+    const void* fn_norm;  // with the q/k RMSNorm
     size_t (*smem)(int);
 };
 
 template <int NKV, int G>
 TcVariant make_tc_variant() {
-    return TcVariant{NKV, G, reinterpret_cast<const void*>(&decode_tc_kernel<NKV, G>), &TcShape<NKV, G>::smem_bytes};
+    return TcVariant{NKV, G, reinterpret_cast<const void*>(&decode_tc_kernel<NKV, G, false>),
+                     reinterpret_cast<const void*>(&decode_tc_kernel<NKV, G, true>), &TcShape<NKV, G>::smem_bytes};
 }
 
 const TcVariant* find_tc_variant(int nkv, int group) {
@@ -1090,7 +1099,8 @@ int decode_tc_setup(kv_pool* pool) {
     if (cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, c.device) != cudaSuccess)
         return KV_ERR_CUDA;
     if (smem > static_cast<size_t>(optin)) return KV_ERR_INVALID;  // max_seqs too large
-    if (raise_smem_limit(v->fn, c.device, smem) != KV_OK) return KV_ERR_CUDA;
+    if (raise_smem_limit(v->fn, c.device, smem) != KV_OK || raise_smem_limit(v->fn_norm, c.device, smem) != KV_OK)
+        return KV_ERR_CUDA;
     int per_sm = 0;
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, v->fn, kThreads, smem) != cudaSuccess || per_sm < 1)
         return KV_ERR_CUDA;
@@ -1131,7 +1141,8 @@ int launch_decode_tc(kv_pool* pool, const void* q, const uint32_t* bt, int32_t b
     a.eps = eps;
     void* args[] = {&pool->head_map, &a};
     const cudaError_t e =
-        cudaLaunchKernel(v->fn, dim3(pool->decode_grid), dim3(kThreads), args, pool->decode_smem, stream);
+        cudaLaunchKernel(q_norm != nullptr ? v->fn_norm : v->fn, dim3(pool->decode_grid), dim3(kThreads), args,
+                         pool->decode_smem, stream);
     return e == cudaSuccess ? KV_OK : KV_ERR_CUDA;
 }
 
