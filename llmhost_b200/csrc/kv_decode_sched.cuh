@@ -39,12 +39,16 @@ __device__ __forceinline__ int cta_of(int x, int grid, int total) {
 
 // Warp 0 (all lanes): start[s] = units of unit_pages pages (the last one of
 // a sequence may be partial) in sequences before s, start[n] = all units.
-// With mult > 1, each unit counts mult times (work items per unit).
+// With mult > 1, each unit counts mult times (work items per unit); a
+// sequence with pages counts lead more (a cost charged to its start).
 __device__ __forceinline__ void scan_units(const int32_t* seq_lens, int n, int window, int unit_pages, int* start,
-                                           int lane, int mult = 1) {
+                                           int lane, int mult = 1, int lead = 0) {
     const int per = (n + 31) >> 5;
     const int b = min(n, lane * per), e = min(n, b + per);
-    auto units = [&](int s) { return mult * ((seq_pages(__ldg(seq_lens + s), window) + unit_pages - 1) / unit_pages); };
+    auto units = [&](int s) {
+        const int pages = seq_pages(__ldg(seq_lens + s), window);
+        return pages > 0 ? mult * ((pages + unit_pages - 1) / unit_pages) + lead : 0;
+    };
     int local = 0;
     for (int s = b; s < e; ++s) local += units(s);
     int incl = local;

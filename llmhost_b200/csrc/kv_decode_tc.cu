@@ -131,14 +131,21 @@ struct Chunk {
     static constexpr int kStages = NKV >= 2 ? NKV / 2 : 1;
 };
 
+// Slices are cut by cost, not by stages alone: the start of a sequence in a
+// CTA (its Q tiles, a pipeline restart, a partial last chunk before it) costs
+// about as much as kLead stages, so each sequence's stage list begins with
+// kLead stages that hold no work.
+constexpr int kLead = 2;
+
 // One sequence's stages [g, min(ge, s_end)) inside this CTA's slice [gb, ge)
 // (global stage indices; s_begin / s_end are the sequence's first and end
-// stage).  j0, j1: the same range counted from the sequence's first stage;
-// c0: the chunk of stage j0; pg0, np: block-table index of chunk c0's first
+// stage, s_first = s_begin + kLead its first stage with work).  j0, j1: the
+// stages with work counted from s_first (nst = j1 - j0, possibly none); c0:
+// the chunk of stage j0; pg0, np: block-table index of chunk c0's first
 // page, and the pages from there to the end of the segment's last chunk;
 // last_chunk: the chunk holding the sequence's last page.
 struct Seg {
-    int s, nt, lo, pg0, np, s_begin, s_end, j0, j1, c0, nst, last_chunk;
+    int s, nt, lo, pg0, np, s_begin, s_first, s_end, j0, j1, c0, nst, last_chunk;
 };
 
 template <int NKV>
@@ -149,18 +156,33 @@ __device__ __forceinline__ Seg make_seg(const TcArgs& a, const int* sstart, int 
     q.nt = __ldg(a.seq_lens + s);
     q.lo = seq_lo(q.nt, a.window);
     q.s_begin = sstart[s];
+    q.s_first = q.s_begin + kLead;
     q.s_end = sstart[s + 1];
-    q.j0 = g - q.s_begin;
-    q.j1 = min(ge, q.s_end) - q.s_begin;
+    q.j0 = max(g, q.s_first) - q.s_first;
+    q.j1 = min(ge, q.s_end) - q.s_first;
+    q.nst = q.j1 - q.j0;
+    q.c0 = q.np = q.pg0 = q.last_chunk = 0;
+    if (q.nst <= 0) return q;  // only lead stages of s in this slice
     q.c0 = q.j0 / kSt;
     const int pages = seq_pages(q.nt, a.window);
     const int p0 = kCp * q.c0;
     const int p1 = min(pages, kCp * ((q.j1 - 1) / kSt + 1));
     q.np = p1 - p0;
     q.pg0 = q.lo / kPageTokens + p0;
-    q.nst = q.j1 - q.j0;
     q.last_chunk = (pages - 1) / kCp;
     return q;
+}
+
+// The first segment with work at or after stage g of the slice; g moves to
+// its start.  False if there is none.
+template <int NKV>
+__device__ __forceinline__ bool seek_seg(const TcArgs& a, const int* sstart, int n, int& g, int ge, Seg& q) {
+    while (g < ge) {
+        q = make_seg<NKV>(a, sstart, find_seq(sstart, n, g), g, ge);
+        if (q.nst > 0) return true;
+        g = min(ge, q.s_end);
+    }
+    return false;
 }
 
 // Stage jj of a segment: each unit's block (counted from chunk c0) and its
@@ -184,7 +206,7 @@ __device__ __forceinline__ void stage_units(const Seg& q, int jj, int& b0, int& 
 // Walks a CTA's stages in schedule order: stage i, stage j of segment q.
 template <int NKV>
 struct StageCursor {
-    int i, j, g, s, seg_no, ge, n;
+    int i, j, g, seg_no, ge, n;
     bool done;
     Seg q;
     __device__ __forceinline__ void start(const TcArgs& a, const int* pstart, int n_, int gb, int ge_) {
@@ -192,21 +214,14 @@ struct StageCursor {
         n = n_;
         ge = ge_;
         g = gb;
-        s = find_seq(pstart, n, gb);
-        q = make_seg<NKV>(a, pstart, s, g, ge);
-        done = false;
+        done = !seek_seg<NKV>(a, pstart, n, g, ge, q);
     }
     __device__ __forceinline__ void next(const TcArgs& a, const int* pstart) {
         ++i;
         if (++j < q.nst) return;
         j = 0;
         g = min(ge, q.s_end);
-        if (g >= ge) {
-            done = true;
-            return;
-        }
-        s = find_seq(pstart, n, g);
-        q = make_seg<NKV>(a, pstart, s, g, ge);
+        done = !seek_seg<NKV>(a, pstart, n, g, ge, q);
         ++seg_no;
     }
 };
@@ -326,7 +341,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(const __grid_con
             prefetch_tmap(&hmap);
         }
         __syncwarp();
-        scan_units(a.seq_lens, n, a.window, Chunk<NKV>::kPages, pstart, lane, Chunk<NKV>::kStages);
+        scan_units(a.seq_lens, n, a.window, Chunk<NKV>::kPages, pstart, lane, Chunk<NKV>::kStages, kLead);
         __syncwarp();
         named_bar_arrive(kSetupBar, kThreads);
     } else {
@@ -397,7 +412,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(const __grid_con
         };
         StageCursor<NKV> cur;
         cur.start(a, pstart, n, gb, ge);
-        Fetch fc = fetch(cur);
+        Fetch fc = cur.done ? Fetch{0u, false} : fetch(cur);  // a slice may hold lead stages only
         int issued = 0;
         bool issuing = true, app = false, have_ksc = false;
         float ksc = 0.f;  // lane h < NKV: RMSNorm scale of the new k of head h
@@ -682,18 +697,19 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(const __grid_con
 
         float m[NKV][G], l[NKV][G];
         int i = 0, segk = 0;
-        Seg q = make_seg<NKV>(a, pstart, find_seq(pstart, n, gb), gb, ge);
-        prefetch_q(q);
-        build_q(q);
-        for (;;) {
+        Seg q;
+        int g0 = gb;
+        const bool any = seek_seg<NKV>(a, pstart, n, g0, ge, q);
+        if (any) {
+            prefetch_q(q);
+            build_q(q);
+        }
+        for (; any;) {
             // the next segment of this slice, its q fetched while this one streams
-            const int g_next = min(ge, q.s_end);
-            const bool more = g_next < ge;
+            int g_next = min(ge, q.s_end);
             Seg nq = q;
-            if (more) {
-                nq = make_seg<NKV>(a, pstart, find_seq(pstart, n, g_next), g_next, ge);
-                prefetch_q(nq);
-            }
+            const bool more = seek_seg<NKV>(a, pstart, n, g_next, ge, nq);
+            if (more) prefetch_q(nq);
 #pragma unroll
             for (int h = 0; h < NKV; ++h)
 #pragma unroll
@@ -871,9 +887,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(const __grid_con
         const int ut = row >> 6, d = row & 63;
         const int ew = warp - kEpiWarp0;  // 0-3
         int k = 0;
-        int g = gb, s = find_seq(pstart, n, gb);
-        while (g < ge) {
-            const Seg cur = make_seg<NKV>(a, pstart, s, g, ge);
+        int g = gb;
+        Seg cur;
+        while (seek_seg<NKV>(a, pstart, n, g, ge, cur)) {
             const int eb = k & 1;
             const uint32_t ph = static_cast<uint32_t>(k >> 1) & 1u;
             const bool okE = __all_sync(kAll, wait_bar(&o_full[eb], ph, abort_flag, a.err)) &&
@@ -917,8 +933,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(const __grid_con
             }
             tc_fence_before();
             mbar_arrive(&o_free[eb]);  // O buffer eb and its sums may be reused
-            const bool whole = cur.s_begin >= gb && cur.s_end <= ge;
-            const int pslot = (cur.s_begin < gb) ? 2 * cta : 2 * cta + 1;
+            // whole: this CTA holds every stage of s with work; otherwise its
+            // partial goes to slot 2 cta + 1 if it holds the first such stage
+            const bool whole = cur.s_first >= gb && cur.s_end <= ge;
+            const int pslot = (cur.s_first < gb) ? 2 * cta : 2 * cta + 1;
             if (NKV >= 2 || ut == 0) {
 #pragma unroll
                 for (int p = 0; p < kPairs; ++p) {
@@ -939,14 +957,14 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(const __grid_con
                 }
             }
             if (!whole) {
-                // Contributors: the CTAs whose slice holds a stage of s; every
-                // CTA holds at least one stage, so they are consecutive.  CTA c
+                // Contributors: the CTAs whose slice holds a stage of s with
+                // work; those stages are consecutive, so are they.  CTA c
                 // wrote its partial to slot 2c + (c == c_first).  Up to kGroup
                 // contributors: the last to arrive merges them all.  More: the
                 // last of each run of kGroup contributors merges its run into
                 // the run's slot in the second half of the workspace, and the
                 // last run to finish merges the run partials.
-                const int c_first = cta_of(cur.s_begin, grid, total);
+                const int c_first = cta_of(cur.s_first, grid, total);
                 const int n_contrib = cta_of(cur.s_end - 1, grid, total) - c_first + 1;
                 auto slot_of = [&](int c) { return static_cast<size_t>((c == c_first) ? 2 * c + 1 : 2 * c); };
                 constexpr int kGroup = 16;
@@ -1052,7 +1070,6 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(const __grid_con
             }
             ++k;
             g = min(ge, cur.s_end);
-            if (g < ge) s = find_seq(pstart, n, g);
         }
     }
     tc_fence_before();
