@@ -121,6 +121,16 @@ __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
+// Programmatic dependent launch.  grid_dep_wait: block until the grids this
+// one depends on have completed and their memory is visible (a no-op when the
+// launch has no programmatic dependency); every global access of a kernel
+// launched with programmatic serialization comes after it.
+// grid_dep_trigger: let the next grid in the stream launch once every CTA of
+// this one has triggered or exited (its CTAs then do their set-up on SMs this
+// grid has left and wait in grid_dep_wait).
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dep_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // Named barrier over a subset of warps (id 0 is __syncthreads).
 __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");

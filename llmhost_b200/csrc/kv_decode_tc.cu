@@ -340,6 +340,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(const __grid_con
             fence_mbar_init();
             prefetch_tmap(&hmap);
         }
+        grid_dep_wait();  // the inputs are read from here on
         __syncwarp();
         scan_units(a.seq_lens, n, a.window, Chunk<NKV>::kPages, pstart, lane, Chunk<NKV>::kStages, kLead);
         __syncwarp();
@@ -358,11 +359,15 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(const __grid_con
                          : "memory");
             asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
         }
+        grid_dep_wait();
         tc_fence_before();
         named_bar_sync(kSetupBar, kThreads);
         tc_fence_after();
     }
 
+    // The grid is persistent (every CTA resident at once), so the next
+    // launch's CTAs can only take SMs this grid has left: let it launch now.
+    grid_dep_trigger();
     const int total = pstart[n];
     const int cta = blockIdx.x;
     const int grid = max(1, min(static_cast<int>(gridDim.x), total));  // at least one stage per CTA
@@ -1157,9 +1162,20 @@ int launch_decode_tc(kv_pool* pool, const void* q, const uint32_t* bt, int32_t b
     a.k_norm = k_norm;
     a.eps = eps;
     void* args[] = {&pool->head_map, &a};
-    const cudaError_t e =
-        cudaLaunchKernel(q_norm != nullptr ? v->fn_norm : v->fn, dim3(pool->decode_grid), dim3(kThreads), args,
-                         pool->decode_smem, stream);
+    // Programmatic serialization: this launch may start while the kernel
+    // before it in the stream finishes; it reads nothing before that kernel
+    // has completed (grid_dep_wait), so stream order holds for the data.
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t lc = {};
+    lc.gridDim = dim3(pool->decode_grid);
+    lc.blockDim = dim3(kThreads);
+    lc.dynamicSmemBytes = pool->decode_smem;
+    lc.stream = stream;
+    lc.attrs = attr;
+    lc.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelExC(&lc, q_norm != nullptr ? v->fn_norm : v->fn, args);
     return e == cudaSuccess ? KV_OK : KV_ERR_CUDA;
 }
 
