@@ -1027,7 +1027,8 @@ def run_spec(args, ctx):
             stats["accepted"] += acc
             stats["verified"] += ntok
             stats["cow"] += len(fb.cow_src)
-            vis = fb.prefix[fb.tok_seq] + np.array([bin(int(x)).count("1") for x in fb.masks.view(np.uint64)])
+            ones = np.unpackbits(fb.masks.view(np.uint8)).reshape(-1, 64).sum(axis=1)  # popcount per mask
+            vis = fb.prefix[fb.tok_seq] + ones
             stats["flops"].append(4.0 * 64 * wl.n_q * float(vis.sum()))
 
     for w in range(args.warmup):

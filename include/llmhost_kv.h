@@ -257,6 +257,37 @@ int kv_state_accept(kv_state *st, uint64_t seq_id, const int64_t *accepted, int3
 int kv_state_rollback(kv_state *st, uint64_t seq_id, const int64_t *rejected, int32_t n, int32_t *move_src,
                       int32_t *move_dst, int32_t move_cap, int32_t *n_moves, kv_token_move *tok_moves,
                       int32_t tok_cap, int32_t *n_tok_moves, int64_t *bad_index);
+/* kv_state_forward for a batch of sequences, in order, flattened into the
+ * arrays one kv_append and one kv_prefill_attn launch per layer take.
+ * Sequence i stages tokens[tok_off[i] .. tok_off[i+1]) (tok_off: n_seqs + 1
+ * entries, tok_off[0] = 0) with the parent array trees + tok_off[i] (trees
+ * NULL: every draft a chain).  Outputs: tok_row / slots / positions [total
+ * tokens] (batch row, storage slot, RoPE position of each token); prefix
+ * [n_seqs] (committed tokens before each draft); masks [total tokens], if not
+ * NULL, the ancestor-or-self bit masks kv_prefill_attn takes (every draft at
+ * most 64 tokens); cow_* (capacity >= n_layers * n_seqs) the page copies to
+ * run first, *n_cow of them; tables [n_layers][n_seqs][stride] the drafts'
+ * block tables padded with KV_PAGE_NONE.  Sizes are checked before any state
+ * changes; an error from sequence i (tree, OOM) returns with sequences
+ * 0 .. i-1 staged, *n_done = i and *err filled for a tree error. */
+int kv_state_forward_batch(kv_state *st, const uint64_t *seq_ids, int32_t n_seqs, const uint32_t *tokens,
+                           const int32_t *tok_off, const int32_t *trees, int32_t *tok_row, int32_t *slots,
+                           int32_t *positions, int32_t *prefix, uint64_t *masks, uint32_t *cow_src,
+                           uint32_t *cow_dst, int32_t cow_cap, int32_t *n_cow, uint32_t *tables, int32_t stride,
+                           int32_t *n_done, kv_tree_error *err);
+/* kv_state_accept for a batch: sequence i commits paths[path_off[i] ..
+ * path_off[i+1]).  tok_moves (capacity tok_cap >= staged tokens of all
+ * sequences * n_layers; *tok_need receives that number, also when tok_cap is
+ * too small and the call returns KV_ERR_INVALID with no change made)
+ * receives the page-addressed token moves, one group per
+ * (sequence, layer) in that order: group g is tok_moves[group_off[g] ..
+ * group_off[g+1]), group_off having n_seqs * n_layers + 1 entries -- the
+ * groups kv_move_tokens takes.  An error from sequence i returns with
+ * sequences 0 .. i-1 committed, *n_done = i (*bad_index set on
+ * KV_ERR_INVALID_ACCEPT). */
+int kv_state_accept_batch(kv_state *st, const uint64_t *seq_ids, int32_t n_seqs, const int64_t *paths,
+                          const int32_t *path_off, kv_token_move *tok_moves, int32_t tok_cap, int64_t *tok_need,
+                          int32_t *group_off, int32_t *n_done, int64_t *bad_index);
 /* Free the pages wholly below token_count - window (entries become KV_PAGE_NONE). */
 int kv_state_evict_window(kv_state *st, uint64_t seq_id, int64_t window, int64_t *n_freed);
 /* Move used pages into the lowest ids; *n_moves receives the count (also on

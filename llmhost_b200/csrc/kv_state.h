@@ -83,6 +83,7 @@ public:
 
     uint32_t n_pages() const { return n_pages_; }
     int n_layers() const { return n_layers_; }
+    int page_tokens() const { return P_; }
     uint32_t free_pages() const { return static_cast<uint32_t>(free_.size()); }
     uint32_t refcount(uint32_t page) const { return page < n_pages_ ? ref_[page] : 0; }
     // Pages in pop order (next page handed out first).

@@ -3,6 +3,7 @@
 // Output buffers are checked against their capacities before the state
 // changes, so a call that returns an error leaves the state as it was
 // (except forward, which drops the previous draft first, as the reference does).
+#include <algorithm>
 #include <new>
 
 #include "../../include/llmhost_kv.h"
@@ -184,6 +185,125 @@ int kv_state_rollback(kv_state* st, uint64_t seq_id, const int64_t* rejected, in
                       int32_t tok_cap, int32_t* n_tok_moves, int64_t* bad_index) {
     return finish_commit(st, seq_id, false, rejected, n, move_src, move_dst, move_cap, n_moves, tok_moves, tok_cap,
                          n_tok_moves, bad_index);
+}
+
+int kv_state_forward_batch(kv_state* st, const uint64_t* seq_ids, int32_t n_seqs, const uint32_t* tokens,
+                           const int32_t* tok_off, const int32_t* trees, int32_t* tok_row, int32_t* slots,
+                           int32_t* positions, int32_t* prefix, uint64_t* masks, uint32_t* cow_src,
+                           uint32_t* cow_dst, int32_t cow_cap, int32_t* n_cow, uint32_t* tables, int32_t stride,
+                           int32_t* n_done, kv_tree_error* err) {
+    if (n_done) *n_done = 0;
+    if (n_cow) *n_cow = 0;
+    if (!st || n_seqs < 0) return KV_ERR_INVALID;
+    if (n_seqs == 0) return KV_OK;
+    if (!seq_ids || !tok_off || tok_off[0] != 0 || !prefix || !tables || stride <= 0) return KV_ERR_INVALID;
+    const int layers = st->impl.n_layers();
+    if (static_cast<int64_t>(cow_cap) < static_cast<int64_t>(layers) * n_seqs || !cow_src || !cow_dst)
+        return KV_ERR_INVALID;
+    const int P = st->impl.page_tokens();
+    for (int32_t i = 0; i < n_seqs; ++i) {
+        const int32_t n = tok_off[i + 1] - tok_off[i];
+        if (n < 0 || (masks && n > 64)) return KV_ERR_INVALID;
+        // the draft's tables: the committed ones grown to hold L + n tokens
+        int64_t L = 0, len = 0;
+        if (st->impl.token_count(seq_ids[i], &L) == StateStatus::Ok) {
+            for (int l = 0; l < layers; ++l) {
+                const std::vector<uint32_t>* t = nullptr;
+                st->impl.table(seq_ids[i], l, 0, &t);
+                len = std::max<int64_t>(len, static_cast<int64_t>(t->size()));
+            }
+        }
+        if (std::max<int64_t>(len, (L + n + P - 1) / P) > stride) return KV_ERR_INVALID;
+    }
+    const int32_t total = tok_off[n_seqs];
+    if (total > 0 && (!tokens || !tok_row || !slots || !positions)) return KV_ERR_INVALID;
+    std::vector<int32_t> sl, po;
+    std::vector<PageCopy> cow;
+    int32_t nc = 0;
+    for (int32_t i = 0; i < n_seqs; ++i) {
+        const int32_t off = tok_off[i], n = tok_off[i + 1] - off;
+        const int32_t* tree = trees ? trees + off : nullptr;
+        TreeError e;
+        cow.clear();
+        const StateStatus s = st->impl.forward(seq_ids[i], tokens + off, static_cast<size_t>(n), tree,
+                                               tree ? static_cast<size_t>(n) : 0, &e, &sl, &po, &cow);
+        put_tree_error(e, err);
+        if (s != StateStatus::Ok) return to_status(s);
+        for (int32_t k = 0; k < n; ++k) {
+            tok_row[off + k] = i;
+            slots[off + k] = sl[k];
+            positions[off + k] = po[k];
+        }
+        if (masks) {  // ancestor-or-self bits; the tree was validated (parents precede)
+            for (int32_t k = 0; k < n; ++k) {
+                const int32_t par = tree ? tree[k] : k - 1;
+                masks[off + k] = (par >= 0 ? masks[off + par] : 0ull) | (1ull << k);
+            }
+        }
+        for (const PageCopy& c : cow) {
+            cow_src[nc] = c.src;
+            cow_dst[nc] = c.dst;
+            ++nc;
+        }
+        int64_t base = 0;
+        st->impl.pending_base(seq_ids[i], &base);
+        prefix[i] = static_cast<int32_t>(base);
+        if (n_done) *n_done = i + 1;
+        if (n_cow) *n_cow = nc;
+    }
+    for (int l = 0; l < layers; ++l) {
+        for (int32_t i = 0; i < n_seqs; ++i) {
+            const std::vector<uint32_t>* t = nullptr;
+            st->impl.table(seq_ids[i], l, 1, &t);
+            uint32_t* row = tables + (static_cast<size_t>(l) * n_seqs + i) * stride;
+            const int32_t m = static_cast<int32_t>(t->size());
+            for (int32_t j = 0; j < stride; ++j) row[j] = j < m ? (*t)[j] : KV_PAGE_NONE;
+        }
+    }
+    return KV_OK;
+}
+
+int kv_state_accept_batch(kv_state* st, const uint64_t* seq_ids, int32_t n_seqs, const int64_t* paths,
+                          const int32_t* path_off, kv_token_move* tok_moves, int32_t tok_cap, int64_t* tok_need,
+                          int32_t* group_off, int32_t* n_done, int64_t* bad_index) {
+    if (n_done) *n_done = 0;
+    if (tok_need) *tok_need = 0;
+    if (!st || n_seqs < 0) return KV_ERR_INVALID;
+    if (n_seqs == 0) return KV_OK;
+    if (!seq_ids || !path_off || path_off[0] != 0 || !group_off) return KV_ERR_INVALID;
+    const int layers = st->impl.n_layers();
+    int64_t need = 0;
+    for (int32_t i = 0; i < n_seqs; ++i) {
+        if (path_off[i + 1] < path_off[i]) return KV_ERR_INVALID;
+        int64_t pend = 0;
+        const StateStatus ps = st->impl.pending_size(seq_ids[i], &pend);
+        if (ps != StateStatus::Ok) return to_status(ps);
+        need += pend * layers;
+    }
+    if (tok_need) *tok_need = need;
+    if (need > tok_cap || (need > 0 && !tok_moves) || (path_off[n_seqs] > 0 && !paths)) return KV_ERR_INVALID;
+    std::vector<SlotMove> moves;
+    std::vector<TokenMove> pages;
+    int32_t nt = 0;
+    group_off[0] = 0;
+    for (int32_t i = 0; i < n_seqs; ++i) {
+        const int32_t off = path_off[i], n = path_off[i + 1] - off;
+        moves.clear();
+        pages.clear();
+        const StateStatus s = st->impl.accept(seq_ids[i], n ? paths + off : nullptr, static_cast<size_t>(n),
+                                              bad_index, &moves, &pages);
+        if (s != StateStatus::Ok) return to_status(s);
+        const int32_t per = static_cast<int32_t>(pages.size()) / layers;  // layer-major, the same per layer
+        for (int l = 0; l < layers; ++l) {
+            for (int32_t k = 0; k < per; ++k) {
+                const TokenMove& m = pages[static_cast<size_t>(l) * per + k];
+                tok_moves[nt++] = kv_token_move{m.src_page, m.src_slot, m.dst_page, m.dst_slot};
+            }
+            group_off[i * layers + l + 1] = nt;
+        }
+        if (n_done) *n_done = i + 1;
+    }
+    return KV_OK;
 }
 
 int kv_state_evict_window(kv_state* st, uint64_t seq_id, int64_t window, int64_t* n_freed) {

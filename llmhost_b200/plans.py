@@ -64,42 +64,20 @@ class ForwardBatch:
 
 
 def plan_forward(st: KvState, seqs, tokens, parents, stride: int) -> ForwardBatch:
-    """KvState.forward for every session (tokens[i], parents[i]), flattened."""
-    cs, cd, tseq, slots, pos, qoff, prefix, masks = [], [], [], [], [], [0], [], []
-    for row, s in enumerate(seqs):
-        plan = st.forward(s, tokens[row], parents[row])
-        for a, b in plan.cow:
-            cs.append(a)
-            cd.append(b)
-        n = len(plan.slots)
-        tseq.append(np.full(n, row, np.int32))
-        slots.append(plan.slots.astype(np.int32))
-        pos.append(plan.positions.astype(np.int32))
-        qoff.append(qoff[-1] + n)
-        prefix.append(st.pending_base(s))
-        masks.append(tree_masks(parents[row]))
-    tables = np.stack([st.export_tables(seqs, layer, stride, draft=True) for layer in range(st.n_layers)])
-    return ForwardBatch(list(seqs), np.asarray(cs, np.uint32), np.asarray(cd, np.uint32),
-                        np.concatenate(tseq), np.concatenate(slots), np.concatenate(pos),
-                        np.asarray(qoff, np.int32), np.asarray(prefix, np.int32), np.concatenate(masks), tables,
-                        max(np.diff(qoff)) if len(seqs) else 0)
+    """KvState.forward for every session (tokens[i], parents[i]), flattened;
+    one native call (kv_state_forward_batch)."""
+    f = st.forward_batch(seqs, tokens, parents, stride)
+    qoff = f["q_offsets"]
+    return ForwardBatch(list(seqs), f["cow_src"], f["cow_dst"], f["tok_row"], f["slots"], f["positions"], qoff,
+                        f["prefix"], f["masks"], f["tables"], int(np.diff(qoff).max()) if len(seqs) else 0)
 
 
 def commit_moves(st: KvState, seqs, paths):
     """KvState.accept for every session; the page-addressed token moves of all
-    sessions and layers, one group per (session, layer), and group offsets."""
-    moves, offs = [], [0]
-    accepted = 0
-    for s, path in zip(seqs, paths):
-        _, tm = st.accept(s, path, with_pages=True)
-        accepted += len(path)
-        per = len(tm) // st.n_layers
-        for layer in range(st.n_layers):
-            part = tm[layer * per:(layer + 1) * per]
-            moves.append(part)
-            offs.append(offs[-1] + len(part))
-    mv = np.concatenate(moves).astype(np.int32) if moves else np.zeros((0, 4), np.int32)
-    return mv.reshape(-1, 4), np.asarray(offs, np.int32), accepted
+    sessions and layers, one group per (session, layer), and group offsets
+    (one native call, kv_state_accept_batch)."""
+    mv, offs = st.accept_batch(seqs, paths)
+    return mv, offs, sum(len(p) for p in paths)
 
 
 @dataclass

@@ -80,6 +80,12 @@ STATE_SIGNATURES = [
     ("kv_state_free_list", c_int32, [c_void_p, c_void_p, c_int64, POINTER(c_int64)]),
     ("kv_state_refcount", c_int32, [c_void_p, c_uint32, POINTER(c_uint32)]),
     ("kv_state_pending_base", c_int32, [c_void_p, c_uint64, POINTER(c_int64)]),
+    ("kv_state_forward_batch", c_int32, [c_void_p, c_void_p, c_int32, c_void_p, c_void_p, c_void_p, c_void_p,
+                                         c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int32,
+                                         POINTER(c_int32), c_void_p, c_int32, POINTER(c_int32),
+                                         POINTER(KvTreeError)]),
+    ("kv_state_accept_batch", c_int32, [c_void_p, c_void_p, c_int32, c_void_p, c_void_p, c_void_p, c_int32,
+                                        POINTER(c_int64), c_void_p, POINTER(c_int32), POINTER(c_int64)]),
 ]
 _bound = False
 
@@ -152,6 +158,7 @@ class KvState:
                                              0 if order is None else len(order), h), "kv_state_create")
         self._h = h.value
         self.n_pages = n_pages
+        self._accept_cap = 1024  # token-move buffer of accept_batch, grown on demand
 
     def close_all(self):
         if getattr(self, "_h", None):
@@ -230,6 +237,72 @@ class KvState:
 
     def rollback(self, seq: int, rejected, with_pages: bool = False):
         return self._commit(self.lib.kv_state_rollback, seq, rejected, with_pages)
+
+    def forward_batch(self, seqs, tokens, trees, stride: int, masks: bool = True) -> dict:
+        """forward() for every sequence in one native call (kv_state_forward_batch):
+        tokens[i] / trees[i] (trees None: chains) of sequence seqs[i].  Returns
+        the flat launch arrays: tok_row, slots, positions, q_offsets, prefix,
+        masks (int64 view; None unless masks), cow_src, cow_dst and tables
+        [n_layers, n_seqs, stride].  A failing sequence raises like forward()
+        with the sequences before it staged."""
+        n = len(seqs)
+        ids = np.ascontiguousarray(seqs, dtype=np.uint64)
+        lens = np.fromiter((len(t) for t in tokens), np.int64, n)
+        off = np.zeros(n + 1, np.int32)
+        np.cumsum(lens, out=off[1:])
+        total = int(off[-1])
+        tok = np.ascontiguousarray(np.concatenate([np.asarray(t, np.uint32) for t in tokens]) if total
+                                   else np.zeros(1, np.uint32), dtype=np.uint32)
+        tr = None
+        if trees is not None:
+            tr = _i32(np.concatenate([np.asarray(t, np.int32) for t in trees]) if total else np.zeros(1, np.int32))
+            if len(tr) < total:
+                raise ValueError("every sequence needs a tree of its token count")
+        k = max(total, 1)
+        tok_row, slots, pos = np.empty(k, np.int32), np.empty(k, np.int32), np.empty(k, np.int32)
+        prefix = np.empty(max(n, 1), np.int32)
+        mk = np.empty(k, np.uint64) if masks else None
+        cap = max(self.n_layers * n, 1)
+        cs, cd = np.empty(cap, np.uint32), np.empty(cap, np.uint32)
+        tables = np.empty((self.n_layers, max(n, 1), stride), np.uint32)
+        nc, done, err = c_int32(0), c_int32(0), KvTreeError()
+        rc = self.lib.kv_state_forward_batch(self._h, ids.ctypes.data, n, tok.ctypes.data, off.ctypes.data,
+                                             None if tr is None else tr.ctypes.data, tok_row.ctypes.data,
+                                             slots.ctypes.data, pos.ctypes.data, prefix.ctypes.data,
+                                             None if mk is None else mk.ctypes.data, cs.ctypes.data,
+                                             cd.ctypes.data, cap, nc, tables.ctypes.data, stride, done, err)
+        if rc == _capi_status("KV_ERR_TREE"):
+            raise EngineError("Tree", int(seqs[done.value]), tree=TreeError(err))
+        self._engine_check(rc, int(seqs[done.value]) if done.value < n else -1)
+        return {"tok_row": tok_row[:total], "slots": slots[:total], "positions": pos[:total], "q_offsets": off,
+                "prefix": prefix[:n], "masks": None if mk is None else mk[:total].view(np.int64),
+                "cow_src": cs[:nc.value], "cow_dst": cd[:nc.value], "tables": tables[:, :n]}
+
+    def accept_batch(self, seqs, paths):
+        """accept() for every sequence in one native call (kv_state_accept_batch).
+        Returns (token moves [n, 4] int32, group offsets [n_seqs * n_layers + 1]):
+        one group per (sequence, layer), as KvPool.move_tokens takes them."""
+        n = len(seqs)
+        ids = np.ascontiguousarray(seqs, dtype=np.uint64)
+        off = np.zeros(n + 1, np.int32)
+        np.cumsum([len(p) for p in paths], out=off[1:])
+        pa = np.ascontiguousarray(np.concatenate([np.asarray(p, np.int64) for p in paths]) if off[-1]
+                                  else np.zeros(1, np.int64), dtype=np.int64)
+        groups = np.empty(n * self.n_layers + 1, np.int32)
+        groups[0] = 0
+        done, bad, need = c_int32(0), c_int64(0), c_int64(0)
+        cap = max(self._accept_cap, 1)
+        for _ in range(2):  # a second try when the staged drafts outgrew the last size
+            tm = np.empty((cap, 4), np.int32)
+            rc = self.lib.kv_state_accept_batch(self._h, ids.ctypes.data, n, pa.ctypes.data, off.ctypes.data,
+                                                tm.ctypes.data, cap, need, groups.ctypes.data, done, bad)
+            if need.value <= cap:
+                break
+            cap = self._accept_cap = int(need.value)
+        if rc == _capi_status("KV_ERR_INVALID_ACCEPT"):
+            raise EngineError("InvalidAccept", int(seqs[done.value]), index=int(bad.value))
+        self._engine_check(rc, int(seqs[done.value]) if done.value < n else -1)
+        return tm[:groups[-1]], groups
 
     def evict_window(self, seq: int, window: int) -> int:
         n = c_int64(0)

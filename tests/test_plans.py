@@ -54,6 +54,82 @@ def test_plan_forward_and_commit_match_per_session_calls():
         assert a.table(s, 0) == b.table(s, 0)
 
 
+def test_forward_batch_masks_chains_and_errors():
+    import pytest
+
+    from llmhost_b200.plans import tree_masks
+    from llmhost_b200.state import EngineError
+
+    a, b = _two_states()
+    for st in (a, b):
+        for s in (0, 1, 2):
+            st.open(s)
+            st.append(s, 5 + 7 * s)
+    rng = np.random.default_rng(3)
+    trees = [draft_tree(rng, 20)[0], [-1, 0, 0, 1], list(range(-1, 63))]
+    f = a.forward_batch([0, 1, 2], [list(range(len(t))) for t in trees], trees, stride=16)
+    np.testing.assert_array_equal(f["masks"], np.concatenate([tree_masks(t) for t in trees]))
+    np.testing.assert_array_equal(f["prefix"], [5, 12, 19])
+    # no trees: chains, whose masks are the prefixes 0..i
+    f = b.forward_batch([0, 1], [[1, 2, 3], [4]], None, stride=16)
+    assert f["masks"].view(np.uint64).tolist() == [1, 3, 7, 1]
+    np.testing.assert_array_equal(f["positions"], [5, 6, 7, 12])
+
+    # a bad tree in the second sequence: the first is staged, the third is not
+    c, _ = _two_states()
+    for s in (0, 1, 2):
+        c.open(s)
+    with pytest.raises(EngineError) as e:
+        c.forward_batch([0, 1, 2], [[1], [1, 2], [1]], [[-1], [-1, 1], [-1]], stride=4)
+    assert e.value.kind == "Tree" and e.value.seq_id == 1
+    assert c.pending_base(0) == 0
+    with pytest.raises(EngineError) as e:
+        c.pending_base(2)
+    assert e.value.kind == "NoPendingForward"
+    # tables wider than the stride: refused before any state changes
+    d, _ = _two_states()
+    d.open(0)
+    d.append(0, 40)
+    with pytest.raises(Exception):
+        d.forward_batch([0], [list(range(30))], None, stride=4)  # 70 tokens need 5 pages
+    with pytest.raises(EngineError):
+        d.pending_base(0)
+    # more than 64 tokens cannot be described by masks
+    with pytest.raises(Exception):
+        d.forward_batch([0], [list(range(65))], None, stride=16)
+
+
+def test_accept_batch_grows_its_buffer_and_stops_at_a_bad_path():
+    import pytest
+
+    from llmhost_b200.state import EngineError
+
+    a, b = _two_states()
+    for st in (a, b):
+        for s in (0, 1):
+            st.open(s)
+            st.append(s, 30)
+    trees = [[-1, 0, 1, 1], [-1, 0]]
+    toks = [[7, 8, 9, 10], [5, 6]]
+    plan_forward(a, [0, 1], toks, trees, stride=16)
+    for s in (0, 1):
+        b.forward(s, toks[s], trees[s])
+    a._accept_cap = 1  # too small: the call reports the size and runs again
+    mv, offs, acc = commit_moves(a, [0, 1], [[0, 1, 3], [0]])
+    assert acc == 4 and len(offs) == 1 + 2 * 2
+    ref = [b.accept(s, p, with_pages=True)[1] for s, p in ((0, [0, 1, 3]), (1, [0]))]
+    want = np.concatenate([r[layer * (len(r) // 2):(layer + 1) * (len(r) // 2)] for r in ref for layer in range(2)])
+    np.testing.assert_array_equal(mv, want.reshape(-1, 4))
+    for s in (0, 1):
+        assert a.committed(s) == b.committed(s) and a.table(s, 1) == b.table(s, 1)
+    # a path that is not closed under parents, in the second sequence
+    plan_forward(a, [0, 1], toks, trees, stride=16)
+    with pytest.raises(EngineError) as e:
+        commit_moves(a, [0, 1], [[0], [1]])
+    assert e.value.kind == "InvalidAccept" and e.value.seq_id == 1
+    assert len(a.committed(0)) == 34  # the first sequence committed its path
+
+
 def test_plan_decode_step_publishes_new_pages_and_evicts():
     st = KvState(256, 2)
     for s in (0, 1):
