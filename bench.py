@@ -334,8 +334,10 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     K = args.steps
     # Every launch of every EV_EVERY-th timed step is bracketed by events (the
     # kernel's live duration for the roofline); an event pair around every
-    # launch would itself slow the step by a few percent.
-    EV_EVERY = 4
+    # launch would itself slow the step by a few percent (an event between two
+    # launches also stops the next one's set-up from overlapping this one's
+    # tail, so the sampled launches read a little long).
+    EV_EVERY = 16
     kev = {i: [[torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)] for _ in range(L)]
            for i in range(0, K, EV_EVERY)}
     sampler = ClockSampler(local_rank)

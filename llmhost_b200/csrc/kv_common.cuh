@@ -166,26 +166,51 @@ __device__ __forceinline__ uint32_t swz128(uint32_t lin) {
 // the sum of squares in double, in dimension order, as separate rounded
 // products and sums (Rust does not contract), then
 // (float)(1 / sqrt(sumsq / 64 + eps)) with IEEE square root and reciprocal.
-// Out of line: called once per row, it must not grow the kernels' hot code.
-static __device__ __noinline__ float rms_scale_row(const __nv_bfloat16* row, float eps) {
-    double s = 0.0;
-#pragma unroll 4
-    for (int i = 0; i < 64; ++i) {
-        const double v = static_cast<double>(__bfloat162float(row[i]));
-        s = __dadd_rn(s, __dmul_rn(v, v));
-    }
+// The row is read with 16-byte loads (it must be 16-byte aligned) and each
+// chunk's squares are taken before the running sum reaches them, so the
+// 64-term chain of rounded adds is the only serial part.  Out of line:
+// called once per row, it must not grow the kernels' hot code.
+__device__ __forceinline__ float rms_mean_to_scale(double s, float eps) {
     const double m = __dadd_rn(__dmul_rn(s, 1.0 / 64.0), static_cast<double>(eps));
     return __double2float_rn(__drcp_rn(__dsqrt_rn(m)));
 }
-static __device__ __noinline__ float rms_scale_row(const float* row, float eps) {
+static __device__ __noinline__ float rms_scale_row(const __nv_bfloat16* row, float eps) {
+    const uint4* r4 = reinterpret_cast<const uint4*>(row);
     double s = 0.0;
-#pragma unroll 4
-    for (int i = 0; i < 64; ++i) {
-        const double v = static_cast<double>(row[i]);
-        s = __dadd_rn(s, __dmul_rn(v, v));
+    uint4 w = r4[0];
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+        const uint4 wn = r4[c < 7 ? c + 1 : c];  // the next chunk in flight
+        const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+        double sq[8];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const float2 f = bf16x2_to_float2(u[e]);
+            sq[2 * e] = __dmul_rn(static_cast<double>(f.x), static_cast<double>(f.x));
+            sq[2 * e + 1] = __dmul_rn(static_cast<double>(f.y), static_cast<double>(f.y));
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) s = __dadd_rn(s, sq[i]);
+        w = wn;
     }
-    const double m = __dadd_rn(__dmul_rn(s, 1.0 / 64.0), static_cast<double>(eps));
-    return __double2float_rn(__drcp_rn(__dsqrt_rn(m)));
+    return rms_mean_to_scale(s, eps);
+}
+static __device__ __noinline__ float rms_scale_row(const float* row, float eps) {
+    const float4* r4 = reinterpret_cast<const float4*>(row);
+    double s = 0.0;
+    float4 w = r4[0];
+#pragma unroll
+    for (int c = 0; c < 16; ++c) {
+        const float4 wn = r4[c < 15 ? c + 1 : c];
+        const double sq[4] = {__dmul_rn(static_cast<double>(w.x), static_cast<double>(w.x)),
+                              __dmul_rn(static_cast<double>(w.y), static_cast<double>(w.y)),
+                              __dmul_rn(static_cast<double>(w.z), static_cast<double>(w.z)),
+                              __dmul_rn(static_cast<double>(w.w), static_cast<double>(w.w))};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) s = __dadd_rn(s, sq[i]);
+        w = wn;
+    }
+    return rms_mean_to_scale(s, eps);
 }
 
 // x' = w * (x * scale): RMSNorm's two rounded products (ops.rs:19-21).

@@ -109,7 +109,8 @@ struct TcShape {
     static constexpr int kOffQstg = kOffStg + kStgBytes;            // next segment's q rows and RoPE row
     static constexpr int kQstgBytes = NQ * 128 + 256;
     static constexpr int kOffQsc = kOffQstg + kQstgBytes;           // float [NQ]: q RMSNorm scales
-    static constexpr int kOffMax = kOffQsc + ((NQ * 4 + 15) & ~15); // float [2][4 warps][2 units][4]
+    static constexpr int kOffQw = kOffQsc + ((NQ * 4 + 15) & ~15);  // float [64]: q RMSNorm weights
+    static constexpr int kOffMax = kOffQw + 64 * 4;                 // float [2][4 warps][2 units][4]
     static constexpr int kOffM = kOffMax + 2 * 4 * 8 * 4;           // float [2 buffers][NQ]: reference maxima
     static constexpr int kOffL = kOffM + 2 * NQ * 4;                // float [2 buffers][4 warps][NQ]: row sums
     static constexpr int kOffOb = kOffL + 2 * 4 * NQ * 4;           // float [64][4]
@@ -352,6 +353,12 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(const __grid_con
                 z[i] = make_uint4(0, 0, 0, 0);
             proxy_fence();
         }
+        if constexpr (kNorm) {  // the q RMSNorm weights, read where the Q tiles are built
+            if (threadIdx.x < 64) {
+                grid_dep_wait();
+                reinterpret_cast<float*>(base + Sh::kOffQw)[threadIdx.x] = __ldg(a.q_norm + threadIdx.x);
+            }
+        }
         if (warp == kMmaWarp) {
             asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                              smem_addr(tmem_slot)),
@@ -415,6 +422,12 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(const __grid_con
             return Fetch{pg < a.bt_stride ? __ldg(a.bt + static_cast<size_t>(c.q.s) * a.bt_stride + pg) : kPageNone,
                          true};
         };
+        // k RMSNorm weights of this lane's dims (2 ii, 2 ii + 1, 32 + 2 ii, 33 + 2 ii)
+        float2 kwx = make_float2(1.f, 1.f), kwy = make_float2(1.f, 1.f);
+        if constexpr (kNorm) {
+            kwx = __ldg(reinterpret_cast<const float2*>(a.k_norm) + (lane & 15));
+            kwy = __ldg(reinterpret_cast<const float2*>(a.k_norm + 32) + (lane & 15));
+        }
         StageCursor<NKV> cur;
         cur.start(a, pstart, n, gb, ge);
         Fetch fc = cur.done ? Fetch{0u, false} : fetch(cur);  // a slice may hold lead stages only
@@ -498,10 +511,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(const __grid_con
                                 float2 x = bf16x2_to_float2(*reinterpret_cast<const uint32_t*>(in + 4 * ii));
                                 float2 y = bf16x2_to_float2(*reinterpret_cast<const uint32_t*>(in + 64 + 4 * ii));
                                 if constexpr (kNorm) {
-                                    const float2 wx = __ldg(reinterpret_cast<const float2*>(a.k_norm + 2 * ii));
-                                    const float2 wy = __ldg(reinterpret_cast<const float2*>(a.k_norm + 32 + 2 * ii));
-                                    x = make_float2(rms_apply(x.x, sc, wx.x), rms_apply(x.y, sc, wx.y));
-                                    y = make_float2(rms_apply(y.x, sc, wy.x), rms_apply(y.y, sc, wy.y));
+                                    x = make_float2(rms_apply(x.x, sc, kwx.x), rms_apply(x.y, sc, kwx.y));
+                                    y = make_float2(rms_apply(y.x, sc, kwy.x), rms_apply(y.y, sc, kwy.y));
                                 }
                                 const float x0 = __fadd_rn(__fmul_rn(x.x, c.x), __fmul_rn(-y.x, c.y));
                                 const float x1 = __fadd_rn(__fmul_rn(x.y, c.z), __fmul_rn(-y.y, c.w));
@@ -652,6 +663,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(const __grid_con
         // one thread per row; worked out during the segment before when it
         // has a second stage, where the softmax warps have slack.
         float* qsc = reinterpret_cast<float*>(base + Sh::kOffQsc);
+        const float* qw = reinterpret_cast<const float*>(base + Sh::kOffQw);
         bool qsc_ready = false;
         auto q_scales = [&]() {
             cp_async_wait<0>();
@@ -678,8 +690,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(const __grid_con
                     float2 x = bf16x2_to_float2(*reinterpret_cast<const uint32_t*>(row_in + 16 * c + 4 * e));
                     float2 y = bf16x2_to_float2(*reinterpret_cast<const uint32_t*>(row_in + 64 + 16 * c + 4 * e));
                     if constexpr (kNorm) {
-                        const float2 wx = __ldg(reinterpret_cast<const float2*>(a.q_norm + 8 * c + 2 * e));
-                        const float2 wy = __ldg(reinterpret_cast<const float2*>(a.q_norm + 32 + 8 * c + 2 * e));
+                        const float2 wx = reinterpret_cast<const float2*>(qw)[4 * c + e];
+                        const float2 wy = reinterpret_cast<const float2*>(qw)[16 + 4 * c + e];
                         x = make_float2(rms_apply(x.x, sc, wx.x), rms_apply(x.y, sc, wx.y));
                         y = make_float2(rms_apply(y.x, sc, wy.x), rms_apply(y.y, sc, wy.y));
                     }
