@@ -28,6 +28,7 @@
 // kLazyLog2 is m raised, O (in TMEM) and the row sum rescaled and P redone.
 // P therefore stays below 2^kLazyLog2.  Pages past the sequence load as
 // out-of-range boxes (zero fill).
+#include <algorithm>
 #include <cmath>
 
 #include "kv_common.cuh"
@@ -443,9 +444,18 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
         // tcgen05.ld / st are warp-collective (.sync.aligned): every branch
         // around them below is decided by a warp vote, never per row.
         constexpr unsigned kAll = 0xffffffffu;
+        // A warp of padding rows only (the tail of the last tile) never
+        // sweeps S: its P and O rows are never read back, and each row of an
+        // MMA is independent of the others.  It still waits for each S before
+        // it arrives on p_full, which keeps the barrier phases in step.
+        const bool idle = __all_sync(kAll, !row_valid);
         int j = 0;
         for (; j < nb; ++j) {
             if (!__all_sync(kAll, wait_bar(&s_full[tq], static_cast<uint32_t>(j) & 1u, abort_flag, a.err))) break;
+            if (idle) {
+                mbar_arrive(&p_full[tq]);
+                continue;
+            }
             tc_fence_after();
             const int k0 = j * kBlockKeys;
             const bool need_mask = k0 + kBlockKeys > L;  // block-level, so warp-uniform
@@ -476,7 +486,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
             const float2 s01 = __fadd2_rn(sum2[0], sum2[1]);
             l += s01.x + s01.y;
         }
-        if (j == nb &&
+        if (j == nb && !idle &&
             __all_sync(kAll, wait_bar(&pv_full[tq], static_cast<uint32_t>(nb - 1) & 1u, abort_flag, a.err))) {
             tc_fence_after();
             const float inv = l > 0.f ? 1.f / l : 0.f;
@@ -537,7 +547,11 @@ int launch_prefill(kv_pool* pool, const void* q, const int32_t* q_pos, const int
     a.n_q = c.n_q_heads;
     a.nkv = c.n_kv_heads;
     a.group = group;
-    a.tile_tokens = kRows / group;
+    // Tokens per 128-row tile: as many as fit, except that chunks short
+    // enough for one CTA are split evenly over its tiles, so that the rows
+    // left over are whole warps of padding (which skip the softmax).
+    const int fit = kRows / group;
+    a.tile_tokens = max_q <= kTiles * fit ? std::max(1, (max_q + kTiles - 1) / kTiles) : fit;
     a.max_q = max_q;
     a.rope = pool->rope;
     a.max_pos = c.max_positions;
