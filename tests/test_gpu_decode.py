@@ -332,3 +332,64 @@ def test_norm_fused_decode_against_oracle(cuda, dtype, name):
         pages = pool.read_pages(ids)
     np.testing.assert_array_equal(pages, host.data[ids], err_msg="stored pages differ from the oracle")
     assert_close_rows(out, ref, RTOL[dtype], f"{dtype} norm-fused {name}")
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "f32"])
+def test_back_to_back_fused_steps(cuda, dtype):
+    # Twenty decode steps enqueued without a host synchronisation: each launch
+    # reads the K/V row the launch before it stored (steps cross page
+    # boundaries at 16 and 32 tokens), so a launch that began reading before
+    # its predecessor finished would show up here.  Every step's output
+    # against the oracle's step-by-step run; the pages bit for bit.
+    import torch
+
+    from llmhost_b200.kv import KvPool
+    from llmhost_b200.workloads import PAGE_TOKENS, normal_bits
+    from oracle import oracle as O
+    from paged_case import PAGE_NONE
+
+    rng = np.random.default_rng(21)
+    n_q, n_kv, steps = 24, 8, 20
+    lens0 = np.array([0, 15, 16, 30, 100, 2047, 5000], np.int64)
+    n = len(lens0)
+    pages = -(-(lens0 + steps) // PAGE_TOKENS)
+    n_pages = int(pages.sum()) + 4
+    perm = rng.permutation(n_pages).astype(np.uint32)
+    bt = np.full((n, int(pages.max())), PAGE_NONE, np.uint32)
+    cur = 0
+    for s in range(n):
+        bt[s, :pages[s]] = perm[cur:cur + pages[s]]
+        cur += pages[s]
+    k_pre = [normal_bits(rng, (int(L), n_kv, 64), dtype) for L in lens0]
+    v_pre = [normal_bits(rng, (int(L), n_kv, 64), dtype) for L in lens0]
+    qs = [normal_bits(rng, (n, n_q, 64), dtype) for _ in range(steps)]
+    ks = [normal_bits(rng, (n, n_kv, 64), dtype) for _ in range(steps)]
+    vs = [normal_bits(rng, (n, n_kv, 64), dtype) for _ in range(steps)]
+
+    host = O.HostPages(n_pages, O.BF16 if dtype == "bf16" else O.F32, n_q, n_kv)
+    for s in range(n):
+        for t in range(int(lens0[s])):
+            host.append_token(bt[s], t, t, k_pre[s][t], v_pre[s][t])
+    refs = [host.decode_step(bt, (lens0 + i + 1).astype(np.int32), 0, qs[i], ks[i], vs[i]) for i in range(steps)]
+
+    with KvPool(dtype=dtype, n_q_heads=n_q, n_kv_heads=n_kv, n_pages=n_pages,
+                max_positions=int(lens0.max()) + steps + 16, max_seqs=n) as pool:
+        dev = pool.device
+        bt_d = torch.from_numpy(bt.view(np.int32)).to(dev)
+        tok_seq = np.concatenate([np.full(int(L), s, np.int32) for s, L in enumerate(lens0)])
+        tok_slot = np.concatenate([np.arange(int(L), dtype=np.int32) for L in lens0])
+        ts, tl = torch.from_numpy(tok_seq).to(dev), torch.from_numpy(tok_slot).to(dev)
+        pool.append(to_torch(np.concatenate([a.reshape(-1) for a in k_pre]), dtype, dev),
+                    to_torch(np.concatenate([a.reshape(-1) for a in v_pre]), dtype, dev), ts, tl, tl, bt_d)
+        lens_d = [torch.from_numpy((lens0 + i + 1).astype(np.int32)).to(dev) for i in range(steps)]
+        qd = [to_torch(x, dtype, dev) for x in qs]
+        kd = [to_torch(x, dtype, dev) for x in ks]
+        vd = [to_torch(x, dtype, dev) for x in vs]
+        torch.cuda.synchronize()
+        outs = [pool.append_decode_attn(kd[i], vd[i], qd[i], bt_d, lens_d[i]) for i in range(steps)]
+        torch.cuda.synchronize()
+        assert pool.last_error() == 0
+        ids = np.sort(bt[bt != PAGE_NONE])
+        np.testing.assert_array_equal(pool.read_pages(ids), host.data[ids], err_msg="stored pages differ")
+        for i in range(steps):
+            assert_close_rows(to_numpy_f32(outs[i]), refs[i], RTOL[dtype], f"{dtype} step {i}")
