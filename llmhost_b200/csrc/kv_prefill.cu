@@ -340,39 +340,50 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
 
     if (warp == kProducerWarp) {
         // ---------------- producer: K/V head slices, 8 pages per block ----------------
-        if (lane == 0) {
-            const int total_rows = static_cast<int>(a.n_pages) * a.page_rows;
-            int issued = 0;
-            for (int j = 0; j < nb; ++j) {
-                const int st = j % kStages;
-                if (j >= kStages &&
-                    !wait_bar(&empty[st], static_cast<uint32_t>(j / kStages - 1) & 1u, abort_flag, a.err))
-                    break;
-                mbar_arrive_expect_tx(&full[st], kStageBytes);
+        // Lane i < 8 owns page i of every block: its block-table entry for
+        // block j + 1 is loaded while block j's stage is waited for, and it
+        // issues that page's K and V boxes (lane 0 first sets the stage's
+        // expected bytes), so no copy waits on a serial chain of loads.
+        const int total_rows = static_cast<int>(a.n_pages) * a.page_rows;
+        // page pi of the sequence holds keys this CTA can see
+        auto used = [&](int j) { return lane < kPagesPerBlock && (j * kPagesPerBlock + lane) * kPageTokens < kmax; };
+        auto entry = [&](int j) -> uint32_t {
+            const int pi = j * kPagesPerBlock + lane;
+            if (!used(j)) return 0u;
+            return pi < a.bt_stride ? __ldg(a.bt + static_cast<size_t>(s) * a.bt_stride + pi) : kPageNone;
+        };
+        int issued = 0;
+        uint32_t next = nb > 0 ? entry(0) : 0u;
+        for (int j = 0; j < nb; ++j) {
+            const int st = j % kStages;
+            const uint32_t phys = next;
+            if (j + 1 < nb) next = entry(j + 1);  // in flight during the wait below
+            bool ok = true;
+            if (lane == 0 && j >= kStages)
+                ok = wait_bar(&empty[st], static_cast<uint32_t>(j / kStages - 1) & 1u, abort_flag, a.err);
+            if (!__shfl_sync(0xffffffffu, ok, 0)) break;
+            if (lane == 0) mbar_arrive_expect_tx(&full[st], kStageBytes);
+            __syncwarp();
+            if (lane < kPagesPerBlock) {
                 uint8_t* kt = base + kOffStage + st * kStageBytes;
-                for (int i = 0; i < kPagesPerBlock; ++i) {
-                    const int pi = j * kPagesPerBlock + i;
-                    int rk = total_rows, rv = total_rows;  // out of range: zero fill
-                    if (pi * kPageTokens < kmax) {
-                        const uint32_t phys = pi < a.bt_stride ? __ldg(a.bt + static_cast<size_t>(s) * a.bt_stride + pi)
-                                                               : kPageNone;
-                        if (phys < a.n_pages) {
-                            rk = static_cast<int>(phys) * a.page_rows + h * kPageTokens;
-                            rv = static_cast<int>(phys) * a.page_rows + (a.nkv + h) * kPageTokens;
-                        } else {
-                            flag_error(a.err, kDevErrBadPage);
-                        }
+                int rk = total_rows, rv = total_rows;  // out of range: zero fill
+                if (used(j)) {
+                    if (phys < a.n_pages) {
+                        rk = static_cast<int>(phys) * a.page_rows + h * kPageTokens;
+                        rv = static_cast<int>(phys) * a.page_rows + (a.nkv + h) * kPageTokens;
+                    } else {
+                        flag_error(a.err, kDevErrBadPage);
                     }
-                    tma_load_2d(kt + i * kSliceBytes, &hmap, &full[st], 0, rk);
-                    tma_load_2d(kt + kKvBytes + i * kSliceBytes, &hmap, &full[st], 0, rv);
                 }
-                issued = j + 1;
+                tma_load_2d(kt + lane * kSliceBytes, &hmap, &full[st], 0, rk);
+                tma_load_2d(kt + kKvBytes + lane * kSliceBytes, &hmap, &full[st], 0, rv);
             }
-            if (*abort_flag) {  // wait (bounded) for the newest copy issued into each stage
-                for (int st = 0; st < kStages && st < issued; ++st) {
-                    const int last = st + ((issued - 1 - st) / kStages) * kStages;
-                    mbar_wait(&full[st], static_cast<uint32_t>(last / kStages) & 1u);
-                }
+            issued = j + 1;
+        }
+        if (lane == 0 && *abort_flag) {  // wait (bounded) for the newest copy issued into each stage
+            for (int st = 0; st < kStages && st < issued; ++st) {
+                const int last = st + ((issued - 1 - st) / kStages) * kStages;
+                mbar_wait(&full[st], static_cast<uint32_t>(last / kStages) & 1u);
             }
         }
     } else if (warp == kMmaWarp) {
