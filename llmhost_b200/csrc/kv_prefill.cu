@@ -10,11 +10,14 @@
 // One CTA per (sequence, kv head, 2 x 128 query rows); a row is a (token,
 // query head of the group) pair.  Keys are consumed in blocks of 128 (8 pages).
 // Roles:
-//   warps 0-7   softmax, one thread per row: warps 4t..4t+3 own tile t
-//   warp 8      TMA producer: per page one {64 x 16} bf16 box of K and one of
+//   warps 0-15  softmax, two threads per row: warps 8t..8t+7 own tile t, warp
+//               8t + 4h + q rows 32q..32q+31 and keys 64h..64h+63 of each
+//               block (TMEM lane quarter q); the halves of a row agree on the
+//               block maximum through shared memory
+//   warp 16     TMA producer: per page one {64 x 16} bf16 box of K and one of
 //               V for this kv head (128-byte swizzle, no multicast) into a
 //               4-stage ring
-//   warp 9      TMEM owner; one thread issues the tensor-core MMAs:
+//   warp 17     TMEM owner; one thread issues the tensor-core MMAs:
 //                 S_t  = Q_t K^T : M 128, N 128, K 64; Q_t and K K-major in
 //                                  shared memory; fp32 S_t in TMEM
 //                 O_t += P_t V   : M 128, N 64, K 128; P_t (bf16) in TMEM, V
@@ -48,9 +51,12 @@ constexpr int kSliceBytes = kPageTokens * 128;            // one page's K (or V)
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kTileCols = 256;                       // TMEM columns per tile
 constexpr uint32_t kColP = 128, kColO = 192;              // within a tile; S at 0
-constexpr int kSoftmaxThreads = kTiles * kRows;           // warps 0-7
-constexpr int kProducerWarp = kSoftmaxThreads / 32;       // warp 8: TMA
-constexpr int kMmaWarp = kProducerWarp + 1;               // warp 9: TMEM owner, MMA issue
+constexpr int kHalves = 2;                                // softmax threads per row
+constexpr int kHalfKeys = kBlockKeys / kHalves;           // keys of a block one thread sweeps
+constexpr int kTileThreads = kRows * kHalves;             // softmax threads of one tile
+constexpr int kSoftmaxThreads = kTiles * kTileThreads;    // warps 0-15
+constexpr int kProducerWarp = kSoftmaxThreads / 32;       // warp 16: TMA
+constexpr int kMmaWarp = kProducerWarp + 1;               // warp 17: TMEM owner, MMA issue
 constexpr int kThreads = kSoftmaxThreads + 64;
 
 // smem: Q tiles (128 rows x 128 B, 128-byte swizzle), the K/V ring (stage st:
@@ -59,7 +65,8 @@ constexpr int kQBytes = kRows * 128;
 constexpr int kStageBytes = 2 * kKvBytes;
 constexpr int kOffStage = kTiles * kQBytes;
 constexpr int kOffBar = kOffStage + kStages * kStageBytes;
-constexpr int kSmemBytes = 1024 + kOffBar + 256;
+constexpr int kOffX = kOffBar + 256;  // float [2][kTiles][kHalves][kRows]: half-row maxima / sums
+constexpr int kSmemBytes = 1024 + kOffX + 2 * kTiles * kHalves * kRows * 4;
 
 // P entries stay below 2^kLazyLog2 times the row's reference maximum; the
 // reference is raised only when a block's maximum exceeds it by more.
@@ -138,24 +145,18 @@ __device__ __forceinline__ void group32(uint32_t (&rr)[32], int g, int k0, bool 
     tmem_st16(t_p + 16 * g, w);
 }
 
-// One pass over the four 32-key groups of this thread's S row (block maximum
-// and P against the reference mu), each TMEM load issued while the previous
-// group is processed.  Warp-collective.
+// One pass over this thread's two 32-key groups of its S row (t_s, keys k0
+// ..: its half of the block): the half's maximum and P against the
+// reference mu.  Warp-collective.
 __device__ __forceinline__ void sweep_s(uint32_t t_s, uint32_t t_p, int k0, bool need_mask, const RowMask& rm,
                                         float mu, float& bm, float2 (&sum2)[2]) {
     uint32_t ra[32], rb[32];
     tmem_ld32(t_s, ra);
-    tmem_wait32(ra);
     tmem_ld32(t_s + 32, rb);
+    tmem_wait32(ra);
     group32(ra, 0, k0, need_mask, rm, mu, t_p, bm, sum2);
     tmem_wait32(rb);
-    tmem_ld32(t_s + 64, ra);
     group32(rb, 1, k0, need_mask, rm, mu, t_p, bm, sum2);
-    tmem_wait32(ra);
-    tmem_ld32(t_s + 96, rb);
-    group32(ra, 2, k0, need_mask, rm, mu, t_p, bm, sum2);
-    tmem_wait32(rb);
-    group32(rb, 3, k0, need_mask, rm, mu, t_p, bm, sum2);
 }
 
 // S values of a 16-key group as floats, masked keys at -inf.
@@ -170,12 +171,12 @@ __device__ __forceinline__ void s_group(const uint32_t (&rr)[16], int key0, bool
     }
 }
 
-// Block maximum of this thread's S row (rarely needed: first block only).
-// A rolled loop, to keep the instruction footprint of the softmax small.
+// Maximum of this thread's half of its S row (rarely needed: first block
+// only).  A rolled loop, to keep the instruction footprint of the softmax small.
 __device__ __forceinline__ float row_max(uint32_t taddr, int k0, bool need_mask, const RowMask& rm) {
     float bm = -INFINITY;
 #pragma unroll 1
-    for (int g = 0; g < 8; ++g) {
+    for (int g = 0; g < kHalfKeys / 16; ++g) {
         uint32_t rr[16];
         tmem_ld16(taddr + 16 * g, rr);
         tmem_wait16(rr);
@@ -186,14 +187,15 @@ __device__ __forceinline__ float row_max(uint32_t taddr, int k0, bool need_mask,
     return bm;
 }
 
-// P = 2^(S - mu) straight into the P columns of TMEM (rarely needed: a block
-// that raised a row's reference), plus the row sum.  Rolled loop.
+// P = 2^(S - mu) of this thread's half row straight into its P columns of
+// TMEM (rarely needed: a block that raised a row's reference), plus the sum.
+// Rolled loop.
 __device__ __forceinline__ float2 row_exp_to_tmem(uint32_t t_s, uint32_t t_p, int k0, bool need_mask,
                                                   const RowMask& rm, float mu) {
     const float2 nmu = make_float2(-mu, -mu);
     float2 sum2 = make_float2(0.f, 0.f);
 #pragma unroll 1
-    for (int g = 0; g < 8; ++g) {
+    for (int g = 0; g < kHalfKeys / 16; ++g) {
         uint32_t rr[16];
         tmem_ld16(t_s + 16 * g, rr);
         tmem_wait16(rr);
@@ -212,11 +214,12 @@ __device__ __forceinline__ float2 row_exp_to_tmem(uint32_t t_s, uint32_t t_p, in
     return sum2;
 }
 
-// O row (64 fp32 columns) scaled in place in TMEM.  Warp-collective.
+// This thread's half of its O row (32 fp32 columns) scaled in place in TMEM.
+// Warp-collective.
 __device__ __forceinline__ void scale_o(uint32_t t_o, float f) {
     const float2 f2 = make_float2(f, f);
 #pragma unroll
-    for (int c = 0; c < 4; ++c) {
+    for (int c = 0; c < 2; ++c) {
         uint32_t x[16];
         tmem_ld16(t_o + 16 * c, x);
         tmem_wait16(x);
@@ -269,7 +272,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
         }
         for (int t = 0; t < kTiles; ++t) {
             mbar_init(&s_full[t], 1);
-            mbar_init(&p_full[t], kRows);  // every softmax thread of the tile arrives
+            mbar_init(&p_full[t], kTileThreads);  // every softmax thread of the tile arrives
             mbar_init(&pv_full[t], 1);
         }
         mbar_init(mma_done, 1);
@@ -284,10 +287,11 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
     }
     if (warp == kProducerWarp && lane == 0) prefetch_tmap(&hmap);
 
-    // ---- Q tiles (warps 0-7): thread = (tile tq, row r); row r of tile tq is
-    // (token t_begin + tq * tile_tokens + r / G, head h*G + r % G).  RoPE at
-    // q_pos (rope.rs:76 form), scaled into log2 units, bf16, into TMEM.
-    const int tq = threadIdx.x / kRows, r = threadIdx.x % kRows;
+    // ---- Q tiles (warps 0-15): thread = (tile tq, half hf, row r); row r of
+    // tile tq is (token t_begin + tq * tile_tokens + r / G, head h*G + r % G).
+    // RoPE at q_pos (rope.rs:76 form), scaled into log2 units, bf16, into
+    // shared memory; each half builds half of the row's dims.
+    const int tq = (warp >> 3) & 1, hf = (warp >> 2) & 1, r = 32 * (warp & 3) + lane;
     const int rt = r / a.group, rg = r % a.group;
     const int t_row = t_begin + tq * a.tile_tokens + rt;
     const bool row_valid = (threadIdx.x < kSoftmaxThreads) && (rt < a.tile_tokens) && (t_row < t_end);
@@ -308,9 +312,11 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
                 pos = 0;
             }
             const float2* cs = a.rope + static_cast<size_t>(pos) * (kHeadDim / 2);
-            // dims 8c .. 8c+7 rotate together with dims 32+8c .. 32+8c+7
+            // dims 8c .. 8c+7 rotate together with dims 32+8c .. 32+8c+7; this
+            // half takes c = 2 hf, 2 hf + 1
 #pragma unroll
-            for (int c = 0; c < 4; ++c) {
+            for (int cc = 0; cc < 2; ++cc) {
+                const int c = 2 * hf + cc;
                 const uint4 u0 = __ldg(src + c), u1 = __ldg(src + c + 4);
                 const uint32_t w0[4] = {u0.x, u0.y, u0.z, u0.w}, w1[4] = {u1.x, u1.y, u1.z, u1.w};
                 uint32_t lo[4], hi[4];
@@ -330,7 +336,10 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
             }
         } else {
 #pragma unroll
-            for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(qrow + (c << 4)) = make_uint4(0, 0, 0, 0);
+            for (int cc = 0; cc < 4; ++cc) {
+                const int c = 2 * hf + (cc & 1) + 4 * (cc >> 1);  // 16-byte chunks 2hf, 2hf+1, 2hf+4, 2hf+5
+                *reinterpret_cast<uint4*>(qrow + (c << 4)) = make_uint4(0, 0, 0, 0);
+            }
         }
         proxy_fence();  // the tensor core reads Q through the async proxy
     }
@@ -438,7 +447,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
             mbar_wait(mma_done, 0);
         }
     } else {
-        // ---------------- softmax: thread (tq, r) owns row r of tile tq ----------------
+        // ---------------- softmax: thread (tq, hf, r) owns half hf of row r of tile tq ----------------
         RowMask rm;
         rm.L = L;
         rm.T = T;
@@ -453,60 +462,87 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
         // ask for a first pass or a redo; their results are not written.
         float m = row_valid ? -INFINITY : 0.f, l = 0.f;
         // tcgen05.ld / st are warp-collective (.sync.aligned): every branch
-        // around them below is decided by a warp vote, never per row.
+        // around them below is decided by a warp vote, never per row.  The two
+        // halves of a row sit in warps 4 apart and hold the same rows, so
+        // their votes agree.
         constexpr unsigned kAll = 0xffffffffu;
         // A warp of padding rows only (the tail of the last tile) never
         // sweeps S: its P and O rows are never read back, and each row of an
         // MMA is independent of the others.  It still waits for each S before
         // it arrives on p_full, which keeps the barrier phases in step.
         const bool idle = __all_sync(kAll, !row_valid);
-        int j = 0;
-        for (; j < nb; ++j) {
-            if (!__all_sync(kAll, wait_bar(&s_full[tq], static_cast<uint32_t>(j) & 1u, abort_flag, a.err))) break;
-            if (idle) {
-                mbar_arrive(&p_full[tq]);
-                continue;
-            }
-            tc_fence_after();
-            const int k0 = j * kBlockKeys;
-            const bool need_mask = k0 + kBlockKeys > L;  // block-level, so warp-uniform
+        const uint32_t t_s = t_tile + kHalfKeys * hf;         // this half's S columns
+        const uint32_t t_p = t_tile + kColP + kHalfKeys / 2 * hf;  // and P columns (bf16 pairs)
+        const uint32_t t_o = t_tile + kColO + kHeadDim / 2 * hf;   // and O dims
+        // Half-row maxima and sums pass between the halves through shared
+        // memory, double-buffered by block parity, behind a named barrier of
+        // the tile's 256 softmax threads.  Every warp of the tile reaches that
+        // barrier once per block and once after the last, also a warp of
+        // padding rows and a warp that gave up after a timed-out wait (it
+        // goes on without waiting or working), so the counts always match.
+        float* xch = reinterpret_cast<float*>(base + kOffX);
+        auto xslot = [&](int par, int half) { return xch + ((par * kTiles + tq) * kHalves + half) * kRows + r; };
+        const int xbar = 1 + tq;  // named barrier id of the tile
+        bool dead = false;
+        for (int j = 0; j < nb; ++j) {
+            if (!dead && !__all_sync(kAll, wait_bar(&s_full[tq], static_cast<uint32_t>(j) & 1u, abort_flag, a.err)))
+                dead = true;
+            const bool work = !dead && !idle;
+            const int k0 = j * kBlockKeys + kHalfKeys * hf;
+            const bool need_mask = (j + 1) * kBlockKeys > L;  // block-level, so warp-uniform
             float2 sum2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
             float bm = -INFINITY;
-            const bool first = __any_sync(kAll, m == -INFINITY);  // some row has no reference yet
-            if (!first)  // one pass: block maximum and P against the current reference
-                sweep_s(t_tile, t_tile + kColP, k0, need_mask, rm, m, bm, sum2);
-            else
-                bm = row_max(t_tile, k0, need_mask, rm);
-            // raise this row's reference to the block maximum?
-            const bool raise = bm > m + kLazyLog2 || (m == -INFINITY && bm != -INFINITY);
-            if (first || __any_sync(kAll, raise)) {
-                const bool rescale = raise && m != -INFINITY;
-                const float alpha = rescale ? ex2f(m - bm) : 1.f;
-                if (__any_sync(kAll, rescale)) scale_o(t_tile + kColO, alpha);  // O *= alpha (1 for other rows)
-                l *= alpha;
-                if (raise) m = bm;
-                // P again for the whole warp; rows with no visible key yet
-                // have S = -inf everywhere, so mu = 0 gives P = 0
-                tmem_wait_st();
-                sum2[0] = row_exp_to_tmem(t_tile, t_tile + kColP, k0, need_mask, rm, m == -INFINITY ? 0.f : m);
-                sum2[1] = make_float2(0.f, 0.f);
+            bool first = false;
+            if (work) {
+                tc_fence_after();
+                first = __any_sync(kAll, m == -INFINITY);  // some row has no reference yet
+                if (!first)  // one pass: the half's maximum and P against the current reference
+                    sweep_s(t_s, t_p, k0, need_mask, rm, m, bm, sum2);
+                else
+                    bm = row_max(t_s, k0, need_mask, rm);
             }
-            tmem_wait_st();
-            tc_fence_before();
-            mbar_arrive(&p_full[tq]);
+            // the row's block maximum over both halves
+            *xslot(j & 1, hf) = bm;
+            named_bar_sync(xbar, kTileThreads);
+            bm = fmaxf(bm, *xslot(j & 1, hf ^ 1));
+            if (work) {
+                // raise this row's reference to the block maximum?
+                const bool raise = bm > m + kLazyLog2 || (m == -INFINITY && bm != -INFINITY);
+                if (first || __any_sync(kAll, raise)) {
+                    const bool rescale = raise && m != -INFINITY;
+                    const float alpha = rescale ? ex2f(m - bm) : 1.f;
+                    if (__any_sync(kAll, rescale)) scale_o(t_o, alpha);  // O *= alpha (1 for other rows)
+                    l *= alpha;
+                    if (raise) m = bm;
+                    // P again for the whole warp; rows with no visible key yet
+                    // have S = -inf everywhere, so mu = 0 gives P = 0
+                    tmem_wait_st();
+                    sum2[0] = row_exp_to_tmem(t_s, t_p, k0, need_mask, rm, m == -INFINITY ? 0.f : m);
+                    sum2[1] = make_float2(0.f, 0.f);
+                }
+                tmem_wait_st();
+                tc_fence_before();
+            }
+            if (!dead) mbar_arrive(&p_full[tq]);
             const float2 s01 = __fadd2_rn(sum2[0], sum2[1]);
             l += s01.x + s01.y;
         }
-        if (j == nb && !idle &&
+        // the row sum over both halves (slot parity nb & 1: its last readers
+        // passed the barrier of block nb - 1)
+        *xslot(nb & 1, hf) = l;
+        named_bar_sync(xbar, kTileThreads);
+        const float lt = l + *xslot(nb & 1, hf ^ 1);
+        if (!dead && !idle &&
             __all_sync(kAll, wait_bar(&pv_full[tq], static_cast<uint32_t>(nb - 1) & 1u, abort_flag, a.err))) {
             tc_fence_after();
-            const float inv = l > 0.f ? 1.f / l : 0.f;
-            __nv_bfloat16* dst = a.out + (static_cast<size_t>(q0 + t_row) * a.n_q + h * a.group + rg) * kHeadDim;
+            const float inv = lt > 0.f ? 1.f / lt : 0.f;
+            __nv_bfloat16* dst = a.out + (static_cast<size_t>(q0 + t_row) * a.n_q + h * a.group + rg) * kHeadDim +
+                                 kHeadDim / 2 * hf;
             const bool write = row_valid && !*abort_flag;
 #pragma unroll
-            for (int c = 0; c < 4; ++c) {
+            for (int c = 0; c < 2; ++c) {
                 uint32_t x[16];
-                tmem_ld16(t_tile + kColO + 16 * c, x);
+                tmem_ld16(t_o + 16 * c, x);
                 tmem_wait16(x);
                 uint32_t w[8];
 #pragma unroll
