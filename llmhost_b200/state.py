@@ -240,22 +240,35 @@ class KvState:
 
     def forward_batch(self, seqs, tokens, trees, stride: int, masks: bool = True) -> dict:
         """forward() for every sequence in one native call (kv_state_forward_batch):
-        tokens[i] / trees[i] (trees None: chains) of sequence seqs[i].  Returns
-        the flat launch arrays: tok_row, slots, positions, q_offsets, prefix,
-        masks (int64 view; None unless masks), cow_src, cow_dst and tables
-        [n_layers, n_seqs, stride].  A failing sequence raises like forward()
-        with the sequences before it staged."""
+        tokens[i] / trees[i] (trees None: chains) of sequence seqs[i]; drafts of
+        one length may come as [n_seqs, T] arrays.  Returns the flat launch
+        arrays: tok_row, slots, positions, q_offsets, prefix, masks (int64 view;
+        None unless masks), cow_src, cow_dst and tables [n_layers, n_seqs,
+        stride].  A failing sequence raises like forward() with the sequences
+        before it staged."""
         n = len(seqs)
         ids = np.ascontiguousarray(seqs, dtype=np.uint64)
-        lens = np.fromiter((len(t) for t in tokens), np.int64, n)
-        off = np.zeros(n + 1, np.int32)
-        np.cumsum(lens, out=off[1:])
+        if isinstance(tokens, np.ndarray) and tokens.ndim == 2:
+            if tokens.shape[0] != n:
+                raise ValueError("tokens must have one row per sequence")
+            off = np.arange(0, n * tokens.shape[1] + 1, tokens.shape[1], dtype=np.int32)
+            tok = np.ascontiguousarray(tokens.reshape(-1) if tokens.size else np.zeros(1), dtype=np.uint32)
+        else:
+            lens = np.fromiter((len(t) for t in tokens), np.int64, n)
+            off = np.zeros(n + 1, np.int32)
+            np.cumsum(lens, out=off[1:])
+            tok = np.ascontiguousarray(np.concatenate([np.asarray(t, np.uint32) for t in tokens]) if off[-1]
+                                       else np.zeros(1, np.uint32), dtype=np.uint32)
         total = int(off[-1])
-        tok = np.ascontiguousarray(np.concatenate([np.asarray(t, np.uint32) for t in tokens]) if total
-                                   else np.zeros(1, np.uint32), dtype=np.uint32)
         tr = None
         if trees is not None:
-            tr = _i32(np.concatenate([np.asarray(t, np.int32) for t in trees]) if total else np.zeros(1, np.int32))
+            if isinstance(trees, np.ndarray) and trees.ndim == 2:
+                if trees.shape[0] != n or trees.shape[1] != off[1] - off[0] or total != trees.size:
+                    raise ValueError("trees must be [n_seqs, T] like tokens")
+                tr = _i32(trees.reshape(-1) if total else np.zeros(1, np.int32))
+            else:
+                tr = _i32(np.concatenate([np.asarray(t, np.int32) for t in trees]) if total
+                          else np.zeros(1, np.int32))
             if len(tr) < total:
                 raise ValueError("every sequence needs a tree of its token count")
         k = max(total, 1)
@@ -280,14 +293,22 @@ class KvState:
 
     def accept_batch(self, seqs, paths):
         """accept() for every sequence in one native call (kv_state_accept_batch).
-        Returns (token moves [n, 4] int32, group offsets [n_seqs * n_layers + 1]):
-        one group per (sequence, layer), as KvPool.move_tokens takes them."""
+        paths: one accepted path per sequence, or (flat int64 array, offsets
+        [n_seqs + 1]).  Returns (token moves [n, 4] int32, group offsets
+        [n_seqs * n_layers + 1]): one group per (sequence, layer), as
+        KvPool.move_tokens takes them."""
         n = len(seqs)
         ids = np.ascontiguousarray(seqs, dtype=np.uint64)
-        off = np.zeros(n + 1, np.int32)
-        np.cumsum([len(p) for p in paths], out=off[1:])
-        pa = np.ascontiguousarray(np.concatenate([np.asarray(p, np.int64) for p in paths]) if off[-1]
-                                  else np.zeros(1, np.int64), dtype=np.int64)
+        if isinstance(paths, tuple) and len(paths) == 2 and isinstance(paths[0], np.ndarray):
+            off = np.ascontiguousarray(paths[1], dtype=np.int32)
+            if len(off) != n + 1 or off[0] != 0:
+                raise ValueError("path offsets must have n_seqs + 1 entries starting at 0")
+            pa = np.ascontiguousarray(paths[0] if off[-1] else np.zeros(1), dtype=np.int64)
+        else:
+            off = np.zeros(n + 1, np.int32)
+            np.cumsum([len(p) for p in paths], out=off[1:])
+            pa = np.ascontiguousarray(np.concatenate([np.asarray(p, np.int64) for p in paths]) if off[-1]
+                                      else np.zeros(1, np.int64), dtype=np.int64)
         groups = np.empty(n * self.n_layers + 1, np.int32)
         groups[0] = 0
         done, bad, need = c_int32(0), c_int64(0), c_int64(0)

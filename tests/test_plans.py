@@ -186,3 +186,28 @@ def test_chunked_prefill_flops_match_closed_form():
     # 4 d n_q sum_c [C * 512 c + C (C + 1) / 2] per (session, layer)
     per = 4 * 64 * 32 * sum(512 * 512 * c + 512 * 513 / 2 for c in range(32))
     assert abs(wl.total_flops() - per * 16 * 6) < 1e3
+
+
+def test_batched_calls_take_arrays_like_lists():
+    a, b = _two_states()
+    for st in (a, b):
+        for s in (0, 1, 2):
+            st.open(s)
+            st.append(s, 20 + 9 * s)
+    rng = np.random.default_rng(7)
+    trees = [draft_tree(rng, 12)[0] for _ in range(3)]
+    toks = [list(range(50 + 12 * i, 62 + 12 * i)) for i in range(3)]
+    fa = a.forward_batch([0, 1, 2], toks, trees, stride=16)
+    fb = b.forward_batch([0, 1, 2], np.array(toks, np.int64), np.array(trees, np.int32), stride=16)
+    for k in fa:
+        np.testing.assert_array_equal(fa[k], fb[k], err_msg=k)
+    paths = [[0, 1], [0], [0, 2]]
+    flat = np.array([0, 1, 0, 0, 2], np.int64)
+    off = np.array([0, 2, 3, 5], np.int32)
+    ma, ga, na = commit_moves(a, [0, 1, 2], paths)
+    mb, gb, nb = commit_moves(b, [0, 1, 2], (flat, off))
+    np.testing.assert_array_equal(ma, mb)
+    np.testing.assert_array_equal(ga, gb)
+    assert na == nb == 5
+    for s in (0, 1, 2):
+        assert a.committed(s) == b.committed(s)
