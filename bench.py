@@ -1349,6 +1349,9 @@ def main():
         import torch.distributed as dist
 
         torch.cuda.set_device(local_rank)
+        # NCCL logs (its version line included) to stdout by default; stdout
+        # carries the one JSON result line, so send them to stderr
+        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local_rank))
     try:
