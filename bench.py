@@ -33,6 +33,28 @@ from pathlib import Path
 
 import numpy as np
 
+# NCCL's log lines go to stderr unless the caller chose a file (read when NCCL
+# first initialises, which importing torch.distributed can trigger)
+os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
+
+
+class _stdout_to_stderr:
+    """File descriptor 1 redirected to descriptor 2 for the duration (output
+    written by native code included)."""
+
+    def __enter__(self):
+        sys.stdout.flush()
+        self.saved = os.dup(1)
+        os.dup2(2, 1)
+        return self
+
+    def __exit__(self, *exc):
+        sys.stdout.flush()
+        os.dup2(self.saved, 1)
+        os.close(self.saved)
+        return False
+
+
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
@@ -1349,11 +1371,13 @@ def main():
         import torch.distributed as dist
 
         torch.cuda.set_device(local_rank)
-        # NCCL logs (its version line included) to stdout by default; stdout
-        # carries the one JSON result line, so send them to stderr
-        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
-                                device_id=torch.device("cuda", local_rank))
+        # NCCL may print (its version line, at communicator set-up) on file
+        # descriptor 1, which carries the one JSON result line: set the group
+        # and its communicator up with descriptor 1 pointing at stderr
+        with _stdout_to_stderr():
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                    device_id=torch.device("cuda", local_rank))
+            dist.barrier()
     try:
         if args.workload == "decode":
             run_ours(args, rank, world, local_rank)
