@@ -199,3 +199,14 @@ def test_prefill_chunk_longer_than_max_q_is_flagged(cuda, dtype):
         case.run_gpu(pool, max_q=10)
         assert pool.last_error() == 1  # KV_ERR_INVALID
         assert pool.last_error() == 0  # the word was cleared
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("n_q,n_kv", [(8, 2), (16, 4)])
+def test_prefill_kv_head_shards(cuda, n_q, n_kv, dtype):
+    # the per-GPU shapes of a KV-head-sharded session (group 4 over 2 and 4
+    # kv heads): causal chunks and trees
+    rng = np.random.default_rng(40 + n_q + n_kv)
+    tree = [-1] + [int(rng.integers(0, i)) for i in range(1, 30)]
+    check(PrefillCase(n_q, n_kv, [(0, 7), (130, 200), (17, 64)], seed=31, dtype=dtype), f"{dtype} {n_q}q/{n_kv}kv causal")
+    check(PrefillCase(n_q, n_kv, [(40, tree), (0, [-1, 0, 0, 1])], seed=32, dtype=dtype), f"{dtype} {n_q}q/{n_kv}kv tree")
