@@ -38,6 +38,13 @@
 // it by more than kLazyLog2.  P is stored as bf16 and the row sums add the
 // same rounded values.  Every wait is bounded; a timeout sets the error word
 // and an abort flag, and the CTA runs its schedule out without work.
+//
+// Work split: every sequence's stages (one per head pair of each 8-page
+// chunk), each sequence's list led by kLead stages that stand for the cost of
+// opening it, are laid end to end and cut into equal slices, one per CTA of
+// the persistent grid.  The kernel is launched with programmatic stream
+// serialization: it reads nothing global before griddepcontrol.wait, and lets
+// the next launch start on the SMs it has left.
 #include <cmath>
 
 #include "kv_common.cuh"
