@@ -65,7 +65,8 @@ class ForwardBatch:
 
 def plan_forward(st: KvState, seqs, tokens, parents, stride: int) -> ForwardBatch:
     """KvState.forward for every session (tokens[i], parents[i]), flattened;
-    one native call (kv_state_forward_batch)."""
+    one native call (kv_state_forward_batch).  Drafts of one length may come
+    as [n, T] arrays."""
     f = st.forward_batch(seqs, tokens, parents, stride)
     qoff = f["q_offsets"]
     return ForwardBatch(list(seqs), f["cow_src"], f["cow_dst"], f["tok_row"], f["slots"], f["positions"], qoff,
@@ -74,8 +75,9 @@ def plan_forward(st: KvState, seqs, tokens, parents, stride: int) -> ForwardBatc
 
 def commit_moves(st: KvState, seqs, paths):
     """KvState.accept for every session; the page-addressed token moves of all
-    sessions and layers, one group per (session, layer), and group offsets
-    (one native call, kv_state_accept_batch)."""
+    sessions and layers, one group per (session, layer), group offsets and the
+    number of accepted tokens (one native call, kv_state_accept_batch).  paths:
+    one accepted path per session, or (flat int64 array, offsets [n + 1])."""
     mv, offs = st.accept_batch(seqs, paths)
     accepted = int(paths[1][-1]) if isinstance(paths, tuple) else sum(len(p) for p in paths)
     return mv, offs, accepted
