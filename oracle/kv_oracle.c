@@ -145,42 +145,77 @@ void orc_attention_decode_cached(const float *q, const float *k_cache, const flo
     }
 }
 
-/* Shared body of attention_forward (lfm2.rs:1058-1111): the masked predicate
- * is `(causal && s > t) || !key_valid[s]` there, `!mask[t*kv_len+s]` here. */
-static void attention_rows(const float *q, const float *k, const float *v, size_t n_q,
-                           size_t n_kv, size_t q_len, size_t kv_len, size_t dim, int causal,
-                           const uint8_t *key_valid, const uint8_t *mask, float *out) {
+/* Which (query t, key s) pairs are masked.  EXPLICIT: !mask[t*kv_len+s];
+ * FORWARD: lfm2.rs:1083 `(causal && s > t) || !key_valid[s]`; PREFIX: the
+ * build's chunk after `prefix` cached keys (every cached key visible; chunk
+ * key j = s - prefix visible when j <= t, or when bit j of bits[t] is set). */
+enum { MASK_EXPLICIT, MASK_FORWARD, MASK_PREFIX };
+typedef struct {
+    int kind;
+    const uint8_t *mask;      /* EXPLICIT */
+    int causal;               /* FORWARD */
+    const uint8_t *key_valid; /* FORWARD, may be NULL */
+    size_t prefix;            /* PREFIX */
+    const uint64_t *bits;     /* PREFIX: NULL = causal chunk */
+} mask_desc;
+
+static inline int is_masked(const mask_desc *m, size_t kv_len, size_t t, size_t s) {
+    switch (m->kind) {
+    case MASK_EXPLICIT:
+        return !m->mask[t * kv_len + s];
+    case MASK_FORWARD:
+        return (m->causal && s > t) || (m->key_valid && !m->key_valid[s]);
+    default:
+        if (s < m->prefix) return 0;
+        return m->bits ? !((m->bits[t] >> (s - m->prefix)) & 1u) : (s - m->prefix > t);
+    }
+}
+
+/* One query head of attention_forward (lfm2.rs:1058-1111): q rows [q_len][dim],
+ * the head's K and V [kv_len][dim], scores [q_len * kv_len] scratch; output row
+ * t goes to out + t * out_stride.  Heads are independent in the reference's
+ * loop, so running them one at a time gives the same bits. */
+static void attention_one_head(const float *q, const float *k, const float *v, size_t q_len,
+                               size_t kv_len, size_t dim, const mask_desc *m, float *scores,
+                               float *out, size_t out_stride) {
     float scale = 1.0f / sqrtf((float)dim);
+    for (size_t t = 0; t < q_len; t++) {
+        const float *qv = q + t * dim;
+        for (size_t s = 0; s < kv_len; s++) {
+            if (is_masked(m, kv_len, t, s)) {
+                scores[t * kv_len + s] = -INFINITY;
+                continue;
+            }
+            const float *kv = k + s * dim;
+            float acc = 0.0f;
+            for (size_t d = 0; d < dim; d++) acc = fmaf(qv[d], kv[d], acc);
+            scores[t * kv_len + s] = acc * scale;
+        }
+    }
+    orc_softmax_last_axis(scores, q_len * kv_len, kv_len);
+    for (size_t t = 0; t < q_len; t++) {
+        float *dst = out + t * out_stride;
+        memset(dst, 0, dim * sizeof(float));
+        for (size_t s = 0; s < kv_len; s++) {
+            float w = scores[t * kv_len + s];
+            if (w == 0.0f) continue;
+            const float *vv = v + s * dim;
+            for (size_t d = 0; d < dim; d++) dst[d] = fmaf(w, vv[d], dst[d]);
+        }
+    }
+}
+
+/* Shared body of attention_forward (lfm2.rs:1058-1111) and attention_masked:
+ * q [n_q, q_len, dim], k/v [n_kv, kv_len, dim], out [n_q, q_len, dim]. */
+static void attention_rows(const float *q, const float *k, const float *v, size_t n_q,
+                           size_t n_kv, size_t q_len, size_t kv_len, size_t dim, const mask_desc *m,
+                           float *out) {
     size_t n_rep = n_q / n_kv;
-    memset(out, 0, n_q * q_len * dim * sizeof(float));
     float *scores = (float *)malloc((q_len * kv_len + 1) * sizeof(float));
     for (size_t qh = 0; qh < n_q; qh++) {
         size_t kv_h = qh / n_rep;
-        for (size_t t = 0; t < q_len; t++) {
-            const float *qv = q + (qh * q_len + t) * dim;
-            for (size_t s = 0; s < kv_len; s++) {
-                int masked = mask ? !mask[t * kv_len + s]
-                                  : ((causal && s > t) || (key_valid && !key_valid[s]));
-                if (masked) {
-                    scores[t * kv_len + s] = -INFINITY;
-                    continue;
-                }
-                const float *kv = k + (kv_h * kv_len + s) * dim;
-                float acc = 0.0f;
-                for (size_t d = 0; d < dim; d++) acc = fmaf(qv[d], kv[d], acc);
-                scores[t * kv_len + s] = acc * scale;
-            }
-        }
-        orc_softmax_last_axis(scores, q_len * kv_len, kv_len);
-        for (size_t t = 0; t < q_len; t++) {
-            float *dst = out + (qh * q_len + t) * dim;
-            for (size_t s = 0; s < kv_len; s++) {
-                float w = scores[t * kv_len + s];
-                if (w == 0.0f) continue;
-                const float *vv = v + (kv_h * kv_len + s) * dim;
-                for (size_t d = 0; d < dim; d++) dst[d] = fmaf(w, vv[d], dst[d]);
-            }
-        }
+        attention_one_head(q + qh * q_len * dim, k + kv_h * kv_len * dim, v + kv_h * kv_len * dim, q_len,
+                           kv_len, dim, m, scores, out + qh * q_len * dim, dim);
     }
     free(scores);
 }
@@ -189,13 +224,15 @@ static void attention_rows(const float *q, const float *k, const float *v, size_
 void orc_attention_forward(const float *q, const float *k, const float *v, size_t n_q,
                            size_t n_kv, size_t q_len, size_t kv_len, size_t dim, int causal,
                            const uint8_t *key_valid, float *out) {
-    attention_rows(q, k, v, n_q, n_kv, q_len, kv_len, dim, causal, key_valid, NULL, out);
+    mask_desc m = {MASK_FORWARD, NULL, causal, key_valid, 0, NULL};
+    attention_rows(q, k, v, n_q, n_kv, q_len, kv_len, dim, &m, out);
 }
 
 void orc_attention_masked(const float *q, const float *k, const float *v, size_t n_q,
                           size_t n_kv, size_t q_len, size_t kv_len, size_t dim,
                           const uint8_t *mask, float *out) {
-    attention_rows(q, k, v, n_q, n_kv, q_len, kv_len, dim, 0, NULL, mask, out);
+    mask_desc m = {MASK_EXPLICIT, mask, 0, NULL, 0, NULL};
+    attention_rows(q, k, v, n_q, n_kv, q_len, kv_len, dim, &m, out);
 }
 
 /* ---- paged layout (build-defined) ---------------------------------------- */
@@ -261,15 +298,19 @@ void orc_paged_append_token(void *pages, int dtype, size_t n_kv, size_t P, size_
     append_token_impl(pages, dtype, n_kv, P, d, bt, slot, k_raw, v, cos_row, sin_row, NULL, 0.f);
 }
 
-void orc_paged_gather(const void *pages, int dtype, size_t n_kv, size_t P, size_t d,
-                      const uint32_t *bt, size_t n_tokens, float *k_out, float *v_out) {
+/* Tokens [t0, t1) of KV heads [h0, h1) of one sequence into fp32
+ * [h1 - h0, t1 - t0, d]; pages marked ORC_PAGE_NONE read as zero. */
+static void gather_range(const void *pages, int dtype, size_t n_kv, size_t P, size_t d,
+                         const uint32_t *bt, size_t t0, size_t t1, size_t h0, size_t h1,
+                         float *k_out, float *v_out) {
     size_t page_elems = 2 * n_kv * P * d;
-    for (size_t t = 0; t < n_tokens; t++) {
+    size_t n_tokens = t1 - t0;
+    for (size_t t = t0; t < t1; t++) {
         uint32_t page = bt[t / P];
         size_t j = t % P;
-        for (size_t h = 0; h < n_kv; h++) {
-            float *kd = k_out + (h * n_tokens + t) * d;
-            float *vd = v_out + (h * n_tokens + t) * d;
+        for (size_t h = h0; h < h1; h++) {
+            float *kd = k_out + ((h - h0) * n_tokens + (t - t0)) * d;
+            float *vd = v_out + ((h - h0) * n_tokens + (t - t0)) * d;
             if (page == ORC_PAGE_NONE) {
                 memset(kd, 0, d * sizeof(float));
                 memset(vd, 0, d * sizeof(float));
@@ -285,6 +326,11 @@ void orc_paged_gather(const void *pages, int dtype, size_t n_kv, size_t P, size_
     }
 }
 
+void orc_paged_gather(const void *pages, int dtype, size_t n_kv, size_t P, size_t d,
+                      const uint32_t *bt, size_t n_tokens, float *k_out, float *v_out) {
+    gather_range(pages, dtype, n_kv, P, d, bt, 0, n_tokens, 0, n_kv, k_out, v_out);
+}
+
 /* q_norm non-NULL: lfm2.rs:797-804 rms_norm_heads on q (heads = n_q) first. */
 static void paged_decode_impl(const void *pages, int dtype, size_t n_q, size_t n_kv, size_t P, size_t d,
                               const uint32_t *bt, size_t seq_len, size_t window, const void *q_raw,
@@ -293,25 +339,27 @@ static void paged_decode_impl(const void *pages, int dtype, size_t n_q, size_t n
         memset(out, 0, n_q * d * sizeof(float));
         return;
     }
-    float *k = (float *)malloc(n_kv * seq_len * d * sizeof(float));
-    float *v = (float *)malloc(n_kv * seq_len * d * sizeof(float));
+    /* Keys below the window are masked (score -inf).  In attention_decode_cached
+     * such a key leaves the max fold unchanged (fmaxf(m, -inf) = m), adds
+     * expf(-inf) = +0 to the sum (x + 0 = x for the non-negative partial sums)
+     * and is skipped by the PV loop (w == 0), so attending over the keys
+     * [lo, seq_len) alone, in the same order, gives the same bits as the
+     * masked row.  The gather then never touches evicted pages, and a 128k-token
+     * session under a 32k window costs a quarter of the work. */
+    size_t lo = (window > 0 && seq_len > window) ? seq_len - window : 0;
+    size_t n_att = seq_len - lo;
+    float *k = (float *)malloc(n_kv * n_att * d * sizeof(float));
+    float *v = (float *)malloc(n_kv * n_att * d * sizeof(float));
     float *q = (float *)malloc(n_q * d * sizeof(float));
     float *cs = (float *)malloc(2 * d * sizeof(float));
-    float *scores = (float *)malloc(n_q * seq_len * sizeof(float));
-    uint8_t *valid = NULL;
-    orc_paged_gather(pages, dtype, n_kv, P, d, bt, seq_len, k, v);
+    float *scores = (float *)malloc(n_q * n_att * sizeof(float));
+    gather_range(pages, dtype, n_kv, P, d, bt, lo, seq_len, 0, n_kv, k, v);
     for (size_t i = 0; i < n_q * d; i++) q[i] = load_elem(q_raw, dtype, i);
     if (q_norm) orc_rms_norm(q, q_norm, eps, d, n_q, q);
     /* lfm2.rs:816-822: cos_sin at pos, RoPE on q with heads = n_q, tokens = 1 */
     orc_cos_sin(inv_freq, seq_len - 1, 1, d, cs, cs + d);
     orc_apply_rope_in_place(q, cs, cs + d, n_q, 1, d);
-    if (window > 0 && seq_len > window) {
-        valid = (uint8_t *)malloc(seq_len);
-        for (size_t s = 0; s < seq_len; s++) valid[s] = (s + window >= seq_len);
-    }
-    orc_attention_decode_cached(q, k, v, n_q, n_kv, seq_len, seq_len, d, valid,
-                                valid ? seq_len : 0, scores, out);
-    free(valid);
+    orc_attention_decode_cached(q, k, v, n_q, n_kv, n_att, n_att, d, NULL, 0, scores, out);
     free(scores);
     free(cs);
     free(q);
@@ -399,6 +447,124 @@ static void run_steps(step_job *j, int n_threads) {
     for (int i = 0; i < nt; i++) pthread_create(&th[i], NULL, step_worker, j);
     for (int i = 0; i < nt; i++) pthread_join(th[i], NULL);
     free(th);
+}
+
+/* ---- bulk helpers for large parity cases -------------------------------- */
+
+/* Run fn(ctx, i) for i in [0, n) on nt POSIX threads (dynamic assignment). */
+typedef struct {
+    void (*fn)(void *, size_t);
+    void *ctx;
+    size_t n;
+    atomic_long next;
+} par_job;
+
+static void *par_worker(void *arg) {
+    par_job *j = (par_job *)arg;
+    for (;;) {
+        long i = atomic_fetch_add(&j->next, 1);
+        if (i >= (long)j->n) break;
+        j->fn(j->ctx, (size_t)i);
+    }
+    return NULL;
+}
+
+static void par_for(size_t n, int n_threads, void (*fn)(void *, size_t), void *ctx) {
+    int nt = n_threads > 0 ? n_threads : orc_max_threads();
+    if ((size_t)nt > n) nt = (int)n;
+    if (nt <= 1) {
+        for (size_t i = 0; i < n; i++) fn(ctx, i);
+        return;
+    }
+    par_job j = {fn, ctx, n, 0};
+    pthread_t *th = (pthread_t *)malloc((size_t)nt * sizeof(pthread_t));
+    for (int i = 0; i < nt; i++) pthread_create(&th[i], NULL, par_worker, &j);
+    for (int i = 0; i < nt; i++) pthread_join(th[i], NULL);
+    free(th);
+}
+
+typedef struct {
+    void *pages;
+    int dtype;
+    size_t n_kv, P, d, bt_stride;
+    const uint32_t *bt;
+    const int32_t *tok_row, *tok_slot, *tok_pos;
+    const void *k_raw, *v;
+    const float *inv_freq;
+} append_bulk;
+
+static void append_bulk_one(void *arg, size_t i) {
+    const append_bulk *a = (const append_bulk *)arg;
+    size_t esz = a->dtype == ORC_BF16 ? 2 : 4;
+    float cs[2 * 256];
+    orc_cos_sin(a->inv_freq, (size_t)a->tok_pos[i], 1, a->d, cs, cs + a->d);
+    append_token_impl(a->pages, a->dtype, a->n_kv, a->P, a->d, a->bt + (size_t)a->tok_row[i] * a->bt_stride,
+                      (size_t)a->tok_slot[i], (const char *)a->k_raw + i * a->n_kv * a->d * esz,
+                      (const char *)a->v + i * a->n_kv * a->d * esz, cs, cs + a->d, NULL, 0.f);
+}
+
+void orc_paged_append_tokens(void *pages, int dtype, size_t n_kv, size_t P, size_t d, const uint32_t *bt,
+                             size_t bt_stride, const int32_t *tok_row, const int32_t *tok_slot,
+                             const int32_t *tok_pos, size_t n_tokens, const void *k_raw, const void *v,
+                             const float *inv_freq, int n_threads) {
+    append_bulk a = {pages, dtype, n_kv, P, d, bt_stride, bt, tok_row, tok_slot, tok_pos, k_raw, v, inv_freq};
+    par_for(n_tokens, n_threads, append_bulk_one, &a);
+}
+
+typedef struct {
+    const void *pages;
+    int dtype;
+    size_t n_q, n_kv, P, d, bt_stride;
+    const uint32_t *bt;
+    const int32_t *cached, *q_off, *q_pos;
+    const uint64_t *masks;
+    const void *q_raw;
+    const float *inv_freq;
+    float *out;
+} prefill_bulk;
+
+/* One (sequence, KV head) of orc_paged_prefill: the head's K/V gathered once,
+ * then each of its query heads through attention_one_head. */
+static void prefill_one(void *arg, size_t job) {
+    const prefill_bulk *a = (const prefill_bulk *)arg;
+    size_t s = job / a->n_kv, kh = job % a->n_kv;
+    size_t L = (size_t)a->cached[s];
+    size_t q0 = (size_t)a->q_off[s], T = (size_t)a->q_off[s + 1] - q0;
+    if (T == 0) return;
+    size_t n = L + T, d = a->d, g = a->n_q / a->n_kv;
+    float *kh_rows = (float *)malloc(n * d * sizeof(float));
+    float *vh_rows = (float *)malloc(n * d * sizeof(float));
+    float *q = (float *)malloc(T * d * sizeof(float));
+    float *scores = (float *)malloc(T * n * sizeof(float));
+    float cs[2 * 256];
+    gather_range(a->pages, a->dtype, a->n_kv, a->P, d, a->bt + s * a->bt_stride, 0, n, kh, kh + 1, kh_rows,
+                 vh_rows);
+    mask_desc m = {MASK_PREFIX, NULL, 0, NULL, L, a->masks ? a->masks + q0 : NULL};
+    for (size_t qh = kh * g; qh < (kh + 1) * g; qh++) {
+        for (size_t t = 0; t < T; t++) {
+            const void *src = a->q_raw;
+            size_t base = ((q0 + t) * a->n_q + qh) * d;
+            for (size_t e = 0; e < d; e++) q[t * d + e] = load_elem(src, a->dtype, base + e);
+            /* RoPE of one token's head at its position (rope.rs:56-81, heads = tokens = 1) */
+            orc_cos_sin(a->inv_freq, (size_t)a->q_pos[q0 + t], 1, d, cs, cs + d);
+            orc_apply_rope_in_place(q + t * d, cs, cs + d, 1, 1, d);
+        }
+        attention_one_head(q, kh_rows, vh_rows, T, n, d, &m, scores,
+                           a->out + (q0 * a->n_q + qh) * d, a->n_q * d);
+    }
+    free(scores);
+    free(q);
+    free(vh_rows);
+    free(kh_rows);
+}
+
+void orc_paged_prefill(const void *pages, int dtype, size_t n_q, size_t n_kv, size_t P, size_t d,
+                       const uint32_t *bt, size_t bt_stride, size_t n_seqs, const int32_t *cached,
+                       const int32_t *q_off, const int32_t *q_pos, const uint64_t *masks, const void *q_raw,
+                       const float *inv_freq, float *out, int n_threads) {
+    prefill_bulk a = {pages, dtype, n_q, n_kv, P, d, bt_stride, bt, cached, q_off, q_pos, masks, q_raw,
+                      inv_freq, out};
+    par_for(n_seqs * n_kv, n_threads, prefill_one, &a);
 }
 
 int orc_max_threads(void) {

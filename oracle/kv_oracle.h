@@ -93,7 +93,8 @@ void orc_paged_gather(const void *pages, int dtype, size_t n_kv, size_t P, size_
 /* Decode attention of one sequence holding seq_len tokens (the new token is
  * already appended).  q_raw [n_q, d] in dtype, rotated at pos seq_len - 1.
  * window == 0: all keys; else keys s < seq_len - window are masked out (the
- * build's sliding window).  out [n_q, d] fp32. */
+ * build's sliding window; masked keys contribute exact zeros, so only the
+ * window's keys are gathered and attended).  out [n_q, d] fp32. */
 void orc_paged_decode(const void *pages, int dtype, size_t n_q, size_t n_kv, size_t P,
                       size_t d, const uint32_t *bt, size_t seq_len, size_t window,
                       const void *q_raw, const float *inv_freq, float *out);
@@ -122,6 +123,30 @@ void orc_decode_step_norm(void *pages, int dtype, size_t n_q, size_t n_kv, size_
                           size_t n_seqs, size_t window, const void *q_raw, const void *k_raw,
                           const void *v, const float *inv_freq, const float *q_norm,
                           const float *k_norm, float eps, float *out, int n_threads);
+
+/* ---- bulk helpers for large parity cases (same arithmetic as above) ------ */
+
+/* n_tokens calls of orc_paged_append_token: token i goes to row tok_row[i] of
+ * bt ([rows, bt_stride]), slot tok_slot[i], rotated at position tok_pos[i];
+ * k_raw / v are [n_tokens, n_kv, d].  Tokens must write distinct slots; they
+ * are spread over n_threads threads (0 = one per online CPU). */
+void orc_paged_append_tokens(void *pages, int dtype, size_t n_kv, size_t P, size_t d, const uint32_t *bt,
+                             size_t bt_stride, const int32_t *tok_row, const int32_t *tok_slot,
+                             const int32_t *tok_pos, size_t n_tokens, const void *k_raw, const void *v,
+                             const float *inv_freq, int n_threads);
+
+/* Chunked-prefill / tree-verify attention on paged K/V, the arithmetic of
+ * attention_forward (lfm2.rs:1058-1111) with the build's masks: sequence s
+ * has cached[s] committed tokens followed by the chunk's q_off[s+1] - q_off[s]
+ * tokens (row s of bt).  Query token i (global index) is rotated at q_pos[i]
+ * and sees every cached key, plus chunk key j when j <= its index in the chunk
+ * (masks == NULL) or when bit j of masks[i] is set (ancestor-or-self).
+ * q_raw [n_tok, n_q, d] in dtype; out [n_tok, n_q, d] fp32.  Work is spread
+ * over (sequence, KV head) pairs on n_threads threads. */
+void orc_paged_prefill(const void *pages, int dtype, size_t n_q, size_t n_kv, size_t P, size_t d,
+                       const uint32_t *bt, size_t bt_stride, size_t n_seqs, const int32_t *cached,
+                       const int32_t *q_off, const int32_t *q_pos, const uint64_t *masks, const void *q_raw,
+                       const float *inv_freq, float *out, int n_threads);
 
 #ifdef __cplusplus
 }

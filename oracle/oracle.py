@@ -66,6 +66,12 @@ def lib() -> ctypes.CDLL:
                                            c_void_p, c_size_t, c_void_p, c_size_t, c_size_t, c_void_p,
                                            c_void_p, c_void_p, fp, fp, fp, c_float, fp, c_int]
         h.orc_rms_norm.argtypes = [fp, fp, c_float, c_size_t, c_size_t, fp]
+        h.orc_paged_append_tokens.argtypes = [c_void_p, c_int, c_size_t, c_size_t, c_size_t, c_void_p,
+                                              c_size_t, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p,
+                                              c_void_p, fp, c_int]
+        h.orc_paged_prefill.argtypes = [c_void_p, c_int, c_size_t, c_size_t, c_size_t, c_size_t, c_void_p,
+                                        c_size_t, c_size_t, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                        fp, fp, c_int]
         h.orc_max_threads.restype = c_int
         _lib = h
     return _lib
@@ -171,6 +177,42 @@ class HostPages:
         lib().orc_paged_append_token(self.data.ctypes.data, self.dtype, self.n_kv, self.P, self.d,
                                      bt.ctypes.data, slot, k_raw.ctypes.data, v.ctypes.data,
                                      _f(c), _f(s))
+
+    def append_tokens(self, bt2d, tok_row, slots, positions, k_raw, v, n_threads: int = 0) -> None:
+        """Many append_token calls in one (orc_paged_append_tokens): token i to
+        row tok_row[i] of bt2d, slot slots[i], RoPE position positions[i];
+        k_raw / v are [n_tokens, n_kv, d].  Slots must be distinct."""
+        bt2d = np.ascontiguousarray(bt2d, np.uint32)
+        if bt2d.ndim == 1:
+            bt2d = bt2d[None, :]
+        tok_row, slots, positions = (np.ascontiguousarray(a, np.int32) for a in (tok_row, slots, positions))
+        n = len(slots)
+        assert len(tok_row) == n and len(positions) == n
+        k_raw, v = self._raw(k_raw), self._raw(v)
+        assert k_raw.size == n * self.n_kv * self.d and v.size == k_raw.size
+        if n == 0:
+            return
+        lib().orc_paged_append_tokens(self.data.ctypes.data, self.dtype, self.n_kv, self.P, self.d,
+                                      bt2d.ctypes.data, bt2d.shape[1], tok_row.ctypes.data, slots.ctypes.data,
+                                      positions.ctypes.data, n, k_raw.ctypes.data, v.ctypes.data, _f(self.inv),
+                                      n_threads)
+
+    def prefill(self, bt2d, cached, q_off, q_pos, q_raw, masks=None, n_threads: int = 0) -> np.ndarray:
+        """Chunked-prefill (masks None: causal chunk) or tree-verify (masks:
+        ancestor-or-self bits per query token) attention over the stored pages
+        (orc_paged_prefill).  Returns [n_tok, n_q, d] float32."""
+        bt2d = np.ascontiguousarray(bt2d, np.uint32)
+        cached, q_off, q_pos = (np.ascontiguousarray(a, np.int32) for a in (cached, q_off, q_pos))
+        q_raw = self._raw(q_raw)
+        n_tok = int(q_off[-1])
+        assert len(q_pos) == n_tok and q_raw.size == n_tok * self.n_q * self.d
+        m = None if masks is None else np.ascontiguousarray(np.asarray(masks).view(np.uint64))
+        out = np.zeros((n_tok, self.n_q, self.d), np.float32)
+        lib().orc_paged_prefill(self.data.ctypes.data, self.dtype, self.n_q, self.n_kv, self.P, self.d,
+                                bt2d.ctypes.data, bt2d.shape[1], len(cached), cached.ctypes.data,
+                                q_off.ctypes.data, q_pos.ctypes.data, _p(m), q_raw.ctypes.data, _f(self.inv),
+                                _f(out), n_threads)
+        return out
 
     def gather(self, bt, n_tokens: int):
         bt = np.ascontiguousarray(bt, np.uint32)
