@@ -108,10 +108,21 @@ def allocate_in_order(l0: np.ndarray, steps: int, n_layers: int, order: np.ndarr
 
 def decode_config(steps: int = 512, seed: int = 1, n_seqs: int = 64, pool_pages: int = 1 << 20,
                   lo: int = 128, hi: int = 8192, dtype: str = "bf16", n_q: int = 24, n_kv: int = 8,
-                  n_layers: int = 6, window: int = 0) -> DecodeWorkload:
-    """The batched-decode configuration (defaults) or a scaled variant of it."""
+                  n_layers: int = 6, window: int = 0, world: int = 1, rank: int = 0) -> DecodeWorkload:
+    """The batched-decode configuration (defaults) or a scaled variant of it.
+
+    With world > 1 the lengths of n_seqs * world sessions are drawn at once
+    and split into world shares by LPT on their cached length (the bytes a
+    step reads); this returns share `rank`.  world = 1 is the configuration
+    itself.  Every share draws its pages from the same permutation of its own
+    pool."""
     rng = np.random.default_rng(seed)
-    l0 = rng.integers(lo, hi, endpoint=True, size=n_seqs).astype(np.int64)
+    lengths = rng.integers(lo, hi, endpoint=True, size=n_seqs * world).astype(np.int64)
+    if world > 1:
+        share = lpt_partition(lengths.tolist(), world)[rank]
+        l0 = lengths[share]
+    else:
+        l0 = lengths
     order = rng.permutation(pool_pages).astype(np.uint32)
     bt = allocate_in_order(l0, steps, n_layers, order)
     return DecodeWorkload("bf16 batched decode" if dtype == "bf16" else "f32 batched decode",
@@ -123,8 +134,9 @@ def normal_bits(rng: np.random.Generator, shape, dtype: str) -> np.ndarray:
     x = rng.standard_normal(shape, dtype=np.float32)
     if dtype == "f32":
         return x
-    u = x.view(np.uint32).astype(np.uint64)
-    return ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+    # finite draws stay below 0xFF800000, so the 32-bit sum cannot wrap
+    u = x.view(np.uint32)
+    return ((u + np.uint32(0x7FFF) + ((u >> np.uint32(16)) & np.uint32(1))) >> np.uint32(16)).astype(np.uint16)
 
 
 # ---- fp32 single session --------------------------------------------------------------
