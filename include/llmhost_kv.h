@@ -311,7 +311,7 @@ int kv_state_pending_base(const kv_state *st, uint64_t seq_id, int64_t *base);
 
 /* Decode attention for callers that cannot allocate device memory.
  *
- * No counterpart in the reference.  Same arithmetic and arguments as
+ * No counterpart in the reference.  The arguments and results of
  * kv_decode_attn, but without a pool: some callers cannot call cudaMalloc
  * (their device memory all comes from a fixed arena they manage, or they may
  * not grow their footprint after start-up), so they cannot create a kv_pool.
@@ -323,6 +323,14 @@ int kv_state_pending_base(const kv_state *st, uint64_t seq_id, int64_t *base);
  * error bits of this call (1 bad page id, 2 wait timeout, 4 position out of
  * range; 0 when clean).
  *
+ * Kernel: both dtypes run the CUDA-core decode kernel (kv_decode_attn runs
+ * it for fp32 pools only; its bf16 pools use the tensor-core kernel, which
+ * rounds the probabilities to bf16 before P·V).  So fp32 results equal
+ * kv_decode_attn's, and bf16 results differ from them by rounding, within
+ * the bf16 tolerance (2e-2 normwise per row) of the reference arithmetic.
+ * Head layouts: (n_kv_heads, n_q_heads / n_kv_heads) = (8, 3), (8, 4), (1, 4),
+ * (2, 4), (4, 4); others return KV_ERR_UNSUPPORTED.
+ *
  * The call itself allocates nothing.  Its scratch is one 4 MiB array in the
  * library's device image, held by every GPU that loads the library until
  * exit.  Limits: n_seqs <= 1024 and n_q_heads <= 32; larger calls return
@@ -330,7 +338,10 @@ int kv_state_pending_base(const kv_state *st, uint64_t seq_id, int64_t *base);
  * part that must start at zero, but two calls whose kernels overlap on the
  * GPU (different streams or threads) race on it, so serialise them.  The
  * first call on a device sets up with that device current (it looks up the
- * array's address); make that first call before any stream capture. */
+ * array's address); make that first call before any stream capture.  The
+ * address is kept for the life of the process, so a device reset
+ * (cudaDeviceReset, or a reset of the primary context) after the first call
+ * on that device is not supported. */
 int kv_decode_attn_noalloc(const void *pages, uint32_t n_pages, int32_t dtype, int32_t n_q_heads,
                            int32_t n_kv_heads, const void *rope_cs, int32_t max_positions,
                            const void *q, const uint32_t *block_tables, int32_t bt_stride,

@@ -24,7 +24,11 @@
 // Set-up: the first call on a device, with that device current, looks up
 // the array's device address (cudaGetSymbolAddress), the SM count and the
 // kernel's launch shape; later calls reuse them.  Make that first call
-// before any stream capture begins.
+// before any stream capture begins.  The address is kept until the process
+// exits, so a device reset after the first call is not supported.
+//
+// Kernel: the CUDA-core decode kernel for both dtypes (kv_decode_attn runs
+// the tensor-core kernel for bf16 pools), through its raw launch interface.
 #include <cudaTypedefs.h>
 
 #include <mutex>
@@ -61,8 +65,18 @@ struct DeviceSetup {
 
 std::mutex g_mu;
 DeviceSetup g_dev[kMaxDevices];
+// The driver's tensor-map encoder; looked up once, under g_mu.
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 
 int setup_device(int dev, DeviceSetup& d) {
+    if (!g_encode) {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess || !fn)
+            return KV_ERR_CUDA;
+        g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    }
     void* ptr = nullptr;
     if (cudaGetSymbolAddress(&ptr, g_scratch) != cudaSuccess || ptr == nullptr) return KV_ERR_CUDA;
     if (cudaDeviceGetAttribute(&d.sm_count, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
@@ -91,17 +105,8 @@ const ShapeSetup* setup_shape(int dev, DeviceSetup& d, int dtype, int nkv, int g
     return &d.shapes[d.n_shapes++];
 }
 
-int encode_map(const void* pages, uint32_t n_pages, int dtype, int nkv, CUtensorMap* map) {
-    static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
-    if (!encode) {
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", reinterpret_cast<void**>(&encode),
-                                    cudaEnableDefault, &q) != cudaSuccess ||
-            q != cudaDriverEntryPointSuccess || !encode) {
-            encode = nullptr;
-            return KV_ERR_CUDA;
-        }
-    }
+int encode_map(PFN_cuTensorMapEncodeTiled_v12000 encode, const void* pages, uint32_t n_pages, int dtype, int nkv,
+               CUtensorMap* map) {
     const cuuint64_t elem = dtype == KV_DTYPE_BF16 ? 2 : 4;
     const cuuint64_t row_elems = 128 / elem;
     const cuuint64_t page_rows = 2ull * nkv * kvb200::kPageTokens * kvb200::kHeadDim * elem / 128;
@@ -144,6 +149,7 @@ extern "C" int kv_decode_attn_noalloc(const void* pages, uint32_t n_pages, int32
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return KV_ERR_CUDA;
     const ShapeSetup* shape = nullptr;
     unsigned char* scratch = nullptr;
+    PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
     {
         std::lock_guard<std::mutex> lock(g_mu);
         DeviceSetup& d = g_dev[dev];
@@ -155,6 +161,7 @@ extern "C" int kv_decode_attn_noalloc(const void* pages, uint32_t n_pages, int32
         shape = setup_shape(dev, d, dtype, n_kv_heads, n_q_heads / n_kv_heads, &rc);
         if (!shape) return rc;
         scratch = d.scratch;
+        encode = g_encode;
     }
     // Scratch layout: merge counters, then (max, sum) pairs, then partial outputs.
     const size_t slots = 2 * static_cast<size_t>(shape->grid);
@@ -163,7 +170,7 @@ extern "C" int kv_decode_attn_noalloc(const void* pages, uint32_t n_pages, int32
     if (kCountersBytes + ml_bytes + o_bytes > kNoAllocScratchBytes) return KV_ERR_INVALID;
 
     CUtensorMap map;
-    int rc = encode_map(pages, n_pages, dtype, n_kv_heads, &map);
+    int rc = encode_map(encode, pages, n_pages, dtype, n_kv_heads, &map);
     if (rc != KV_OK) return rc;
 
     int* counters = reinterpret_cast<int*>(scratch);

@@ -5,7 +5,10 @@ comes from an arena they manage, so they cannot create a kv_pool): they pass
 every buffer, and the kernel's scratch lives in a fixed array inside the
 library.  This file is collected last on purpose, so that a run stopping at
 the first failure has already run every other test.  It checks, through the
-C ABI, two calls in a row against kv_decode_attn on the same inputs.
+C ABI, two calls in a row against the CPU oracle and against kv_decode_attn
+on the same pages.  Both dtypes run the CUDA-core decode kernel here, so the
+cases cover its sliding window (with the pages below it evicted) and the
+KV-head-shard layouts as well as the full 8-KV-head ones.
 """
 import numpy as np
 import pytest
@@ -26,15 +29,21 @@ def rope_table(max_positions: int, theta: float = 1e6, dim: int = 64) -> np.ndar
     return np.ascontiguousarray(np.stack([c[:, : dim // 2], s[:, : dim // 2]], axis=-1))
 
 
-@pytest.mark.parametrize("dtype,n_q,n_kv,lens", [
-    ("bf16", 24, 8, [0, 5, 17, 300, 2047, 4500]),
-    ("f32", 32, 8, [1, 64, 1000]),
+@pytest.mark.parametrize("dtype,n_q,n_kv,lens,window", [
+    ("bf16", 24, 8, [0, 5, 17, 300, 2047, 4500], 0),
+    ("f32", 32, 8, [1, 64, 1000], 0),
+    ("bf16", 24, 8, [5000, 40, 1030, 2047], 1024),
+    ("f32", 32, 8, [3000, 600], 512),
+    ("bf16", 8, 2, [3000, 70, 0, 900], 0),
+    ("bf16", 16, 4, [1500, 33, 4100], 700),
+    ("f32", 4, 1, [2500, 16], 0),
 ])
-def test_noalloc_matches_pool_entry_point(cuda, dtype, n_q, n_kv, lens):
+def test_noalloc_matches_oracle_and_pool_entry_point(cuda, dtype, n_q, n_kv, lens, window):
     import torch
     from llmhost_b200 import _capi
 
-    case = DecodeCase(dtype, n_q, n_kv, lens, seed=31)
+    case = DecodeCase(dtype, n_q, n_kv, lens, seed=31, window=window, evict_below_window=window > 0)
+    _, oracle_out = case.run_oracle()
     lib = _capi.lib()
     with case.make_pool() as pool:
         case.prefill_gpu(pool)
@@ -60,7 +69,8 @@ def test_noalloc_matches_pool_entry_point(cuda, dtype, n_q, n_kv, lens):
             torch.cuda.synchronize()
             assert int(status.item()) == 0, f"call {call}: device error bits {int(status.item())}"
             got = to_numpy_f32(out)
-            assert_close_rows(got, ref_np, RTOL[dtype], f"{dtype} no-alloc call {call}")
+            assert_close_rows(got, oracle_out, RTOL[dtype], f"{dtype} no-alloc call {call} vs the oracle")
+            assert_close_rows(got, ref_np, RTOL[dtype], f"{dtype} no-alloc call {call} vs kv_decode_attn")
 
 
 def test_noalloc_rejects_sizes_beyond_its_limit(cuda):
