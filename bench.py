@@ -3,8 +3,9 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
 Workload (one GPU's share; sessions are independent, so N GPUs run N
-independent batches -- weak scaling, no collective on the data path):
-64 sessions, cached lengths uniform in [128, 8192] (seed 1 + 1000*rank), bf16,
+batches -- weak scaling, no collective on the data path): 64 sessions per
+GPU, cached lengths uniform in [128, 8192] (64 * N lengths drawn from seed 1,
+split into N shares by LPT on length), bf16,
 24 query / 8 KV heads, head_dim 64, page 16, pages drawn in order from a seeded
 permutation of a 2^20-page pool, 6 attention layers.  A step is one token per
 session through all 6 layers: per layer one kv_append_decode_attn (the
@@ -269,8 +270,8 @@ def run_ours(args, rank: int, world: int, local_rank: int):
 
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
-    wl = decode_config(steps=args.schedule, seed=1 + 1000 * rank, n_layers=args.layers,
-                       pool_pages=args.pool_pages)
+    wl = decode_config(steps=args.schedule, seed=1, n_layers=args.layers, pool_pages=args.pool_pages,
+                       world=world, rank=rank)
     n, L = wl.n_seqs, wl.n_layers
     S = wl.steps
     max_pos = int(wl.l0.max()) + S + 16
@@ -353,15 +354,11 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     pool.check_device_error()
 
     # ---- device-timed region ----
+    # Nothing but the decode launches goes into the stream between the two
+    # events, so the launches run back to back as in serving (each one's
+    # set-up overlaps the previous one's tail through programmatic dependent
+    # launch) and the region's time per launch is the kernel's own.
     K = args.steps
-    # Every launch of every EV_EVERY-th timed step is bracketed by events (the
-    # kernel's live duration for the roofline); an event pair around every
-    # launch would itself slow the step by a few percent (an event between two
-    # launches also stops the next one's set-up from overlapping this one's
-    # tail, so the sampled launches read a little long).
-    EV_EVERY = 16
-    kev = {i: [[torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)] for _ in range(L)]
-           for i in range(0, K, EV_EVERY)}
     sampler = ClockSampler(local_rank)
     sampler.start()
     barrier()
@@ -370,7 +367,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     t_end = torch.cuda.Event(enable_timing=True)
     t_start.record(stream)
     for i in range(K):
-        step(args.warmup + i, kev.get(i))
+        step(args.warmup + i)
     t_end.record(stream)
     torch.cuda.synchronize()
     barrier()
@@ -378,20 +375,40 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     pool.check_device_error()
     ms_local = t_start.elapsed_time(t_end)
     ms = max_over_ranks(ms_local)
-    kernel_ms = [kev[i][l][0].elapsed_time(kev[i][l][1]) for i in kev for l in range(L)]
+    launches = K * L * (1 if fused else 2)
     # The fused launch moves the whole layer's algorithmic bytes (append
     # included); the plain decode launch only the attention's.
     step_bytes = [wl.step_bytes((args.warmup + i) % S) for i in range(K)]
-    attn_bytes = [(step_bytes[i] // L if fused else wl.attn_bytes((args.warmup + i) % S))
-                  for i in kev for _ in range(L)]
+    attn_bytes = [(step_bytes[i] / L if fused else wl.attn_bytes((args.warmup + i) % S)) for i in range(K)]
     tokens = n * K * world
     value = tokens / (ms / 1e3)
     ms_per_step = ms / K
 
+    # Per-rank figures (all ranks take part in the same collective).
+    per_rank = [[float(sum(step_bytes)) / K, ms_local, float(n)]]
+    if world > 1:
+        mine = torch.tensor(per_rank[0], device=dev, dtype=torch.float64)
+        allr = [torch.empty_like(mine) for _ in range(world)]
+        dist.all_gather(allr, mine)
+        per_rank = [t.tolist() for t in allr]
+
     hbm, peak_kind = peaks()
-    mean_kernel_s = float(np.mean(kernel_ms)) / 1e3
+    launch_s = ms_local / 1e3 / launches if fused else None
     mean_attn_bytes = float(np.mean(attn_bytes))
-    achieved = mean_attn_bytes / mean_kernel_s / 1e9
+    # A separate, untimed pass brackets single launches with events: a note
+    # only, since an event between two launches stops the next one's set-up
+    # from overlapping (the sampled launches read a little long).
+    n_sample = min(16, K)
+    kev = [[[torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)] for _ in range(L)]
+           for _ in range(n_sample)]
+    for i in range(n_sample):
+        step(args.warmup + K + i, kev[i])
+    torch.cuda.synchronize()
+    pool.check_device_error()
+    sampled_us = float(np.mean([e[0].elapsed_time(e[1]) for r in kev for e in r])) * 1e3
+    if not fused:  # two launches per layer: the decode launch's time comes from the sampled pass
+        launch_s = sampled_us / 1e6
+    achieved = mean_attn_bytes / launch_s / 1e9
     ratio, prof = load_traffic_ratio()
     roofline = {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
                 "traffic": (ratio * mean_attn_bytes) if ratio else None,
@@ -400,8 +417,13 @@ def run_ours(args, rank: int, world: int, local_rank: int):
                 else "decode_tc_kernel (kv_append_decode_attn: append + attention, one launch per layer)"
                 if fused else "decode_tc_kernel (kv_decode_attn)",
                 "algorithmic_bytes_per_launch": mean_attn_bytes,
-                "mean_launch_us": mean_kernel_s * 1e6,
-                "launches_timed": len(kernel_ms), "timed_steps_sampled": f"every {EV_EVERY}th",
+                "mean_launch_us": launch_s * 1e6,
+                "launch_time": ("timed region / launches: the region holds only these launches, back to back"
+                                if fused else "sampled launches (events around each decode launch)"),
+                "launches_timed": launches,
+                "sampled_launch_us": sampled_us,
+                "sampled_note": f"{n_sample} untimed steps with events around every launch (breaks the "
+                                "launch overlap, so a little long)",
                 "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
                 else "fallback 6.65 TB/s"}
     step_gbs = float(np.mean(step_bytes)) / (ms_per_step / 1e3) / 1e9
@@ -514,12 +536,15 @@ def run_ours(args, rank: int, world: int, local_rank: int):
                        "sessions_per_gpu": n, "layers": L, "q_heads": wl.n_q,
                        "kv_heads": wl.n_kv, "head_dim": 64, "page_tokens": 16,
                        "pool_pages": wl.pool_pages, "schedule_steps": S,
-                       "lengths": "uniform [128, 8192] + step",
+                       "lengths": "uniform [128, 8192] + step" + (
+                           f"; {n * world} drawn at once, LPT shares by length" if world > 1 else ""),
                        "l2": "no flush: K/V read per step (~3.5 GB) >> 126 MB L2",
                        "parallelism": f"batch-sharded x{world} (independent sessions per GPU)"},
             "step_gbs": step_gbs, "step_frac_of_peak": step_gbs / hbm,
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
-            "gpu_launches": K * L * (1 if fused else 2), "clocks": clocks,
+            "gpu_launches": launches, "clocks": clocks,
+            "per_rank": [{"rank": r, "sessions": int(x[2]), "bytes_per_step": x[0], "ms": x[1],
+                          "gbs": x[0] * K / (x[1] / 1e3) / 1e9} for r, x in enumerate(per_rank)],
         }
         print(json.dumps(line), flush=True)
     pool.close()
@@ -1224,6 +1249,7 @@ def run_longctx(args, ctx):
     vs = rnd(4, L, n, wl.n_kv, 64)
     bq = rnd(4, L, 1, 4 * hpr, 64)
     bk = rnd(4, L, 1, hpr, 64)
+    bv = rnd(4, L, 1, hpr, 64)
     out = torch.empty(n, wl.n_q, 64, device=dev, dtype=torch.bfloat16)
     bout = torch.empty(L, 4 * hpr, 64, device=dev, dtype=torch.bfloat16)
     gathered = torch.empty(ctx.world, L, 4 * hpr, 64, device=dev, dtype=torch.bfloat16)
@@ -1256,7 +1282,7 @@ def run_longctx(args, ctx):
         if eb:
             eb[0].record(stm)
         for l in range(L):
-            big.append_decode_attn(bk[j, l], bk[j, l], bq[j, l], big_bt[l], big_len_dev, out=bout[l], stream=stm)
+            big.append_decode_attn(bk[j, l], bv[j, l], bq[j, l], big_bt[l], big_len_dev, out=bout[l], stream=stm)
         if eb:
             eb[1].record(stm)
             brec.append(eb)
