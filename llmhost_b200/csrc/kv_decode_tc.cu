@@ -121,8 +121,9 @@ struct TcShape {
     static constexpr int kOffM = kOffMax + 2 * 4 * 8 * 4;           // float [2 buffers][NQ]: reference maxima
     static constexpr int kOffL = kOffM + 2 * NQ * 4;                // float [2 buffers][4 warps][NQ]: row sums
     static constexpr int kOffOb = kOffL + 2 * 4 * NQ * 4;           // float [64][4]
-    static constexpr int kOffBar = (kOffOb + 64 * 4 * 4 + 7) & ~7;  // 24 mbarriers
-    static constexpr int kOffInt = kOffBar + 24 * 8;                // int [16]
+    static constexpr int kBars = 24;                                // mbarrier slots (2 kStages + 16 used)
+    static constexpr int kOffBar = (kOffOb + 64 * 4 * 4 + 7) & ~7;
+    static constexpr int kOffInt = kOffBar + kBars * 8;             // int [16]
     static constexpr int kOffScan = kOffInt + 16 * 4;               // int [n_seqs + 1]
     static size_t smem_bytes(int max_seqs) { return 1024 + kOffScan + (static_cast<size_t>(max_seqs) + 1) * 4; }
 };
@@ -297,18 +298,22 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(const __grid_con
     constexpr int kPairs = Sh::kPairs;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    // Every barrier's slot follows from kStages, so no ring depth can make two
+    // of them share an mbarrier (a TMA's byte count and an MMA commit landing
+    // on one barrier would corrupt both phases).
     uint64_t* bars = reinterpret_cast<uint64_t*>(base + Sh::kOffBar);
-    uint64_t* full = bars;            // [kStages]  TMA landed
-    uint64_t* empty = bars + 3;       // [kStages]  PV done with the stage
-    uint64_t* s_full = bars + 6;      // [2]        S MMAs done
-    uint64_t* s_free = bars + 8;      // [2]        S read by the softmax
-    uint64_t* p_full = bars + 10;     // [2]        P (and zeroed V rows) written
-    uint64_t* pv_done = bars + 12;    // [2]        PV MMAs done
-    uint64_t* q_full = bars + 14;     //            Q tiles of the next segment written
-    uint64_t* mma_done = bars + 15;
-    uint64_t* o_full = bars + 16;     // [2]        a segment's last PV done (O buffer e)
-    uint64_t* seg_done = bars + 18;   // [2]        its reference maxima and row sums written
-    uint64_t* o_free = bars + 20;     // [2]        the epilogue is done with O buffer e and its sums
+    uint64_t* full = bars;                    // [kStages]  TMA landed
+    uint64_t* empty = full + kStages;         // [kStages]  PV done with the stage
+    uint64_t* s_full = empty + kStages;       // [2]        S MMAs done
+    uint64_t* s_free = s_full + 2;            // [2]        S read by the softmax
+    uint64_t* p_full = s_free + 2;            // [2]        P (and zeroed V rows) written
+    uint64_t* pv_done = p_full + 2;           // [2]        PV MMAs done
+    uint64_t* q_full = pv_done + 2;           //            Q tiles of the next segment written
+    uint64_t* mma_done = q_full + 1;
+    uint64_t* o_full = mma_done + 1;          // [2]        a segment's last PV done (O buffer e)
+    uint64_t* seg_done = o_full + 2;          // [2]        its reference maxima and row sums written
+    uint64_t* o_free = seg_done + 2;          // [2]        the epilogue is done with O buffer e and its sums
+    static_assert(2 * kStages + 16 <= Sh::kBars, "the barrier slots fit the reserved space");
     int* ints = reinterpret_cast<int*>(base + Sh::kOffInt);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ints);
     volatile int* abort_flag = ints + 1;
