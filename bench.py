@@ -4,8 +4,9 @@
 
 Workload (one GPU's share; sessions are independent, so N GPUs run N
 batches -- weak scaling, no collective on the data path): 64 sessions per
-GPU, cached lengths uniform in [128, 8192] (64 * N lengths drawn from seed 1,
-split into N shares by LPT on length), bf16,
+GPU, cached lengths uniform in [128, 8192] (seed 1; the job holds those 64
+lengths once per GPU and LPT on length hands each GPU one session of every
+length, so per-GPU work is the same at every N), bf16,
 24 query / 8 KV heads, head_dim 64, page 16, pages drawn in order from a seeded
 permutation of a 2^20-page pool, 6 attention layers.  A step is one token per
 session through all 6 layers: per layer one kv_append_decode_attn (the
@@ -537,7 +538,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
                        "kv_heads": wl.n_kv, "head_dim": 64, "page_tokens": 16,
                        "pool_pages": wl.pool_pages, "schedule_steps": S,
                        "lengths": "uniform [128, 8192] + step" + (
-                           f"; {n * world} drawn at once, LPT shares by length" if world > 1 else ""),
+                           f"; the 64 lengths once per GPU, LPT shares by length (one of each per GPU)" if world > 1 else ""),
                        "l2": "no flush: K/V read per step (~3.5 GB) >> 126 MB L2",
                        "parallelism": f"batch-sharded x{world} (independent sessions per GPU)"},
             "step_gbs": step_gbs, "step_frac_of_peak": step_gbs / hbm,

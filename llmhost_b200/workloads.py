@@ -111,16 +111,18 @@ def decode_config(steps: int = 512, seed: int = 1, n_seqs: int = 64, pool_pages:
                   n_layers: int = 6, window: int = 0, world: int = 1, rank: int = 0) -> DecodeWorkload:
     """The batched-decode configuration (defaults) or a scaled variant of it.
 
-    With world > 1 the lengths of n_seqs * world sessions are drawn at once
-    and split into world shares by LPT on their cached length (the bytes a
-    step reads); this returns share `rank`.  world = 1 is the configuration
-    itself.  Every share draws its pages from the same permutation of its own
+    With world > 1 the job is n_seqs * world sessions: the configuration's
+    n_seqs lengths once per GPU, split into world shares by LPT on cached
+    length (the bytes a step reads).  LPT hands each share one session of
+    every length, so each GPU's work is the configuration's exactly, at every
+    world size (weak scaling with fixed work per GPU); this returns share
+    `rank`.  Every share draws its pages from the same permutation of its own
     pool."""
     rng = np.random.default_rng(seed)
-    lengths = rng.integers(lo, hi, endpoint=True, size=n_seqs * world).astype(np.int64)
+    lengths = rng.integers(lo, hi, endpoint=True, size=n_seqs).astype(np.int64)
     if world > 1:
-        share = lpt_partition(lengths.tolist(), world)[rank]
-        l0 = lengths[share]
+        job = np.tile(lengths, world)
+        l0 = job[lpt_partition(job.tolist(), world)[rank]]
     else:
         l0 = lengths
     order = rng.permutation(pool_pages).astype(np.uint32)
