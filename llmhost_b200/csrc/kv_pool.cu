@@ -115,6 +115,8 @@ void free_pool(kv_pool* p) {
     cudaFree(p->part_o);
     cudaFree(p->part_ml);
     cudaFree(p->counters);
+    cudaFree(p->pre_part);
+    cudaFree(p->pre_counters);
     delete p;
 }
 
@@ -190,6 +192,18 @@ int kv_pool_create(const kv_pool_config* cfg, kv_pool** out) {
         (rc = alloc_dev(reinterpret_cast<void**>(&p->counters), kvb200::decode_counter_count(p) * sizeof(int)))) {
         free_pool(p);
         return rc;
+    }
+    const size_t pre_bytes = kvb200::prefill_workspace_bytes(p);
+    const size_t pre_counters = kvb200::prefill_counter_count(p);
+    if (pre_bytes &&
+        ((rc = alloc_dev(reinterpret_cast<void**>(&p->pre_part), pre_bytes)) ||
+         (rc = alloc_dev(reinterpret_cast<void**>(&p->pre_counters), pre_counters * sizeof(int))))) {
+        free_pool(p);
+        return rc;
+    }
+    if (pre_counters && cudaMemset(p->pre_counters, 0, pre_counters * sizeof(int)) != cudaSuccess) {
+        free_pool(p);
+        return KV_ERR_CUDA;
     }
     std::vector<float2> table;
     build_rope_table(cfg->max_positions, cfg->head_dim, cfg->rope_theta, table);

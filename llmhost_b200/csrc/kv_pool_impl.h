@@ -21,6 +21,10 @@ struct kv_pool {
     int* counters = nullptr;      // [decode_counter_count]: per sequence, then per CTA run
     int decode_grid = 0;
     size_t decode_smem = 0;
+    // prefill split workspace (bf16 pools): partial rows of the units that the
+    // persistent prefill schedule cuts between CTAs, and one merge counter per unit
+    float* pre_part = nullptr;    // [prefill_workspace_slots][256 rows][head_dim + 2]
+    int* pre_counters = nullptr;  // [prefill_counter_count]
     CUtensorMap page_map;         // TMA view of the pool as 128-byte rows
     CUtensorMap head_map;         // same rows, one head's page_tokens rows per box (bf16)
 };
@@ -60,6 +64,9 @@ int launch_decode_tc(kv_pool* pool, const void* q, const uint32_t* bt, int32_t b
 
 // Prefill / tree-verify attention: tcgen05 for bf16 pools (kv_prefill.cu).
 int prefill_setup(kv_pool* pool);
+// Bytes of the prefill split workspace and of its counters (0 for fp32 pools).
+size_t prefill_workspace_bytes(const kv_pool* pool);
+size_t prefill_counter_count(const kv_pool* pool);
 int launch_prefill(kv_pool* pool, const void* q, const int32_t* q_pos, const int32_t* q_off,
                    const int32_t* prefix, const unsigned long long* tree, int32_t n_seqs, int32_t max_q,
                    const uint32_t* bt, int32_t bt_stride, void* out, cudaStream_t stream);

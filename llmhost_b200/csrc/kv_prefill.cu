@@ -65,12 +65,48 @@ constexpr int kQBytes = kRows * 128;
 constexpr int kStageBytes = 2 * kKvBytes;
 constexpr int kOffStage = kTiles * kQBytes;
 constexpr int kOffBar = kOffStage + kStages * kStageBytes;
-constexpr int kOffX = kOffBar + 256;  // float [2][kTiles][kHalves][kRows]: half-row maxima / sums
-constexpr int kSmemBytes = 1024 + kOffX + 2 * kTiles * kHalves * kRows * 4;
+// float [3][kTiles][kHalves][kRows]: half-row maxima (slots 0, 1 by block
+// parity) and half-row sums (slot 2) passed between the halves of a row
+constexpr int kOffX = kOffBar + 256;
+constexpr int kXBytes = 3 * kTiles * kHalves * kRows * 4;
+// The CTA's work list: segments of units (see Seg), then its length and the
+// merge flag
+constexpr int kMaxSegs = 512;
+constexpr int kOffSeg = kOffX + kXBytes;
+constexpr int kOffSegN = kOffSeg + kMaxSegs * 32;
+// persistent-grid set-up: each unit's visible key count and the inclusive
+// prefix of the unit costs (64-bit), warp totals, and the parts this CTA
+// merges at its end
+constexpr int kOffScan = kOffSegN + 64;
+constexpr int kScanBytes = kMaxSegs * 4 + kMaxSegs * 8 + 16 * 8 + 64;
+constexpr int kSmemBytes = 1024 + kOffScan + kScanBytes;
+
+// Work schedule.  A unit is one (sequence, kv head, pair of query tiles),
+// the work of one CTA of the plain grid: its query rows against key blocks
+// 0 .. nb-1.  With more units than SMs (and at most kPersistMaxUnits), the
+// grid is persistent instead: the units' key blocks are laid end to end, each
+// unit led by kLeadBlocks blocks of no work that stand for the cost of
+// starting it (its Q tiles, the pipeline restart, its epilogue), and every
+// CTA takes an equal run of that list.  A unit cut between CTAs is computed
+// in parts; each part leaves its rows' unnormalised sums (reference maximum,
+// row sum, O) in the pool's prefill workspace and the last part to arrive
+// merges them (log-sum-exp of the parts, Milakov & Gimelshein 2018).
+constexpr int kLeadBlocks = 1;
+constexpr int kPersistMaxUnits = kMaxSegs;
+constexpr int kPartRows = kTiles * kRows;                        // rows of a unit
+constexpr size_t kSlotFloats = static_cast<size_t>(kPartRows) * (kHeadDim + 2);  // O rows, then (m, l) pairs
+constexpr int kMergeBar = 3;                                     // named barrier of all softmax threads
 
 // P entries stay below 2^kLazyLog2 times the row's reference maximum; the
 // reference is raised only when a block's maximum exceeds it by more.
 constexpr float kLazyLog2 = 8.f;
+
+// One entry of a CTA's work list: unit u's key blocks [b0, b1) of nb, kmax
+// its last visible key + 1; the unit's parts are computed by CTAs c_first ..
+// c_first + n_parts - 1 (n_parts = 1: this CTA does the whole unit).
+struct Seg {
+    int u, b0, b1, nb, kmax, c_first, n_parts, pad;
+};
 
 struct PrefillArgs {
     const __nv_bfloat16* q;
@@ -88,7 +124,88 @@ struct PrefillArgs {
     __nv_bfloat16* out;
     int* err;
     float qscale;
+    int nx;           // query-tile pairs per (sequence, kv head)
+    int n_seqs;
+    int persist;      // 1: persistent grid over the unit list (gridDim.x CTAs)
+    float* part;      // persistent: [2 gridDim.x][kSlotFloats] partial rows
+    int* counters;    // persistent: [units] parts arrived (reset by the merger)
 };
+
+// Where unit u's rows are and which keys they can see.
+struct UnitInfo {
+    int s, h, q0, T, L, t_begin, t_end, kmax, nb;
+    bool bad;  // sequence lengths out of range
+};
+
+__device__ __forceinline__ UnitInfo unit_info(const PrefillArgs& a, int u) {
+    UnitInfo r;
+    const int x = u % a.nx;
+    r.h = (u / a.nx) % a.nkv;
+    r.s = u / (a.nx * a.nkv);
+    r.q0 = __ldg(a.q_off + r.s);
+    r.T = __ldg(a.q_off + r.s + 1) - r.q0;
+    r.L = __ldg(a.prefix + r.s);
+    const bool tree = a.tree != nullptr;
+    r.bad = r.T < 0 || r.L < 0 || r.T > a.max_q || (tree && r.T > 64);
+    r.t_begin = x * kTiles * a.tile_tokens;
+    r.t_end = min(r.T, r.t_begin + kTiles * a.tile_tokens);
+    r.kmax = tree ? r.L + r.T : r.L + r.t_end;  // keys [0, kmax) can be visible to the unit
+    r.nb = (r.bad || r.t_begin >= r.T) ? 0 : (r.kmax + kBlockKeys - 1) / kBlockKeys;
+    return r;
+}
+
+// The CTA (of G) whose run of the unit list [c C / G, (c + 1) C / G) holds
+// position p.
+__device__ __forceinline__ int cta_of(long long p, long long C, long long G) {
+    return static_cast<int>(((p + 1) * G + C - 1) / C - 1);
+}
+
+__device__ __forceinline__ int unit_cost(int kmax) {
+    return kmax > 0 ? (kmax + kBlockKeys - 1) / kBlockKeys + kLeadBlocks : 0;
+}
+
+// This CTA's run of the persistent grid's unit list (one thread): the units'
+// costs are laid end to end (prefix[u]: inclusive, 64-bit), the list of C
+// positions is cut into G equal runs, and every unit whose work positions
+// meet this CTA's run becomes a segment.  With C >= G every run holds at
+// least one position, so the CTAs between a unit's first and last part all
+// hold a part of it; with fewer positions than CTAs only the first C CTAs
+// take one each.
+__device__ int cut_run(int n_units, const int* ukmax, const long long* prefix, Seg* segs) {
+    const long long C = n_units > 0 ? prefix[n_units - 1] : 0;
+    const long long G = C < gridDim.x ? C : gridDim.x, c = blockIdx.x;
+    if (c >= G) return 0;
+    const long long gb = c * C / G, ge = (c + 1) * C / G;
+    int lo = 0, hi = n_units;  // the first unit whose positions end past gb
+    while (lo < hi) {
+        const int mid = (lo + hi) >> 1;
+        if (prefix[mid] > gb)
+            hi = mid;
+        else
+            lo = mid + 1;
+    }
+    int n = 0;
+    for (int u = lo; u < n_units; ++u) {
+        const int cost = unit_cost(ukmax[u]);
+        if (cost == 0) continue;
+        const long long w1 = prefix[u], w0 = w1 - cost + kLeadBlocks;  // the unit's work positions
+        if (w1 - cost >= ge) break;
+        const long long b = max(gb, w0), e = min(ge, w1);
+        if (b < e) {
+            Seg sg;
+            sg.u = u;
+            sg.nb = cost - kLeadBlocks;
+            sg.b0 = static_cast<int>(b - w0);
+            sg.b1 = static_cast<int>(e - w0);
+            sg.kmax = ukmax[u];
+            sg.c_first = cta_of(w0, C, G);
+            sg.n_parts = cta_of(w1 - 1, C, G) - sg.c_first + 1;
+            sg.pad = 0;
+            segs[n++] = sg;
+        }
+    }
+    return n;
+}
 
 __device__ __forceinline__ float max3f(float a, float b, float c) {
     float r;
@@ -235,23 +352,8 @@ __device__ __forceinline__ void scale_o(uint32_t t_o, float f) {
 }
 
 __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_constant__ CUtensorMap hmap,
-                                                              const PrefillArgs a) {
-    const int s = blockIdx.z, h = blockIdx.y;
-    const int q0 = __ldg(a.q_off + s);
-    const int T = __ldg(a.q_off + s + 1) - q0;
-    const int L = __ldg(a.prefix + s);
+                                                              const __grid_constant__ PrefillArgs a) {
     const bool tree = a.tree != nullptr;
-    const int cta_tokens = kTiles * a.tile_tokens;
-    if (T < 0 || L < 0 || T > a.max_q || (tree && T > 64)) {
-        if (blockIdx.x == 0 && h == 0 && threadIdx.x == 0) flag_error(a.err, kDevErrBadArg);
-        return;
-    }
-    const int t_begin = blockIdx.x * cta_tokens;
-    if (t_begin >= T) return;
-    const int t_end = min(T, t_begin + cta_tokens);
-    const int kmax = tree ? L + T : L + t_end;  // keys [0, kmax) can be visible to this CTA
-    const int nb = (kmax + kBlockKeys - 1) / kBlockKeys;
-
     extern __shared__ uint8_t smem_raw[];
     uint8_t* base = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -261,8 +363,11 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
     uint64_t* p_full = s_full + kTiles;                             // [kTiles]
     uint64_t* pv_full = p_full + kTiles;                            // [kTiles]
     uint64_t* mma_done = pv_full + kTiles;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+    uint64_t* q_full = mma_done + 1;                                // a segment's Q tiles written
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(q_full + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    Seg* segs = reinterpret_cast<Seg*>(base + kOffSeg);
+    int* n_segs_p = reinterpret_cast<int*>(base + kOffSegN);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
@@ -276,6 +381,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
             mbar_init(&pv_full[t], 1);
         }
         mbar_init(mma_done, 1);
+        mbar_init(q_full, kSoftmaxThreads);
         *abort_flag = 0;
         fence_mbar_init();
     }
@@ -286,97 +392,106 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
     if (warp == kProducerWarp && lane == 0) prefetch_tmap(&hmap);
-
-    // ---- Q tiles (warps 0-15): thread = (tile tq, half hf, row r); row r of
-    // tile tq is (token t_begin + tq * tile_tokens + r / G, head h*G + r % G).
-    // RoPE at q_pos (rope.rs:76 form), scaled into log2 units, bf16, into
-    // shared memory; each half builds half of the row's dims.
-    const int tq = (warp >> 3) & 1, hf = (warp >> 2) & 1, r = 32 * (warp & 3) + lane;
-    const int rt = r / a.group, rg = r % a.group;
-    const int t_row = t_begin + tq * a.tile_tokens + rt;
-    const bool row_valid = (threadIdx.x < kSoftmaxThreads) && (rt < a.tile_tokens) && (t_row < t_end);
-    tc_fence_before();
-    __syncthreads();  // the TMEM address is published
-    tc_fence_after();
-    const uint32_t tmem = *tmem_slot;
-    const uint32_t lane_base = tmem + (static_cast<uint32_t>(32 * (warp & 3)) << 16);
-    const uint32_t t_tile = lane_base + kTileCols * tq;  // this thread's row of its tile
-    if (threadIdx.x < kSoftmaxThreads) {
-        uint8_t* qrow = base + tq * kQBytes + r * 128;
-        if (row_valid) {
-            const uint4* src = reinterpret_cast<const uint4*>(
-                a.q + (static_cast<size_t>(q0 + t_row) * a.n_q + h * a.group + rg) * kHeadDim);
-            int pos = __ldg(a.q_pos + q0 + t_row);
-            if (pos < 0 || pos >= a.max_pos) {
-                flag_error(a.err, kDevErrBadPos);
-                pos = 0;
+    // The work list: the whole unit of this CTA (plain grid), or this CTA's
+    // run of every unit's key blocks (persistent grid: each softmax thread
+    // works out one unit, the costs are scanned across the 512 softmax
+    // threads, thread 0 cuts the run).
+    int* ukmax = reinterpret_cast<int*>(base + kOffScan);                 // [kMaxSegs]
+    long long* uprefix = reinterpret_cast<long long*>(ukmax + kMaxSegs);   // [kMaxSegs]
+    long long* wsum = uprefix + kMaxSegs;                                   // [16]
+    int* pend = reinterpret_cast<int*>(wsum + 16);                          // [4] segments to merge, then count
+    if (a.persist) {
+        if (threadIdx.x < kSoftmaxThreads) {
+            const int n_units = a.nx * a.nkv * a.n_seqs;
+            const int u = threadIdx.x;
+            int km = 0;
+            if (u < n_units) {
+                const UnitInfo ui = unit_info(a, u);
+                km = ui.nb > 0 ? ui.kmax : 0;
+                if (ui.bad && blockIdx.x == 0 && u % (a.nx * a.nkv) == 0) flag_error(a.err, kDevErrBadArg);
             }
-            const float2* cs = a.rope + static_cast<size_t>(pos) * (kHeadDim / 2);
-            // dims 8c .. 8c+7 rotate together with dims 32+8c .. 32+8c+7; this
-            // half takes c = 2 hf, 2 hf + 1
+            ukmax[u] = km;
+            long long incl = unit_cost(km);
 #pragma unroll
-            for (int cc = 0; cc < 2; ++cc) {
-                const int c = 2 * hf + cc;
-                const uint4 u0 = __ldg(src + c), u1 = __ldg(src + c + 4);
-                const uint32_t w0[4] = {u0.x, u0.y, u0.z, u0.w}, w1[4] = {u1.x, u1.y, u1.z, u1.w};
-                uint32_t lo[4], hi[4];
+            for (int d = 1; d < 32; d <<= 1) {
+                const long long t = __shfl_up_sync(0xffffffffu, incl, d);
+                if (lane >= d) incl += t;
+            }
+            if (lane == 31) wsum[warp] = incl;
+            named_bar_sync(kMergeBar, kSoftmaxThreads);
+            if (warp == 0) {
+                long long x = lane < kSoftmaxThreads / 32 ? wsum[lane] : 0;
 #pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const float2 x = bf16x2_to_float2(w0[i]), y = bf16x2_to_float2(w1[i]);
-                    const float2 c0 = __ldg(cs + 8 * c + 2 * i), c1 = __ldg(cs + 8 * c + 2 * i + 1);
-                    const float a0 = __fadd_rn(__fmul_rn(x.x, c0.x), __fmul_rn(-y.x, c0.y)) * a.qscale;
-                    const float a1 = __fadd_rn(__fmul_rn(x.y, c1.x), __fmul_rn(-y.y, c1.y)) * a.qscale;
-                    const float b0 = __fadd_rn(__fmul_rn(y.x, c0.x), __fmul_rn(x.x, c0.y)) * a.qscale;
-                    const float b1 = __fadd_rn(__fmul_rn(y.y, c1.x), __fmul_rn(x.y, c1.y)) * a.qscale;
-                    lo[i] = float2_to_bf16x2(a0, a1);
-                    hi[i] = float2_to_bf16x2(b0, b1);
+                for (int d = 1; d < 32; d <<= 1) {
+                    const long long t = __shfl_up_sync(0xffffffffu, x, d);
+                    if (lane >= d) x += t;
                 }
-                *reinterpret_cast<uint4*>(qrow + ((c ^ (r & 7)) << 4)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
-                *reinterpret_cast<uint4*>(qrow + (((c + 4) ^ (r & 7)) << 4)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+                if (lane < kSoftmaxThreads / 32) wsum[lane] = x;
             }
-        } else {
-#pragma unroll
-            for (int cc = 0; cc < 4; ++cc) {
-                const int c = 2 * hf + (cc & 1) + 4 * (cc >> 1);  // 16-byte chunks 2hf, 2hf+1, 2hf+4, 2hf+5
-                *reinterpret_cast<uint4*>(qrow + (c << 4)) = make_uint4(0, 0, 0, 0);
+            named_bar_sync(kMergeBar, kSoftmaxThreads);
+            uprefix[u] = incl + (warp > 0 ? wsum[warp - 1] : 0);
+            named_bar_sync(kMergeBar, kSoftmaxThreads);
+            if (threadIdx.x == 0) {
+                *n_segs_p = cut_run(n_units, ukmax, uprefix, segs);
+                pend[3] = 0;
             }
         }
-        proxy_fence();  // the tensor core reads Q through the async proxy
+    } else if (threadIdx.x == 0) {
+        const int u = (blockIdx.z * a.nkv + blockIdx.y) * a.nx + blockIdx.x;
+        const UnitInfo ui = unit_info(a, u);
+        if (ui.bad && blockIdx.x == 0 && blockIdx.y == 0) flag_error(a.err, kDevErrBadArg);
+        int n = 0;
+        if (ui.nb > 0) {
+            segs[0] = Seg{u, 0, ui.nb, ui.nb, ui.kmax, 0, 1, 0};
+            n = 1;
+        }
+        *n_segs_p = n;
+        pend[3] = 0;
     }
     tc_fence_before();
-    __syncthreads();
+    __syncthreads();  // the TMEM address, the barriers and the work list are published
     tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const int n_segs = *n_segs_p;
 
     if (warp == kProducerWarp) {
         // ---------------- producer: K/V head slices, 8 pages per block ----------------
-        // Lane i < 8 owns page i of every block: its block-table entry for
-        // block j + 1 is loaded while block j's stage is waited for, and it
-        // issues that page's K and V boxes (lane 0 first sets the stage's
-        // expected bytes), so no copy waits on a serial chain of loads.
+        // Lane i < 8 owns page i of every block: its block-table entry for the
+        // next block (which may be the next segment's first) is loaded while
+        // this block's stage is waited for, and it issues that page's K and V
+        // boxes (lane 0 first sets the stage's expected bytes), so no copy
+        // waits on a serial chain of loads.
         const int total_rows = static_cast<int>(a.n_pages) * a.page_rows;
-        // page pi of the sequence holds keys this CTA can see
-        auto used = [&](int j) { return lane < kPagesPerBlock && (j * kPagesPerBlock + lane) * kPageTokens < kmax; };
-        auto entry = [&](int j) -> uint32_t {
-            const int pi = j * kPagesPerBlock + lane;
-            if (!used(j)) return 0u;
-            return pi < a.bt_stride ? __ldg(a.bt + static_cast<size_t>(s) * a.bt_stride + pi) : kPageNone;
+        // page pi of the segment's sequence holds keys its unit can see
+        auto used = [&](int k, int j) {
+            return lane < kPagesPerBlock && (j * kPagesPerBlock + lane) * kPageTokens < segs[k].kmax;
         };
-        int issued = 0;
-        uint32_t next = nb > 0 ? entry(0) : 0u;
-        for (int j = 0; j < nb; ++j) {
-            const int st = j % kStages;
+        auto seq_of = [&](int k) { return segs[k].u / (a.nx * a.nkv); };
+        auto entry = [&](int k, int j) -> uint32_t {
+            const int pi = j * kPagesPerBlock + lane;
+            if (!used(k, j)) return 0u;
+            return pi < a.bt_stride ? __ldg(a.bt + static_cast<size_t>(seq_of(k)) * a.bt_stride + pi) : kPageNone;
+        };
+        int issued = 0, J = 0;
+        int k = 0, j = n_segs > 0 ? segs[0].b0 : 0;
+        uint32_t next = n_segs > 0 ? entry(0, j) : 0u;
+        while (k < n_segs) {
+            const int st = J % kStages;
             const uint32_t phys = next;
-            if (j + 1 < nb) next = entry(j + 1);  // in flight during the wait below
+            const int ck = k, cj = j;
+            if (++j == segs[k].b1 && ++k < n_segs) j = segs[k].b0;
+            if (k < n_segs) next = entry(k, j);  // in flight during the wait below
             bool ok = true;
-            if (lane == 0 && j >= kStages)
-                ok = wait_bar(&empty[st], static_cast<uint32_t>(j / kStages - 1) & 1u, abort_flag, a.err);
+            if (lane == 0 && J >= kStages)
+                ok = wait_bar(&empty[st], static_cast<uint32_t>(J / kStages - 1) & 1u, abort_flag, a.err);
             if (!__shfl_sync(0xffffffffu, ok, 0)) break;
             if (lane == 0) mbar_arrive_expect_tx(&full[st], kStageBytes);
             __syncwarp();
             if (lane < kPagesPerBlock) {
+                const int h = (segs[ck].u / a.nx) % a.nkv;
                 uint8_t* kt = base + kOffStage + st * kStageBytes;
                 int rk = total_rows, rv = total_rows;  // out of range: zero fill
-                if (used(j)) {
+                if (used(ck, cj)) {
                     if (phys < a.n_pages) {
                         rk = static_cast<int>(phys) * a.page_rows + h * kPageTokens;
                         rv = static_cast<int>(phys) * a.page_rows + (a.nkv + h) * kPageTokens;
@@ -387,7 +502,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
                 tma_load_2d(kt + lane * kSliceBytes, &hmap, &full[st], 0, rk);
                 tma_load_2d(kt + kKvBytes + lane * kSliceBytes, &hmap, &full[st], 0, rv);
             }
-            issued = j + 1;
+            issued = ++J;
         }
         if (lane == 0 && *abort_flag) {  // wait (bounded) for the newest copy issued into each stage
             for (int st = 0; st < kStages && st < issued; ++st) {
@@ -397,39 +512,68 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
         }
     } else if (warp == kMmaWarp) {
         // ---------------- MMA issuer (one thread) ----------------
-        // Per block j and tile t: O_t += P_t(j-1) V(j-1) once P_t(j-1) is
-        // written, then S_t(j).  tcgen05.mma executes in issue order, so when
-        // S_t(j) completes P_t(j-1) V(j-1) has too: the softmax may then
-        // overwrite P_t and rescale O_t.  The K/V stage of block j-1 is
-        // released after the last tile's PV.
+        // Per block J (counted over all segments) and tile t: O_t += P_t(J-1)
+        // V(J-1) once P_t(J-1) is written, then S_t(J).  tcgen05.mma executes in
+        // issue order, so when S_t(J) completes P_t(J-1) V(J-1) has too: the
+        // softmax may then overwrite P_t and rescale O_t.  The K/V stage of
+        // block J-1 is released after the last tile's PV.  A segment's first S
+        // waits for its Q tiles; its first P V starts O afresh, which the
+        // softmax threads allow only after the previous segment's epilogue has
+        // read O (they arrive on p_full for that block after it).
         if (lane == 0) {
             constexpr uint32_t kIdescS = instr_desc(kBlockKeys, kRows, false);
             constexpr uint32_t kIdescPV = instr_desc(kHeadDim, kRows, true);
             const uint32_t q_addr = smem_addr(base);
             const uint32_t stage_addr = smem_addr(base + kOffStage);
-            for (int j = 0; j <= nb; ++j) {
-                const int st = j % kStages, pst = (j + kStages - 1) % kStages;
-                if (j < nb && !wait_bar(&full[st], static_cast<uint32_t>(j / kStages) & 1u, abort_flag, a.err))
-                    break;
-                tc_fence_after();
-                bool ok = true;
+            int J = 0;
+            bool prev_first = false;  // block J-1 opened its segment (its P V starts O)
+            bool ok = true;
+            auto issue_pv = [&](int t, int pst) {
+                const uint32_t tt = tmem + kTileCols * t;
+                const uint32_t v_addr = stage_addr + pst * kStageBytes + kKvBytes;
 #pragma unroll
-                for (int t = 0; t < kTiles; ++t) {
-                    const uint32_t tt = tmem + kTileCols * t;
-                    if (j > 0) {
-                        if (!wait_bar(&p_full[t], static_cast<uint32_t>(j - 1) & 1u, abort_flag, a.err)) {
+                for (int kk = 0; kk < kBlockKeys / 16; ++kk)
+                    mma_ts(tt + kColO, tt + kColP + 8 * kk, smem_desc(v_addr + 2048 * kk, kKvBytes, 1024), kIdescPV,
+                           !prev_first || kk > 0);
+                mma_commit(&pv_full[t]);
+            };
+            for (int k = 0; ok && k < n_segs; ++k) {
+                const int b0 = segs[k].b0, b1 = segs[k].b1;
+                for (int j = b0; j < b1; ++j, ++J) {
+                    const int st = J % kStages, pst = (J + kStages - 1) % kStages;
+                    if (j == b0) {
+                        // A segment's first block: the previous segment's last P V
+                        // goes first (its epilogue waits for it), then the new Q
+                        // tiles are waited for.
+                        for (int t = 0; J > 0 && t < kTiles; ++t) {
+                            if (!wait_bar(&p_full[t], static_cast<uint32_t>(J - 1) & 1u, abort_flag, a.err)) {
+                                ok = false;
+                                break;
+                            }
+                            tc_fence_after();
+                            issue_pv(t, pst);
+                        }
+                        if (!ok || !wait_bar(q_full, static_cast<uint32_t>(k) & 1u, abort_flag, a.err)) {
                             ok = false;
                             break;
                         }
-                        tc_fence_after();
-                        const uint32_t v_addr = stage_addr + pst * kStageBytes + kKvBytes;
-#pragma unroll
-                        for (int kk = 0; kk < kBlockKeys / 16; ++kk)
-                            mma_ts(tt + kColO, tt + kColP + 8 * kk, smem_desc(v_addr + 2048 * kk, kKvBytes, 1024),
-                                   kIdescPV, j > 1 || kk > 0);
-                        mma_commit(&pv_full[t]);
                     }
-                    if (j < nb) {
+                    if (!wait_bar(&full[st], static_cast<uint32_t>(J / kStages) & 1u, abort_flag, a.err)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+#pragma unroll
+                    for (int t = 0; t < kTiles; ++t) {
+                        if (J > 0 && j > b0) {
+                            if (!wait_bar(&p_full[t], static_cast<uint32_t>(J - 1) & 1u, abort_flag, a.err)) {
+                                ok = false;
+                                break;
+                            }
+                            tc_fence_after();
+                            issue_pv(t, pst);
+                        }
+                        const uint32_t tt = tmem + kTileCols * t;
                         const uint32_t k_addr = stage_addr + st * kStageBytes;
                         const uint32_t qa = q_addr + t * kQBytes;
 #pragma unroll
@@ -438,9 +582,19 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
                                    kk > 0);
                         mma_commit(&s_full[t]);
                     }
+                    if (!ok) break;
+                    if (J > 0) mma_commit(&empty[pst]);
+                    prev_first = j == b0;
                 }
-                if (!ok) break;
-                if (j > 0) mma_commit(&empty[pst]);
+            }
+            if (ok && J > 0) {  // the last block's P V
+                const int pst = (J - 1) % kStages;
+                for (int t = 0; t < kTiles; ++t) {
+                    if (!wait_bar(&p_full[t], static_cast<uint32_t>(J - 1) & 1u, abort_flag, a.err)) break;
+                    tc_fence_after();
+                    issue_pv(t, pst);
+                }
+                mma_commit(&empty[pst]);
             }
             // Every MMA issued above has finished before TMEM is released.
             mma_commit(mma_done);
@@ -448,110 +602,302 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
         }
     } else {
         // ---------------- softmax: thread (tq, hf, r) owns half hf of row r of tile tq ----------------
-        RowMask rm;
-        rm.L = L;
-        rm.T = T;
-        rm.t_chunk = t_row;
-        rm.tree = tree;
-        rm.valid = row_valid;
-        rm.bits = (tree && row_valid) ? __ldg(a.tree + q0 + t_row) : 0ull;
-        // m: the row's reference maximum (log2 units; -inf until a key is seen).
-        // O (in TMEM) and l are sums of 2^(S - m) terms.  Padding rows (past
-        // the chunk, or the last rows of a tile when G does not divide 128)
-        // have Q = 0, so S = 0 on unmasked keys: they start at m = 0 and never
-        // ask for a first pass or a redo; their results are not written.
-        float m = row_valid ? -INFINITY : 0.f, l = 0.f;
+        // Row r of tile tq of a unit is (token t_begin + tq * tile_tokens + r / G,
+        // head h*G + r % G).
+        const int tq = (warp >> 3) & 1, hf = (warp >> 2) & 1, r = 32 * (warp & 3) + lane;
+        const int rt = r / a.group, rg = r % a.group;
+        const uint32_t lane_base = tmem + (static_cast<uint32_t>(32 * (warp & 3)) << 16);
+        const uint32_t t_tile = lane_base + kTileCols * tq;  // this thread's row of its tile
+        // Q tiles of segment k: RoPE at q_pos (rope.rs:76 form), scaled into
+        // log2 units, bf16, into shared memory; each half builds half of the
+        // row's dims.  Then every softmax thread arrives on q_full.  Its
+        // indices are worked out here again, so that none stays live through
+        // the block loop.
+        auto build_q = [&](int k) {
+            const int w = threadIdx.x >> 5, tq = (w >> 3) & 1, hf = (w >> 2) & 1, r = 32 * (w & 3) + (threadIdx.x & 31);
+            const int rt = r / a.group, rg = r % a.group;
+            uint8_t* qrow = base + tq * kQBytes + r * 128;
+            const UnitInfo ui = unit_info(a, segs[k].u);
+            const int t_row = ui.t_begin + tq * a.tile_tokens + rt;
+            if (rt < a.tile_tokens && t_row < ui.t_end) {
+                const uint4* src = reinterpret_cast<const uint4*>(
+                    a.q + (static_cast<size_t>(ui.q0 + t_row) * a.n_q + ui.h * a.group + rg) * kHeadDim);
+                int pos = __ldg(a.q_pos + ui.q0 + t_row);
+                if (pos < 0 || pos >= a.max_pos) {
+                    flag_error(a.err, kDevErrBadPos);
+                    pos = 0;
+                }
+                const float2* cs = a.rope + static_cast<size_t>(pos) * (kHeadDim / 2);
+                // dims 8c .. 8c+7 rotate together with dims 32+8c .. 32+8c+7; this
+                // half takes c = 2 hf, 2 hf + 1
+#pragma unroll
+                for (int cc = 0; cc < 2; ++cc) {
+                    const int c = 2 * hf + cc;
+                    const uint4 u0 = __ldg(src + c), u1 = __ldg(src + c + 4);
+                    const uint32_t w0[4] = {u0.x, u0.y, u0.z, u0.w}, w1[4] = {u1.x, u1.y, u1.z, u1.w};
+                    uint32_t lo[4], hi[4];
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const float2 x = bf16x2_to_float2(w0[i]), y = bf16x2_to_float2(w1[i]);
+                        const float2 c0 = __ldg(cs + 8 * c + 2 * i), c1 = __ldg(cs + 8 * c + 2 * i + 1);
+                        const float a0 = __fadd_rn(__fmul_rn(x.x, c0.x), __fmul_rn(-y.x, c0.y)) * a.qscale;
+                        const float a1 = __fadd_rn(__fmul_rn(x.y, c1.x), __fmul_rn(-y.y, c1.y)) * a.qscale;
+                        const float b0 = __fadd_rn(__fmul_rn(y.x, c0.x), __fmul_rn(x.x, c0.y)) * a.qscale;
+                        const float b1 = __fadd_rn(__fmul_rn(y.y, c1.x), __fmul_rn(x.y, c1.y)) * a.qscale;
+                        lo[i] = float2_to_bf16x2(a0, a1);
+                        hi[i] = float2_to_bf16x2(b0, b1);
+                    }
+                    *reinterpret_cast<uint4*>(qrow + ((c ^ (r & 7)) << 4)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+                    *reinterpret_cast<uint4*>(qrow + (((c + 4) ^ (r & 7)) << 4)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+                }
+            } else {
+#pragma unroll
+                for (int cc = 0; cc < 4; ++cc) {
+                    const int c = 2 * hf + (cc & 1) + 4 * (cc >> 1);  // 16-byte chunks 2hf, 2hf+1, 2hf+4, 2hf+5
+                    *reinterpret_cast<uint4*>(qrow + (c << 4)) = make_uint4(0, 0, 0, 0);
+                }
+            }
+            proxy_fence();  // the tensor core reads Q through the async proxy
+            mbar_arrive(q_full);
+        };
         // tcgen05.ld / st are warp-collective (.sync.aligned): every branch
         // around them below is decided by a warp vote, never per row.  The two
         // halves of a row sit in warps 4 apart and hold the same rows, so
         // their votes agree.
         constexpr unsigned kAll = 0xffffffffu;
-        // A warp of padding rows only (the tail of the last tile) never
-        // sweeps S: its P and O rows are never read back, and each row of an
-        // MMA is independent of the others.  It still waits for each S before
-        // it arrives on p_full, which keeps the barrier phases in step.
-        const bool idle = __all_sync(kAll, !row_valid);
-        const uint32_t t_s = t_tile + kHalfKeys * hf;         // this half's S columns
+        const uint32_t t_s = t_tile + kHalfKeys * hf;              // this half's S columns
         const uint32_t t_p = t_tile + kColP + kHalfKeys / 2 * hf;  // and P columns (bf16 pairs)
         const uint32_t t_o = t_tile + kColO + kHeadDim / 2 * hf;   // and O dims
         // Half-row maxima and sums pass between the halves through shared
-        // memory, double-buffered by block parity, behind a named barrier of
-        // the tile's 256 softmax threads.  Every warp of the tile reaches that
-        // barrier once per block and once after the last, also a warp of
-        // padding rows and a warp that gave up after a timed-out wait (it
-        // goes on without waiting or working), so the counts always match.
+        // memory (maxima double-buffered by block parity, sums in a third
+        // slot), behind a named barrier of the tile's 256 softmax threads.
+        // Every warp of the tile reaches that barrier once per block and once
+        // after a segment's last, also a warp of padding rows and a warp that
+        // gave up after a timed-out wait (it goes on without waiting or
+        // working), so the counts always match.
         float* xch = reinterpret_cast<float*>(base + kOffX);
         auto xslot = [&](int par, int half) { return xch + ((par * kTiles + tq) * kHalves + half) * kRows + r; };
         const int xbar = 1 + tq;  // named barrier id of the tile
         bool dead = false;
-        for (int j = 0; j < nb; ++j) {
-            if (!dead && !__all_sync(kAll, wait_bar(&s_full[tq], static_cast<uint32_t>(j) & 1u, abort_flag, a.err)))
-                dead = true;
-            const bool work = !dead && !idle;
-            const int k0 = j * kBlockKeys + kHalfKeys * hf;
-            const bool need_mask = (j + 1) * kBlockKeys > L;  // block-level, so warp-uniform
-            float2 sum2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
-            float bm = -INFINITY;
-            bool first = false;
-            if (work) {
-                tc_fence_after();
-                first = __any_sync(kAll, m == -INFINITY);  // some row has no reference yet
-                if (!first)  // one pass: the half's maximum and P against the current reference
-                    sweep_s(t_s, t_p, k0, need_mask, rm, m, bm, sum2);
-                else
-                    bm = row_max(t_s, k0, need_mask, rm);
+        int J = 0;
+        if (n_segs > 0) build_q(0);
+        for (int k = 0; k < *n_segs_p; ++k) {
+            // Only the row mask and the block range stay live through the block
+            // loop; the rest is read again for the epilogue (register budget).
+            RowMask rm;
+            int b0, b1;
+            {
+                const Seg& sg = segs[k];
+                b0 = sg.b0;
+                b1 = sg.b1;
+                const UnitInfo ui = unit_info(a, sg.u);
+                const int t_row = ui.t_begin + tq * a.tile_tokens + rt;
+                rm.L = ui.L;
+                rm.T = ui.T;
+                rm.t_chunk = t_row;
+                rm.tree = tree;
+                rm.valid = (rt < a.tile_tokens) && (t_row < ui.t_end);
+                rm.bits = (tree && rm.valid) ? __ldg(a.tree + ui.q0 + t_row) : 0ull;
             }
-            // the row's block maximum over both halves
-            *xslot(j & 1, hf) = bm;
-            named_bar_sync(xbar, kTileThreads);
-            bm = fmaxf(bm, *xslot(j & 1, hf ^ 1));
-            if (work) {
-                // raise this row's reference to the block maximum?
-                const bool raise = bm > m + kLazyLog2 || (m == -INFINITY && bm != -INFINITY);
-                if (first || __any_sync(kAll, raise)) {
-                    const bool rescale = raise && m != -INFINITY;
-                    const float alpha = rescale ? ex2f(m - bm) : 1.f;
-                    if (__any_sync(kAll, rescale)) scale_o(t_o, alpha);  // O *= alpha (1 for other rows)
-                    l *= alpha;
-                    if (raise) m = bm;
-                    // P again for the whole warp; rows with no visible key yet
-                    // have S = -inf everywhere, so mu = 0 gives P = 0
+            const bool row_valid = rm.valid;
+            // m: the row's reference maximum (log2 units; -inf until a key is
+            // seen).  O (in TMEM) and l are sums of 2^(S - m) terms.  Padding
+            // rows (past the chunk, or the last rows of a tile when G does not
+            // divide 128) have Q = 0, so S = 0 on unmasked keys: they start at
+            // m = 0 and never ask for a first pass or a redo; their results are
+            // not written.
+            float m = row_valid ? -INFINITY : 0.f, l = 0.f;
+            // A warp of padding rows only (the tail of the last tile) never
+            // sweeps S: its P and O rows are never read back, and each row of
+            // an MMA is independent of the others.  It still waits for each S
+            // before it arrives on p_full, which keeps the barrier phases in step.
+            const bool idle = __all_sync(kAll, !row_valid);
+            for (int j = b0; j < b1; ++j, ++J) {
+                if (!dead && !__all_sync(kAll, wait_bar(&s_full[tq], static_cast<uint32_t>(J) & 1u, abort_flag, a.err)))
+                    dead = true;
+                const bool work = !dead && !idle;
+                const int k0 = j * kBlockKeys + kHalfKeys * hf;
+                const bool need_mask = (j + 1) * kBlockKeys > rm.L;  // block-level, so warp-uniform
+                float2 sum2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+                float bm = -INFINITY;
+                bool first = false;
+                if (work) {
+                    tc_fence_after();
+                    first = __any_sync(kAll, m == -INFINITY);  // some row has no reference yet
+                    if (!first)  // one pass: the half's maximum and P against the current reference
+                        sweep_s(t_s, t_p, k0, need_mask, rm, m, bm, sum2);
+                    else
+                        bm = row_max(t_s, k0, need_mask, rm);
+                }
+                // the row's block maximum over both halves
+                *xslot(J & 1, hf) = bm;
+                named_bar_sync(xbar, kTileThreads);
+                bm = fmaxf(bm, *xslot(J & 1, hf ^ 1));
+                if (work) {
+                    // raise this row's reference to the block maximum?
+                    const bool raise = bm > m + kLazyLog2 || (m == -INFINITY && bm != -INFINITY);
+                    if (first || __any_sync(kAll, raise)) {
+                        const bool rescale = raise && m != -INFINITY;
+                        const float alpha = rescale ? ex2f(m - bm) : 1.f;
+                        if (__any_sync(kAll, rescale)) scale_o(t_o, alpha);  // O *= alpha (1 for other rows)
+                        l *= alpha;
+                        if (raise) m = bm;
+                        // P again for the whole warp; rows with no visible key yet
+                        // have S = -inf everywhere, so mu = 0 gives P = 0
+                        tmem_wait_st();
+                        sum2[0] = row_exp_to_tmem(t_s, t_p, k0, need_mask, rm, m == -INFINITY ? 0.f : m);
+                        sum2[1] = make_float2(0.f, 0.f);
+                    }
                     tmem_wait_st();
-                    sum2[0] = row_exp_to_tmem(t_s, t_p, k0, need_mask, rm, m == -INFINITY ? 0.f : m);
-                    sum2[1] = make_float2(0.f, 0.f);
+                    tc_fence_before();
                 }
-                tmem_wait_st();
-                tc_fence_before();
+                if (!dead) mbar_arrive(&p_full[tq]);
+                const float2 s01 = __fadd2_rn(sum2[0], sum2[1]);
+                l += s01.x + s01.y;
             }
-            if (!dead) mbar_arrive(&p_full[tq]);
-            const float2 s01 = __fadd2_rn(sum2[0], sum2[1]);
-            l += s01.x + s01.y;
-        }
-        // the row sum over both halves (slot parity nb & 1: its last readers
-        // passed the barrier of block nb - 1)
-        *xslot(nb & 1, hf) = l;
-        named_bar_sync(xbar, kTileThreads);
-        const float lt = l + *xslot(nb & 1, hf ^ 1);
-        if (!dead && !idle &&
-            __all_sync(kAll, wait_bar(&pv_full[tq], static_cast<uint32_t>(nb - 1) & 1u, abort_flag, a.err))) {
-            tc_fence_after();
-            const float inv = lt > 0.f ? 1.f / lt : 0.f;
-            __nv_bfloat16* dst = a.out + (static_cast<size_t>(q0 + t_row) * a.n_q + h * a.group + rg) * kHeadDim +
-                                 kHeadDim / 2 * hf;
-            const bool write = row_valid && !*abort_flag;
+            // The next segment's Q tiles go in now: its first S can then run
+            // while this segment's epilogue reads O (S of this segment's last
+            // block has completed, so the tensor core is done with these tiles).
+            if (k + 1 < *n_segs_p) build_q(k + 1);
+            // the row sum over both halves
+            *xslot(2, hf) = l;
+            named_bar_sync(xbar, kTileThreads);
+            const float lt = l + *xslot(2, hf ^ 1);
+            const bool have_o = !dead && !idle &&
+                                __all_sync(kAll, wait_bar(&pv_full[tq], static_cast<uint32_t>(J - 1) & 1u, abort_flag, a.err));
+            if (have_o) tc_fence_after();
+            const Seg sg = segs[k];
+            __nv_bfloat16* dst;
+            {
+                const UnitInfo ui = unit_info(a, sg.u);
+                dst = a.out + (static_cast<size_t>(ui.q0 + rm.t_chunk) * a.n_q + ui.h * a.group + rg) * kHeadDim +
+                      kHeadDim / 2 * hf;
+            }
+            if (sg.n_parts == 1) {
+                if (have_o) {
+                    const float inv = lt > 0.f ? 1.f / lt : 0.f;
+                    const bool write = row_valid && !*abort_flag;
 #pragma unroll
-            for (int c = 0; c < 2; ++c) {
-                uint32_t x[16];
-                tmem_ld16(t_o + 16 * c, x);
-                tmem_wait16(x);
-                uint32_t w[8];
+                    for (int c = 0; c < 2; ++c) {
+                        uint32_t x[16];
+                        tmem_ld16(t_o + 16 * c, x);
+                        tmem_wait16(x);
+                        uint32_t w[8];
 #pragma unroll
-                for (int i = 0; i < 8; ++i)
-                    w[i] = float2_to_bf16x2(__uint_as_float(x[2 * i]) * inv, __uint_as_float(x[2 * i + 1]) * inv);
-                if (write) {
-                    reinterpret_cast<uint4*>(dst)[2 * c] = make_uint4(w[0], w[1], w[2], w[3]);
-                    reinterpret_cast<uint4*>(dst)[2 * c + 1] = make_uint4(w[4], w[5], w[6], w[7]);
+                        for (int i = 0; i < 8; ++i)
+                            w[i] = float2_to_bf16x2(__uint_as_float(x[2 * i]) * inv, __uint_as_float(x[2 * i + 1]) * inv);
+                        if (write) {
+                            reinterpret_cast<uint4*>(dst)[2 * c] = make_uint4(w[0], w[1], w[2], w[3]);
+                            reinterpret_cast<uint4*>(dst)[2 * c + 1] = make_uint4(w[4], w[5], w[6], w[7]);
+                        }
+                    }
                 }
+                continue;
+            }
+            // ---- a part of a unit: its rows' (m, l, O) into this CTA's slot;
+            // the last part to arrive merges.  Slot 2c + 1 holds the part of the
+            // unit's first CTA (its last segment), slot 2c the other parts (a
+            // CTA's first segment), so no CTA needs both for one launch.
+            const int prow = tq * kRows + r;
+            float* slot = a.part + (2 * static_cast<size_t>(blockIdx.x) + (blockIdx.x == sg.c_first ? 1 : 0)) * kSlotFloats;
+            if (have_o) {
+#pragma unroll
+                for (int c = 0; c < 2; ++c) {
+                    uint32_t x[16];
+                    tmem_ld16(t_o + 16 * c, x);
+                    tmem_wait16(x);
+                    float4* o4 = reinterpret_cast<float4*>(slot + static_cast<size_t>(prow) * kHeadDim + kHeadDim / 2 * hf + 16 * c);
+#pragma unroll
+                    for (int i = 0; i < 4; ++i)
+                        o4[i] = make_float4(__uint_as_float(x[4 * i]), __uint_as_float(x[4 * i + 1]),
+                                            __uint_as_float(x[4 * i + 2]), __uint_as_float(x[4 * i + 3]));
+                }
+                if (hf == 0)
+                    reinterpret_cast<float2*>(slot + static_cast<size_t>(kPartRows) * kHeadDim)[prow] = make_float2(m, lt);
+            }
+            // bar.sync orders every softmax thread's stores before thread 0's
+            // fence, which is cumulative, so one fence publishes the whole part
+            // before its arrival is counted.  The other threads go straight on;
+            // if this part arrived last, the unit is merged at the CTA's end.
+            named_bar_sync(kMergeBar, kSoftmaxThreads);
+            if (threadIdx.x == 0) {
+                __threadfence();
+                const int old = atomicAdd(a.counters + sg.u, 1);
+                if (old == sg.n_parts - 1) {
+                    a.counters[sg.u] = 0;  // ready for the next launch
+                    pend[pend[3]++] = k;
+                }
+            }
+        }
+        // ---- the merges this CTA's parts arrived last for (at most two):
+        // out = sum_p 2^(m_p - M) O_p / sum_p 2^(m_p - M) l_p, M = max_p m_p
+        named_bar_sync(kMergeBar, kSoftmaxThreads);  // pend is complete
+        if (threadIdx.x == 0 && pend[3] > 0) __threadfence();
+        named_bar_sync(kMergeBar, kSoftmaxThreads);
+        for (int pm = 0; pm < pend[3]; ++pm) {
+            const Seg sg = segs[pend[pm]];
+            const UnitInfo ui = unit_info(a, sg.u);
+            const int t_row = ui.t_begin + tq * a.tile_tokens + rt;
+            if (!(rt < a.tile_tokens && t_row < ui.t_end) || *abort_flag) continue;
+            __nv_bfloat16* dst = a.out + (static_cast<size_t>(ui.q0 + t_row) * a.n_q + ui.h * a.group + rg) * kHeadDim +
+                                 kHeadDim / 2 * hf;
+            const int prow = tq * kRows + r;
+            auto pslot = [&](int c) {
+                return a.part + (2 * static_cast<size_t>(c) + (c == sg.c_first ? 1 : 0)) * kSlotFloats;
+            };
+            auto ml_of = [&](int c) {
+                return __ldcg(reinterpret_cast<const float2*>(pslot(c) + static_cast<size_t>(kPartRows) * kHeadDim) + prow);
+            };
+            // the parts' maxima, four loads in flight at a time
+            float M = -INFINITY;
+            for (int p0 = 0; p0 < sg.n_parts; p0 += 4) {
+                float2 ml[4];
+#pragma unroll
+                for (int q = 0; q < 4; ++q) ml[q] = p0 + q < sg.n_parts ? ml_of(sg.c_first + p0 + q) : make_float2(-INFINITY, 0.f);
+#pragma unroll
+                for (int q = 0; q < 4; ++q) M = fmaxf(M, ml[q].x);
+            }
+            // then 16 dims at a time, two parts' loads in flight at a time
+            float lsum = 0.f;
+#pragma unroll 1
+            for (int hh = 0; hh < 2; ++hh) {
+                float o[16];
+#pragma unroll
+                for (int i = 0; i < 16; ++i) o[i] = 0.f;
+                for (int p0 = 0; p0 < sg.n_parts; p0 += 2) {
+                    float2 ml[2];
+                    float4 v[2][4];
+#pragma unroll
+                    for (int q = 0; q < 2; ++q) {
+                        const bool have = p0 + q < sg.n_parts;
+                        const int c = sg.c_first + p0 + (have ? q : 0);
+                        ml[q] = have ? ml_of(c) : make_float2(-INFINITY, 0.f);
+                        const float4* o4 = reinterpret_cast<const float4*>(pslot(c) + static_cast<size_t>(prow) * kHeadDim +
+                                                                           kHeadDim / 2 * hf + 16 * hh);
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) v[q][i] = have ? __ldcg(o4 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+                    }
+#pragma unroll
+                    for (int q = 0; q < 2; ++q) {
+                        const float f = ml[q].x == -INFINITY ? 0.f : ex2f(ml[q].x - M);
+                        if (hh == 0) lsum += f * ml[q].y;
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            o[4 * i] += f * v[q][i].x;
+                            o[4 * i + 1] += f * v[q][i].y;
+                            o[4 * i + 2] += f * v[q][i].z;
+                            o[4 * i + 3] += f * v[q][i].w;
+                        }
+                    }
+                }
+                const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
+#pragma unroll
+                for (int i = 0; i < 2; ++i)
+                    reinterpret_cast<uint4*>(dst)[2 * hh + i] =
+                        make_uint4(float2_to_bf16x2(o[8 * i] * inv, o[8 * i + 1] * inv),
+                                   float2_to_bf16x2(o[8 * i + 2] * inv, o[8 * i + 3] * inv),
+                                   float2_to_bf16x2(o[8 * i + 4] * inv, o[8 * i + 5] * inv),
+                                   float2_to_bf16x2(o[8 * i + 6] * inv, o[8 * i + 7] * inv));
             }
         }
     }
@@ -573,6 +919,16 @@ int prefill_setup(kv_pool* pool) {
         cudaSuccess)
         return KV_ERR_CUDA;
     return KV_OK;
+}
+
+// Two slots per CTA of the persistent grid (at most one per SM).
+size_t prefill_workspace_bytes(const kv_pool* pool) {
+    if (pool->cfg.dtype != KV_DTYPE_BF16) return 0;
+    return 2 * static_cast<size_t>(pool->sm_count) * kSlotFloats * sizeof(float);
+}
+
+size_t prefill_counter_count(const kv_pool* pool) {
+    return pool->cfg.dtype == KV_DTYPE_BF16 ? static_cast<size_t>(kPersistMaxUnits) : 0;
 }
 
 int launch_prefill(kv_pool* pool, const void* q, const int32_t* q_pos, const int32_t* q_off,
@@ -608,7 +964,16 @@ int launch_prefill(kv_pool* pool, const void* q, const int32_t* q_pos, const int
     a.err = pool->dev_error;
     a.qscale = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(c.head_dim)));
     const int cta_tokens = kTiles * a.tile_tokens;
-    const dim3 grid((max_q + cta_tokens - 1) / cta_tokens, c.n_kv_heads, n_seqs);
+    a.nx = std::max(1, (max_q + cta_tokens - 1) / cta_tokens);
+    a.n_seqs = n_seqs;
+    // More units than SMs but few enough for one work list per CTA: the
+    // persistent grid, one CTA per SM, each taking an equal run of the units'
+    // key blocks (the plain grid would leave part of its last wave idle).
+    const long long n_units = static_cast<long long>(a.nx) * c.n_kv_heads * n_seqs;
+    a.persist = n_units > pool->sm_count && n_units <= kPersistMaxUnits && pool->pre_part && pool->pre_counters;
+    a.part = pool->pre_part;
+    a.counters = pool->pre_counters;
+    const dim3 grid = a.persist ? dim3(pool->sm_count) : dim3(a.nx, c.n_kv_heads, n_seqs);
     void* args[] = {&pool->head_map, &a};
     const cudaError_t e = cudaLaunchKernel(reinterpret_cast<const void*>(&prefill_kernel), grid, dim3(kThreads), args,
                                            kSmemBytes, stream);

@@ -66,32 +66,23 @@ class PrefillCase:
         self.max_pos = int(max((p.max(initial=0) for p in self.pos), default=0)) + 16
 
     def run_oracle(self):
+        """Pages filled and attention computed by the oracle's bulk helpers
+        (orc_paged_append_tokens, orc_paged_prefill), which
+        tests/test_oracle_bulk.py pins bit for bit to the per-token append and
+        orc_attention_masked with the explicit mask."""
         host = O.HostPages(self.n_pages, O.BF16 if self.dtype == "bf16" else O.F32, self.n_q, self.n_kv)
-        outs = []
-        for s in range(len(self.L)):
-            L, T = int(self.L[s]), int(self.T[s])
-            for t in range(L + T):
-                host.append_token(self.bt[s], t, int(self.pos[s][t]), self.k[s][t], self.v[s][t])
-            if T == 0:
-                continue
-            k, v = host.gather(self.bt[s], L + T)
-            qr = self.q[self.q_off[s]:self.q_off[s + 1]]
-            q = (O.bf16_bits_to_f32(qr) if self.dtype == "bf16" else np.asarray(qr, np.float32)).copy()  # [T, n_q, d]
-            for i in range(T):
-                c, sn = O.cos_sin(host.inv, int(self.q_pos[self.q_off[s] + i]), 1, 64)
-                O.apply_rope_in_place(q[i], c, sn, self.n_q, 1, 64)
-            mask = np.zeros((T, L + T), np.uint8)
-            mask[:, :L] = 1
-            for i in range(T):
-                if self.parents[s] is None:
-                    mask[i, L:L + i + 1] = 1
-                else:
-                    bits = int(self.masks[self.q_off[s] + i].view(np.uint64))
-                    mask[i, L:] = [(bits >> j) & 1 for j in range(T)]
-            out = O.attention_masked(np.ascontiguousarray(q.transpose(1, 0, 2)), k, v, self.n_q, self.n_kv,
-                                     T, L + T, 64, mask)  # [n_q, T, d]
-            outs.append(out.transpose(1, 0, 2))
-        return host, np.concatenate(outs) if outs else np.zeros((0, self.n_q, 64), np.float32)
+        n = len(self.L)
+        tot = self.L + self.T
+        rows = np.repeat(np.arange(n, dtype=np.int32), tot)
+        slots = np.concatenate([np.arange(int(t), dtype=np.int32) for t in tot]) if n else np.zeros(0, np.int32)
+        pos = np.concatenate(self.pos).astype(np.int32) if n else np.zeros(0, np.int32)
+        k = np.concatenate([a.reshape(-1, self.n_kv, 64) for a in self.k])
+        v = np.concatenate([a.reshape(-1, self.n_kv, 64) for a in self.v])
+        host.append_tokens(self.bt, rows, slots, pos, k, v)
+        if self.q_off[-1] == 0:
+            return host, np.zeros((0, self.n_q, 64), np.float32)
+        out = host.prefill(self.bt, self.L, self.q_off, self.q_pos, self.q, masks=self.masks)
+        return host, out
 
     def make_pool(self):
         from llmhost_b200.kv import KvPool
@@ -210,3 +201,51 @@ def test_prefill_kv_head_shards(cuda, n_q, n_kv, dtype):
     tree = [-1] + [int(rng.integers(0, i)) for i in range(1, 30)]
     check(PrefillCase(n_q, n_kv, [(0, 7), (130, 200), (17, 64)], seed=31, dtype=dtype), f"{dtype} {n_q}q/{n_kv}kv causal")
     check(PrefillCase(n_q, n_kv, [(40, tree), (0, [-1, 0, 0, 1])], seed=32, dtype=dtype), f"{dtype} {n_q}q/{n_kv}kv tree")
+
+
+# ---- the persistent schedule (more (sequence, kv head, tile pair) units than SMs) ----------------
+# Each CTA of the persistent grid takes an equal run of all units' key blocks;
+# a unit cut between CTAs is computed in parts and merged by the last part.
+# These cases reach its edges: a unit longer than several CTAs' runs (middle
+# parts), units with no work (chunk shorter than the launch's max_q), fewer
+# work positions than CTAs, tree masks, and launches repeated on the same
+# pool (the merge counters must come back to zero).
+
+def test_persistent_schedule_long_unit_split_many_ways(cuda):
+    # 24 sequences x 8 kv heads = 192 units; one sequence has 20k cached keys,
+    # so its units each span several CTAs' runs
+    seqs = [(20000, 40)] + [(int(L), 30) for L in np.random.default_rng(50).integers(0, 600, size=23)]
+    case = PrefillCase(24, 8, seqs, seed=51)
+    host, ref = case.run_oracle()
+    with case.make_pool() as pool:
+        for rep in range(3):  # repeated launches on one pool
+            out = case.run_gpu(pool)
+            assert pool.last_error() == 0, rep
+            assert_close_rows(out, ref, RTOL["bf16"], f"persistent long unit, launch {rep}")
+
+
+def test_persistent_schedule_empty_units_and_few_positions(cuda):
+    # max_q 256 at group 3 gives 4 tile pairs per (sequence, head): 5 x 8 x 4 =
+    # 160 units, of which only the first tile pair of each holds tokens, so
+    # the run list has fewer positions than the grid has CTAs
+    seqs = [(0, 1), (5, 2), (100, 1), (0, 3), (17, 1)]
+    case = PrefillCase(24, 8, seqs, seed=52)
+    host, ref = case.run_oracle()
+    with case.make_pool() as pool:
+        for rep in range(2):
+            out = case.run_gpu(pool, max_q=256)
+            assert pool.last_error() == 0, rep
+            assert_close_rows(out, ref, RTOL["bf16"], f"persistent sparse units, launch {rep}")
+
+
+@pytest.mark.parametrize("n_q", [24, 32])
+def test_persistent_schedule_tree_verify(cuda, n_q):
+    # 32 sequences x 8 kv heads = 256 units: the speculative verify's launch
+    # shape, with ragged prefixes and trees
+    rng = np.random.default_rng(53 + n_q)
+
+    def rand_tree(n):
+        return [-1] + [int(rng.integers(0, i)) for i in range(1, n)]
+
+    seqs = [(int(rng.integers(0, 3000)), rand_tree(int(rng.integers(1, 65)))) for _ in range(32)]
+    check(PrefillCase(n_q, 8, seqs, seed=54), f"persistent tree verify {n_q}q/8kv")
