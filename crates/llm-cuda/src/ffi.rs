@@ -45,6 +45,12 @@ pub struct kv_state {
     _opaque: [u8; 0],
 }
 
+/// Opaque continuous-batching scheduler (`kv_sched`).
+#[repr(C)]
+pub struct kv_sched {
+    _opaque: [u8; 0],
+}
+
 /// `kv_pool_config`: field order and types as in the header.
 #[repr(C)]
 #[derive(Clone, Copy, Debug)]
@@ -315,6 +321,36 @@ extern "C" {
     pub fn kv_state_free_list(st: *const kv_state, out: *mut u32, cap: i64, n: *mut i64) -> i32;
     pub fn kv_state_refcount(st: *const kv_state, page: u32, count: *mut u32) -> i32;
     pub fn kv_state_pending_base(st: *const kv_state, seq_id: u64, base: *mut i64) -> i32;
+
+    pub fn kv_draft_tree_best_first(
+        cand_parent: *const i32,
+        cand_token: *const u32,
+        cand_prob: *const f64,
+        n_cand: i32,
+        max_nodes: i32,
+        max_depth: i32,
+        tokens: *mut u32,
+        tree: *mut i32,
+        picked: *mut i32,
+        n_out: *mut i32,
+    ) -> i32;
+    pub fn kv_sched_create(out: *mut *mut kv_sched) -> i32;
+    pub fn kv_sched_destroy(s: *mut kv_sched) -> i32;
+    pub fn kv_sched_add(s: *mut kv_sched, seq_id: u64) -> i32;
+    pub fn kv_sched_remove(s: *mut kv_sched, seq_id: u64) -> i32;
+    pub fn kv_sched_running(s: *const kv_sched, out: *mut u64, cap: i64, n: *mut i64) -> i32;
+    pub fn kv_sched_set_pending(s: *mut kv_sched, seq_id: u64, prefill_tokens: i64) -> i32;
+    pub fn kv_sched_plan_step(
+        s: *mut kv_sched,
+        token_budget: i64,
+        chunk_tokens: i32,
+        seq_ids: *mut u64,
+        n_tokens: *mut i32,
+        is_prefill: *mut i32,
+        cap: i32,
+        n_out: *mut i32,
+    ) -> i32;
+    pub fn kv_sched_lpt(weights: *const i64, n: i32, n_bins: i32, bins: *mut i32) -> i32;
 
     pub fn kv_decode_attn_noalloc(
         pages: *const c_void,

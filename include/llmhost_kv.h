@@ -309,6 +309,48 @@ int kv_state_refcount(const kv_state *st, uint32_t page, uint32_t *count);
 /* Token count at which the staged draft starts (its first slot). */
 int kv_state_pending_base(const kv_state *st, uint64_t seq_id, int64_t *base);
 
+/* ---- the path's callers: draft trees and the batch scheduler ---------------
+ * Host-only.  The reference has both as placeholders: a DraftModel hook that
+ * returns tokens and a parent array (crates/llm-engine/src/draft.rs:9-23) and
+ * a Scheduler of running sequence ids (crates/llm-engine/src/schedule.rs:8-48). */
+
+/* The speculative tree from a draft model's candidates, best first:
+ * candidate c has parent cand_parent[c] (-1: a root; parents precede their
+ * children), token cand_token[c] and probability cand_prob[c] in [0, 1] given
+ * its parent.  Its score is the product of the probabilities on its path.
+ * Nodes are picked one at a time, the highest-scoring eligible candidate
+ * next (ties to the lower index); a candidate is eligible once its parent is
+ * picked (roots from the start) and if its depth (roots 0) is <= max_depth.
+ * At most max_nodes are picked.  Out, in pick order: tokens, tree (parent as
+ * an index into the output, -1 for roots: the DraftProposal form, valid for
+ * kv_tree_validate) and, if not NULL, picked (candidate index); *n_out nodes. */
+int kv_draft_tree_best_first(const int32_t *cand_parent, const uint32_t *cand_token, const double *cand_prob,
+                             int32_t n_cand, int32_t max_nodes, int32_t max_depth, uint32_t *tokens, int32_t *tree,
+                             int32_t *picked, int32_t *n_out);
+
+typedef struct kv_sched kv_sched; /* opaque */
+int kv_sched_create(kv_sched **out);
+int kv_sched_destroy(kv_sched *s);
+/* Scheduler::add (schedule.rs:23-27): appended once, in insertion order. */
+int kv_sched_add(kv_sched *s, uint64_t seq_id);
+/* Scheduler::remove (schedule.rs:29-31). */
+int kv_sched_remove(kv_sched *s, uint64_t seq_id);
+/* Scheduler::running / schedule (schedule.rs:34-47): the running ids in order. */
+int kv_sched_running(const kv_sched *s, uint64_t *out, int64_t cap, int64_t *n);
+/* Prompt tokens still to prefill for a running sequence (0: it decodes). */
+int kv_sched_set_pending(kv_sched *s, uint64_t seq_id, int64_t prefill_tokens);
+/* One step's batch under token_budget: first one decode token for every
+ * running sequence with no prompt left, in running order, then prompt chunks
+ * of up to chunk_tokens in running order while the budget lasts (the chunks
+ * are taken off the sequences' pending counts).  Out: seq_ids, n_tokens,
+ * is_prefill for *n_out entries (cap >= running sequences). */
+int kv_sched_plan_step(kv_sched *s, int64_t token_budget, int32_t chunk_tokens, uint64_t *seq_ids,
+                       int32_t *n_tokens, int32_t *is_prefill, int32_t cap, int32_t *n_out);
+/* Longest-processing-time assignment of n items to n_bins (sessions to GPUs
+ * by resident KV length): items by decreasing weight (ties to the lower
+ * index), each to the currently lightest bin (ties to the lower bin). */
+int kv_sched_lpt(const int64_t *weights, int32_t n, int32_t n_bins, int32_t *bins);
+
 /* Decode attention for callers that cannot allocate device memory.
  *
  * No counterpart in the reference.  The arguments and results of

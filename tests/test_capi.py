@@ -33,9 +33,10 @@ def test_library_exports_every_declared_symbol():
 
 
 def test_python_binding_covers_header():
-    from llmhost_b200 import state
+    from llmhost_b200 import sched, state
 
-    bound = {name for name, _, _ in _capi.SIGNATURES} | {name for name, _, _ in state.STATE_SIGNATURES}
+    bound = ({name for name, _, _ in _capi.SIGNATURES} | {name for name, _, _ in state.STATE_SIGNATURES}
+             | {name for name, _, _ in sched.SCHED_SIGNATURES})
     assert declared_functions() <= bound
 
 

@@ -17,6 +17,7 @@ FFI = CRATE / "src" / "ffi.rs"
 
 C_TO_RUST = {
     "int": "i32", "int32_t": "i32", "uint32_t": "u32", "int64_t": "i64", "uint64_t": "u64", "float": "f32",
+    "double": "f64", "kv_sched": "kv_sched",
     "size_t": "usize", "void": "c_void", "char": "c_char",
     "kv_pool": "kv_pool", "kv_state": "kv_state", "kv_pool_config": "kv_pool_config",
     "kv_token_move": "kv_token_move", "kv_tree_error": "kv_tree_error",
