@@ -32,6 +32,101 @@ float orc_bf16_to_f32(uint16_t h) {
     return f;
 }
 
+/* IEEE binary16 <-> binary32, round to nearest even (the `half` crate's
+ * f16::from_f32 / to_f32, which llm-quant uses for block scales). */
+uint16_t orc_f32_to_f16(float f) {
+    uint32_t u;
+    memcpy(&u, &f, 4);
+    const uint32_t sign = (u >> 16) & 0x8000u;
+    const uint32_t ex = (u >> 23) & 0xffu;
+    uint32_t man = u & 0x7fffffu;
+    if (ex == 0xffu) return (uint16_t)(sign | 0x7c00u | (man ? 0x200u | (man >> 13) : 0u)); /* inf / nan */
+    const int e = (int)ex - 127 + 15;                                                    /* rebiased */
+    if (e >= 31) return (uint16_t)(sign | 0x7c00u);                                       /* overflow: inf */
+    if (e <= 0) {                                                                         /* subnormal or zero */
+        if (e < -10) return (uint16_t)sign;
+        man |= 0x800000u;                       /* implicit bit */
+        const int shift = 14 - e;               /* 24-bit significand -> 10 - (1 - e) bits */
+        uint32_t h = man >> shift;
+        const uint32_t rem = man & ((1u << shift) - 1u), half = 1u << (shift - 1);
+        if (rem > half || (rem == half && (h & 1u))) ++h;
+        return (uint16_t)(sign | h);
+    }
+    uint32_t h = ((uint32_t)e << 10) | (man >> 13);
+    const uint32_t rem = man & 0x1fffu;
+    if (rem > 0x1000u || (rem == 0x1000u && (h & 1u))) ++h; /* may carry into the exponent: still right */
+    return (uint16_t)(sign | h);
+}
+
+float orc_f16_to_f32(uint16_t h) {
+    const uint32_t sign = (uint32_t)(h & 0x8000u) << 16;
+    const uint32_t ex = (h >> 10) & 0x1fu, man = h & 0x3ffu;
+    uint32_t u;
+    if (ex == 0x1fu)
+        u = sign | 0x7f800000u | (man << 13);
+    else if (ex != 0)
+        u = sign | ((ex - 15 + 127) << 23) | (man << 13);
+    else if (man == 0)
+        u = sign;
+    else { /* subnormal: normalise */
+        int e = -1;
+        uint32_t m = man;
+        do {
+            ++e;
+            m <<= 1;
+        } while (!(m & 0x400u));
+        u = sign | ((uint32_t)(127 - 15 - e) << 23) | ((m & 0x3ffu) << 13);
+    }
+    float f;
+    memcpy(&f, &u, 4);
+    return f;
+}
+
+/* crates/llm-quant/src/lib.rs:26-36 (BlockQ8_0::quantize)
+ *   amax = fold(0.0, |acc, v| acc.max(v.abs())); scale = f16::from_f32(amax / 127.0);
+ *   inv = if scale_f == 0.0 { 0.0 } else { 1.0 / scale_f };
+ *   q = (src * inv).round().clamp(-127.0, 127.0) as i8 */
+void orc_quantize_q8_0(const float *src, uint16_t *scale, int8_t *qs) {
+    float amax = 0.0f;
+    for (int i = 0; i < 32; i++) amax = fmaxf(amax, fabsf(src[i]));
+    const uint16_t sc = orc_f32_to_f16(amax / 127.0f);
+    const float sf = orc_f16_to_f32(sc);
+    const float inv = sf == 0.0f ? 0.0f : 1.0f / sf;
+    for (int i = 0; i < 32; i++) {
+        float q = roundf(src[i] * inv);
+        q = q < -127.0f ? -127.0f : (q > 127.0f ? 127.0f : q);
+        qs[i] = (int8_t)q;
+    }
+    *scale = sc;
+}
+
+/* crates/llm-quant/src/lib.rs:63-78 (BlockQ4::quantize): scale amax / 8,
+ * q clamped to -8..7, element 2i in the low nibble of byte i, 2i + 1 high. */
+void orc_quantize_q4(const float *src, uint16_t *scale, uint8_t *qs) {
+    float amax = 0.0f;
+    for (int i = 0; i < 32; i++) amax = fmaxf(amax, fabsf(src[i]));
+    const uint16_t sc = orc_f32_to_f16(amax / 8.0f);
+    const float sf = orc_f16_to_f32(sc);
+    const float inv = sf == 0.0f ? 0.0f : 1.0f / sf;
+    for (int i = 0; i < 16; i++) qs[i] = 0;
+    for (int i = 0; i < 32; i++) {
+        float q = roundf(src[i] * inv);
+        q = q < -8.0f ? -8.0f : (q > 7.0f ? 7.0f : q);
+        const uint8_t nib = (uint8_t)((int8_t)q) & 0x0fu;
+        qs[i / 2] |= (i & 1) ? (uint8_t)(nib << 4) : nib;
+    }
+    *scale = sc;
+}
+
+/* BlockQ8_0::dequantize / BlockQ4::dequantize (lib.rs:40-45, 83-100):
+ * f32::from(q) * scale. */
+static inline float deq_q8(int8_t q, float scale) { return (float)q * scale; }
+static inline float deq_q4(uint8_t packed, int hi, float scale) {
+    const uint8_t nib = hi ? (uint8_t)(packed >> 4) : (uint8_t)(packed & 0x0fu);
+    const int8_t v = (int8_t)(nib << 4) >> 4;
+    return (float)v * scale;
+}
+
 /* rope.rs:6-14
  *   let dim_f = dim as f32;
  *   for i in (0..dim).step_by(2) { let expo = i as f32 / dim_f;
@@ -268,6 +363,71 @@ void orc_rms_norm(const float *x, const float *weight, float eps, size_t dim, si
     }
 }
 
+/* Quantised pages (ORC_Q8: K and V as Q8_0 blocks; ORC_K8V4: K as Q8_0, V as
+ * Q4), head_dim 64 = two 32-element blocks per (head, token).  A page holds,
+ * in order: K codes [n_kv][P][64] int8, V codes [n_kv][P][64] int8 (Q8) or
+ * [n_kv][P][32] packed nibbles (K8V4), K scales [n_kv][P][2] f16, V scales
+ * [n_kv][P][2] f16.  Queries, outputs and the appended k/v stay bf16. */
+static inline int is_quant(int dtype) { return dtype == ORC_Q8 || dtype == ORC_K8V4; }
+static inline int io_dtype(int dtype) { return is_quant(dtype) ? ORC_BF16 : dtype; }
+static inline size_t q_vrow(int dtype) { return dtype == ORC_Q8 ? 64 : 32; }
+size_t orc_page_bytes(int dtype, size_t n_kv, size_t P, size_t d) {
+    if (is_quant(dtype)) return n_kv * P * (d + q_vrow(dtype) + 8);
+    return 2 * n_kv * P * d * (dtype == ORC_BF16 ? 2 : 4);
+}
+static inline size_t q_koff(size_t n_kv, size_t P, int dtype, size_t h, size_t j) {
+    (void)n_kv; (void)dtype;
+    return (h * P + j) * 64;
+}
+static inline size_t q_voff(size_t n_kv, size_t P, int dtype, size_t h, size_t j) {
+    return n_kv * P * 64 + (h * P + j) * q_vrow(dtype);
+}
+static inline size_t q_ksoff(size_t n_kv, size_t P, int dtype, size_t h, size_t j) {
+    return n_kv * P * (64 + q_vrow(dtype)) + (h * P + j) * 4;
+}
+static inline size_t q_vsoff(size_t n_kv, size_t P, int dtype, size_t h, size_t j) {
+    return n_kv * P * (64 + q_vrow(dtype)) + n_kv * P * 4 + (h * P + j) * 4;
+}
+
+/* One token's rotated K (fp32 [n_kv][64]) and V (bf16 bits) into a quantised page. */
+static void q_store_token(uint8_t *page, int dtype, size_t n_kv, size_t P, size_t j, const float *kr,
+                          const void *v_raw) {
+    for (size_t h = 0; h < n_kv; h++) {
+        float vv[64];
+        for (int e = 0; e < 64; e++) vv[e] = orc_bf16_to_f32(((const uint16_t *)v_raw)[h * 64 + e]);
+        for (int b = 0; b < 2; b++) {
+            uint16_t sc;
+            orc_quantize_q8_0(kr + h * 64 + 32 * b, &sc, (int8_t *)(page + q_koff(n_kv, P, dtype, h, j) + 32 * b));
+            memcpy(page + q_ksoff(n_kv, P, dtype, h, j) + 2 * b, &sc, 2);
+            if (dtype == ORC_Q8)
+                orc_quantize_q8_0(vv + 32 * b, &sc, (int8_t *)(page + q_voff(n_kv, P, dtype, h, j) + 32 * b));
+            else
+                orc_quantize_q4(vv + 32 * b, &sc, page + q_voff(n_kv, P, dtype, h, j) + 16 * b);
+            memcpy(page + q_vsoff(n_kv, P, dtype, h, j) + 2 * b, &sc, 2);
+        }
+    }
+}
+
+/* Dequantised K and V of (head h, slot j) of a quantised page into fp32 rows. */
+static void q_load_token(const uint8_t *page, int dtype, size_t n_kv, size_t P, size_t h, size_t j, float *kd,
+                         float *vd) {
+    for (int b = 0; b < 2; b++) {
+        uint16_t ks, vs;
+        memcpy(&ks, page + q_ksoff(n_kv, P, dtype, h, j) + 2 * b, 2);
+        memcpy(&vs, page + q_vsoff(n_kv, P, dtype, h, j) + 2 * b, 2);
+        const float kf = orc_f16_to_f32(ks), vf = orc_f16_to_f32(vs);
+        const int8_t *kq = (const int8_t *)(page + q_koff(n_kv, P, dtype, h, j)) + 32 * b;
+        for (int e = 0; e < 32; e++) kd[32 * b + e] = deq_q8(kq[e], kf);
+        if (dtype == ORC_Q8) {
+            const int8_t *vq = (const int8_t *)(page + q_voff(n_kv, P, dtype, h, j)) + 32 * b;
+            for (int e = 0; e < 32; e++) vd[32 * b + e] = deq_q8(vq[e], vf);
+        } else {
+            const uint8_t *vq = page + q_voff(n_kv, P, dtype, h, j) + 16 * b;
+            for (int e = 0; e < 32; e++) vd[32 * b + e] = deq_q4(vq[e / 2], e & 1, vf);
+        }
+    }
+}
+
 /* k_norm non-NULL: lfm2.rs:805-812 rms_norm_heads on k (heads = n_kv) first. */
 static void append_token_impl(void *pages, int dtype, size_t n_kv, size_t P, size_t d, const uint32_t *bt,
                               size_t slot, const void *k_raw, const void *v, const float *cos_row,
@@ -276,11 +436,17 @@ static void append_token_impl(void *pages, int dtype, size_t n_kv, size_t P, siz
     uint32_t page = bt[slot / P];
     size_t j = slot % P;
     float *kr = (float *)malloc(n_kv * d * sizeof(float));
-    for (size_t i = 0; i < n_kv * d; i++) kr[i] = load_elem(k_raw, dtype, i);
+    for (size_t i = 0; i < n_kv * d; i++) kr[i] = load_elem(k_raw, io_dtype(dtype), i);
     if (k_norm) orc_rms_norm(kr, k_norm, eps, d, n_kv, kr);
     /* lfm2.rs:816-825: RoPE on k (heads = n_kv, tokens = 1) before the store
      * at lfm2.rs:828-832. */
     orc_apply_rope_in_place(kr, cos_row, sin_row, n_kv, 1, d);
+    if (is_quant(dtype)) {
+        q_store_token((uint8_t *)pages + (size_t)page * orc_page_bytes(dtype, n_kv, P, d), dtype, n_kv, P, j, kr,
+                      v);
+        free(kr);
+        return;
+    }
     for (size_t h = 0; h < n_kv; h++) {
         size_t kofs = (size_t)page * page_elems + (h * P + j) * d;
         size_t vofs = (size_t)page * page_elems + ((n_kv + h) * P + j) * d;
@@ -314,6 +480,11 @@ static void gather_range(const void *pages, int dtype, size_t n_kv, size_t P, si
             if (page == ORC_PAGE_NONE) {
                 memset(kd, 0, d * sizeof(float));
                 memset(vd, 0, d * sizeof(float));
+                continue;
+            }
+            if (is_quant(dtype)) {
+                q_load_token((const uint8_t *)pages + (size_t)page * orc_page_bytes(dtype, n_kv, P, d), dtype, n_kv, P,
+                             h, j, kd, vd);
                 continue;
             }
             size_t kofs = (size_t)page * page_elems + (h * P + j) * d;
@@ -354,7 +525,7 @@ static void paged_decode_impl(const void *pages, int dtype, size_t n_q, size_t n
     float *cs = (float *)malloc(2 * d * sizeof(float));
     float *scores = (float *)malloc(n_q * n_att * sizeof(float));
     gather_range(pages, dtype, n_kv, P, d, bt, lo, seq_len, 0, n_kv, k, v);
-    for (size_t i = 0; i < n_q * d; i++) q[i] = load_elem(q_raw, dtype, i);
+    for (size_t i = 0; i < n_q * d; i++) q[i] = load_elem(q_raw, io_dtype(dtype), i);
     if (q_norm) orc_rms_norm(q, q_norm, eps, d, n_q, q);
     /* lfm2.rs:816-822: cos_sin at pos, RoPE on q with heads = n_q, tokens = 1 */
     orc_cos_sin(inv_freq, seq_len - 1, 1, d, cs, cs + d);
@@ -389,7 +560,7 @@ typedef struct {
 } step_job;
 
 static void step_one(step_job *j, size_t s) {
-    size_t esz = j->dtype == ORC_BF16 ? 2 : 4;
+    size_t esz = io_dtype(j->dtype) == ORC_BF16 ? 2 : 4;
     size_t len = (size_t)j->seq_lens[s];
     const uint32_t *row = j->bt + s * j->bt_stride;
     if (len > 0) {
@@ -495,7 +666,7 @@ typedef struct {
 
 static void append_bulk_one(void *arg, size_t i) {
     const append_bulk *a = (const append_bulk *)arg;
-    size_t esz = a->dtype == ORC_BF16 ? 2 : 4;
+    size_t esz = io_dtype(a->dtype) == ORC_BF16 ? 2 : 4;
     float cs[2 * 256];
     orc_cos_sin(a->inv_freq, (size_t)a->tok_pos[i], 1, a->d, cs, cs + a->d);
     append_token_impl(a->pages, a->dtype, a->n_kv, a->P, a->d, a->bt + (size_t)a->tok_row[i] * a->bt_stride,
@@ -544,7 +715,7 @@ static void prefill_one(void *arg, size_t job) {
         for (size_t t = 0; t < T; t++) {
             const void *src = a->q_raw;
             size_t base = ((q0 + t) * a->n_q + qh) * d;
-            for (size_t e = 0; e < d; e++) q[t * d + e] = load_elem(src, a->dtype, base + e);
+            for (size_t e = 0; e < d; e++) q[t * d + e] = load_elem(src, io_dtype(a->dtype), base + e);
             /* RoPE of one token's head at its position (rope.rs:56-81, heads = tokens = 1) */
             orc_cos_sin(a->inv_freq, (size_t)a->q_pos[q0 + t], 1, d, cs, cs + d);
             orc_apply_rope_in_place(q + t * d, cs, cs + d, 1, 1, d);

@@ -33,12 +33,22 @@
 extern "C" {
 #endif
 
-enum { ORC_F32 = 0, ORC_BF16 = 1 };
+enum { ORC_F32 = 0, ORC_BF16 = 1, ORC_Q8 = 2, ORC_K8V4 = 3 };
 #define ORC_PAGE_NONE 0xFFFFFFFFu
 
 /* bf16 <-> f32, round to nearest even (the build's bf16 storage rule). */
 uint16_t orc_f32_to_bf16(float f);
 float orc_bf16_to_f32(uint16_t h);
+
+/* IEEE binary16 <-> binary32, round to nearest even. */
+uint16_t orc_f32_to_f16(float f);
+float orc_f16_to_f32(uint16_t h);
+/* crates/llm-quant/src/lib.rs:26-36 and :63-78: one 32-element block. */
+void orc_quantize_q8_0(const float *src, uint16_t *scale, int8_t *qs);
+void orc_quantize_q4(const float *src, uint16_t *scale, uint8_t *qs);
+/* Bytes of one page: quantised pages (ORC_Q8, ORC_K8V4) hold per (head,
+ * token) the K codes, the V codes and two f16 scales each (see kv_oracle.c). */
+size_t orc_page_bytes(int dtype, size_t n_kv, size_t P, size_t d);
 
 /* rope.rs:6-14 */
 void orc_inv_freq(size_t dim, float theta, float *out);

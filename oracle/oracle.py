@@ -20,6 +20,8 @@ LIB_PATH = HERE / "_build" / "libkv_oracle.so"
 
 F32 = 0
 BF16 = 1
+Q8 = 2     # K and V as Q8_0 blocks (crates/llm-quant/src/lib.rs:14-46)
+K8V4 = 3   # K as Q8_0, V as Q4 blocks (lib.rs:48-101)
 PAGE_NONE = 0xFFFFFFFF
 
 _lib = None
@@ -72,6 +74,14 @@ def lib() -> ctypes.CDLL:
         h.orc_paged_prefill.argtypes = [c_void_p, c_int, c_size_t, c_size_t, c_size_t, c_size_t, c_void_p,
                                         c_size_t, c_size_t, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                         fp, fp, c_int]
+        h.orc_f32_to_f16.restype = c_uint16
+        h.orc_f32_to_f16.argtypes = [c_float]
+        h.orc_f16_to_f32.restype = c_float
+        h.orc_f16_to_f32.argtypes = [c_uint16]
+        h.orc_quantize_q8_0.argtypes = [fp, c_void_p, c_void_p]
+        h.orc_quantize_q4.argtypes = [fp, c_void_p, c_void_p]
+        h.orc_page_bytes.restype = c_size_t
+        h.orc_page_bytes.argtypes = [c_int, c_size_t, c_size_t, c_size_t]
         h.orc_max_threads.restype = c_int
         _lib = h
     return _lib
@@ -149,15 +159,51 @@ def attention_masked(q, k, v, n_q, n_kv, q_len, kv_len, dim, mask):
 
 
 # ---- paged layout ---------------------------------------------------------------
+def quantize_q8_0(block) -> tuple[int, np.ndarray]:
+    """One 32-element Q8_0 block (orc_quantize_q8_0): (f16 scale bits, int8 codes)."""
+    x = np.ascontiguousarray(block, np.float32)
+    assert x.size == 32
+    sc = np.zeros(1, np.uint16)
+    qs = np.zeros(32, np.int8)
+    lib().orc_quantize_q8_0(_f(x), sc.ctypes.data, qs.ctypes.data)
+    return int(sc[0]), qs
+
+
+def quantize_q4(block) -> tuple[int, np.ndarray]:
+    """One 32-element Q4 block (orc_quantize_q4): (f16 scale bits, 16 packed bytes)."""
+    x = np.ascontiguousarray(block, np.float32)
+    assert x.size == 32
+    sc = np.zeros(1, np.uint16)
+    qs = np.zeros(16, np.uint8)
+    lib().orc_quantize_q4(_f(x), sc.ctypes.data, qs.ctypes.data)
+    return int(sc[0]), qs
+
+
+def f32_to_f16_bits(x: float) -> int:
+    return int(lib().orc_f32_to_f16(x))
+
+
+def f16_bits_to_f32(h: int) -> float:
+    return float(lib().orc_f16_to_f32(h))
+
+
 class HostPages:
-    """A host copy of a page pool in the build's layout ([K|V][n_kv][P][d] per page)."""
+    """A host copy of a page pool in the build's layout: [K|V][n_kv][P][d] per
+    page for F32 / BF16; for the quantised types Q8 / K8V4 the page is bytes
+    (K codes, V codes, K scales, V scales; see kv_oracle.c), and the appended
+    k / v and the queries are bf16."""
 
     def __init__(self, n_pages: int, dtype: int, n_q: int, n_kv: int, page_tokens: int = 16,
                  head_dim: int = 64, theta: float = 1e6, data: np.ndarray | None = None):
         self.dtype, self.n_q, self.n_kv = dtype, n_q, n_kv
         self.P, self.d = page_tokens, head_dim
-        self.page_elems = 2 * n_kv * page_tokens * head_dim
-        np_dt = np.uint16 if dtype == BF16 else np.float32
+        self.quant = dtype in (Q8, K8V4)
+        if self.quant:
+            self.page_elems = int(lib().orc_page_bytes(dtype, n_kv, page_tokens, head_dim))
+            np_dt = np.uint8
+        else:
+            self.page_elems = 2 * n_kv * page_tokens * head_dim
+            np_dt = np.uint16 if dtype == BF16 else np.float32
         if data is None:
             data = np.zeros((n_pages, self.page_elems), np_dt)
         assert data.dtype == np_dt and data.shape == (n_pages, self.page_elems)
@@ -165,7 +211,7 @@ class HostPages:
         self.inv = inv_freq(head_dim, theta)
 
     def _raw(self, a) -> np.ndarray:
-        np_dt = np.uint16 if self.dtype == BF16 else np.float32
+        np_dt = np.uint16 if self.dtype in (BF16, Q8, K8V4) else np.float32
         a = np.ascontiguousarray(a)
         assert a.dtype == np_dt, (a.dtype, np_dt)
         return a
