@@ -139,11 +139,14 @@ fn check_seq(status: i32, seq_id: u64, bad_index: i64, tree: Option<&ffi::kv_tre
     })
 }
 
-/// KV storage type (the reference's `KvDtype` tags F16/Q8/K8V4 and implements none).
+/// KV storage type (the reference's `KvDtype` tags F16/Q8/K8V4 and implements
+/// none; `Q8` and `K8V4` here use llm-quant's Q8_0 / Q4 block formats).
 #[derive(Clone, Copy, Debug, PartialEq, Eq)]
 pub enum KvDtype {
     F32,
     Bf16,
+    Q8,
+    K8V4,
 }
 
 /// Shape and size of a pool (`kv_pool_config`).
@@ -165,6 +168,8 @@ impl PoolConfig {
             dtype: match self.dtype {
                 KvDtype::F32 => ffi::KV_DTYPE_F32,
                 KvDtype::Bf16 => ffi::KV_DTYPE_BF16,
+                KvDtype::Q8 => ffi::KV_DTYPE_Q8,
+                KvDtype::K8V4 => ffi::KV_DTYPE_K8V4,
             },
             n_q_heads: self.n_q_heads,
             n_kv_heads: self.n_kv_heads,

@@ -42,8 +42,22 @@ extern "C" {
 #define KV_PAGE_NONE 0xFFFFFFFFu /* block-table entry of an evicted / absent page */
 
 /* KV storage type.  The reference's KvDtype (crates/llm-quant/src/formats.rs:59-68)
- * tags F16/Q8/K8V4 and implements none; this library stores F32 and BF16. */
-typedef enum { KV_DTYPE_F32 = 0, KV_DTYPE_BF16 = 1 } kv_dtype;
+ * tags F16/Q8/K8V4 and implements none.  This library stores F32, BF16 and
+ * the two quantised tags, with the block quantisers of the same crate
+ * (crates/llm-quant/src/lib.rs:14-101, 32 elements and one f16 scale per
+ * block, two blocks per 64-dim head row):
+ *   KV_DTYPE_Q8    K and V as Q8_0 blocks (int8 codes, scale max|x| / 127)
+ *   KV_DTYPE_K8V4  K as Q8_0, V as Q4 blocks (4-bit codes, scale max|x| / 8)
+ * A quantised page is n_kv head blocks, each holding in order: K codes
+ * [P][64] int8, V codes [P][64] int8 (Q8) or [P][32] packed nibbles (K8V4:
+ * element 2i in the low nibble of byte i), K scales [P][2] f16, V scales
+ * [P][2] f16 (2176 or 1664 bytes a head at P = 16).  K is rotated (RoPE) in fp32 and then quantised.  For
+ * quantised pools the appended k / v, q and out are bf16.  They take
+ * appends, decode attention (kv_decode_attn, and kv_append_decode_attn as an
+ * append launch followed by the attention launch), page copies and token
+ * moves; kv_norm_append_decode_attn and kv_prefill_attn return
+ * KV_ERR_UNSUPPORTED for them. */
+typedef enum { KV_DTYPE_F32 = 0, KV_DTYPE_BF16 = 1, KV_DTYPE_Q8 = 2, KV_DTYPE_K8V4 = 3 } kv_dtype;
 
 typedef enum {
     KV_OK = 0,

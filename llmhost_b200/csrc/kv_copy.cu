@@ -12,7 +12,10 @@
 //                  chunk is read into shared memory before any destination is
 //                  written.  That is exact for the moves kv_state_accept /
 //                  kv_state_rollback produce (a later move never reads a slot
-//                  an earlier move wrote).  Groups run in parallel.
+//                  an earlier move wrote).  Groups run in parallel.  A token
+//                  is its row of every page section (K and V; or K codes, V
+//                  codes, K scales and V scales of every head block in
+//                  quantised pools).
 // Page ids past the pool and slots past a page are skipped and flagged in the
 // pool's error word.
 #include <algorithm>
@@ -41,39 +44,86 @@ __global__ void __launch_bounds__(256) copy_pages_kernel(uint4* __restrict__ pag
 
 constexpr int kMoveSmem = 48 * 1024;
 
-// One CTA per group of moves.  A token's K/V is 2 * nkv rows of row_vecs
-// 16-byte chunks (K rows of every head, then V rows), one row per head.
-__global__ void __launch_bounds__(256) move_tokens_kernel(uint4* __restrict__ pages, const kv_token_move* moves,
+// A page as sections: token (head h, slot j) of section i is the row of
+// row[i] words at base[i] + h * head[i] + j * row[i].  f32 / bf16 pools: K
+// rows then V rows, each [nkv][16][row] (16-byte words).  Quantised pools:
+// nkv head blocks of K codes, V codes, K scales, V scales (4-byte words, as
+// the 4-byte scale rows need).
+struct PageSections {
+    int n;          // sections
+    int row[4];     // words per (head, slot) row
+    int base[4];    // section start in a page (head 0), in words
+    int head[4];    // words between heads
+    int tok_words;  // words of one token: nkv * sum(row)
+    int page_words;
+};
+
+PageSections page_sections(const kv_pool* pool, int word_bytes) {
+    PageSections ps{};
+    const int nkv = pool->cfg.n_kv_heads;
+    if (is_quant(pool->cfg.dtype)) {
+        const int bytes[4] = {kHeadDim, quant_vrow(pool->cfg.dtype), 4, 4};
+        const int block = kPageTokens * (bytes[0] + bytes[1] + bytes[2] + bytes[3]) / word_bytes;
+        ps.n = 4;
+        int at = 0;
+        for (int i = 0; i < 4; ++i) {
+            ps.row[i] = bytes[i] / word_bytes;
+            ps.base[i] = at;
+            ps.head[i] = block;
+            at += kPageTokens * ps.row[i];
+            ps.tok_words += nkv * ps.row[i];
+        }
+        ps.page_words = nkv * block;
+    } else {
+        const int r = kHeadDim * static_cast<int>(pool->elem_bytes) / word_bytes;
+        ps.n = 2;
+        for (int i = 0; i < 2; ++i) {
+            ps.row[i] = r;
+            ps.base[i] = i * nkv * kPageTokens * r;
+            ps.head[i] = kPageTokens * r;
+            ps.tok_words += nkv * r;
+        }
+        ps.page_words = 2 * nkv * kPageTokens * r;
+    }
+    return ps;
+}
+
+// One CTA per group of moves.  A token is its rows of every section, one row
+// per (section, head).
+template <typename Word>
+__global__ void __launch_bounds__(256) move_tokens_kernel(Word* __restrict__ pages, const kv_token_move* moves,
                                                           const int32_t* group_off, int n_moves, int nkv,
-                                                          int row_vecs, uint32_t n_pages, int* err) {
-    extern __shared__ uint4 buf[];
+                                                          const PageSections ps, uint32_t n_pages, int* err) {
+    extern __shared__ uint4 buf_raw[];
+    Word* buf = reinterpret_cast<Word*>(buf_raw);
     const int beg = __ldg(group_off + blockIdx.x), end = __ldg(group_off + blockIdx.x + 1);
     if (beg < 0 || end > n_moves || beg > end) {  // offsets outside the move array
         if (threadIdx.x == 0) flag_error(err, kDevErrBadPage);
         return;
     }
-    const int tok_vecs = 2 * nkv * row_vecs;
-    const int page_vecs = tok_vecs * kPageTokens;
-    const int chunk = kMoveSmem / (tok_vecs * 16);
-    // 16-byte chunk v of the token in (page, slot), or nullptr if out of range.
-    auto addr = [&](uint32_t page, int slot, int v) -> uint4* {
+    const int tok_words = ps.tok_words;
+    const int chunk = kMoveSmem / (tok_words * static_cast<int>(sizeof(Word)));
+    // word v of the token in (page, slot), or nullptr if out of range.
+    auto addr = [&](uint32_t page, int slot, int v) -> Word* {
         if (page >= n_pages || slot < 0 || slot >= kPageTokens) return nullptr;
-        const int row = v / row_vecs;  // K heads, then V heads
-        return pages + static_cast<size_t>(page) * page_vecs +
-               (static_cast<size_t>(row) * kPageTokens + slot) * row_vecs + v % row_vecs;
+        int sec = 0;
+        while (sec + 1 < ps.n && v >= nkv * ps.row[sec]) v -= nkv * ps.row[sec++];
+        const int head = v / ps.row[sec];
+        return pages + static_cast<size_t>(page) * ps.page_words + ps.base[sec] +
+               static_cast<size_t>(head) * ps.head[sec] + static_cast<size_t>(slot) * ps.row[sec] + v % ps.row[sec];
     };
     for (int c0 = beg; c0 < end; c0 += chunk) {
         const int cn = min(chunk, end - c0);
-        for (int e = threadIdx.x; e < cn * tok_vecs; e += blockDim.x) {
-            const kv_token_move m = moves[c0 + e / tok_vecs];
-            const uint4* p = addr(m.src_page, m.src_slot, e % tok_vecs);
+        for (int e = threadIdx.x; e < cn * tok_words; e += blockDim.x) {
+            const kv_token_move m = moves[c0 + e / tok_words];
+            const Word* p = addr(m.src_page, m.src_slot, e % tok_words);
             if (p) buf[e] = *p;
             else flag_error(err, kDevErrBadPage);
         }
         __syncthreads();
-        for (int e = threadIdx.x; e < cn * tok_vecs; e += blockDim.x) {
-            const kv_token_move m = moves[c0 + e / tok_vecs];
-            uint4* p = addr(m.dst_page, m.dst_slot, e % tok_vecs);
+        for (int e = threadIdx.x; e < cn * tok_words; e += blockDim.x) {
+            const kv_token_move m = moves[c0 + e / tok_words];
+            Word* p = addr(m.dst_page, m.dst_slot, e % tok_words);
             if (p) *p = buf[e];
             else flag_error(err, kDevErrBadPage);
         }
@@ -118,10 +168,15 @@ int kv_move_tokens(kv_pool* pool, const kv_token_move* moves, int32_t n_moves, c
     int prev = -1;
     cudaGetDevice(&prev);
     if (prev != pool->cfg.device) cudaSetDevice(pool->cfg.device);
-    const int row_vecs = kHeadDim * static_cast<int>(pool->elem_bytes) / 16;
-    move_tokens_kernel<<<n_groups, 256, kMoveSmem, static_cast<cudaStream_t>(stream)>>>(
-        static_cast<uint4*>(pool->pages), moves, group_offsets, n_moves, pool->cfg.n_kv_heads, row_vecs,
-        pool->cfg.n_pages, pool->dev_error);
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (is_quant(pool->cfg.dtype))
+        move_tokens_kernel<uint32_t><<<n_groups, 256, kMoveSmem, st>>>(
+            static_cast<uint32_t*>(pool->pages), moves, group_offsets, n_moves, pool->cfg.n_kv_heads,
+            page_sections(pool, 4), pool->cfg.n_pages, pool->dev_error);
+    else
+        move_tokens_kernel<uint4><<<n_groups, 256, kMoveSmem, st>>>(
+            static_cast<uint4*>(pool->pages), moves, group_offsets, n_moves, pool->cfg.n_kv_heads,
+            page_sections(pool, 16), pool->cfg.n_pages, pool->dev_error);
     const cudaError_t e = cudaGetLastError();
     if (prev >= 0 && prev != pool->cfg.device) cudaSetDevice(prev);
     return e == cudaSuccess ? KV_OK : KV_ERR_CUDA;

@@ -904,7 +904,7 @@ int raise_smem_limit(const void* fn, int device, size_t bytes) {
 
 int decode_setup(kv_pool* pool) {
     const auto& c = pool->cfg;
-    if (c.dtype == KV_DTYPE_BF16) return decode_tc_setup(pool);
+    if (c.dtype == KV_DTYPE_BF16 || is_quant(c.dtype)) return decode_tc_setup(pool);
     const DecodeVariant* v = find_variant(c.dtype, c.n_kv_heads, c.n_q_heads / c.n_kv_heads);
     if (!v) return KV_ERR_UNSUPPORTED;
     const size_t smem = v->smem(c.max_seqs);
@@ -926,7 +926,7 @@ int decode_setup(kv_pool* pool) {
 // Partial rows: two per CTA; the tensor-core kernel (bf16 pools) keeps two
 // more per CTA for the run partials of a long sequence's two-level merge.
 size_t decode_workspace_slots(const kv_pool* pool) {
-    return (pool->cfg.dtype == KV_DTYPE_BF16 ? 4 : 2) * static_cast<size_t>(pool->decode_grid);
+    return (pool->cfg.dtype == KV_DTYPE_F32 ? 2 : 4) * static_cast<size_t>(pool->decode_grid);
 }
 
 // Merge counters: one per sequence, then two per CTA for the runs.
@@ -942,6 +942,17 @@ int launch_decode(kv_pool* pool, const void* q, const uint32_t* bt, int32_t bt_s
     if (c.dtype == KV_DTYPE_BF16)
         return launch_decode_tc(pool, q, bt, bt_stride, seq_lens, n_seqs, window, out, stream, new_k, new_v, q_norm,
                                 k_norm, eps);
+    if (is_quant(c.dtype)) {
+        // The append (quantise on store) and the attention as two launches.
+        if (q_norm != nullptr || k_norm != nullptr) return KV_ERR_UNSUPPORTED;
+        if (new_k != nullptr) {
+            const int rc = launch_append(pool, new_k, new_v, nullptr, nullptr, nullptr, seq_lens, n_seqs, n_seqs, bt,
+                                         bt_stride, stream);
+            if (rc != KV_OK) return rc;
+        }
+        return launch_decode_tc(pool, q, bt, bt_stride, seq_lens, n_seqs, window, out, stream, nullptr, nullptr,
+                                nullptr, nullptr, 0.f);
+    }
     const DecodeVariant* v = find_variant(c.dtype, c.n_kv_heads, c.n_q_heads / c.n_kv_heads);
     if (!v) return KV_ERR_UNSUPPORTED;
     DecodeArgs a;

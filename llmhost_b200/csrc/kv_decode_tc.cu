@@ -45,6 +45,8 @@
 // the persistent grid.  The kernel is launched with programmatic stream
 // serialization: it reads nothing global before griddepcontrol.wait, and lets
 // the next launch start on the SMs it has left.
+#include <cuda_fp16.h>
+
 #include <cmath>
 
 #include "kv_common.cuh"
@@ -59,13 +61,26 @@ constexpr int kUnitKeys = 128;                        // keys per unit (MMA M of
 constexpr int kUnitPages = kUnitKeys / kPageTokens;   // 8
 constexpr int kUnitBytes = kUnitKeys * 128;           // 16 KiB: K (or V) of one unit
 constexpr int kStageBytes = 4 * kUnitBytes;           // K_0 K_1 V_0 V_1
-constexpr int kStages = 3;
+constexpr int kStagesBf16 = 3;                       // tile ring of bf16 pools
 constexpr int kSoftThreads = 128;                     // warps 0-3
 constexpr int kProducerWarp = 4;
 constexpr int kMmaWarp = 5;
 constexpr int kEpiWarp0 = 6;                          // warps 6-9
 constexpr int kEpiThreads = 128;
 constexpr int kThreads = 320;
+// Quantised pools: a fourth warpgroup (warps 12-15) turns the pages' int8 /
+// int4 codes into the f16 K and V tiles of a stage (in place of the TMA
+// boxes); warps 10-11 have no role.  Sixteen warps launch with 128 registers
+// each; the converters hand 32 of theirs to the softmax warpgroup
+// (setmaxnreg: 4 x 96 + 4 x 160 + 8 x 128 = 16 x 128).
+constexpr int kConvWarp0 = 12;                        // warps 12-15
+constexpr int kConvWarps = 4;
+constexpr int kConvRegs = 96;
+constexpr int kSoftRegsQ = 160;
+constexpr int kConvPages = kUnitPages / kConvWarps;   // pages of a unit per converter warp
+constexpr int kPrefetchStages = 4;                    // L2 prefetch distance of quantised page blocks
+template <int kQ>
+__host__ __device__ constexpr int block_threads() { return kQ ? 512 : kThreads; }
 constexpr uint32_t kTmemCols = 256;
 constexpr uint32_t kColS = 0;   // S of buffer sb, unit u: columns kColS + 32 sb + 16 u ..
 constexpr uint32_t kColO = 64;  // O of segment buffer e, accumulator c: kColO + 64 e + 16 c; unit u's queries at + 8 u
@@ -102,14 +117,21 @@ struct TcArgs {
     float eps;
 };
 
-template <int NKV, int G>
+template <int NKV, int G, int kQ = 0>
 struct TcShape {
     static_assert(G >= 1 && G <= 4, "query heads per kv head");
     static_assert(NKV == 1 || NKV == 2 || NKV == 4 || NKV == 8, "kv heads");
     static constexpr int NQ = NKV * G;
     static constexpr int kPairs = NKV >= 2 ? NKV / 2 : 1;  // stages per block round = O accumulators
     // shared memory, from a 1024-aligned base
-    static constexpr int kOffQ = kStages * kStageBytes;             // Q tiles: head h at + 1024 h (8 rows)
+    // Tile ring: three stages for bf16 pools; two for quantised pools, which
+    // also keep two stages of raw page blocks (8 pages x 2 units) that the
+    // converter warps expand into the tiles.
+    static constexpr int kRing = kQ ? 2 : kStagesBf16;
+    static constexpr int kHeadBlock = kQ ? kPageTokens * (kHeadDim + (kQ == 2 ? 32 : 64) + 8) : 0;
+    static constexpr int kRawStage = 2 * kUnitPages * kHeadBlock;
+    static constexpr int kOffRaw = kRing * kStageBytes;
+    static constexpr int kOffQ = kOffRaw + (kQ ? kRing * kRawStage : 0);  // Q tiles: head h at + 1024 h (8 rows)
     static constexpr int kOffP = kOffQ + (NKV + 1) * 1024;          // P, two buffers
     static constexpr int kOffStg = kOffP + 2 * kPBytes;             // fused append inputs
     static constexpr int kStgBytes = NKV * 256 + 256;               // per head K row, V row; RoPE row
@@ -121,10 +143,11 @@ struct TcShape {
     static constexpr int kOffM = kOffMax + 2 * 4 * 8 * 4;           // float [2 buffers][NQ]: reference maxima
     static constexpr int kOffL = kOffM + 2 * NQ * 4;                // float [2 buffers][4 warps][NQ]: row sums
     static constexpr int kOffOb = kOffL + 2 * 4 * NQ * 4;           // float [64][4]
-    static constexpr int kBars = 24;                                // mbarrier slots (2 kStages + 16 used)
+    static constexpr int kBars = 28;                                // mbarrier slots (4 kRing + 16 used)
     static constexpr int kOffBar = (kOffOb + 64 * 4 * 4 + 7) & ~7;
     static constexpr int kOffInt = kOffBar + kBars * 8;             // int [16]
-    static constexpr int kOffScan = kOffInt + 16 * 4;               // int [n_seqs + 1]
+    static constexpr int kOffLdm = kOffInt + 16 * 4;                // int [4]: quantised pages loaded per stage
+    static constexpr int kOffScan = kOffLdm + 4 * 4;                // int [n_seqs + 1]
     static size_t smem_bytes(int max_seqs) { return 1024 + kOffScan + (static_cast<size_t>(max_seqs) + 1) * 4; }
 };
 
@@ -290,21 +313,100 @@ __device__ __forceinline__ void warp_reduce_scatter_store(float (&v)[N], float* 
 
 // kNorm: the q/k RMSNorm of kv_norm_append_decode_attn is compiled in (a
 // separate instantiation, so that the plain kernel's hot loops stay as they are).
-template <int NKV, int G, bool kNorm>
-__global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(const __grid_constant__ CUtensorMap hmap,
-                                                                const TcArgs a) {
-    using Sh = TcShape<NKV, G>;
+
+// ---- quantised pages -------------------------------------------------------
+// Prefetch of `bytes` (a multiple of 16, 16-byte aligned) into L2.
+__device__ __forceinline__ void prefetch_l2(const void* gsrc, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(gsrc), "r"(bytes) : "memory");
+}
+
+// Plain (non-tensor, no multicast) bulk copy of `bytes` (a multiple of 16,
+// both addresses 16-byte aligned) into this CTA's shared memory, completing
+// on `bar`'s transaction count.
+__device__ __forceinline__ void bulk_load(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 ::"r"(smem_addr(smem_dst)), "l"(gsrc), "r"(bytes), "r"(smem_addr(bar))
+                 : "memory");
+}
+
+// Codes to f16 tile rows (quantised pools run the MMAs on f16 operands: the
+// code-to-value steps then stay on the ALU and FMA pipes).  A code c biased
+// to a byte u = c + o becomes the f16 1024 + u through the bit pattern
+// 0x6400 | u (a byte permute places two at once), less 1024 + o gives c
+// exactly, and c * scale (f16 scale, one f16 rounding to nearest even) is
+// the dequantised element of crates/llm-quant/src/lib.rs (BlockQ8_0 and
+// BlockQ4 dequantize) to f16 precision.
+__device__ __forceinline__ uint2 codes4_to_f16(uint32_t biased, __half2 off, __half2 s) {
+    const uint32_t lo = __byte_perm(biased, 0x64646464u, 0x5140);  // bytes 0, 1
+    const uint32_t hi = __byte_perm(biased, 0x64646464u, 0x7362);  // bytes 2, 3
+    __half2 a = __hmul2(__hsub2(*reinterpret_cast<const __half2*>(&lo), off), s);
+    __half2 b = __hmul2(__hsub2(*reinterpret_cast<const __half2*>(&hi), off), s);
+    return make_uint2(*reinterpret_cast<uint32_t*>(&a), *reinterpret_cast<uint32_t*>(&b));
+}
+
+// 16 int8 codes (one uint4) -> 16 f16 (two uint4); codes biased by 128.
+__device__ __forceinline__ void q8x16_to_f16(uint4 c, __half2 s, uint4& o0, uint4& o1) {
+    const __half2 off = __half2half2(__ushort_as_half(0x6480));  // 1152 = 1024 + 128
+    const uint2 a = codes4_to_f16(c.x ^ 0x80808080u, off, s), b = codes4_to_f16(c.y ^ 0x80808080u, off, s);
+    const uint2 d = codes4_to_f16(c.z ^ 0x80808080u, off, s), e = codes4_to_f16(c.w ^ 0x80808080u, off, s);
+    o0 = make_uint4(a.x, a.y, b.x, b.y);
+    o1 = make_uint4(d.x, d.y, e.x, e.y);
+}
+
+// 8 packed 4-bit codes (one word, element 2i in the low nibble of byte i) ->
+// 8 f16 (one uint4); nibbles biased by 8.
+__device__ __forceinline__ uint4 q4x8_to_f16(uint32_t w, __half2 s) {
+    const __half2 off = __half2half2(__ushort_as_half(0x6408));     // 1032 = 1024 + 8
+    const uint32_t even = (w & 0x0F0F0F0Fu) ^ 0x08080808u;         // elements 0, 2, 4, 6
+    const uint32_t odd = ((w >> 4) & 0x0F0F0F0Fu) ^ 0x08080808u;  // elements 1, 3, 5, 7
+    const uint2 a = codes4_to_f16(__byte_perm(even, odd, 0x5140), off, s);  // elements 0..3
+    const uint2 b = codes4_to_f16(__byte_perm(even, odd, 0x7362), off, s);  // elements 4..7
+    return make_uint4(a.x, a.y, b.x, b.y);
+}
+
+// The 16-bit operand type of the MMAs: bf16 (bf16 pools) or f16 (quantised).
+template <bool kF16>
+__device__ __forceinline__ uint32_t pack_ab(float a, float b) {
+    if constexpr (kF16) {
+        const __half2 h = __floats2half2_rn(a, b);
+        return *reinterpret_cast<const uint32_t*>(&h);
+    } else {
+        return float2_to_bf16x2(a, b);
+    }
+}
+
+// x rounded to the operand type: its bits, and the rounded value in `xr`.
+template <bool kF16>
+__device__ __forceinline__ unsigned short round_ab(float x, float& xr) {
+    if constexpr (kF16) {
+        const __half h = __float2half_rn(x);
+        xr = __half2float(h);
+        return __half_as_ushort(h);
+    } else {
+        const __nv_bfloat16 h = __float2bfloat16_rn(x);
+        xr = __bfloat162float(h);
+        return __bfloat16_as_ushort(h);
+    }
+}
+
+template <int NKV, int G, bool kNorm, int kQ>
+__global__ void __launch_bounds__(block_threads<kQ>(), 1) decode_tc_kernel(const __grid_constant__ CUtensorMap hmap,
+                                                                           const TcArgs a) {
+    static_assert(!(kNorm && kQ), "quantised pools take the norm-free form");
+    constexpr int kNT = block_threads<kQ>();
+    using Sh = TcShape<NKV, G, kQ>;
+    constexpr int kRing = Sh::kRing;
     constexpr int NQ = Sh::NQ;
     constexpr int kPairs = Sh::kPairs;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    // Every barrier's slot follows from kStages, so no ring depth can make two
+    // Every barrier's slot follows from kRing, so no ring depth can make two
     // of them share an mbarrier (a TMA's byte count and an MMA commit landing
     // on one barrier would corrupt both phases).
     uint64_t* bars = reinterpret_cast<uint64_t*>(base + Sh::kOffBar);
-    uint64_t* full = bars;                    // [kStages]  TMA landed
-    uint64_t* empty = full + kStages;         // [kStages]  PV done with the stage
-    uint64_t* s_full = empty + kStages;       // [2]        S MMAs done
+    uint64_t* full = bars;                    // [kRing]    tiles landed (TMA) or written (converters)
+    uint64_t* empty = full + kRing;           // [kRing]    PV done with the stage
+    uint64_t* s_full = empty + kRing;         // [2]        S MMAs done
     uint64_t* s_free = s_full + 2;            // [2]        S read by the softmax
     uint64_t* p_full = s_free + 2;            // [2]        P (and zeroed V rows) written
     uint64_t* pv_done = p_full + 2;           // [2]        PV MMAs done
@@ -313,7 +415,11 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(const __grid_con
     uint64_t* o_full = mma_done + 1;          // [2]        a segment's last PV done (O buffer e)
     uint64_t* seg_done = o_full + 2;          // [2]        its reference maxima and row sums written
     uint64_t* o_free = seg_done + 2;          // [2]        the epilogue is done with O buffer e and its sums
-    static_assert(2 * kStages + 16 <= Sh::kBars, "the barrier slots fit the reserved space");
+    uint64_t* rfull = o_free + 2;             // [kRing]    quantised pools: a stage's page blocks landed
+    uint64_t* rempty = rfull + kRing;         // [kRing]    and were read by the converters
+    static_assert(4 * kRing + 16 <= Sh::kBars, "the barrier slots fit the reserved space");
+    static_assert(kRing <= 4, "one loaded-page mask per stage");
+    int* ldmask = reinterpret_cast<int*>(base + Sh::kOffLdm);
     int* ints = reinterpret_cast<int*>(base + Sh::kOffInt);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ints);
     volatile int* abort_flag = ints + 1;
@@ -327,13 +433,16 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(const __grid_con
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n = a.n_seqs;
+    static_assert(4 * kConvRegs + 4 * kSoftRegsQ + 8 * 128 == 16 * 128, "the register split adds up");
     // Set-up.  The producer warp initialises the barriers, scans the stage
     // counts and goes straight on to its first copies; the other warps clear
     // the Q padding and P buffers, allocate TMEM and wait for the scan.
     if (warp == kProducerWarp) {
         if (lane == 0) {
-            for (int i = 0; i < kStages; ++i) {
-                mbar_init(&full[i], 1);
+            for (int i = 0; i < kRing; ++i) {
+                mbar_init(&full[i], kQ ? kConvWarps * 32 : 1);  // TMA arrival, or every converter thread
+                mbar_init(&rfull[i], 1);
+                mbar_init(&rempty[i], kConvWarps * 32);
                 mbar_init(&empty[i], 1);
             }
             for (int i = 0; i < 2; ++i) {
@@ -351,13 +460,13 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(const __grid_con
             }
             *abort_flag = 0;
             fence_mbar_init();
-            prefetch_tmap(&hmap);
+            if constexpr (kQ == 0) prefetch_tmap(&hmap);
         }
         grid_dep_wait();  // the inputs are read from here on
         __syncwarp();
         scan_units(a.seq_lens, n, a.window, Chunk<NKV>::kPages, pstart, lane, Chunk<NKV>::kStages, kLead);
         __syncwarp();
-        named_bar_arrive(kSetupBar, kThreads);
+        named_bar_arrive(kSetupBar, kNT);
     } else {
         if (threadIdx.x < kSoftThreads) {  // Q padding rows and P rows never written stay zero
             uint4* z = reinterpret_cast<uint4*>(base + Sh::kOffQ);
@@ -380,7 +489,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(const __grid_con
         }
         grid_dep_wait();
         tc_fence_before();
-        named_bar_sync(kSetupBar, kThreads);
+        named_bar_sync(kSetupBar, kNT);
         tc_fence_after();
     }
 
@@ -392,7 +501,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(const __grid_con
     const int grid = max(1, min(static_cast<int>(gridDim.x), total));  // at least one stage per CTA
     const int gb = static_cast<int>((static_cast<long long>(cta) * total) / grid);
     const int ge = static_cast<int>((static_cast<long long>(cta + 1) * total) / grid);
-    if (warp >= kEpiWarp0) {  // sequences with no tokens: zeros (every CTA, idle ones too)
+    if (warp >= kEpiWarp0 && warp < kEpiWarp0 + 4) {  // sequences with no tokens: zeros (every CTA, idle ones too)
         for (int s = cta; s < n; s += gridDim.x) {
             if (__ldg(a.seq_lens + s) <= 0) {
                 __nv_bfloat16* o = a.out + static_cast<size_t>(s) * NQ * kHeadDim;
@@ -443,6 +552,25 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(const __grid_con
         StageCursor<NKV> cur;
         cur.start(a, pstart, n, gb, ge);
         Fetch fc = cur.done ? Fetch{0u, false} : fetch(cur);  // a slice may hold lead stages only
+        // Quantised pools: the page blocks of the stage kPrefetchStages ahead
+        // are prefetched into L2, so that the raw ring (two stages, all the
+        // shared memory leaves) is filled from L2 rather than across the
+        // whole HBM latency.
+        StageCursor<NKV> pfc = cur;
+        Fetch fpf{0u, false};
+        int hpf = 0;  // head of this lane's unit in the prefetched stage
+        auto fetch_pf = [&]() {
+            fpf = pfc.done ? Fetch{0u, false} : fetch(pfc);
+            if (!pfc.done) {
+                int b0, b1, n0, n1, pp;
+                stage_units<NKV>(pfc.q, pfc.j, b0, b1, n0, n1, pp);
+                hpf = NKV >= 2 ? 2 * pp + u : 0;
+            }
+        };
+        if constexpr (kQ != 0) {
+            for (int d = 0; d < kPrefetchStages && !pfc.done; ++d) pfc.next(a, pstart);
+            fetch_pf();
+        }
         int issued = 0;
         bool issuing = true, app = false, have_ksc = false;
         float ksc = 0.f;  // lane h < NKV: RMSNorm scale of the new k of head h
@@ -486,11 +614,12 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(const __grid_con
             StageCursor<NKV> nxt = cur;
             nxt.next(a, pstart);
             const Fetch fn = nxt.done ? Fetch{0u, false} : fetch(nxt);  // in flight during the wait below
-            const int i = cur.i, st = i % kStages;
+            const int i = cur.i, st = i % kRing;
             if (issuing) {
                 bool ok = true;
-                if (lane == 0 && i >= kStages)
-                    ok = wait_bar(&empty[st], static_cast<uint32_t>(i / kStages - 1) & 1u, abort_flag, a.err);
+                if (lane == 0 && i >= kRing)
+                    ok = wait_bar(kQ ? &rempty[st] : &empty[st], static_cast<uint32_t>(i / kRing - 1) & 1u, abort_flag,
+                                  a.err);
                 issuing = __shfl_sync(kAll, ok, 0);
             }
             if (issuing) {
@@ -542,18 +671,50 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(const __grid_con
                     }
                     __syncwarp();
                 }
-                if (lane == 0) mbar_arrive_expect_tx(&full[st], kStageBytes);
-                __syncwarp();
                 const int hu = NKV >= 2 ? 2 * p + u : 0;
-                int row = total_rows;  // out of range: zero fill
-                if (fc.load) {
-                    if (fc.phys < a.n_pages)
-                        row = static_cast<int>(fc.phys) * a.page_rows + (kv ? NKV + hu : hu) * kPageTokens;
-                    else
-                        flag_error(a.err, kDevErrBadPage);
+                if constexpr (kQ == 0) {
+                    if (lane == 0) mbar_arrive_expect_tx(&full[st], kStageBytes);
+                    __syncwarp();
+                    int row = total_rows;  // out of range: zero fill
+                    if (fc.load) {
+                        if (fc.phys < a.n_pages)
+                            row = static_cast<int>(fc.phys) * a.page_rows + (kv ? NKV + hu : hu) * kPageTokens;
+                        else
+                            flag_error(a.err, kDevErrBadPage);
+                    }
+                    tma_load_2d(base + st * kStageBytes + kv * 2 * kUnitBytes + u * kUnitBytes + k * 2048, &hmap,
+                                &full[st], 0, row);
+                } else {
+                    // Quantised pages: each loaded page's head blocks (K codes,
+                    // V codes, K scales, V scales; heads 2p, 2p + 1 adjacent)
+                    // with plain bulk copies (no multicast) into raw slot st,
+                    // block (u, k) at (2k + u) head blocks: one copy of both
+                    // units' blocks per page (lane (k, K, 0)), or one per unit
+                    // with a single kv head (lanes (k, K, u)).  The mask of
+                    // loaded pages goes with the stage.
+                    constexpr uint32_t kHB = static_cast<uint32_t>(Sh::kHeadBlock);
+                    const bool ld = fc.load && fc.phys < a.n_pages;
+                    if (fc.load && !ld) flag_error(a.err, kDevErrBadPage);
+                    const unsigned m = __ballot_sync(kAll, ld);
+                    if (lane == 0) {
+                        ldmask[st] = static_cast<int>(m);
+                        mbar_arrive_expect_tx(&rfull[st], NKV >= 2 ? __popc(m & 0x11111111u) * 2 * kHB
+                                                                   : __popc(m & 0x33333333u) * kHB);
+                    }
+                    __syncwarp();
+                    if (ld && kv == 0 && (NKV == 1 || u == 0)) {
+                        const uint8_t* blk = a.pages + (static_cast<size_t>(fc.phys) * NKV + hu) * kHB;
+                        bulk_load(base + Sh::kOffRaw + st * Sh::kRawStage + (2 * k + u) * kHB, blk,
+                                  NKV >= 2 ? 2 * kHB : kHB, &rfull[st]);
+                    }
+                    if (fpf.load && fpf.phys < a.n_pages && kv == 0 && (NKV == 1 || u == 0))
+                        prefetch_l2(a.pages + (static_cast<size_t>(fpf.phys) * NKV + hpf) * kHB,
+                                    NKV >= 2 ? 2 * kHB : kHB);
+                    if (!pfc.done) {
+                        pfc.next(a, pstart);
+                        fetch_pf();
+                    }
                 }
-                tma_load_2d(base + st * kStageBytes + kv * 2 * kUnitBytes + u * kUnitBytes + k * 2048, &hmap, &full[st],
-                            0, row);
                 issued = i + 1;
             }
             cur = nxt;
@@ -563,9 +724,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(const __grid_con
         // Do not leave while a copy may still be landing: the newest copy
         // issued into each stage covers every older one.
         if (lane == 0) {
-            for (int st = 0; st < kStages && st < issued; ++st) {
-                const int last = st + ((issued - 1 - st) / kStages) * kStages;
-                mbar_wait(&full[st], static_cast<uint32_t>(last / kStages) & 1u);
+            for (int st = 0; st < kRing && st < issued; ++st) {
+                const int last = st + ((issued - 1 - st) / kRing) * kRing;
+                mbar_wait(kQ ? &rfull[st] : &full[st], static_cast<uint32_t>(last / kRing) & 1u);
             }
         }
     } else if (warp == kMmaWarp) {
@@ -576,8 +737,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(const __grid_con
         // its stage back to the producer) never queues behind the next
         // stage's copy.  PV(pi) is issued only after S(pi).
         if (lane == 0) {
-            constexpr uint32_t kIdS = instr_desc(16, 128, false, false);
-            constexpr uint32_t kIdPV = instr_desc(16, 128, false, true);
+            constexpr uint32_t kIdS = instr_desc(16, 128, false, false, kQ != 0);
+            constexpr uint32_t kIdPV = instr_desc(16, 128, false, true, kQ != 0);
             const uint32_t st_addr = smem_addr(base), q_addr = smem_addr(base + Sh::kOffQ);
             const uint32_t p_addr = smem_addr(base + Sh::kOffP);
             StageCursor<NKV> sc, pc;
@@ -597,22 +758,22 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(const __grid_con
                      mbar_test(&o_free[eb], static_cast<uint32_t>((pc.seg_no - 2) >> 1) & 1u))) {
                     tc_fence_after();
                     const int pcc = NKV >= 2 ? (pc.q.j0 + pc.j) % kPairs : 0;
-                    const uint32_t va = st_addr + (pc.i % kStages) * kStageBytes + 2 * kUnitBytes;
+                    const uint32_t va = st_addr + (pc.i % kRing) * kStageBytes + 2 * kUnitBytes;
                     const uint32_t pa = p_addr + (pc.i & 1) * kPBytes;
 #pragma unroll
                     for (int kk = 0; kk < kUnitKeys / 16; ++kk)
                         mma_ss(tmem + kColO + 64 * eb + 16 * pcc, smem_desc(va + 2048 * kk, kUnitBytes, 1024),
                                smem_desc(pa + (kk >> 2) * 2048 + (kk & 3) * 32, 16, 1024), kIdPV, !first || kk > 0);
                     mma_commit(&pv_done[pc.i & 1]);
-                    mma_commit(&empty[pc.i % kStages]);
+                    mma_commit(&empty[pc.i % kRing]);
                     if (pc.j == pc.q.nst - 1) mma_commit(&o_full[eb]);
                     pc.next(a, pstart);
                     progress = true;
                 }
                 if (!sc.done) {
-                    const int st = sc.i % kStages, sb = sc.i & 1;
+                    const int st = sc.i % kRing, sb = sc.i & 1;
                     if (!q_ready) q_ready = mbar_test(q_full, static_cast<uint32_t>(sc.seg_no) & 1u);
-                    if (q_ready && mbar_test(&full[st], static_cast<uint32_t>(sc.i / kStages) & 1u) &&
+                    if (q_ready && mbar_test(&full[st], static_cast<uint32_t>(sc.i / kRing) & 1u) &&
                         (sc.i < 2 || mbar_test(&s_free[sb], static_cast<uint32_t>((sc.i - 2) >> 1) & 1u))) {
                         tc_fence_after();
                         int b0, b1, n0, n1, p;
@@ -649,6 +810,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(const __grid_con
         }
     } else if (warp < kProducerWarp) {
         // ---------------- softmax and Q tiles (warps 0-3) ----------------
+        // (quantised pools: with the registers the converter warpgroup gives up)
+        if constexpr (kQ != 0) asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kSoftRegsQ));
         const int t = threadIdx.x;
         const uint32_t lane_base = tmem + (static_cast<uint32_t>(32 * warp) << 16);
         const int kp = t >> 4, slot = t & 15;  // page of the block and slot of this thread's key
@@ -712,8 +875,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(const __grid_con
                     const float a1 = __fadd_rn(__fmul_rn(x.y, c1.x), __fmul_rn(-y.y, c1.y)) * a.qscale;
                     const float b0 = __fadd_rn(__fmul_rn(y.x, c0.x), __fmul_rn(x.x, c0.y)) * a.qscale;
                     const float b1 = __fadd_rn(__fmul_rn(y.y, c1.x), __fmul_rn(x.y, c1.y)) * a.qscale;
-                    lo[e] = float2_to_bf16x2(a0, a1);
-                    hi[e] = float2_to_bf16x2(b0, b1);
+                    lo[e] = pack_ab<kQ != 0>(a0, a1);
+                    hi[e] = pack_ab<kQ != 0>(b0, b1);
                 }
                 uint8_t* row = base + Sh::kOffQ + h * 1024 + n_ * 128;
                 *reinterpret_cast<uint4*>(row + ((c ^ n_) << 4)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
@@ -759,7 +922,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(const __grid_con
                     constexpr int kH1 = NKV >= 2 ? 1 : 0;
                     const int h0 = NKV >= 2 ? 2 * p : 0;
                     const int h1 = h0 + kH1;
-                    const int sb = i & 1, st = i % kStages;
+                    const int sb = i & 1, st = i % kRing;
                     uint8_t* stage = base + st * kStageBytes;
                     // ---- S of this stage: key t's scores for each unit's query heads
                     const bool okS =
@@ -856,12 +1019,13 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(const __grid_con
                     const int chunk = (t & 63) >> 3, within = (t & 7) * 2;
 #pragma unroll
                     for (int c = 0; c < G; ++c) {
-                        const __nv_bfloat16 p0 = __float2bfloat16_rn(v0 ? ex2f(s0[c] - m[h0][c]) : 0.f);
-                        const __nv_bfloat16 p1 = __float2bfloat16_rn(v1 ? ex2f(s1[c] - m[h1][c]) : 0.f);
-                        l[h0][c] += __bfloat162float(p0);
-                        l[h1][c] += __bfloat162float(p1);
-                        *reinterpret_cast<__nv_bfloat16*>(prow + c * 128 + ((chunk ^ c) << 4) + within) = p0;
-                        *reinterpret_cast<__nv_bfloat16*>(prow + (8 + c) * 128 + ((chunk ^ c) << 4) + within) = p1;
+                        float r0, r1;
+                        const unsigned short p0 = round_ab<kQ != 0>(v0 ? ex2f(s0[c] - m[h0][c]) : 0.f, r0);
+                        const unsigned short p1 = round_ab<kQ != 0>(v1 ? ex2f(s1[c] - m[h1][c]) : 0.f, r1);
+                        l[h0][c] += r0;
+                        l[h1][c] += r1;
+                        *reinterpret_cast<unsigned short*>(prow + c * 128 + ((chunk ^ c) << 4) + within) = p0;
+                        *reinterpret_cast<unsigned short*>(prow + (8 + c) * 128 + ((chunk ^ c) << 4) + within) = p1;
                     }
                     if (okS && !v0 && kp < n0) {
                         uint4* vrow = reinterpret_cast<uint4*>(stage + 2 * kUnitBytes + t * 128);
@@ -904,7 +1068,88 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(const __grid_con
             ++segk;
             if (!more) break;
         }
-    } else if (warp >= kEpiWarp0) {
+    } else if (kQ != 0 && warp >= kConvWarp0) {
+        // ---------------- converters (quantised pools, warps 12-15) ----------------
+        // Warp w expands pages [w P, w P + P) (P = kConvPages) of both units
+        // of a stage from its raw slot (head blocks the producer copied) into
+        // the tile slot once the PV before it has released that slot: lane
+        // (r, hb) takes key r's 32-dim block hb of K and of V and writes it
+        // as four 16-byte chunks of f16 in the 128-byte-swizzled tile row
+        // (the layout the TMA boxes give bf16 pools).  A page not loaded
+        // (past the block's end, or a bad id) is written as zeros.
+        if constexpr (kQ != 0) {
+            asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kConvRegs));
+            constexpr int kVRow = kQ == 2 ? 32 : 64;
+            constexpr int kHB = Sh::kHeadBlock;
+            const int cw = warp - kConvWarp0, r = lane >> 1, hb = lane & 1;
+            const uint32_t sw = static_cast<uint32_t>(r & 7);
+            StageCursor<NKV> cur;
+            cur.start(a, pstart, n, gb, ge);
+            bool going = true;
+            while (!cur.done) {
+                const int i = cur.i, st = i % kRing;
+                if (going) {
+                    bool ok = true;
+                    if (lane == 0) {
+                        ok = wait_bar(&rfull[st], static_cast<uint32_t>(i / kRing) & 1u, abort_flag, a.err);
+                        if (ok && i >= kRing)
+                            ok = wait_bar(&empty[st], static_cast<uint32_t>(i / kRing - 1) & 1u, abort_flag, a.err);
+                    }
+                    going = __shfl_sync(kAll, ok, 0);
+                }
+                if (going) {
+                    const unsigned m = static_cast<unsigned>(ldmask[st]);
+                    const uint8_t* raw = base + Sh::kOffRaw + st * Sh::kRawStage;
+                    uint8_t* stage = base + st * kStageBytes;
+#pragma unroll 1
+                    for (int e = 0; e < kConvPages; ++e) {
+                        const int k = kConvPages * cw + e;
+#pragma unroll
+                        for (int u = 0; u < 2; ++u) {
+                            const bool ld = (m >> (4 * k + u)) & 1u;  // lane (k, K, u) saw this page loaded
+                            const uint8_t* blk = raw + (2 * k + u) * kHB;
+                            uint4 ko[4], vo[4];
+                            if (ld) {
+                                const uint4* kr = reinterpret_cast<const uint4*>(blk + r * kHeadDim + 32 * hb);
+                                const uint4* vr = reinterpret_cast<const uint4*>(blk + kPageTokens * kHeadDim +
+                                                                                 r * kVRow + (kVRow / 2) * hb);
+                                const uint8_t* sc = blk + kPageTokens * (kHeadDim + kVRow) + r * 4 + hb * 2;
+                                const __half2 ks = __half2half2(*reinterpret_cast<const __half*>(sc));
+                                const __half2 vs = __half2half2(*reinterpret_cast<const __half*>(sc + kPageTokens * 4));
+                                q8x16_to_f16(kr[0], ks, ko[0], ko[1]);
+                                q8x16_to_f16(kr[1], ks, ko[2], ko[3]);
+                                if constexpr (kQ == 2) {
+                                    const uint4 v = vr[0];
+                                    vo[0] = q4x8_to_f16(v.x, vs);
+                                    vo[1] = q4x8_to_f16(v.y, vs);
+                                    vo[2] = q4x8_to_f16(v.z, vs);
+                                    vo[3] = q4x8_to_f16(v.w, vs);
+                                } else {
+                                    q8x16_to_f16(vr[0], vs, vo[0], vo[1]);
+                                    q8x16_to_f16(vr[1], vs, vo[2], vo[3]);
+                                }
+                            } else {
+#pragma unroll
+                                for (int x = 0; x < 4; ++x) ko[x] = vo[x] = make_uint4(0, 0, 0, 0);
+                            }
+                            uint8_t* krow = stage + u * kUnitBytes + k * 2048 + r * 128;
+                            uint8_t* vrow = krow + 2 * kUnitBytes;
+#pragma unroll
+                            for (int x = 0; x < 4; ++x) {
+                                const uint32_t off = (static_cast<uint32_t>(4 * hb + x) ^ sw) << 4;
+                                *reinterpret_cast<uint4*>(krow + off) = ko[x];
+                                *reinterpret_cast<uint4*>(vrow + off) = vo[x];
+                            }
+                        }
+                    }
+                    proxy_fence();  // generic-proxy tile writes, read by the MMAs
+                    mbar_arrive(&full[st]);
+                    mbar_arrive(&rempty[st]);  // the raw slot may take the next copies
+                }
+                cur.next(a, pstart);
+            }
+        }
+    } else if (warp >= kEpiWarp0 && warp < kEpiWarp0 + 4) {
         // ---------------- epilogue (warps 6-9) ----------------
         // Segment k: O buffer k & 1 once its last PV is done (o_full) and its
         // maxima and row sums are written (seg_done).  TMEM lane r holds head
@@ -1113,15 +1358,25 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(const __grid_con
 // ---------------------------------------------------------------------------
 struct TcVariant {
     int nkv, group;
-    const void* fn;       // plain
-    const void* fn_norm;  // with the q/k RMSNorm
-    size_t (*smem)(int);
+    const void* fn;       // bf16 pages
+    const void* fn_norm;  // bf16 pages, with the q/k RMSNorm
+    const void* fn_q8;    // KV_DTYPE_Q8 pages (codes converted in the CTA)
+    const void* fn_k8v4;  // KV_DTYPE_K8V4 pages
+    size_t (*smem)(int);  // dynamic shared memory of each, by max_seqs
+    size_t (*smem_q8)(int);
+    size_t (*smem_k8v4)(int);
 };
 
 template <int NKV, int G>
 TcVariant make_tc_variant() {
-    return TcVariant{NKV, G, reinterpret_cast<const void*>(&decode_tc_kernel<NKV, G, false>),
-                     reinterpret_cast<const void*>(&decode_tc_kernel<NKV, G, true>), &TcShape<NKV, G>::smem_bytes};
+    return TcVariant{NKV,
+                     G,
+                     reinterpret_cast<const void*>(&decode_tc_kernel<NKV, G, false, 0>),
+                     reinterpret_cast<const void*>(&decode_tc_kernel<NKV, G, true, 0>),
+                     reinterpret_cast<const void*>(&decode_tc_kernel<NKV, G, false, 1>),
+                     reinterpret_cast<const void*>(&decode_tc_kernel<NKV, G, false, 2>),
+                     &TcShape<NKV, G, 0>::smem_bytes, &TcShape<NKV, G, 1>::smem_bytes,
+                     &TcShape<NKV, G, 2>::smem_bytes};
 }
 
 const TcVariant* find_tc_variant(int nkv, int group) {
@@ -1134,21 +1389,33 @@ const TcVariant* find_tc_variant(int nkv, int group) {
     return nullptr;
 }
 
+// The kernel for a pool's storage type (and the norm form for bf16 pools).
+const void* tc_kernel_for(const TcVariant* v, int dtype, bool norm) {
+    if (dtype == KV_DTYPE_Q8) return v->fn_q8;
+    if (dtype == KV_DTYPE_K8V4) return v->fn_k8v4;
+    return norm ? v->fn_norm : v->fn;
+}
+
+int tc_threads_for(int dtype) { return is_quant(dtype) ? block_threads<1>() : block_threads<0>(); }
+
 }  // namespace
 
 int decode_tc_setup(kv_pool* pool) {
     const auto& c = pool->cfg;
     const TcVariant* v = find_tc_variant(c.n_kv_heads, c.n_q_heads / c.n_kv_heads);
     if (!v) return KV_ERR_UNSUPPORTED;
-    const size_t smem = v->smem(c.max_seqs);
+    const size_t smem = (c.dtype == KV_DTYPE_Q8 ? v->smem_q8 : c.dtype == KV_DTYPE_K8V4 ? v->smem_k8v4 : v->smem)(c.max_seqs);
     int optin = 0;
     if (cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, c.device) != cudaSuccess)
         return KV_ERR_CUDA;
     if (smem > static_cast<size_t>(optin)) return KV_ERR_INVALID;  // max_seqs too large
-    if (raise_smem_limit(v->fn, c.device, smem) != KV_OK || raise_smem_limit(v->fn_norm, c.device, smem) != KV_OK)
+    const void* fn = tc_kernel_for(v, c.dtype, false);
+    if (raise_smem_limit(fn, c.device, smem) != KV_OK ||
+        (c.dtype == KV_DTYPE_BF16 && raise_smem_limit(v->fn_norm, c.device, smem) != KV_OK))
         return KV_ERR_CUDA;
     int per_sm = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, v->fn, kThreads, smem) != cudaSuccess || per_sm < 1)
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, tc_threads_for(c.dtype), smem) != cudaSuccess ||
+        per_sm < 1)
         return KV_ERR_CUDA;
     pool->decode_grid = pool->sm_count * per_sm;
     pool->decode_smem = smem;
@@ -1161,6 +1428,8 @@ int launch_decode_tc(kv_pool* pool, const void* q, const uint32_t* bt, int32_t b
     const auto& c = pool->cfg;
     const TcVariant* v = find_tc_variant(c.n_kv_heads, c.n_q_heads / c.n_kv_heads);
     if (!v) return KV_ERR_UNSUPPORTED;
+    // Quantised pools: the append is its own launch, and no norm form.
+    if (is_quant(c.dtype) && (new_k != nullptr || q_norm != nullptr)) return KV_ERR_UNSUPPORTED;
     TcArgs a;
     a.q = static_cast<const __nv_bfloat16*>(q);
     a.out = static_cast<__nv_bfloat16*>(out);
@@ -1194,12 +1463,12 @@ int launch_decode_tc(kv_pool* pool, const void* q, const uint32_t* bt, int32_t b
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cudaLaunchConfig_t lc = {};
     lc.gridDim = dim3(pool->decode_grid);
-    lc.blockDim = dim3(kThreads);
+    lc.blockDim = dim3(tc_threads_for(c.dtype));
     lc.dynamicSmemBytes = pool->decode_smem;
     lc.stream = stream;
     lc.attrs = attr;
     lc.numAttrs = 1;
-    const cudaError_t e = cudaLaunchKernelExC(&lc, q_norm != nullptr ? v->fn_norm : v->fn, args);
+    const cudaError_t e = cudaLaunchKernelExC(&lc, tc_kernel_for(v, c.dtype, q_norm != nullptr), args);
     return e == cudaSuccess ? KV_OK : KV_ERR_CUDA;
 }
 

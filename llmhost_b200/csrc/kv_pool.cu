@@ -36,7 +36,8 @@ struct DeviceScope {
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 bool valid_config(const kv_pool_config& c) {
-    if (c.dtype != KV_DTYPE_F32 && c.dtype != KV_DTYPE_BF16) return false;
+    if (c.dtype != KV_DTYPE_F32 && c.dtype != KV_DTYPE_BF16 && c.dtype != KV_DTYPE_Q8 && c.dtype != KV_DTYPE_K8V4)
+        return false;
     if (c.head_dim != kvb200::kHeadDim || c.page_tokens != kvb200::kPageTokens) return false;
     if (c.n_kv_heads != 1 && c.n_kv_heads != 2 && c.n_kv_heads != 4 && c.n_kv_heads != 8) return false;
     if (c.n_q_heads <= 0 || c.n_q_heads % c.n_kv_heads != 0) return false;
@@ -162,8 +163,10 @@ int kv_pool_create(const kv_pool_config* cfg, kv_pool** out) {
     kv_pool* p = new (std::nothrow) kv_pool();
     if (!p) return KV_ERR_OOM;
     p->cfg = *cfg;
-    p->elem_bytes = cfg->dtype == KV_DTYPE_BF16 ? 2 : 4;
-    p->page_bytes = 2ull * cfg->n_kv_heads * cfg->page_tokens * cfg->head_dim * p->elem_bytes;
+    p->elem_bytes = cfg->dtype == KV_DTYPE_F32 ? 4 : 2;  // quantised pools take bf16 k, v, q, out
+    p->page_bytes = kvb200::is_quant(cfg->dtype)
+                        ? kvb200::quant_page_bytes(cfg->dtype, cfg->n_kv_heads)
+                        : 2ull * cfg->n_kv_heads * cfg->page_tokens * cfg->head_dim * p->elem_bytes;
     if (static_cast<uint64_t>(cfg->n_pages) * (p->page_bytes / 128) >= (1ull << 31)) {
         delete p;
         return KV_ERR_INVALID;  // TMA row coordinates are int32
@@ -216,7 +219,7 @@ int kv_pool_create(const kv_pool_config* cfg, kv_pool** out) {
         free_pool(p);
         return KV_ERR_CUDA;
     }
-    if ((rc = encode_page_map(p)) != KV_OK) {
+    if (!kvb200::is_quant(cfg->dtype) && (rc = encode_page_map(p)) != KV_OK) {
         free_pool(p);
         return rc;
     }
@@ -343,6 +346,7 @@ int kv_norm_append_decode_attn(kv_pool* pool, const void* k, const void* v, cons
     if (!k || !v || !q || !q_norm || !k_norm || !block_tables || !seq_lens || !out || bt_stride <= 0 ||
         !aligned16(k) || !aligned16(v) || !aligned16(q) || !aligned16(q_norm) || !aligned16(k_norm))
         return KV_ERR_INVALID;
+    if (kvb200::is_quant(pool->cfg.dtype)) return KV_ERR_UNSUPPORTED;
     DeviceScope dev(pool->cfg.device);
     return kvb200::launch_decode(pool, q, block_tables, bt_stride, seq_lens, n_seqs, window, out,
                                  static_cast<cudaStream_t>(stream), k, v, q_norm, k_norm, eps);
@@ -356,6 +360,7 @@ int kv_prefill_attn(kv_pool* pool, const void* q, const int32_t* q_pos, const in
     if (!q || !q_pos || !q_offsets || !prefix_lens || !block_tables || !out || bt_stride <= 0 ||
         n_seqs > 65535 || (tree_masks && max_q_per_seq > 64))
         return KV_ERR_INVALID;
+    if (kvb200::is_quant(pool->cfg.dtype)) return KV_ERR_UNSUPPORTED;
     DeviceScope dev(pool->cfg.device);
     return kvb200::launch_prefill(pool, q, q_pos, q_offsets, prefix_lens,
                                   reinterpret_cast<const unsigned long long*>(tree_masks), n_seqs,

@@ -31,6 +31,15 @@ struct kv_pool {
 
 namespace kvb200 {
 
+// Quantised pools (KV_DTYPE_Q8, KV_DTYPE_K8V4): per (head, token) 64 K code
+// bytes, 64 (Q8) or 32 (K8V4) V code bytes and two f16 scales each for K and
+// V.  A page is n_kv head blocks (one contiguous copy each): K codes, V codes,
+// K scales, V scales, each [16 tokens][row].
+inline bool is_quant(int dtype) { return dtype == KV_DTYPE_Q8 || dtype == KV_DTYPE_K8V4; }
+inline int quant_vrow(int dtype) { return dtype == KV_DTYPE_Q8 ? 64 : 32; }
+inline size_t quant_head_block(int dtype) { return static_cast<size_t>(16) * (64 + quant_vrow(dtype) + 8); }
+inline size_t quant_page_bytes(int dtype, int nkv) { return static_cast<size_t>(nkv) * quant_head_block(dtype); }
+
 // Launchers implemented in the .cu files; they return a kv_status.
 int launch_append(kv_pool* pool, const void* k, const void* v, const int32_t* tok_seq,
                   const int32_t* tok_slot, const int32_t* tok_pos, const int32_t* seq_lens,
@@ -55,8 +64,8 @@ int launch_decode(kv_pool* pool, const void* q, const uint32_t* bt, int32_t bt_s
                   cudaStream_t stream, const void* new_k = nullptr, const void* new_v = nullptr,
                   const float* q_norm = nullptr, const float* k_norm = nullptr, float eps = 0.f);
 
-// Decode attention on tcgen05 for bf16 pools (kv_decode_tc.cu); decode_setup
-// and launch_decode route bf16 pools here.
+// Decode attention on tcgen05 for bf16 and quantised pools (kv_decode_tc.cu);
+// decode_setup and launch_decode route those pools here.
 int decode_tc_setup(kv_pool* pool);
 int launch_decode_tc(kv_pool* pool, const void* q, const uint32_t* bt, int32_t bt_stride, const int32_t* seq_lens,
                      int32_t n_seqs, int32_t window, void* out, cudaStream_t stream, const void* new_k,

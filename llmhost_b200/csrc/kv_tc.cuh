@@ -14,11 +14,14 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint3
            (static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46) | (2ull << 61);
 }
 
-// Instruction descriptor, kind::f16: fp32 accumulate, bf16 A and B; A
-// (bit 15) and B (bit 16) K-major unless marked MN-major.
-__host__ __device__ constexpr uint32_t instr_desc(int n, int m, bool b_mn_major, bool a_mn_major = false) {
-    return (1u << 4) | (1u << 7) | (1u << 10) | ((a_mn_major ? 1u : 0u) << 15) | ((b_mn_major ? 1u : 0u) << 16) |
-           (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);
+// Instruction descriptor, kind::f16: fp32 accumulate, bf16 A and B (f16 A
+// and B when `f16`: both operands always have the same type); A (bit 15) and
+// B (bit 16) K-major unless marked MN-major.
+__host__ __device__ constexpr uint32_t instr_desc(int n, int m, bool b_mn_major, bool a_mn_major = false,
+                                                  bool f16 = false) {
+    return (1u << 4) | (f16 ? 0u : (1u << 7) | (1u << 10)) | ((a_mn_major ? 1u : 0u) << 15) |
+           ((b_mn_major ? 1u : 0u) << 16) | (static_cast<uint32_t>(n >> 3) << 17) |
+           (static_cast<uint32_t>(m >> 4) << 24);
 }
 
 // tcgen05.mma kind::f16 (bf16 in, fp32 accumulate), both operands in shared memory.

@@ -25,11 +25,17 @@ device at most):
   verify       kv_prefill_attn with ancestor masks: the speculative config's
                verify launch (32 sessions sharing a 4096-token prefix, one
                64-node tree each, 24q/8kv)
+  decode_q8    kv_append_decode_attn on a Q8 pool (quantise-on-append, then
+  decode_k8v4  tcgen05 decode of the converted tiles; K8V4: 4-bit V): the batched-decode
+               configuration's 64 session lengths (U[128, 8192]) and six
+               layers' block tables taken in turn, as bench.py does
 
 Algorithmic bytes: append reads k, v and writes them (4 n_kv d e per token);
 a page copy reads and writes a page; a token move reads and writes one
 token's K and V rows; decode counts attended K/V, the new token's K/V read and
-written, q, out and block-table entries.  Algorithmic FLOPs (prefill,
+written, q, out and block-table entries (quantised pools: codes and scales of
+every attended key, 136 bytes per key and head for Q8, 104 for K8V4, against
+256 for bf16).  Algorithmic FLOPs (prefill,
 verify): 4 d per visible (query row, key) pair.
 """
 from __future__ import annotations
@@ -255,8 +261,59 @@ def case_verify(d: _Dev):
                           "flops": flops, "kv_bytes_streamed": kv_bytes, "sessions": n, "nodes": T}
 
 
+def _decode_quant(d: _Dev, store: str):
+    from .kv import KvPool
+    from .workloads import decode_config
+
+    wl = decode_config()
+    n_q, n_kv, n_seq, n_layers = wl.n_q, wl.n_kv, wl.n_seqs, wl.n_layers
+    lens = np.asarray(wl.l0, np.int64)
+    per_layer = int((-(-(lens + 1) // PAGE_TOKENS)).sum())
+    n_pages = n_layers * per_layer + 64
+    perm = d.rng.permutation(n_pages).astype(np.uint32)
+    pool = KvPool(dtype=store, n_q_heads=n_q, n_kv_heads=n_kv, n_pages=n_pages, max_positions=int(lens.max()) + 32,
+                  max_seqs=n_seq)
+    tot = int(lens.sum())
+    rows = d.i32(np.repeat(np.arange(n_seq), lens))
+    slots = d.i32(np.concatenate([np.arange(x) for x in lens]))
+    tables = []
+    for layer in range(n_layers):  # disjoint pages per layer
+        bt = _tables(np.random.default_rng(layer), lens + 1, per_layer)
+        bt = np.where(bt == NONE, NONE, perm[layer * per_layer:(layer + 1) * per_layer][np.minimum(bt, per_layer - 1)])
+        tables.append(d.u32(bt))
+        k, v = d.bf16((tot, n_kv, 64)), d.bf16((tot, n_kv, 64))
+        pool.append(k, v, rows, slots, slots, tables[-1])
+        del k, v
+    q, k, v = d.bf16((n_seq, n_q, 64)), d.bf16((n_seq, n_kv, 64)), d.bf16((n_seq, n_kv, 64))
+    seq_lens = d.i32(lens + 1)
+    out = d.torch.empty_like(q)
+    key_bytes = 64 + (64 if store == "q8" else 32) + 8
+    n_tok = lens + 1
+    byts = int((n_kv * key_bytes * n_tok + 2 * n_kv * 64 * 2 + 2 * n_q * 64 * 2 + 4 * (-(-n_tok // 16))).sum())
+    state = {"i": 0}
+
+    def launch():
+        pool.append_decode_attn(k, v, q, tables[state["i"] % n_layers], seq_lens, out=out)
+        state["i"] += 1
+
+    return pool, launch, {"kernel": f"append_q_kernel + decode_tc_kernel with converter warps ({store} pool)",
+                          "bound": "hbm", "bytes": byts, "sessions": n_seq, "keys": int(n_tok.sum()),
+                          "layers_in_turn": n_layers, "bf16_equivalent_bytes":
+                              int((n_kv * 256 * n_tok + 2 * n_kv * 64 * 4 + 2 * n_q * 64 * 2
+                                   + 4 * (-(-n_tok // 16))).sum())}
+
+
+def case_decode_q8(d: _Dev):
+    return _decode_quant(d, "q8")
+
+
+def case_decode_k8v4(d: _Dev):
+    return _decode_quant(d, "k8v4")
+
+
 CASES = {"append": case_append, "copy": case_copy, "move": case_move, "decode_f32": case_decode_f32,
-         "prefill_f32": case_prefill_f32, "verify": case_verify}
+         "prefill_f32": case_prefill_f32, "verify": case_verify, "decode_q8": case_decode_q8,
+         "decode_k8v4": case_decode_k8v4}
 
 
 def main() -> None:

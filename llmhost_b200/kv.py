@@ -13,10 +13,12 @@ import numpy as np
 import torch
 
 from . import _capi
-from ._capi import KV_DTYPE_BF16, KV_DTYPE_F32, KvPoolConfig, check
+from ._capi import KV_DTYPE_BF16, KV_DTYPE_F32, KV_DTYPE_K8V4, KV_DTYPE_Q8, KvPoolConfig, check
 from .plans import tree_masks  # noqa: F401  (ancestor-or-self masks for prefill_attn)
 
-_TORCH_DTYPE = {KV_DTYPE_F32: torch.float32, KV_DTYPE_BF16: torch.bfloat16}
+# The dtype of k, v, q and out: quantised pools take bf16 and store codes.
+_TORCH_DTYPE = {KV_DTYPE_F32: torch.float32, KV_DTYPE_BF16: torch.bfloat16, KV_DTYPE_Q8: torch.bfloat16,
+                KV_DTYPE_K8V4: torch.bfloat16}
 
 
 def dtype_code(dtype) -> int:
@@ -24,6 +26,10 @@ def dtype_code(dtype) -> int:
         return KV_DTYPE_BF16
     if dtype in ("f32", "fp32", torch.float32, KV_DTYPE_F32):
         return KV_DTYPE_F32
+    if dtype in ("q8", KV_DTYPE_Q8):
+        return KV_DTYPE_Q8
+    if dtype in ("k8v4", KV_DTYPE_K8V4):
+        return KV_DTYPE_K8V4
     raise ValueError(f"unsupported KV dtype {dtype!r}")
 
 
@@ -51,7 +57,16 @@ class PoolShape:
         return _TORCH_DTYPE[self.dtype]
 
     @property
+    def quantised(self) -> bool:
+        return self.dtype in (KV_DTYPE_Q8, KV_DTYPE_K8V4)
+
+    @property
     def page_elems(self) -> int:
+        """Elements of one page: f32 / bf16 values, or bytes of a quantised page
+        (per kv head: K codes, V codes, K scales, V scales)."""
+        if self.quantised:
+            vrow = self.head_dim if self.dtype == KV_DTYPE_Q8 else self.head_dim // 2
+            return self.n_kv_heads * self.page_tokens * (self.head_dim + vrow + 8)
         return 2 * self.n_kv_heads * self.page_tokens * self.head_dim
 
 
@@ -103,9 +118,10 @@ class KvPool:
         check(self.last_error(), "device error word")
 
     def read_pages(self, page_ids) -> np.ndarray:
-        """Pages as a host array [n, page_elems] (bf16 returned as uint16 bits)."""
+        """Pages as a host array [n, page_elems] (bf16 returned as uint16 bits,
+        quantised pages as bytes)."""
         ids = np.ascontiguousarray(page_ids, dtype=np.uint32)
-        np_dt = np.uint16 if self.shape.dtype == KV_DTYPE_BF16 else np.float32
+        np_dt = {KV_DTYPE_BF16: np.uint16, KV_DTYPE_F32: np.float32}.get(self.shape.dtype, np.uint8)
         out = np.empty((len(ids), self.shape.page_elems), dtype=np_dt)
         check(self._lib.kv_pool_read_pages(self._h, ids.ctypes.data, len(ids), out.ctypes.data),
               "kv_pool_read_pages")

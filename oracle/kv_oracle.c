@@ -364,10 +364,10 @@ void orc_rms_norm(const float *x, const float *weight, float eps, size_t dim, si
 }
 
 /* Quantised pages (ORC_Q8: K and V as Q8_0 blocks; ORC_K8V4: K as Q8_0, V as
- * Q4), head_dim 64 = two 32-element blocks per (head, token).  A page holds,
- * in order: K codes [n_kv][P][64] int8, V codes [n_kv][P][64] int8 (Q8) or
- * [n_kv][P][32] packed nibbles (K8V4), K scales [n_kv][P][2] f16, V scales
- * [n_kv][P][2] f16.  Queries, outputs and the appended k/v stay bf16. */
+ * Q4), head_dim 64 = two 32-element blocks per (head, token).  A page is
+ * n_kv head blocks, each holding in order: K codes [P][64] int8, V codes
+ * [P][64] int8 (Q8) or [P][32] packed nibbles (K8V4), K scales [P][2] f16,
+ * V scales [P][2] f16.  Queries, outputs and the appended k/v stay bf16. */
 static inline int is_quant(int dtype) { return dtype == ORC_Q8 || dtype == ORC_K8V4; }
 static inline int io_dtype(int dtype) { return is_quant(dtype) ? ORC_BF16 : dtype; }
 static inline size_t q_vrow(int dtype) { return dtype == ORC_Q8 ? 64 : 32; }
@@ -375,18 +375,22 @@ size_t orc_page_bytes(int dtype, size_t n_kv, size_t P, size_t d) {
     if (is_quant(dtype)) return n_kv * P * (d + q_vrow(dtype) + 8);
     return 2 * n_kv * P * d * (dtype == ORC_BF16 ? 2 : 4);
 }
+static inline size_t q_head(size_t P, int dtype, size_t h) { return h * P * (64 + q_vrow(dtype) + 8); }
 static inline size_t q_koff(size_t n_kv, size_t P, int dtype, size_t h, size_t j) {
-    (void)n_kv; (void)dtype;
-    return (h * P + j) * 64;
+    (void)n_kv;
+    return q_head(P, dtype, h) + j * 64;
 }
 static inline size_t q_voff(size_t n_kv, size_t P, int dtype, size_t h, size_t j) {
-    return n_kv * P * 64 + (h * P + j) * q_vrow(dtype);
+    (void)n_kv;
+    return q_head(P, dtype, h) + P * 64 + j * q_vrow(dtype);
 }
 static inline size_t q_ksoff(size_t n_kv, size_t P, int dtype, size_t h, size_t j) {
-    return n_kv * P * (64 + q_vrow(dtype)) + (h * P + j) * 4;
+    (void)n_kv;
+    return q_head(P, dtype, h) + P * (64 + q_vrow(dtype)) + j * 4;
 }
 static inline size_t q_vsoff(size_t n_kv, size_t P, int dtype, size_t h, size_t j) {
-    return n_kv * P * (64 + q_vrow(dtype)) + n_kv * P * 4 + (h * P + j) * 4;
+    (void)n_kv;
+    return q_head(P, dtype, h) + P * (64 + q_vrow(dtype)) + P * 4 + j * 4;
 }
 
 /* One token's rotated K (fp32 [n_kv][64]) and V (bf16 bits) into a quantised page. */

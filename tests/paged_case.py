@@ -32,11 +32,18 @@ def to_numpy_f32(t) -> np.ndarray:
     return t.detach().to(torch.float32).cpu().numpy()
 
 
+ORACLE_DTYPE = {"bf16": O.BF16, "f32": O.F32, "q8": O.Q8, "k8v4": O.K8V4}
+
+
 class DecodeCase:
+    """`dtype` is the k / v / q type; `store` the pool's storage type when it
+    differs (quantised pools "q8" / "k8v4" take bf16 k, v, q)."""
+
     def __init__(self, dtype: str, n_q: int, n_kv: int, lens, seed: int = 0, window: int = 0,
-                 extra_pages: int = 8, evict_below_window: bool = False):
+                 extra_pages: int = 8, evict_below_window: bool = False, store: str | None = None):
         rng = np.random.default_rng(seed)
         self.dtype, self.n_q, self.n_kv, self.window = dtype, n_q, n_kv, window
+        self.store = store or dtype
         self.lens = np.asarray(lens, dtype=np.int64)
         n = len(self.lens)
         pages = -(-(self.lens + 1) // PAGE_TOKENS)
@@ -66,7 +73,7 @@ class DecodeCase:
     def run_oracle(self, norm=None):
         """norm = (q_norm, k_norm, eps): the decode step RMS-normalises q and
         the new k before RoPE (orc_decode_step_norm)."""
-        host = O.HostPages(self.n_pages, O.BF16 if self.dtype == "bf16" else O.F32, self.n_q, self.n_kv)
+        host = O.HostPages(self.n_pages, ORACLE_DTYPE[self.store], self.n_q, self.n_kv)
         for s in range(len(self.lens)):
             for t in range(int(self.lens[s])):
                 host.append_token(self.bt[s], t, t, self.k_pre[s][t], self.v_pre[s][t])
@@ -81,7 +88,7 @@ class DecodeCase:
     def make_pool(self, **kw):
         from llmhost_b200.kv import KvPool
 
-        args = dict(dtype=self.dtype, n_q_heads=self.n_q, n_kv_heads=self.n_kv, n_pages=self.n_pages,
+        args = dict(dtype=self.store, n_q_heads=self.n_q, n_kv_heads=self.n_kv, n_pages=self.n_pages,
                     max_positions=int(self.seq_lens.max(initial=1)) + 16, max_seqs=max(len(self.lens), 1))
         args.update(kw)
         return KvPool(**args)

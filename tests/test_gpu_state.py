@@ -4,26 +4,32 @@ A speculative round (prefill, copy-on-write fork, draft trees, accepted
 paths) is planned by KvState; the GPU runs the plans with kv_append,
 kv_copy_pages and kv_move_tokens, the oracle replays them on host pages.
 Pages must match bit for bit, and decode attention over the committed
-sequences must match the oracle within the bf16 tolerance.
+sequences must match the oracle within the bf16 tolerance.  The round runs on
+bf16 pools and on both quantised pool types (whose token moves carry the code
+rows and the scale rows of every head).
 """
 import numpy as np
 import pytest
 
 from llmhost_b200.workloads import normal_bits
 from oracle import oracle as O
-from paged_case import assert_close_rows, to_numpy_f32, to_torch
+from paged_case import ORACLE_DTYPE, assert_close_rows, to_numpy_f32, to_torch
 
 pytestmark = pytest.mark.gpu
 NONE = 0xFFFFFFFF
 
 
-def test_copy_pages_bit_exact(cuda):
+@pytest.mark.parametrize("store", ["bf16", "q8", "k8v4"])
+def test_copy_pages_bit_exact(cuda, store):
     import torch
     from llmhost_b200.kv import KvPool
 
     rng = np.random.default_rng(0)
-    with KvPool(dtype="bf16", n_q_heads=24, n_kv_heads=8, n_pages=64, max_positions=64, max_seqs=4) as pool:
-        data = rng.integers(0, 1 << 16, size=(64, 2 * 8 * 16 * 64), dtype=np.uint16)
+    with KvPool(dtype=store, n_q_heads=24, n_kv_heads=8, n_pages=64, max_positions=64, max_seqs=4) as pool:
+        if store == "bf16":
+            data = rng.integers(0, 1 << 16, size=(64, 2 * 8 * 16 * 64), dtype=np.uint16)
+        else:
+            data = rng.integers(0, 256, size=(64, pool.page_bytes), dtype=np.uint8)
         pool.write_pages(np.arange(64), data)
         src = torch.tensor([3, 5, 7, 40], dtype=torch.int32, device=cuda)
         dst = torch.tensor([10, 11, 12, 63], dtype=torch.int32, device=cuda)
@@ -37,15 +43,27 @@ def test_copy_pages_bit_exact(cuda):
 
 
 def _replay_moves(host, moves):
-    """Host replay of page-addressed token moves, in order."""
+    """Host replay of page-addressed token moves, in order: a token is its
+    (head, slot) row of every page section."""
     P, d, nkv = host.P, host.d, host.n_kv
-    pages = host.data.reshape(host.data.shape[0], 2 * nkv, P, d)
+    n = host.data.shape[0]
+    if host.quant:  # head blocks of K codes, V codes, K scales, V scales (bytes)
+        rows = [d, d if host.dtype == O.Q8 else d // 2, 4, 4]
+        blocks = host.data.reshape(n, nkv, -1)
+        views, at = [], 0
+        for r in rows:
+            views.append(blocks[:, :, at:at + P * r].reshape(n, nkv, P, r))
+            at += P * r
+        assert at == blocks.shape[2]
+    else:
+        views = [host.data.reshape(n, 2 * nkv, P, d)]
     for sp, ss, dp, ds in moves:
-        pages[dp, :, ds, :] = pages[sp, :, ss, :]
+        for v in views:
+            v[dp, :, ds, :] = v[sp, :, ss, :]
 
 
-@pytest.mark.parametrize("seed", [1, 2])
-def test_speculative_round_matches_oracle(cuda, seed):
+@pytest.mark.parametrize("seed,store", [(1, "bf16"), (2, "bf16"), (3, "q8"), (4, "k8v4")])
+def test_speculative_round_matches_oracle(cuda, seed, store):
     import torch
     from llmhost_b200.kv import KvPool
     from llmhost_b200.state import KvState
@@ -54,8 +72,8 @@ def test_speculative_round_matches_oracle(cuda, seed):
     L, n_q, n_kv, n_pages = 2, 24, 8, 256
     order = rng.permutation(n_pages).astype(np.uint32)
     st = KvState(n_pages, L, alloc_order=order)
-    host = O.HostPages(n_pages, O.BF16, n_q, n_kv)
-    pool = KvPool(dtype="bf16", n_q_heads=n_q, n_kv_heads=n_kv, n_pages=n_pages, max_positions=512, max_seqs=8)
+    host = O.HostPages(n_pages, ORACLE_DTYPE[store], n_q, n_kv)
+    pool = KvPool(dtype=store, n_q_heads=n_q, n_kv_heads=n_kv, n_pages=n_pages, max_positions=512, max_seqs=8)
 
     def dev_i32(a):
         return torch.from_numpy(np.ascontiguousarray(a, dtype=np.int64).astype(np.int32)).to(cuda)
