@@ -50,8 +50,8 @@ extern "C" {
  *   KV_DTYPE_K8V4  K as Q8_0, V as Q4 blocks (4-bit codes, scale max|x| / 8)
  * A quantised page is n_kv head blocks, each holding in order: K codes
  * [P][64] int8, V codes [P][64] int8 (Q8) or [P][32] packed nibbles (K8V4:
- * element 2i in the low nibble of byte i), K scales [P][2] f16, V scales
- * [P][2] f16 (2176 or 1664 bytes a head at P = 16).  K is rotated (RoPE) in fp32 and then quantised.  For
+ * element 2i in the low nibble of byte i), scales [P][2 blocks][K, V] f16
+ * (2176 or 1664 bytes a head at P = 16).  K is rotated (RoPE) in fp32 and then quantised.  For
  * quantised pools the appended k / v, q and out are bf16.  They take
  * appends, decode attention (kv_decode_attn, and kv_append_decode_attn as an
  * append launch followed by the attention launch), page copies and token

@@ -218,8 +218,7 @@ __global__ void __launch_bounds__(256) append_q_kernel(uint8_t* __restrict__ pag
     uint8_t* blk = pages + (static_cast<size_t>(page) * a.nkv + h) * kHeadBlock;
     uint8_t* kc = blk + j * 64;
     uint8_t* vc = blk + kPageTokens * 64 + j * kVRow;
-    uint8_t* ks = blk + kPageTokens * (64 + kVRow) + j * 4;
-    uint8_t* vs = ks + kPageTokens * 4;
+    uint8_t* sc = blk + kPageTokens * (64 + kVRow) + j * 8;  // [block][K scale, V scale]
     const __nv_bfloat16* ksrc = static_cast<const __nv_bfloat16*>(a.k) + (tok * a.nkv + h) * kHeadDim;
     const __nv_bfloat16* vsrc = static_cast<const __nv_bfloat16*>(a.v) + (tok * a.nkv + h) * kHeadDim;
 
@@ -241,7 +240,6 @@ __global__ void __launch_bounds__(256) append_q_kernel(uint8_t* __restrict__ pag
     const float kinv1 = block_inv(group4_max(ay, mask), 127.f, kb1);
     *reinterpret_cast<uint2*>(kc + 8 * qd) = codes_q8(xo, kinv0);
     *reinterpret_cast<uint2*>(kc + 32 + 8 * qd) = codes_q8(yo, kinv1);
-    if (qd == 0) *reinterpret_cast<uint32_t*>(ks) = static_cast<uint32_t>(kb0) | (static_cast<uint32_t>(kb1) << 16);
 
     load8(vsrc + 8 * qd, x);
     load8(vsrc + 8 * qd + 32, y);
@@ -262,7 +260,9 @@ __global__ void __launch_bounds__(256) append_q_kernel(uint8_t* __restrict__ pag
         *reinterpret_cast<uint2*>(vc + 8 * qd) = codes_q8(x, vinv0);
         *reinterpret_cast<uint2*>(vc + 32 + 8 * qd) = codes_q8(y, vinv1);
     }
-    if (qd == 0) *reinterpret_cast<uint32_t*>(vs) = static_cast<uint32_t>(vb0) | (static_cast<uint32_t>(vb1) << 16);
+    if (qd == 0)
+        *reinterpret_cast<uint2*>(sc) = make_uint2(static_cast<uint32_t>(kb0) | (static_cast<uint32_t>(vb0) << 16),
+                                                  static_cast<uint32_t>(kb1) | (static_cast<uint32_t>(vb1) << 16));
 }
 
 }  // namespace

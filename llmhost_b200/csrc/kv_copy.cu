@@ -14,8 +14,7 @@
 //                  kv_state_rollback produce (a later move never reads a slot
 //                  an earlier move wrote).  Groups run in parallel.  A token
 //                  is its row of every page section (K and V; or K codes, V
-//                  codes, K scales and V scales of every head block in
-//                  quantised pools).
+//                  codes and scales of every head block in quantised pools).
 // Page ids past the pool and slots past a page are skipped and flagged in the
 // pool's error word.
 #include <algorithm>
@@ -47,8 +46,8 @@ constexpr int kMoveSmem = 48 * 1024;
 // A page as sections: token (head h, slot j) of section i is the row of
 // row[i] words at base[i] + h * head[i] + j * row[i].  f32 / bf16 pools: K
 // rows then V rows, each [nkv][16][row] (16-byte words).  Quantised pools:
-// nkv head blocks of K codes, V codes, K scales, V scales (4-byte words, as
-// the 4-byte scale rows need).
+// nkv head blocks of K codes, V codes, scales (4-byte words, as the 8-byte
+// scale rows need).
 struct PageSections {
     int n;          // sections
     int row[4];     // words per (head, slot) row
@@ -62,11 +61,11 @@ PageSections page_sections(const kv_pool* pool, int word_bytes) {
     PageSections ps{};
     const int nkv = pool->cfg.n_kv_heads;
     if (is_quant(pool->cfg.dtype)) {
-        const int bytes[4] = {kHeadDim, quant_vrow(pool->cfg.dtype), 4, 4};
-        const int block = kPageTokens * (bytes[0] + bytes[1] + bytes[2] + bytes[3]) / word_bytes;
-        ps.n = 4;
+        const int bytes[3] = {kHeadDim, quant_vrow(pool->cfg.dtype), 8};
+        const int block = kPageTokens * (bytes[0] + bytes[1] + bytes[2]) / word_bytes;
+        ps.n = 3;
         int at = 0;
-        for (int i = 0; i < 4; ++i) {
+        for (int i = 0; i < 3; ++i) {
             ps.row[i] = bytes[i] / word_bytes;
             ps.base[i] = at;
             ps.head[i] = block;

@@ -686,7 +686,7 @@ __global__ void __launch_bounds__(block_threads<kQ>(), 1) decode_tc_kernel(const
                                 &full[st], 0, row);
                 } else {
                     // Quantised pages: each loaded page's head blocks (K codes,
-                    // V codes, K scales, V scales; heads 2p, 2p + 1 adjacent)
+                    // V codes, scales; heads 2p, 2p + 1 adjacent)
                     // with plain bulk copies (no multicast) into raw slot st,
                     // block (u, k) at (2k + u) head blocks: one copy of both
                     // units' blocks per page (lane (k, K, 0)), or one per unit
@@ -1113,9 +1113,11 @@ __global__ void __launch_bounds__(block_threads<kQ>(), 1) decode_tc_kernel(const
                                 const uint4* kr = reinterpret_cast<const uint4*>(blk + r * kHeadDim + 32 * hb);
                                 const uint4* vr = reinterpret_cast<const uint4*>(blk + kPageTokens * kHeadDim +
                                                                                  r * kVRow + (kVRow / 2) * hb);
-                                const uint8_t* sc = blk + kPageTokens * (kHeadDim + kVRow) + r * 4 + hb * 2;
-                                const __half2 ks = __half2half2(*reinterpret_cast<const __half*>(sc));
-                                const __half2 vs = __half2half2(*reinterpret_cast<const __half*>(sc + kPageTokens * 4));
+                                // this block's scale pair: K scale, V scale
+                                const uint32_t scw = *reinterpret_cast<const uint32_t*>(
+                                    blk + kPageTokens * (kHeadDim + kVRow) + r * 8 + hb * 4);
+                                const __half2 ks = __half2half2(__ushort_as_half(static_cast<unsigned short>(scw & 0xffffu)));
+                                const __half2 vs = __half2half2(__ushort_as_half(static_cast<unsigned short>(scw >> 16)));
                                 q8x16_to_f16(kr[0], ks, ko[0], ko[1]);
                                 q8x16_to_f16(kr[1], ks, ko[2], ko[3]);
                                 if constexpr (kQ == 2) {

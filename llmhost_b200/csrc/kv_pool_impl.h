@@ -33,8 +33,8 @@ namespace kvb200 {
 
 // Quantised pools (KV_DTYPE_Q8, KV_DTYPE_K8V4): per (head, token) 64 K code
 // bytes, 64 (Q8) or 32 (K8V4) V code bytes and two f16 scales each for K and
-// V.  A page is n_kv head blocks (one contiguous copy each): K codes, V codes,
-// K scales, V scales, each [16 tokens][row].
+// V.  A page is n_kv head blocks: K codes [16][64], V codes [16][vrow],
+// scales [16 tokens][2 blocks][K, V].
 inline bool is_quant(int dtype) { return dtype == KV_DTYPE_Q8 || dtype == KV_DTYPE_K8V4; }
 inline int quant_vrow(int dtype) { return dtype == KV_DTYPE_Q8 ? 64 : 32; }
 inline size_t quant_head_block(int dtype) { return static_cast<size_t>(16) * (64 + quant_vrow(dtype) + 8); }

@@ -63,7 +63,7 @@ class PoolShape:
     @property
     def page_elems(self) -> int:
         """Elements of one page: f32 / bf16 values, or bytes of a quantised page
-        (per kv head: K codes, V codes, K scales, V scales)."""
+        (per kv head: K codes, V codes, scales)."""
         if self.quantised:
             vrow = self.head_dim if self.dtype == KV_DTYPE_Q8 else self.head_dim // 2
             return self.n_kv_heads * self.page_tokens * (self.head_dim + vrow + 8)

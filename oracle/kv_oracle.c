@@ -366,8 +366,8 @@ void orc_rms_norm(const float *x, const float *weight, float eps, size_t dim, si
 /* Quantised pages (ORC_Q8: K and V as Q8_0 blocks; ORC_K8V4: K as Q8_0, V as
  * Q4), head_dim 64 = two 32-element blocks per (head, token).  A page is
  * n_kv head blocks, each holding in order: K codes [P][64] int8, V codes
- * [P][64] int8 (Q8) or [P][32] packed nibbles (K8V4), K scales [P][2] f16,
- * V scales [P][2] f16.  Queries, outputs and the appended k/v stay bf16. */
+ * [P][64] int8 (Q8) or [P][32] packed nibbles (K8V4), scales [P][2 blocks]
+ * [K, V] f16.  Queries, outputs and the appended k/v stay bf16. */
 static inline int is_quant(int dtype) { return dtype == ORC_Q8 || dtype == ORC_K8V4; }
 static inline int io_dtype(int dtype) { return is_quant(dtype) ? ORC_BF16 : dtype; }
 static inline size_t q_vrow(int dtype) { return dtype == ORC_Q8 ? 64 : 32; }
@@ -384,13 +384,13 @@ static inline size_t q_voff(size_t n_kv, size_t P, int dtype, size_t h, size_t j
     (void)n_kv;
     return q_head(P, dtype, h) + P * 64 + j * q_vrow(dtype);
 }
+/* K scale of block 0 of token j; block b is 4 bytes on, V scale 2 on. */
 static inline size_t q_ksoff(size_t n_kv, size_t P, int dtype, size_t h, size_t j) {
     (void)n_kv;
-    return q_head(P, dtype, h) + P * (64 + q_vrow(dtype)) + j * 4;
+    return q_head(P, dtype, h) + P * (64 + q_vrow(dtype)) + j * 8;
 }
 static inline size_t q_vsoff(size_t n_kv, size_t P, int dtype, size_t h, size_t j) {
-    (void)n_kv;
-    return q_head(P, dtype, h) + P * (64 + q_vrow(dtype)) + P * 4 + j * 4;
+    return q_ksoff(n_kv, P, dtype, h, j) + 2;
 }
 
 /* One token's rotated K (fp32 [n_kv][64]) and V (bf16 bits) into a quantised page. */
@@ -402,12 +402,12 @@ static void q_store_token(uint8_t *page, int dtype, size_t n_kv, size_t P, size_
         for (int b = 0; b < 2; b++) {
             uint16_t sc;
             orc_quantize_q8_0(kr + h * 64 + 32 * b, &sc, (int8_t *)(page + q_koff(n_kv, P, dtype, h, j) + 32 * b));
-            memcpy(page + q_ksoff(n_kv, P, dtype, h, j) + 2 * b, &sc, 2);
+            memcpy(page + q_ksoff(n_kv, P, dtype, h, j) + 4 * b, &sc, 2);
             if (dtype == ORC_Q8)
                 orc_quantize_q8_0(vv + 32 * b, &sc, (int8_t *)(page + q_voff(n_kv, P, dtype, h, j) + 32 * b));
             else
                 orc_quantize_q4(vv + 32 * b, &sc, page + q_voff(n_kv, P, dtype, h, j) + 16 * b);
-            memcpy(page + q_vsoff(n_kv, P, dtype, h, j) + 2 * b, &sc, 2);
+            memcpy(page + q_vsoff(n_kv, P, dtype, h, j) + 4 * b, &sc, 2);
         }
     }
 }
@@ -417,8 +417,8 @@ static void q_load_token(const uint8_t *page, int dtype, size_t n_kv, size_t P, 
                          float *vd) {
     for (int b = 0; b < 2; b++) {
         uint16_t ks, vs;
-        memcpy(&ks, page + q_ksoff(n_kv, P, dtype, h, j) + 2 * b, 2);
-        memcpy(&vs, page + q_vsoff(n_kv, P, dtype, h, j) + 2 * b, 2);
+        memcpy(&ks, page + q_ksoff(n_kv, P, dtype, h, j) + 4 * b, 2);
+        memcpy(&vs, page + q_vsoff(n_kv, P, dtype, h, j) + 4 * b, 2);
         const float kf = orc_f16_to_f32(ks), vf = orc_f16_to_f32(vs);
         const int8_t *kq = (const int8_t *)(page + q_koff(n_kv, P, dtype, h, j)) + 32 * b;
         for (int e = 0; e < 32; e++) kd[32 * b + e] = deq_q8(kq[e], kf);

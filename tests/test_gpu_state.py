@@ -47,8 +47,8 @@ def _replay_moves(host, moves):
     (head, slot) row of every page section."""
     P, d, nkv = host.P, host.d, host.n_kv
     n = host.data.shape[0]
-    if host.quant:  # head blocks of K codes, V codes, K scales, V scales (bytes)
-        rows = [d, d if host.dtype == O.Q8 else d // 2, 4, 4]
+    if host.quant:  # head blocks of K codes, V codes, scales (bytes)
+        rows = [d, d if host.dtype == O.Q8 else d // 2, 8]
         blocks = host.data.reshape(n, nkv, -1)
         views, at = [], 0
         for r in rows:
