@@ -180,6 +180,23 @@ extern "C" {
         out: *mut c_void,
         stream: *mut c_void,
     ) -> i32;
+    pub fn kv_prefill_shared_workspace_bytes(pool: *const kv_pool, n_seqs: i32, max_q_per_seq: i32) -> usize;
+    pub fn kv_prefill_attn_shared(
+        pool: *mut kv_pool,
+        q: *const c_void,
+        q_pos: *const i32,
+        q_offsets: *const i32,
+        prefix_lens: *const i32,
+        tree_masks: *const u64,
+        block_tables: *const u32,
+        bt_stride: i32,
+        n_seqs: i32,
+        max_q_per_seq: i32,
+        shared_tokens: i32,
+        workspace: *mut c_void,
+        out: *mut c_void,
+        stream: *mut c_void,
+    ) -> i32;
     pub fn kv_copy_pages(pool: *mut kv_pool, src: *const u32, dst: *const u32, n: i32, stream: *mut c_void) -> i32;
     pub fn kv_move_tokens(
         pool: *mut kv_pool,

@@ -184,6 +184,28 @@ int kv_prefill_attn(kv_pool *pool, const void *q, const int32_t *q_pos, const in
                     const uint32_t *block_tables, int32_t bt_stride, int32_t n_seqs,
                     int32_t max_q_per_seq, void *out, void *stream);
 
+/* Shared-prefix (cascade) form of kv_prefill_attn, for a batch whose
+ * sequences all begin with the same shared_tokens tokens on the same pages
+ * (block-table entries 0 .. shared_tokens / 16 - 1 equal in every row, as
+ * after kv_state_fork of one prompt).  The shared keys are attended once for
+ * all queries of the batch together (one dense pass over those pages, whose
+ * unnormalised rows go to the workspace), then each sequence's remaining keys
+ * (cached and chunk, with the same causal or tree masks), merged with the
+ * first pass by the log-sum-exp identity.  Same arguments and results as
+ * kv_prefill_attn (to rounding), plus
+ *   shared_tokens  a multiple of 16, at most every prefix_lens[s] (a shorter
+ *                  prefix is flagged in the error word as an invalid argument)
+ *   workspace      16-byte aligned device memory of
+ *                  kv_prefill_shared_workspace_bytes(pool, n_seqs, max_q_per_seq)
+ *                  bytes, not shared with a launch still in flight
+ * Two launches on the stream.  bf16 pools only (KV_ERR_UNSUPPORTED otherwise). */
+size_t kv_prefill_shared_workspace_bytes(const kv_pool *pool, int32_t n_seqs, int32_t max_q_per_seq);
+int kv_prefill_attn_shared(kv_pool *pool, const void *q, const int32_t *q_pos, const int32_t *q_offsets,
+                           const int32_t *prefix_lens, const uint64_t *tree_masks,
+                           const uint32_t *block_tables, int32_t bt_stride, int32_t n_seqs,
+                           int32_t max_q_per_seq, int32_t shared_tokens, void *workspace, void *out,
+                           void *stream);
+
 /* One token's K/V (every head of one layer) from page slot to page slot. */
 typedef struct {
     uint32_t src_page;

@@ -86,6 +86,10 @@ SIGNATURES = [
     ("kv_prefill_attn", c_int32,
      [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32,
       c_void_p, c_void_p]),
+    ("kv_prefill_shared_workspace_bytes", c_size_t, [c_void_p, c_int32, c_int32]),
+    ("kv_prefill_attn_shared", c_int32,
+     [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32, c_int32,
+      c_void_p, c_void_p, c_void_p]),
     ("kv_copy_pages", c_int32, [c_void_p, c_void_p, c_void_p, c_int32, c_void_p]),
     ("kv_move_tokens", c_int32, [c_void_p, c_void_p, c_int32, c_void_p, c_int32, c_void_p]),
     ("kv_decode_attn_noalloc", c_int32,

@@ -367,4 +367,29 @@ int kv_prefill_attn(kv_pool* pool, const void* q, const int32_t* q_pos, const in
                                   max_q_per_seq, block_tables, bt_stride, out, static_cast<cudaStream_t>(stream));
 }
 
+size_t kv_prefill_shared_workspace_bytes(const kv_pool* pool, int32_t n_seqs, int32_t max_q_per_seq) {
+    if (!pool || n_seqs <= 0 || max_q_per_seq <= 0) return 0;
+    return kvb200::prefill_shared_workspace_bytes(pool, n_seqs, max_q_per_seq);
+}
+
+int kv_prefill_attn_shared(kv_pool* pool, const void* q, const int32_t* q_pos, const int32_t* q_offsets,
+                           const int32_t* prefix_lens, const uint64_t* tree_masks, const uint32_t* block_tables,
+                           int32_t bt_stride, int32_t n_seqs, int32_t max_q_per_seq, int32_t shared_tokens,
+                           void* workspace, void* out, void* stream) {
+    if (!pool || n_seqs < 0 || max_q_per_seq < 0) return KV_ERR_INVALID;
+    if (n_seqs == 0 || max_q_per_seq == 0) return KV_OK;
+    if (!q || !q_pos || !q_offsets || !prefix_lens || !block_tables || !out || !workspace || bt_stride <= 0 ||
+        n_seqs > 65535 || (tree_masks && max_q_per_seq > 64) || !aligned16(workspace))
+        return KV_ERR_INVALID;
+    if (shared_tokens <= 0 || shared_tokens % kvb200::kPageTokens != 0 ||
+        shared_tokens / kvb200::kPageTokens > bt_stride)
+        return KV_ERR_INVALID;
+    if (pool->cfg.dtype != KV_DTYPE_BF16) return KV_ERR_UNSUPPORTED;
+    DeviceScope dev(pool->cfg.device);
+    return kvb200::launch_prefill_shared(pool, q, q_pos, q_offsets, prefix_lens,
+                                         reinterpret_cast<const unsigned long long*>(tree_masks), n_seqs,
+                                         max_q_per_seq, block_tables, bt_stride, shared_tokens, workspace, out,
+                                         static_cast<cudaStream_t>(stream));
+}
+
 }  // extern "C"

@@ -79,6 +79,13 @@ size_t prefill_counter_count(const kv_pool* pool);
 int launch_prefill(kv_pool* pool, const void* q, const int32_t* q_pos, const int32_t* q_off,
                    const int32_t* prefix, const unsigned long long* tree, int32_t n_seqs, int32_t max_q,
                    const uint32_t* bt, int32_t bt_stride, void* out, cudaStream_t stream);
+// Shared-prefix form (bf16 pools): every token against the first `shared`
+// keys (table row 0) into ws, then each sequence against the rest, merged.
+size_t prefill_shared_workspace_bytes(const kv_pool* pool, int32_t n_seqs, int32_t max_q);
+int launch_prefill_shared(kv_pool* pool, const void* q, const int32_t* q_pos, const int32_t* q_off,
+                          const int32_t* prefix, const unsigned long long* tree, int32_t n_seqs, int32_t max_q,
+                          const uint32_t* bt, int32_t bt_stride, int32_t shared, void* ws, void* out,
+                          cudaStream_t stream);
 // fp32 pools: CUDA-core kernel (kv_prefill_f32.cu), same arguments.
 int launch_prefill_f32(kv_pool* pool, const void* q, const int32_t* q_pos, const int32_t* q_off,
                        const int32_t* prefix, const unsigned long long* tree, int32_t n_seqs, int32_t max_q,

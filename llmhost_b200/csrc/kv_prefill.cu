@@ -116,6 +116,7 @@ struct PrefillArgs {
     const unsigned long long* tree;
     const uint32_t* bt;
     long long bt_stride;
+    long long bt_cols;  // entries of a row from bt on (bt_stride, less the shared pages in the suffix pass)
     int n_q, nkv, group, tile_tokens, max_q;
     const float2* rope;
     int max_pos;
@@ -129,6 +130,13 @@ struct PrefillArgs {
     int persist;      // 1: persistent grid over the unit list (gridDim.x CTAs)
     float* part;      // persistent: [2 gridDim.x][kSlotFloats] partial rows
     int* counters;    // persistent: [units] parts arrived (reset by the merger)
+    // Shared-prefix (cascade) passes; row R = token * n_q + query head.
+    int virt;         // 1: the prefix pass, one sequence of every token of the batch
+    int virt_L;       //    (q_off[n_seqs] tokens) against the first virt_L keys of table row 0 only
+    float* pout;      // non-null: rows written as (O [R][64] unnormalised, then (m, l) [R]) instead of out
+    const float* pin; // non-null: rows merged with such partial rows before out is written
+    long long prow_total;  // rows of pout / pin
+    int L_off;        // the suffix pass: tokens of the shared prefix, left out of every prefix length
 };
 
 // Where unit u's rows are and which keys they can see.
@@ -142,14 +150,23 @@ __device__ __forceinline__ UnitInfo unit_info(const PrefillArgs& a, int u) {
     const int x = u % a.nx;
     r.h = (u / a.nx) % a.nkv;
     r.s = u / (a.nx * a.nkv);
-    r.q0 = __ldg(a.q_off + r.s);
-    r.T = __ldg(a.q_off + r.s + 1) - r.q0;
-    r.L = __ldg(a.prefix + r.s);
     const bool tree = a.tree != nullptr;
-    r.bad = r.T < 0 || r.L < 0 || r.T > a.max_q || (tree && r.T > 64);
+    if (a.virt) {  // every token of the batch, the shared keys only
+        r.s = 0;
+        r.q0 = 0;
+        r.T = __ldg(a.q_off + a.n_seqs);
+        r.L = a.virt_L;
+        r.bad = r.T < 0 || r.L < 0 || r.T > a.max_q;  // max_q: n_seqs x the per-sequence bound
+    } else {
+        r.q0 = __ldg(a.q_off + r.s);
+        r.T = __ldg(a.q_off + r.s + 1) - r.q0;
+        r.L = __ldg(a.prefix + r.s) - a.L_off;
+        r.bad = r.T < 0 || r.L < 0 || r.T > a.max_q || (tree && r.T > 64);
+    }
     r.t_begin = x * kTiles * a.tile_tokens;
     r.t_end = min(r.T, r.t_begin + kTiles * a.tile_tokens);
-    r.kmax = tree ? r.L + r.T : r.L + r.t_end;  // keys [0, kmax) can be visible to the unit
+    // keys [0, kmax) can be visible to the unit
+    r.kmax = a.virt ? r.L : tree ? r.L + r.T : r.L + r.t_end;
     r.nb = (r.bad || r.t_begin >= r.T) ? 0 : (r.kmax + kBlockKeys - 1) / kBlockKeys;
     return r;
 }
@@ -351,6 +368,61 @@ __device__ __forceinline__ void scale_o(uint32_t t_o, float f) {
     tmem_wait_st();
 }
 
+// A row's final sums -- reference maximum m (log2 units), row sum l and the
+// unnormalised O -- to their destination: the shared-prefix partial rows
+// (pout), or bf16 out after an optional merge with a partial row (pin) by the
+// log-sum-exp identity.  finish_begin once per row, then finish16 for each 16
+// of this thread's dims (dims 32 hf + 16 c ..).
+struct RowFinish {
+    float f, g, inv;  // weights of this row's O and of the pin row's; 1 / merged row sum
+};
+
+__device__ __forceinline__ RowFinish finish_begin(const PrefillArgs& a, long long row, int hf, float m, float l) {
+    RowFinish rf{1.f, 0.f, 0.f};
+    if (a.pout) {
+        if (hf == 0) reinterpret_cast<float2*>(a.pout + a.prow_total * kHeadDim)[row] = make_float2(m, l);
+        return rf;
+    }
+    if (a.pin) {
+        const float2 ml = __ldg(reinterpret_cast<const float2*>(a.pin + a.prow_total * kHeadDim) + row);
+        const float M = fmaxf(m, ml.x);
+        rf.f = m == -INFINITY ? 0.f : ex2f(m - M);
+        rf.g = ml.x == -INFINITY ? 0.f : ex2f(ml.x - M);
+        l = l * rf.f + ml.y * rf.g;
+    }
+    rf.inv = l > 0.f ? 1.f / l : 0.f;
+    return rf;
+}
+
+__device__ __forceinline__ void finish16(const PrefillArgs& a, long long row, int hf, int c, const RowFinish& rf,
+                                         float (&o)[16], __nv_bfloat16* dst) {
+    const size_t at = static_cast<size_t>(row) * kHeadDim + kHeadDim / 2 * hf + 16 * c;
+    if (a.pout) {
+        float4* o4 = reinterpret_cast<float4*>(a.pout + at);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) o4[i] = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
+        return;
+    }
+    if (a.pin) {
+        const float4* p4 = reinterpret_cast<const float4*>(a.pin + at);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float4 v = __ldg(p4 + i);
+            o[4 * i] = o[4 * i] * rf.f + v.x * rf.g;
+            o[4 * i + 1] = o[4 * i + 1] * rf.f + v.y * rf.g;
+            o[4 * i + 2] = o[4 * i + 2] * rf.f + v.z * rf.g;
+            o[4 * i + 3] = o[4 * i + 3] * rf.f + v.w * rf.g;
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 2; ++i)
+        reinterpret_cast<uint4*>(dst)[2 * c + i] =
+            make_uint4(float2_to_bf16x2(o[8 * i] * rf.inv, o[8 * i + 1] * rf.inv),
+                       float2_to_bf16x2(o[8 * i + 2] * rf.inv, o[8 * i + 3] * rf.inv),
+                       float2_to_bf16x2(o[8 * i + 4] * rf.inv, o[8 * i + 5] * rf.inv),
+                       float2_to_bf16x2(o[8 * i + 6] * rf.inv, o[8 * i + 7] * rf.inv));
+}
+
 __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_constant__ CUtensorMap hmap,
                                                               const __grid_constant__ PrefillArgs a) {
     const bool tree = a.tree != nullptr;
@@ -402,7 +474,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
     int* pend = reinterpret_cast<int*>(wsum + 16);                          // [4] segments to merge, then count
     if (a.persist) {
         if (threadIdx.x < kSoftmaxThreads) {
-            const int n_units = a.nx * a.nkv * a.n_seqs;
+            const int n_units = a.nx * a.nkv * (a.virt ? 1 : a.n_seqs);  // the prefix pass: one sequence
             const int u = threadIdx.x;
             int km = 0;
             if (u < n_units) {
@@ -470,7 +542,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
         auto entry = [&](int k, int j) -> uint32_t {
             const int pi = j * kPagesPerBlock + lane;
             if (!used(k, j)) return 0u;
-            return pi < a.bt_stride ? __ldg(a.bt + static_cast<size_t>(seq_of(k)) * a.bt_stride + pi) : kPageNone;
+            return pi < a.bt_cols ? __ldg(a.bt + static_cast<size_t>(seq_of(k)) * a.bt_stride + pi) : kPageNone;
         };
         int issued = 0, J = 0;
         int k = 0, j = n_segs > 0 ? segs[0].b0 : 0;
@@ -693,7 +765,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
                 const UnitInfo ui = unit_info(a, sg.u);
                 const int t_row = ui.t_begin + tq * a.tile_tokens + rt;
                 rm.L = ui.L;
-                rm.T = ui.T;
+                rm.T = a.virt ? 0 : ui.T;  // the prefix pass sees no chunk keys
                 rm.t_chunk = t_row;
                 rm.tree = tree;
                 rm.valid = (rt < a.tile_tokens) && (t_row < ui.t_end);
@@ -775,21 +847,23 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
             }
             if (sg.n_parts == 1) {
                 if (have_o) {
-                    const float inv = lt > 0.f ? 1.f / lt : 0.f;
                     const bool write = row_valid && !*abort_flag;
+                    long long row = 0;
+                    RowFinish rf{};
+                    if (write) {
+                        const UnitInfo ui = unit_info(a, sg.u);
+                        row = (static_cast<long long>(ui.q0) + rm.t_chunk) * a.n_q + ui.h * a.group + rg;
+                        rf = finish_begin(a, row, hf, m, lt);
+                    }
 #pragma unroll
                     for (int c = 0; c < 2; ++c) {
                         uint32_t x[16];
                         tmem_ld16(t_o + 16 * c, x);
                         tmem_wait16(x);
-                        uint32_t w[8];
+                        float o[16];
 #pragma unroll
-                        for (int i = 0; i < 8; ++i)
-                            w[i] = float2_to_bf16x2(__uint_as_float(x[2 * i]) * inv, __uint_as_float(x[2 * i + 1]) * inv);
-                        if (write) {
-                            reinterpret_cast<uint4*>(dst)[2 * c] = make_uint4(w[0], w[1], w[2], w[3]);
-                            reinterpret_cast<uint4*>(dst)[2 * c + 1] = make_uint4(w[4], w[5], w[6], w[7]);
-                        }
+                        for (int i = 0; i < 16; ++i) o[i] = __uint_as_float(x[i]);
+                        if (write) finish16(a, row, hf, c, rf, o, dst);
                     }
                 }
                 continue;
@@ -859,6 +933,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
             }
             // then 16 dims at a time, two parts' loads in flight at a time
             float lsum = 0.f;
+            const long long row = (static_cast<long long>(ui.q0) + t_row) * a.n_q + ui.h * a.group + rg;
+            RowFinish rf{};
 #pragma unroll 1
             for (int hh = 0; hh < 2; ++hh) {
                 float o[16];
@@ -890,14 +966,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
                         }
                     }
                 }
-                const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
-#pragma unroll
-                for (int i = 0; i < 2; ++i)
-                    reinterpret_cast<uint4*>(dst)[2 * hh + i] =
-                        make_uint4(float2_to_bf16x2(o[8 * i] * inv, o[8 * i + 1] * inv),
-                                   float2_to_bf16x2(o[8 * i + 2] * inv, o[8 * i + 3] * inv),
-                                   float2_to_bf16x2(o[8 * i + 4] * inv, o[8 * i + 5] * inv),
-                                   float2_to_bf16x2(o[8 * i + 6] * inv, o[8 * i + 7] * inv));
+                if (hh == 0) rf = finish_begin(a, row, hf, M, lsum);  // lsum is complete after the first pass
+                finish16(a, row, hf, hh, rf, o, dst);
             }
         }
     }
@@ -931,22 +1001,29 @@ size_t prefill_counter_count(const kv_pool* pool) {
     return pool->cfg.dtype == KV_DTYPE_BF16 ? static_cast<size_t>(kPersistMaxUnits) : 0;
 }
 
-int launch_prefill(kv_pool* pool, const void* q, const int32_t* q_pos, const int32_t* q_off,
-                   const int32_t* prefix, const unsigned long long* tree, int32_t n_seqs, int32_t max_q,
-                   const uint32_t* bt, int32_t bt_stride, void* out, cudaStream_t stream) {
+namespace {
+
+// One prefill_kernel launch.  shared > 0: the pass given by `pass` of the
+// shared-prefix form (0: every token against the first `shared` keys into
+// ws; 1: each sequence against the rest of its keys, merged with ws).
+int launch_prefill_pass(kv_pool* pool, const void* q, const int32_t* q_pos, const int32_t* q_off,
+                        const int32_t* prefix, const unsigned long long* tree, int32_t n_seqs, int32_t max_q,
+                        const uint32_t* bt, int32_t bt_stride, void* out, cudaStream_t stream, int shared, int pass,
+                        float* ws) {
     const auto& c = pool->cfg;
-    if (c.dtype == KV_DTYPE_F32)
-        return launch_prefill_f32(pool, q, q_pos, q_off, prefix, tree, n_seqs, max_q, bt, bt_stride, out, stream);
     const int group = c.n_q_heads / c.n_kv_heads;
     if (group < 1 || group > kRows) return KV_ERR_UNSUPPORTED;
-    PrefillArgs a;
+    PrefillArgs a{};
+    const bool virt = shared > 0 && pass == 0;
+    const int mq = virt ? n_seqs * max_q : max_q;  // the prefix pass is one sequence of every token
     a.q = static_cast<const __nv_bfloat16*>(q);
     a.q_pos = q_pos;
     a.q_off = q_off;
     a.prefix = prefix;
-    a.tree = tree;
-    a.bt = bt;
+    a.tree = virt ? nullptr : tree;
+    a.bt = (shared > 0 && pass == 1) ? bt + shared / kPageTokens : bt;
     a.bt_stride = bt_stride;
+    a.bt_cols = (shared > 0 && pass == 1) ? bt_stride - shared / kPageTokens : bt_stride;
     a.n_q = c.n_q_heads;
     a.nkv = c.n_kv_heads;
     a.group = group;
@@ -954,8 +1031,8 @@ int launch_prefill(kv_pool* pool, const void* q, const int32_t* q_pos, const int
     // enough for one CTA are split evenly over its tiles, so that the rows
     // left over are whole warps of padding (which skip the softmax).
     const int fit = kRows / group;
-    a.tile_tokens = max_q <= kTiles * fit ? std::max(1, (max_q + kTiles - 1) / kTiles) : fit;
-    a.max_q = max_q;
+    a.tile_tokens = mq <= kTiles * fit ? std::max(1, (mq + kTiles - 1) / kTiles) : fit;
+    a.max_q = mq;
     a.rope = pool->rope;
     a.max_pos = c.max_positions;
     a.n_pages = c.n_pages;
@@ -964,20 +1041,53 @@ int launch_prefill(kv_pool* pool, const void* q, const int32_t* q_pos, const int
     a.err = pool->dev_error;
     a.qscale = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(c.head_dim)));
     const int cta_tokens = kTiles * a.tile_tokens;
-    a.nx = std::max(1, (max_q + cta_tokens - 1) / cta_tokens);
+    a.nx = std::max(1, (mq + cta_tokens - 1) / cta_tokens);
     a.n_seqs = n_seqs;
+    a.virt = virt ? 1 : 0;
+    a.virt_L = virt ? shared : 0;
+    a.L_off = (shared > 0 && pass == 1) ? shared : 0;
+    a.prow_total = static_cast<long long>(n_seqs) * max_q * c.n_q_heads;
+    a.pout = virt ? ws : nullptr;
+    a.pin = (shared > 0 && pass == 1) ? ws : nullptr;
     // More units than SMs but few enough for one work list per CTA: the
     // persistent grid, one CTA per SM, each taking an equal run of the units'
     // key blocks (the plain grid would leave part of its last wave idle).
-    const long long n_units = static_cast<long long>(a.nx) * c.n_kv_heads * n_seqs;
+    const int seqs = virt ? 1 : n_seqs;
+    const long long n_units = static_cast<long long>(a.nx) * c.n_kv_heads * seqs;
     a.persist = n_units > pool->sm_count && n_units <= kPersistMaxUnits && pool->pre_part && pool->pre_counters;
     a.part = pool->pre_part;
     a.counters = pool->pre_counters;
-    const dim3 grid = a.persist ? dim3(pool->sm_count) : dim3(a.nx, c.n_kv_heads, n_seqs);
+    const dim3 grid = a.persist ? dim3(pool->sm_count) : dim3(a.nx, c.n_kv_heads, seqs);
     void* args[] = {&pool->head_map, &a};
     const cudaError_t e = cudaLaunchKernel(reinterpret_cast<const void*>(&prefill_kernel), grid, dim3(kThreads), args,
                                            kSmemBytes, stream);
     return e == cudaSuccess ? KV_OK : KV_ERR_CUDA;
+}
+
+}  // namespace
+
+int launch_prefill(kv_pool* pool, const void* q, const int32_t* q_pos, const int32_t* q_off,
+                   const int32_t* prefix, const unsigned long long* tree, int32_t n_seqs, int32_t max_q,
+                   const uint32_t* bt, int32_t bt_stride, void* out, cudaStream_t stream) {
+    if (pool->cfg.dtype == KV_DTYPE_F32)
+        return launch_prefill_f32(pool, q, q_pos, q_off, prefix, tree, n_seqs, max_q, bt, bt_stride, out, stream);
+    return launch_prefill_pass(pool, q, q_pos, q_off, prefix, tree, n_seqs, max_q, bt, bt_stride, out, stream, 0, 0,
+                               nullptr);
+}
+
+size_t prefill_shared_workspace_bytes(const kv_pool* pool, int32_t n_seqs, int32_t max_q) {
+    return static_cast<size_t>(n_seqs) * max_q * pool->cfg.n_q_heads * (kHeadDim + 2) * sizeof(float);
+}
+
+int launch_prefill_shared(kv_pool* pool, const void* q, const int32_t* q_pos, const int32_t* q_off,
+                          const int32_t* prefix, const unsigned long long* tree, int32_t n_seqs, int32_t max_q,
+                          const uint32_t* bt, int32_t bt_stride, int32_t shared, void* ws, void* out,
+                          cudaStream_t stream) {
+    int rc = launch_prefill_pass(pool, q, q_pos, q_off, prefix, tree, n_seqs, max_q, bt, bt_stride, out, stream,
+                                 shared, 0, static_cast<float*>(ws));
+    if (rc != KV_OK) return rc;
+    return launch_prefill_pass(pool, q, q_pos, q_off, prefix, tree, n_seqs, max_q, bt, bt_stride, out, stream, shared,
+                               1, static_cast<float*>(ws));
 }
 
 }  // namespace kvb200

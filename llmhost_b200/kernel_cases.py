@@ -25,6 +25,9 @@ device at most):
   verify       kv_prefill_attn with ancestor masks: the speculative config's
                verify launch (32 sessions sharing a 4096-token prefix, one
                64-node tree each, 24q/8kv)
+  verify_shared the same launch through kv_prefill_attn_shared: the 4096
+               shared tokens in one pass for all 32 sessions, then each
+               session's tree, merged
   decode_q8    kv_append_decode_attn on a Q8 pool (quantise-on-append, then
   decode_k8v4  tcgen05 decode of the converted tiles; K8V4: 4-bit V): the batched-decode
                configuration's 64 session lengths (U[128, 8192]) and six
@@ -214,7 +217,7 @@ def case_prefill_f32(d: _Dev):
                           "flops": flops, "tokens": T}
 
 
-def case_verify(d: _Dev):
+def case_verify(d: _Dev, shared_pass: bool = False):
     from .kv import KvPool, tree_masks
 
     wl = SpecTreeWorkload()
@@ -254,11 +257,26 @@ def case_verify(d: _Dev):
     flops = 4.0 * 64 * wl.n_q * float((P0 + ones).sum())
     kv_bytes = 2 * wl.n_kv * 64 * 2 * (P0 * n + n * T)
 
+    if shared_pass:
+        ws = pool.prefill_shared_workspace(n, T)
+
+        def launch():
+            pool.prefill_attn_shared(q, q_pos_d, q_off, prefix, bt_d, shared_tokens=shared * PAGE_TOKENS, max_q=T,
+                                     tree_masks=masks_d, workspace=ws, out=out)
+
+        return pool, launch, {"kernel": "prefill_kernel x 2 (kv_prefill_attn_shared: shared-prefix pass, then "
+                                        "each session's keys merged)", "bound": "tensor", "flops": flops,
+                              "kv_bytes_streamed": 2 * wl.n_kv * 64 * 2 * (P0 + n * T), "sessions": n, "nodes": T}
+
     def launch():
         pool.prefill_attn(q, q_pos_d, q_off, prefix, bt_d, tree_masks=masks_d, max_q=T, out=out)
 
     return pool, launch, {"kernel": "prefill_kernel (kv_prefill_attn, tree masks, tcgen05)", "bound": "tensor",
                           "flops": flops, "kv_bytes_streamed": kv_bytes, "sessions": n, "nodes": T}
+
+
+def case_verify_shared(d: _Dev):
+    return case_verify(d, shared_pass=True)
 
 
 def _decode_quant(d: _Dev, store: str):
@@ -312,7 +330,8 @@ def case_decode_k8v4(d: _Dev):
 
 
 CASES = {"append": case_append, "copy": case_copy, "move": case_move, "decode_f32": case_decode_f32,
-         "prefill_f32": case_prefill_f32, "verify": case_verify, "decode_q8": case_decode_q8,
+         "prefill_f32": case_prefill_f32, "verify": case_verify, "verify_shared": case_verify_shared,
+         "decode_q8": case_decode_q8,
          "decode_k8v4": case_decode_k8v4}
 
 

@@ -266,3 +266,36 @@ class KvPool:
               "kv_prefill_attn")
         return out
 
+    def prefill_shared_workspace(self, n_seqs: int, max_q: int) -> torch.Tensor:
+        """A workspace for prefill_attn_shared (device bytes)."""
+        nbytes = int(self._lib.kv_prefill_shared_workspace_bytes(self._h, int(n_seqs), int(max_q)))
+        return torch.empty(max(nbytes, 16), dtype=torch.uint8, device=self.device)
+
+    def prefill_attn_shared(self, q, q_pos, q_offsets, prefix_lens, block_tables, shared_tokens: int, max_q: int,
+                            tree_masks=None, workspace=None, out=None, stream=None):
+        """prefill_attn for sequences that all begin with the same shared_tokens
+        tokens on the same pages (kv_prefill_attn_shared): the shared keys in
+        one pass for the whole batch, each sequence's own keys in a second,
+        merged.  Returns `out`."""
+        dt = self.shape.torch_dtype
+        self._check_tensor(q, "q", dt)
+        for t, nm in ((q_pos, "q_pos"), (q_offsets, "q_offsets"), (prefix_lens, "prefix_lens"),
+                      (block_tables, "block_tables")):
+            self._check_tensor(t, nm, torch.int32)
+        if tree_masks is not None:
+            self._check_tensor(tree_masks, "tree_masks", torch.int64)
+        n_seqs = prefix_lens.numel()
+        if q_offsets.numel() != n_seqs + 1:
+            raise ValueError("q_offsets must hold n_seqs + 1 entries")
+        if workspace is None:
+            workspace = self.prefill_shared_workspace(n_seqs, max_q)
+        if out is None:
+            out = torch.empty_like(q)
+        self._check_tensor(out, "out", dt)
+        check(self._lib.kv_prefill_attn_shared(self._h, _ptr(q), _ptr(q_pos), _ptr(q_offsets), _ptr(prefix_lens),
+                                               _ptr(tree_masks), _ptr(block_tables), block_tables.shape[-1],
+                                               n_seqs, int(max_q), int(shared_tokens), _ptr(workspace), _ptr(out),
+                                               _stream_ptr(stream)),
+              "kv_prefill_attn_shared")
+        return out
+
