@@ -54,9 +54,10 @@ extern "C" {
  * (2176 or 1664 bytes a head at P = 16).  K is rotated (RoPE) in fp32 and then quantised.  For
  * quantised pools the appended k / v, q and out are bf16.  They take
  * appends, decode attention (kv_decode_attn, and kv_append_decode_attn as an
- * append launch followed by the attention launch), page copies and token
- * moves; kv_norm_append_decode_attn and kv_prefill_attn return
- * KV_ERR_UNSUPPORTED for them. */
+ * append launch followed by the attention launch; tensor cores, head layouts
+ * as for bf16 pools), kv_prefill_attn (CUDA cores, on the dequantised keys and
+ * values in fp32), page copies and token moves; kv_norm_append_decode_attn
+ * and kv_prefill_attn_shared return KV_ERR_UNSUPPORTED for them. */
 typedef enum { KV_DTYPE_F32 = 0, KV_DTYPE_BF16 = 1, KV_DTYPE_Q8 = 2, KV_DTYPE_K8V4 = 3 } kv_dtype;
 
 typedef enum {

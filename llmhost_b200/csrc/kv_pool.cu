@@ -360,7 +360,6 @@ int kv_prefill_attn(kv_pool* pool, const void* q, const int32_t* q_pos, const in
     if (!q || !q_pos || !q_offsets || !prefix_lens || !block_tables || !out || bt_stride <= 0 ||
         n_seqs > 65535 || (tree_masks && max_q_per_seq > 64))
         return KV_ERR_INVALID;
-    if (kvb200::is_quant(pool->cfg.dtype)) return KV_ERR_UNSUPPORTED;
     DeviceScope dev(pool->cfg.device);
     return kvb200::launch_prefill(pool, q, q_pos, q_offsets, prefix_lens,
                                   reinterpret_cast<const unsigned long long*>(tree_masks), n_seqs,

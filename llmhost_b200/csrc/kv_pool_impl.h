@@ -86,7 +86,7 @@ int launch_prefill_shared(kv_pool* pool, const void* q, const int32_t* q_pos, co
                           const int32_t* prefix, const unsigned long long* tree, int32_t n_seqs, int32_t max_q,
                           const uint32_t* bt, int32_t bt_stride, int32_t shared, void* ws, void* out,
                           cudaStream_t stream);
-// fp32 pools: CUDA-core kernel (kv_prefill_f32.cu), same arguments.
+// fp32 and quantised pools: CUDA-core kernel (kv_prefill_f32.cu), same arguments.
 int launch_prefill_f32(kv_pool* pool, const void* q, const int32_t* q_pos, const int32_t* q_off,
                        const int32_t* prefix, const unsigned long long* tree, int32_t n_seqs, int32_t max_q,
                        const uint32_t* bt, int32_t bt_stride, void* out, cudaStream_t stream);

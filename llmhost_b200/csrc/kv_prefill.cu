@@ -1069,7 +1069,7 @@ int launch_prefill_pass(kv_pool* pool, const void* q, const int32_t* q_pos, cons
 int launch_prefill(kv_pool* pool, const void* q, const int32_t* q_pos, const int32_t* q_off,
                    const int32_t* prefix, const unsigned long long* tree, int32_t n_seqs, int32_t max_q,
                    const uint32_t* bt, int32_t bt_stride, void* out, cudaStream_t stream) {
-    if (pool->cfg.dtype == KV_DTYPE_F32)
+    if (pool->cfg.dtype != KV_DTYPE_BF16)  // fp32 and quantised pools: the CUDA-core kernel
         return launch_prefill_f32(pool, q, q_pos, q_off, prefix, tree, n_seqs, max_q, bt, bt_stride, out, stream);
     return launch_prefill_pass(pool, q, q_pos, q_off, prefix, tree, n_seqs, max_q, bt, bt_stride, out, stream, 0, 0,
                                nullptr);

@@ -7,6 +7,10 @@
 // 1e-5 relative bound of attention_forward (crates/llm-engine/src/lfm2.rs:
 // 1058-1111).
 //
+// Quantised pools (KV_DTYPE_Q8, KV_DTYPE_K8V4) run the same kernel: their
+// pages are dequantised into the fp32 staging (code x f16 block scale, exact
+// in fp32) and their q and out are bf16.
+//
 // One CTA (8 warps) per (sequence, kv head, kTokens query tokens); a row is a
 // (token, query head of the group) pair, up to 32 rows per CTA.  Per page of
 // 16 keys the CTA stages this head's K and V slices (4 KiB each) in shared
@@ -14,6 +18,8 @@
 // lanes (2k, 2k+1) split key k's 64-dim dot product, the page maximum and sum
 // are warp reductions, and lane l accumulates output dims 2l, 2l+1.  Scores
 // are in log2 units (q pre-scaled by log2(e)/sqrt(d)) with an online max.
+#include <cuda_fp16.h>
+
 #include <cmath>
 
 #include "kv_common.cuh"
@@ -28,7 +34,7 @@ constexpr int kHalf = 33;             // padded half-row of a staged K slice (fl
 constexpr int kKRow = 2 * kHalf;      // one key's 64 dims in two padded halves
 
 struct PrefillF32Args {
-    const float* q;
+    const void* q;        // fp32 (fp32 pools) or bf16 (quantised pools)
     const int32_t* q_pos;
     const int32_t* q_off;
     const int32_t* prefix;
@@ -39,9 +45,9 @@ struct PrefillF32Args {
     const float2* rope;
     int max_pos;
     uint32_t n_pages;
-    const float* pages;
-    size_t page_floats;
-    float* out;
+    const void* pages;
+    size_t page_bytes;
+    void* out;            // as q
     int* err;
     float qscale;
 };
@@ -57,6 +63,8 @@ struct Stage {
     float v[kPageTokens * kHeadDim];
 };
 
+// kQ: 0 fp32 pages; 1 Q8, 2 K8V4 pages (bf16 q and out)
+template <int kQ>
 __global__ void __launch_bounds__(kWarps * 32) prefill_f32_kernel(const PrefillF32Args a) {
     const int s = blockIdx.z, h = blockIdx.y;
     const int q0 = __ldg(a.q_off + s);
@@ -82,14 +90,23 @@ __global__ void __launch_bounds__(kWarps * 32) prefill_f32_kernel(const PrefillF
     for (int e = threadIdx.x; e < n_rows * (kHeadDim / 2); e += blockDim.x) {
         const int row = e / (kHeadDim / 2), i = e % (kHeadDim / 2);
         const int tok = t_begin + row / a.group, g = row % a.group;
-        const float* src = a.q + (static_cast<size_t>(q0 + tok) * a.n_q + h * a.group + g) * kHeadDim;
+        const size_t qrow = (static_cast<size_t>(q0 + tok) * a.n_q + h * a.group + g) * kHeadDim;
         int pos = __ldg(a.q_pos + q0 + tok);
         if (pos < 0 || pos >= a.max_pos) {
             if (i == 0) flag_error(a.err, kDevErrBadPos);
             pos = 0;
         }
         const float2 c = __ldg(a.rope + static_cast<size_t>(pos) * (kHeadDim / 2) + i);
-        const float x = __ldg(src + i), y = __ldg(src + i + kHeadDim / 2);
+        float x, y;
+        if constexpr (kQ == 0) {
+            const float* src = static_cast<const float*>(a.q) + qrow;
+            x = __ldg(src + i);
+            y = __ldg(src + i + kHeadDim / 2);
+        } else {
+            const __nv_bfloat16* src = static_cast<const __nv_bfloat16*>(a.q) + qrow;
+            x = __bfloat162float(src[i]);
+            y = __bfloat162float(src[i + kHeadDim / 2]);
+        }
         q_s[row][i] = __fadd_rn(__fmul_rn(x, c.x), __fmul_rn(-y, c.y)) * a.qscale;
         q_s[row][kHalf + i] = __fadd_rn(__fmul_rn(y, c.x), __fmul_rn(x, c.y)) * a.qscale;
     }
@@ -100,14 +117,17 @@ __global__ void __launch_bounds__(kWarps * 32) prefill_f32_kernel(const PrefillF
         if (p < a.bt_stride) phys = __ldg(a.bt + static_cast<size_t>(s) * a.bt_stride + p);
         const bool ok = phys < a.n_pages;
         if (!ok && threadIdx.x == 0) flag_error(a.err, kDevErrBadPage);
-        const float* kb = a.pages + static_cast<size_t>(ok ? phys : 0) * a.page_floats +
-                          static_cast<size_t>(h) * kPageTokens * kHeadDim;
-        const float* vb = kb + static_cast<size_t>(a.nkv) * kPageTokens * kHeadDim;
         // 16 keys x 64 dims = 256 float4 per slice: thread t moves one of K and one of V
         const int t = threadIdx.x, kk = t / 16, c4 = t % 16;  // dims 4*c4 .. 4*c4+3
         float* kdst = dst.k + kk * kKRow + (c4 < 8 ? 4 * c4 : kHalf + 4 * (c4 - 8));
         float* vdst = dst.v + kk * kHeadDim + 4 * c4;
-        if (ok) {
+        if (!ok) {
+            kdst[0] = kdst[1] = kdst[2] = kdst[3] = 0.f;
+            *reinterpret_cast<float4*>(vdst) = make_float4(0.f, 0.f, 0.f, 0.f);
+        } else if constexpr (kQ == 0) {
+            const float* kb = static_cast<const float*>(a.pages) + static_cast<size_t>(phys) * (a.page_bytes / 4) +
+                              static_cast<size_t>(h) * kPageTokens * kHeadDim;
+            const float* vb = kb + static_cast<size_t>(a.nkv) * kPageTokens * kHeadDim;
             // the padded K half-rows are not 16-byte aligned: plain loads there
             const float4 kv = __ldg(reinterpret_cast<const float4*>(kb + kk * kHeadDim) + c4);
             kdst[0] = kv.x;
@@ -116,8 +136,34 @@ __global__ void __launch_bounds__(kWarps * 32) prefill_f32_kernel(const PrefillF
             kdst[3] = kv.w;
             cp_async16(vdst, vb + kk * kHeadDim + 4 * c4);
         } else {
-            kdst[0] = kdst[1] = kdst[2] = kdst[3] = 0.f;
-            *reinterpret_cast<float4*>(vdst) = make_float4(0.f, 0.f, 0.f, 0.f);
+            // head block of the page: K codes [16][64], V codes [16][vrow],
+            // scales [16][2 blocks][K, V]; dims 4 c4 .. lie in block c4 / 8
+            constexpr int kVRow = kQ == 2 ? 32 : 64;
+            const uint8_t* blk = static_cast<const uint8_t*>(a.pages) + static_cast<size_t>(phys) * a.page_bytes +
+                                 static_cast<size_t>(h) * kPageTokens * (kHeadDim + kVRow + 8);
+            const uint32_t sc = __ldg(reinterpret_cast<const uint32_t*>(blk + kPageTokens * (kHeadDim + kVRow) +
+                                                                       kk * 8 + (c4 / 8) * 4));
+            const float ks = __half2float(__ushort_as_half(static_cast<unsigned short>(sc & 0xffffu)));
+            const float vs = __half2float(__ushort_as_half(static_cast<unsigned short>(sc >> 16)));
+            const uint32_t kw = __ldg(reinterpret_cast<const uint32_t*>(blk + kk * kHeadDim + 4 * c4));
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+                kdst[e] = static_cast<float>(static_cast<int8_t>((kw >> (8 * e)) & 0xffu)) * ks;
+            float vv[4];
+            if constexpr (kQ == 2) {
+                const uint32_t vw = __ldg(reinterpret_cast<const unsigned short*>(blk + kPageTokens * kHeadDim +
+                                                                                  kk * kVRow + 2 * c4));
+#pragma unroll
+                for (int e = 0; e < 4; ++e)
+                    vv[e] = static_cast<float>(static_cast<int>(vw << (28 - 4 * e)) >> 28) * vs;
+            } else {
+                const uint32_t vw = __ldg(reinterpret_cast<const uint32_t*>(blk + kPageTokens * kHeadDim +
+                                                                           kk * kVRow + 4 * c4));
+#pragma unroll
+                for (int e = 0; e < 4; ++e)
+                    vv[e] = static_cast<float>(static_cast<int8_t>((vw >> (8 * e)) & 0xffu)) * vs;
+            }
+            *reinterpret_cast<float4*>(vdst) = make_float4(vv[0], vv[1], vv[2], vv[3]);
         }
         cp_async_commit();
     };
@@ -197,8 +243,13 @@ __global__ void __launch_bounds__(kWarps * 32) prefill_f32_kernel(const PrefillF
         if (row >= n_rows) break;
         const int tok = t_begin + row / a.group, g = row % a.group;
         const float inv = l[i] > 0.f ? 1.f / l[i] : 0.f;
-        float* dst = a.out + (static_cast<size_t>(q0 + tok) * a.n_q + h * a.group + g) * kHeadDim;
-        reinterpret_cast<float2*>(dst)[lane] = make_float2(acc[i].x * inv, acc[i].y * inv);
+        const size_t orow = (static_cast<size_t>(q0 + tok) * a.n_q + h * a.group + g) * kHeadDim;
+        if constexpr (kQ == 0)
+            reinterpret_cast<float2*>(static_cast<float*>(a.out) + orow)[lane] =
+                make_float2(acc[i].x * inv, acc[i].y * inv);
+        else
+            reinterpret_cast<uint32_t*>(static_cast<__nv_bfloat16*>(a.out) + orow)[lane] =
+                float2_to_bf16x2(acc[i].x * inv, acc[i].y * inv);
     }
 }
 
@@ -211,7 +262,7 @@ int launch_prefill_f32(kv_pool* pool, const void* q, const int32_t* q_pos, const
     const int group = c.n_q_heads / c.n_kv_heads;
     if (group < 1 || group > kMaxRows) return KV_ERR_UNSUPPORTED;
     PrefillF32Args a;
-    a.q = static_cast<const float*>(q);
+    a.q = q;
     a.q_pos = q_pos;
     a.q_off = q_off;
     a.prefix = prefix;
@@ -226,13 +277,18 @@ int launch_prefill_f32(kv_pool* pool, const void* q, const int32_t* q_pos, const
     a.rope = pool->rope;
     a.max_pos = c.max_positions;
     a.n_pages = c.n_pages;
-    a.pages = static_cast<const float*>(pool->pages);
-    a.page_floats = pool->page_bytes / sizeof(float);
-    a.out = static_cast<float*>(out);
+    a.pages = pool->pages;
+    a.page_bytes = pool->page_bytes;
+    a.out = out;
     a.err = pool->dev_error;
     a.qscale = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(c.head_dim)));
     const dim3 grid((max_q + a.tokens - 1) / a.tokens, c.n_kv_heads, n_seqs);
-    prefill_f32_kernel<<<grid, kWarps * 32, 0, stream>>>(a);
+    if (c.dtype == KV_DTYPE_Q8)
+        prefill_f32_kernel<1><<<grid, kWarps * 32, 0, stream>>>(a);
+    else if (c.dtype == KV_DTYPE_K8V4)
+        prefill_f32_kernel<2><<<grid, kWarps * 32, 0, stream>>>(a);
+    else
+        prefill_f32_kernel<0><<<grid, kWarps * 32, 0, stream>>>(a);
     return cudaGetLastError() == cudaSuccess ? KV_OK : KV_ERR_CUDA;
 }
 

@@ -30,11 +30,12 @@ def _depths(parents):
 class PrefillCase:
     """seqs: list of (L, T) for a causal chunk or (L, parents) for a tree."""
 
-    def __init__(self, n_q, n_kv, seqs, seed=0, extra_pages=4, dtype="bf16"):
+    def __init__(self, n_q, n_kv, seqs, seed=0, extra_pages=4, dtype="bf16", store=None):
         from llmhost_b200.kv import tree_masks
 
         rng = np.random.default_rng(seed)
         self.n_q, self.n_kv, self.dtype = n_q, n_kv, dtype
+        self.store = store or dtype  # the pool's storage type (quantised pools take bf16 q / k / v)
         self.L = np.array([s[0] for s in seqs], np.int64)
         self.parents = [None if isinstance(s[1], int) else list(s[1]) for s in seqs]
         self.T = np.array([s[1] if isinstance(s[1], int) else len(s[1]) for s in seqs], np.int64)
@@ -70,7 +71,9 @@ class PrefillCase:
         (orc_paged_append_tokens, orc_paged_prefill), which
         tests/test_oracle_bulk.py pins bit for bit to the per-token append and
         orc_attention_masked with the explicit mask."""
-        host = O.HostPages(self.n_pages, O.BF16 if self.dtype == "bf16" else O.F32, self.n_q, self.n_kv)
+        from paged_case import ORACLE_DTYPE
+
+        host = O.HostPages(self.n_pages, ORACLE_DTYPE[self.store], self.n_q, self.n_kv)
         n = len(self.L)
         tot = self.L + self.T
         rows = np.repeat(np.arange(n, dtype=np.int32), tot)
@@ -87,7 +90,7 @@ class PrefillCase:
     def make_pool(self):
         from llmhost_b200.kv import KvPool
 
-        return KvPool(dtype=self.dtype, n_q_heads=self.n_q, n_kv_heads=self.n_kv, n_pages=self.n_pages,
+        return KvPool(dtype=self.store, n_q_heads=self.n_q, n_kv_heads=self.n_kv, n_pages=self.n_pages,
                       max_positions=self.max_pos, max_seqs=max(len(self.L), 1))
 
     def run_gpu(self, pool, max_q=None):

@@ -75,7 +75,7 @@ def test_quant_long_single_head(cuda, store):
 
 
 @pytest.mark.parametrize("store", STORES)
-def test_quant_unsupported_entry_points(cuda, store):
+def test_quant_norm_and_shared_prefill_refused(cuda, store):
     import torch
     from llmhost_b200 import _capi
 
@@ -93,10 +93,31 @@ def test_quant_unsupported_entry_points(cuda, store):
         assert e.value.status == 6  # KV_ERR_UNSUPPORTED
         qp = torch.zeros(1, dtype=torch.int32, device=dev)
         off = torch.tensor([0, 1], dtype=torch.int32, device=dev)
+        sixteen = torch.full((1,), 16, dtype=torch.int32, device=dev)
         with pytest.raises(_capi.KvError) as e:
-            pool.prefill_attn(q[:1].contiguous(), qp, off, qp, bt, max_q=1)
+            pool.prefill_attn_shared(q[:1].contiguous(), qp, off, sixteen, bt, shared_tokens=16, max_q=1)
         assert e.value.status == 6  # KV_ERR_UNSUPPORTED
         assert pool.last_error() == 0
+
+
+@pytest.mark.parametrize("store", STORES)
+def test_quant_prefill_causal_chunks(cuda, store):
+    # chunked prefill on a quantised pool: the CUDA-core kernel on the
+    # dequantised keys and values; pages bit-exact, outputs within 2e-2
+    import test_gpu_prefill as tp
+
+    case = tp.PrefillCase(24, 8, [(0, 40), (100, 17), (300, 64), (31, 1)], seed=61, store=store)
+    tp.check(case, f"{store} causal chunks")
+
+
+@pytest.mark.parametrize("store", STORES)
+def test_quant_tree_verify(cuda, store):
+    import test_gpu_prefill as tp
+
+    rng = np.random.default_rng(62)
+    trees = [[-1] + [int(rng.integers(0, i)) for i in range(1, n)] for n in (1, 5, 64, 33)]
+    case = tp.PrefillCase(32, 8, [(int(rng.integers(0, 700)), t) for t in trees], seed=63, store=store)
+    tp.check(case, f"{store} tree verify")
 
 
 @pytest.mark.parametrize("store", STORES)
