@@ -56,8 +56,9 @@ extern "C" {
  * appends, decode attention (kv_decode_attn, and kv_append_decode_attn as an
  * append launch followed by the attention launch; tensor cores, head layouts
  * as for bf16 pools), kv_prefill_attn (CUDA cores, on the dequantised keys and
- * values in fp32), page copies and token moves; kv_norm_append_decode_attn
- * and kv_prefill_attn_shared return KV_ERR_UNSUPPORTED for them. */
+ * values in fp32), kv_norm_append_decode_attn (the k norm in the append
+ * launch, the q norm in the attention launch), page copies and token moves;
+ * kv_prefill_attn_shared returns KV_ERR_UNSUPPORTED for them. */
 typedef enum { KV_DTYPE_F32 = 0, KV_DTYPE_BF16 = 1, KV_DTYPE_Q8 = 2, KV_DTYPE_K8V4 = 3 } kv_dtype;
 
 typedef enum {

@@ -36,6 +36,8 @@ struct AppendArgs {
     const float2* rope;
     int max_pos;
     int* err;
+    const float* k_norm;  // quantised pools: RMSNorm weights of k before RoPE (null: none)
+    float eps;
 };
 
 __device__ __forceinline__ void load8(const __nv_bfloat16* p, float (&x)[8]) {
@@ -225,6 +227,16 @@ __global__ void __launch_bounds__(256) append_q_kernel(uint8_t* __restrict__ pag
     float x[8], y[8], xo[8], yo[8];
     load8(ksrc + 8 * qd, x);
     load8(ksrc + 8 * qd + 32, y);
+    if (a.k_norm) {
+        // the row's RMSNorm (ops.rs:8-23, lfm2.rs:805-812) before RoPE; each of
+        // the four threads works the row's scale out itself
+        const float sc = rms_scale_row(ksrc, a.eps);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            x[e] = rms_apply(x[e], sc, __ldg(a.k_norm + 8 * qd + e));
+            y[e] = rms_apply(y[e], sc, __ldg(a.k_norm + 32 + 8 * qd + e));
+        }
+    }
     const float2* cs = a.rope + static_cast<size_t>(pos) * (kHeadDim / 2) + 8 * qd;
     float ax = 0.f, ay = 0.f;
 #pragma unroll
@@ -270,7 +282,8 @@ __global__ void __launch_bounds__(256) append_q_kernel(uint8_t* __restrict__ pag
 int launch_append(kv_pool* pool, const void* k, const void* v, const int32_t* tok_seq,
                   const int32_t* tok_slot, const int32_t* tok_pos, const int32_t* seq_lens,
                   int32_t n_tokens, int32_t n_seqs, const uint32_t* bt, int32_t bt_stride,
-                  cudaStream_t stream) {
+                  cudaStream_t stream, const float* k_norm, float eps) {
+    if (k_norm && !is_quant(pool->cfg.dtype)) return KV_ERR_UNSUPPORTED;  // bf16 / fp32 fold it into the decode
     AppendArgs a;
     a.k = k;
     a.v = v;
@@ -287,6 +300,8 @@ int launch_append(kv_pool* pool, const void* k, const void* v, const int32_t* to
     a.rope = pool->rope;
     a.max_pos = pool->cfg.max_positions;
     a.err = pool->dev_error;
+    a.k_norm = k_norm;
+    a.eps = eps;
     const long long threads = static_cast<long long>(n_tokens) * a.nkv * 4;
     const int block = 256;
     const unsigned grid = static_cast<unsigned>((threads + block - 1) / block);

@@ -943,15 +943,15 @@ int launch_decode(kv_pool* pool, const void* q, const uint32_t* bt, int32_t bt_s
         return launch_decode_tc(pool, q, bt, bt_stride, seq_lens, n_seqs, window, out, stream, new_k, new_v, q_norm,
                                 k_norm, eps);
     if (is_quant(c.dtype)) {
-        // The append (quantise on store) and the attention as two launches.
-        if (q_norm != nullptr || k_norm != nullptr) return KV_ERR_UNSUPPORTED;
+        // The append (k RMSNorm, RoPE, quantise on store) and the attention
+        // (with the q RMSNorm) as two launches.
         if (new_k != nullptr) {
             const int rc = launch_append(pool, new_k, new_v, nullptr, nullptr, nullptr, seq_lens, n_seqs, n_seqs, bt,
-                                         bt_stride, stream);
+                                         bt_stride, stream, k_norm, eps);
             if (rc != KV_OK) return rc;
         }
         return launch_decode_tc(pool, q, bt, bt_stride, seq_lens, n_seqs, window, out, stream, nullptr, nullptr,
-                                nullptr, nullptr, 0.f);
+                                q_norm, nullptr, eps);
     }
     const DecodeVariant* v = find_variant(c.dtype, c.n_kv_heads, c.n_q_heads / c.n_kv_heads);
     if (!v) return KV_ERR_UNSUPPORTED;

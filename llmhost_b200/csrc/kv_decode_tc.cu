@@ -392,7 +392,6 @@ __device__ __forceinline__ unsigned short round_ab(float x, float& xr) {
 template <int NKV, int G, bool kNorm, int kQ>
 __global__ void __launch_bounds__(block_threads<kQ>(), 1) decode_tc_kernel(const __grid_constant__ CUtensorMap hmap,
                                                                            const TcArgs a) {
-    static_assert(!(kNorm && kQ), "quantised pools take the norm-free form");
     constexpr int kNT = block_threads<kQ>();
     using Sh = TcShape<NKV, G, kQ>;
     constexpr int kRing = Sh::kRing;
@@ -545,7 +544,7 @@ __global__ void __launch_bounds__(block_threads<kQ>(), 1) decode_tc_kernel(const
         };
         // k RMSNorm weights of this lane's dims (2 ii, 2 ii + 1, 32 + 2 ii, 33 + 2 ii)
         float2 kwx = make_float2(1.f, 1.f), kwy = make_float2(1.f, 1.f);
-        if constexpr (kNorm) {
+        if constexpr (kNorm && kQ == 0) {  // quantised pools normalise k in their append launch (no k_norm here)
             kwx = __ldg(reinterpret_cast<const float2*>(a.k_norm) + (lane & 15));
             kwy = __ldg(reinterpret_cast<const float2*>(a.k_norm + 32) + (lane & 15));
         }
@@ -1364,6 +1363,8 @@ struct TcVariant {
     const void* fn_norm;  // bf16 pages, with the q/k RMSNorm
     const void* fn_q8;    // KV_DTYPE_Q8 pages (codes converted in the CTA)
     const void* fn_k8v4;  // KV_DTYPE_K8V4 pages
+    const void* fn_q8_norm;  // the same with the q RMSNorm
+    const void* fn_k8v4_norm;
     size_t (*smem)(int);  // dynamic shared memory of each, by max_seqs
     size_t (*smem_q8)(int);
     size_t (*smem_k8v4)(int);
@@ -1377,6 +1378,8 @@ TcVariant make_tc_variant() {
                      reinterpret_cast<const void*>(&decode_tc_kernel<NKV, G, true, 0>),
                      reinterpret_cast<const void*>(&decode_tc_kernel<NKV, G, false, 1>),
                      reinterpret_cast<const void*>(&decode_tc_kernel<NKV, G, false, 2>),
+                     reinterpret_cast<const void*>(&decode_tc_kernel<NKV, G, true, 1>),
+                     reinterpret_cast<const void*>(&decode_tc_kernel<NKV, G, true, 2>),
                      &TcShape<NKV, G, 0>::smem_bytes, &TcShape<NKV, G, 1>::smem_bytes,
                      &TcShape<NKV, G, 2>::smem_bytes};
 }
@@ -1393,8 +1396,8 @@ const TcVariant* find_tc_variant(int nkv, int group) {
 
 // The kernel for a pool's storage type (and the norm form for bf16 pools).
 const void* tc_kernel_for(const TcVariant* v, int dtype, bool norm) {
-    if (dtype == KV_DTYPE_Q8) return v->fn_q8;
-    if (dtype == KV_DTYPE_K8V4) return v->fn_k8v4;
+    if (dtype == KV_DTYPE_Q8) return norm ? v->fn_q8_norm : v->fn_q8;
+    if (dtype == KV_DTYPE_K8V4) return norm ? v->fn_k8v4_norm : v->fn_k8v4;
     return norm ? v->fn_norm : v->fn;
 }
 
@@ -1413,7 +1416,7 @@ int decode_tc_setup(kv_pool* pool) {
     if (smem > static_cast<size_t>(optin)) return KV_ERR_INVALID;  // max_seqs too large
     const void* fn = tc_kernel_for(v, c.dtype, false);
     if (raise_smem_limit(fn, c.device, smem) != KV_OK ||
-        (c.dtype == KV_DTYPE_BF16 && raise_smem_limit(v->fn_norm, c.device, smem) != KV_OK))
+        raise_smem_limit(tc_kernel_for(v, c.dtype, true), c.device, smem) != KV_OK)
         return KV_ERR_CUDA;
     int per_sm = 0;
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, tc_threads_for(c.dtype), smem) != cudaSuccess ||
@@ -1430,8 +1433,8 @@ int launch_decode_tc(kv_pool* pool, const void* q, const uint32_t* bt, int32_t b
     const auto& c = pool->cfg;
     const TcVariant* v = find_tc_variant(c.n_kv_heads, c.n_q_heads / c.n_kv_heads);
     if (!v) return KV_ERR_UNSUPPORTED;
-    // Quantised pools: the append is its own launch, and no norm form.
-    if (is_quant(c.dtype) && (new_k != nullptr || q_norm != nullptr)) return KV_ERR_UNSUPPORTED;
+    // Quantised pools: the append (with the k norm) is its own launch.
+    if (is_quant(c.dtype) && (new_k != nullptr || k_norm != nullptr)) return KV_ERR_UNSUPPORTED;
     TcArgs a;
     a.q = static_cast<const __nv_bfloat16*>(q);
     a.out = static_cast<__nv_bfloat16*>(out);

@@ -346,7 +346,6 @@ int kv_norm_append_decode_attn(kv_pool* pool, const void* k, const void* v, cons
     if (!k || !v || !q || !q_norm || !k_norm || !block_tables || !seq_lens || !out || bt_stride <= 0 ||
         !aligned16(k) || !aligned16(v) || !aligned16(q) || !aligned16(q_norm) || !aligned16(k_norm))
         return KV_ERR_INVALID;
-    if (kvb200::is_quant(pool->cfg.dtype)) return KV_ERR_UNSUPPORTED;
     DeviceScope dev(pool->cfg.device);
     return kvb200::launch_decode(pool, q, block_tables, bt_stride, seq_lens, n_seqs, window, out,
                                  static_cast<cudaStream_t>(stream), k, v, q_norm, k_norm, eps);

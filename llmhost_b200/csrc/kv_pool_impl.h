@@ -44,7 +44,7 @@ inline size_t quant_page_bytes(int dtype, int nkv) { return static_cast<size_t>(
 int launch_append(kv_pool* pool, const void* k, const void* v, const int32_t* tok_seq,
                   const int32_t* tok_slot, const int32_t* tok_pos, const int32_t* seq_lens,
                   int32_t n_tokens, int32_t n_seqs, const uint32_t* bt, int32_t bt_stride,
-                  cudaStream_t stream);
+                  cudaStream_t stream, const float* k_norm = nullptr, float eps = 0.f);
 
 // Raises a kernel's dynamic shared-memory limit on `device` to at least
 // `bytes` (never lowers it: the attribute is shared by every pool).

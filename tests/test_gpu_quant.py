@@ -74,8 +74,37 @@ def test_quant_long_single_head(cuda, store):
     assert_close_rows(out, ref, RTOL, f"{store} 40k")
 
 
+NORM_CASES = {
+    "ragged": dict(n_q=24, n_kv=8, lens=[0, 1, 17, 300, 2999], seed=71),
+    "group4": dict(n_q=32, n_kv=8, lens=[5, 700, 4097, 63], seed=72),
+    "one kv head, long": dict(n_q=4, n_kv=1, lens=[20001], seed=73),
+    "window, evicted": dict(n_q=24, n_kv=8, lens=[5000, 40, 1030], seed=74, window=1024, evict_below_window=True),
+}
+
+
 @pytest.mark.parametrize("store", STORES)
-def test_quant_norm_and_shared_prefill_refused(cuda, store):
+@pytest.mark.parametrize("name", list(NORM_CASES))
+def test_quant_norm_decode_against_oracle(cuda, store, name):
+    # kv_norm_append_decode_attn on a quantised pool: k normalised (sum of
+    # squares in double), rotated and quantised by the append launch, q
+    # normalised in the attention launch; codes and scales bit-exact
+    c = dict(NORM_CASES[name])
+    case = DecodeCase("bf16", c.pop("n_q"), c.pop("n_kv"), c.pop("lens"), store=store, **c)
+    rng = np.random.default_rng(8)
+    norm = (rng.uniform(0.5, 1.5, 64).astype(np.float32), rng.uniform(0.5, 1.5, 64).astype(np.float32), 1e-5)
+    host, ref = case.run_oracle(norm=norm)
+    with case.make_pool() as pool:
+        case.prefill_gpu(pool)
+        out = to_numpy_f32(case.decode_norm_gpu(pool, norm))
+        assert pool.last_error() == 0
+        ids = case.used_pages()
+        pages = pool.read_pages(ids)
+    np.testing.assert_array_equal(pages, host.data[ids], err_msg="stored codes / scales differ from the oracle")
+    assert_close_rows(out, ref, RTOL, f"{store} norm {name}")
+
+
+@pytest.mark.parametrize("store", STORES)
+def test_quant_shared_prefill_refused(cuda, store):
     import torch
     from llmhost_b200 import _capi
 
@@ -87,10 +116,7 @@ def test_quant_norm_and_shared_prefill_refused(cuda, store):
         v = to_torch(case.v_new, "bf16", dev)
         bt = torch.from_numpy(case.bt.view(np.int32)).to(dev)
         lens = torch.from_numpy(case.seq_lens).to(dev)
-        w = torch.ones(64, dtype=torch.float32, device=dev)
-        with pytest.raises(_capi.KvError) as e:
-            pool.norm_append_decode_attn(k, v, q, w, w, 1e-5, bt, lens)
-        assert e.value.status == 6  # KV_ERR_UNSUPPORTED
+        del k, v, lens
         qp = torch.zeros(1, dtype=torch.int32, device=dev)
         off = torch.tensor([0, 1], dtype=torch.int32, device=dev)
         sixteen = torch.full((1,), 16, dtype=torch.int32, device=dev)
