@@ -6,7 +6,8 @@ the GPU and replays it on the CPU oracle from the same seeded inputs:
 
 * config 2, bf16 batched decode: the 64 sessions with lengths U[128, 8192]
   (seed 1) whose pages are drawn from a permutation of the 2^20-page pool;
-  kv_append_decode_attn, kv_decode_attn and kv_norm_append_decode_attn;
+  kv_append_decode_attn, kv_decode_attn and kv_norm_append_decode_attn; the
+  same on Q8 and K8V4 pools (codes and scales bit-exact);
 * config 3, bf16 chunked prefill: the last 512-token causal chunk after
   15 872 cached keys at 32q/8kv, beside the first chunk and a middle one;
 * config 4, speculative tree: 32 sessions forked from a shared prefix, each
@@ -30,7 +31,7 @@ import pytest
 
 from llmhost_b200.workloads import PAGE_TOKENS, normal_bits
 from oracle import oracle as O
-from paged_case import PAGE_NONE, assert_close_rows, to_numpy_f32, to_torch
+from paged_case import ORACLE_DTYPE, PAGE_NONE, assert_close_rows, to_numpy_f32, to_torch
 
 pytestmark = pytest.mark.gpu
 RTOL_BF16 = 2e-2
@@ -65,7 +66,8 @@ def _token_layout(lens):
 
 
 # ---- config 2 -----------------------------------------------------------------------
-def test_config2_batched_decode_full_size(cuda):
+@pytest.mark.parametrize("store", ["bf16", "q8", "k8v4"])
+def test_config2_batched_decode_full_size(cuda, store):
     import torch
     from llmhost_b200.kv import KvPool
     from llmhost_b200.workloads import decode_config
@@ -78,11 +80,11 @@ def test_config2_batched_decode_full_size(cuda):
     rows, slots = _token_layout(wl.l0)
     k = normal_bits(rng, (len(slots), wl.n_kv, 64), "bf16")
     v = normal_bits(rng, (len(slots), wl.n_kv, 64), "bf16")
-    host = O.HostPages(len(ids), O.BF16, wl.n_q, wl.n_kv)
+    host = O.HostPages(len(ids), ORACLE_DTYPE[store], wl.n_q, wl.n_kv)
     host.append_tokens(cbt, rows, slots, slots, k, v)
     lens = wl.seq_lens(0)
     n = wl.n_seqs
-    with KvPool(dtype="bf16", n_q_heads=wl.n_q, n_kv_heads=wl.n_kv, n_pages=wl.pool_pages,
+    with KvPool(dtype=store, n_q_heads=wl.n_q, n_kv_heads=wl.n_kv, n_pages=wl.pool_pages,
                 max_positions=int(lens.max()) + 16, max_seqs=n) as pool:
         bt_d = _u32(bt, cuda)
         pool.append(to_torch(k, "bf16", cuda), to_torch(v, "bf16", cuda), _i32(rows, cuda), _i32(slots, cuda),
@@ -126,7 +128,7 @@ def test_config2_batched_decode_full_size(cuda):
         np.testing.assert_array_equal(pool.read_pages(tail), host.data[np.searchsorted(ids, tail)],
                                       err_msg="config 2: normalised K rows differ")
         e3 = assert_close_rows(to_numpy_f32(out3), ref3, RTOL_BF16, "config 2 kv_norm_append_decode_attn")
-    print(f"config 2 (64 sessions, {int(lens.sum())} keys, 2^20-page pool): worst row errors "
+    print(f"config 2 {store} (64 sessions, {int(lens.sum())} keys, 2^20-page pool): worst row errors "
           f"{e1:.2e} / {e2:.2e} / {e3:.2e}")
 
 
