@@ -139,7 +139,7 @@ def test_shared_prefix_speculative_round(cuda):
 
 
 def test_shared_prefix_ragged_private_keys(cuda):
-    # private cached tokens after the shared ones (a later round), ragged trees
+    # private cached tokens after the shared ones (a later speculative round), ragged trees
     rng = np.random.default_rng(9)
     extra = [int(rng.integers(0, 300)) for _ in range(8)]
     case = SharedCase(24, 8, 512, extra, [_tree(rng, int(rng.integers(1, 65))) for _ in range(8)], seed=10)
