@@ -57,6 +57,25 @@ def test_invalid_config_rejected_before_touching_cuda():
     assert h.value is None
 
 
+def test_quantised_dtypes_accepted_by_the_config_check():
+    # Q8 (2) and K8V4 (3) pass the shape check (without a GPU the call then
+    # fails on CUDA), unlike an unknown dtype, which the check rejects
+    lib = _capi.lib()
+    for dt in (_capi.KV_DTYPE_Q8, _capi.KV_DTYPE_K8V4):
+        h = _capi.c_void_p()
+        cfg = _capi.KvPoolConfig(dt, 24, 8, 64, 16, 1024, 1e6, 1024, 64, 0)
+        rc = lib.kv_pool_create(cfg, h)
+        assert rc != 1
+        if rc == 0:  # a GPU is present: the pool exists
+            assert lib.kv_pool_destroy(h) == 0
+
+
+def test_shared_prefill_argument_checks_without_gpu():
+    lib = _capi.lib()
+    assert lib.kv_prefill_shared_workspace_bytes(None, 32, 64) == 0
+    assert lib.kv_prefill_attn_shared(None, None, None, None, None, None, None, 16, 1, 1, 16, None, None, None) == 1
+
+
 def test_missing_library_fails_loudly(monkeypatch, tmp_path):
     monkeypatch.setattr(_capi, "LIB_PATH", tmp_path / "nope.so")
     monkeypatch.setattr(_capi, "_lib", None)
