@@ -87,7 +87,11 @@ typedef struct {
     uint32_t n_pages;      /* physical pages in the pool */
     float rope_theta;      /* e.g. 1e6 (crates/llm-core/src/config.rs:508) */
     int32_t max_positions; /* RoPE table length: positions 0 .. max_positions-1 */
-    int32_t max_seqs;      /* most sequences one attention call may carry */
+    int32_t max_seqs;      /* most sequences one attention call may carry; the decode
+                              kernel keeps a per-sequence table in shared memory, so
+                              kv_pool_create returns KV_ERR_INVALID past roughly
+                              1800-2200 (bf16) or 840-1190 (quantised pools),
+                              depending on the head layout */
     int32_t device;        /* CUDA device ordinal */
 } kv_pool_config;
 
