@@ -89,9 +89,11 @@ typedef struct {
     int32_t max_positions; /* RoPE table length: positions 0 .. max_positions-1 */
     int32_t max_seqs;      /* most sequences one attention call may carry; the decode
                               kernel keeps a per-sequence table in shared memory, so
-                              kv_pool_create returns KV_ERR_INVALID past roughly
-                              1800-2200 (bf16) or 840-1190 (quantised pools),
-                              depending on the head layout */
+                              kv_pool_create returns KV_ERR_INVALID past a limit set
+                              by the dtype and head layout: with 8 kv heads (group 4
+                              to group 3) 1875-2219 for bf16, 851-1195 for Q8,
+                              4947-5291 for K8V4, over 15000 for fp32 pools; higher
+                              with fewer kv heads */
     int32_t device;        /* CUDA device ordinal */
 } kv_pool_config;
 
