@@ -16,6 +16,7 @@ pub const KV_DTYPE_F32: i32 = 0;
 pub const KV_DTYPE_BF16: i32 = 1;
 pub const KV_DTYPE_Q8: i32 = 2;
 pub const KV_DTYPE_K8V4: i32 = 3;
+pub const KV_DTYPE_F16: i32 = 4;
 
 pub const KV_OK: i32 = 0;
 pub const KV_ERR_INVALID: i32 = 1;

@@ -140,13 +140,15 @@ fn check_seq(status: i32, seq_id: u64, bad_index: i64, tree: Option<&ffi::kv_tre
 }
 
 /// KV storage type (the reference's `KvDtype` tags F16/Q8/K8V4 and implements
-/// none; `Q8` and `K8V4` here use llm-quant's Q8_0 / Q4 block formats).
+/// none; `F16` here stores IEEE half, `Q8` and `K8V4` use llm-quant's Q8_0 /
+/// Q4 block formats).  `llm_quant::KvDtype::F16` maps to `F16`.
 #[derive(Clone, Copy, Debug, PartialEq, Eq)]
 pub enum KvDtype {
     F32,
     Bf16,
     Q8,
     K8V4,
+    F16,
 }
 
 /// Shape and size of a pool (`kv_pool_config`).
@@ -170,6 +172,7 @@ impl PoolConfig {
                 KvDtype::Bf16 => ffi::KV_DTYPE_BF16,
                 KvDtype::Q8 => ffi::KV_DTYPE_Q8,
                 KvDtype::K8V4 => ffi::KV_DTYPE_K8V4,
+                KvDtype::F16 => ffi::KV_DTYPE_F16,
             },
             n_q_heads: self.n_q_heads,
             n_kv_heads: self.n_kv_heads,

@@ -42,8 +42,16 @@ extern "C" {
 #define KV_PAGE_NONE 0xFFFFFFFFu /* block-table entry of an evicted / absent page */
 
 /* KV storage type.  The reference's KvDtype (crates/llm-quant/src/formats.rs:59-68)
- * tags F16/Q8/K8V4 and implements none.  This library stores F32, BF16 and
- * the two quantised tags, with the block quantisers of the same crate
+ * tags F16/Q8/K8V4 and implements none.  This library stores F32, BF16, F16
+ * and the two quantised tags.
+ *   KV_DTYPE_F16   K and V as IEEE half (the reference's default tag, "full
+ *                  f16 keys and values") in the bf16 page layout; the appended
+ *                  k / v, q and out are bf16 (K rotated in fp32, then K and V
+ *                  rounded to half, to nearest even).  Every entry point but
+ *                  kv_prefill_attn_shared and kv_decode_attn_noalloc; decode
+ *                  runs on the tensor cores with f16 operands, prefill on the
+ *                  CUDA cores in fp32.
+ * The quantised tags use the block quantisers of the same crate
  * (crates/llm-quant/src/lib.rs:14-101, 32 elements and one f16 scale per
  * block, two blocks per 64-dim head row):
  *   KV_DTYPE_Q8    K and V as Q8_0 blocks (int8 codes, scale max|x| / 127)
@@ -59,7 +67,7 @@ extern "C" {
  * values in fp32), kv_norm_append_decode_attn (the k norm in the append
  * launch, the q norm in the attention launch), page copies and token moves;
  * kv_prefill_attn_shared returns KV_ERR_UNSUPPORTED for them. */
-typedef enum { KV_DTYPE_F32 = 0, KV_DTYPE_BF16 = 1, KV_DTYPE_Q8 = 2, KV_DTYPE_K8V4 = 3 } kv_dtype;
+typedef enum { KV_DTYPE_F32 = 0, KV_DTYPE_BF16 = 1, KV_DTYPE_Q8 = 2, KV_DTYPE_K8V4 = 3, KV_DTYPE_F16 = 4 } kv_dtype;
 
 typedef enum {
     KV_OK = 0,
@@ -91,7 +99,7 @@ typedef struct {
                               kernel keeps a per-sequence table in shared memory, so
                               kv_pool_create returns KV_ERR_INVALID past a limit set
                               by the dtype and head layout: with 8 kv heads (group 4
-                              to group 3) 1875-2219 for bf16, 851-1195 for Q8,
+                              to group 3) 1875-2219 for bf16 and f16, 851-1195 for Q8,
                               4947-5291 for K8V4, over 15000 for fp32 pools; higher
                               with fewer kv heads */
     int32_t device;        /* CUDA device ordinal */

@@ -16,6 +16,7 @@ KV_DTYPE_F32 = 0
 KV_DTYPE_BF16 = 1
 KV_DTYPE_Q8 = 2    # K and V as Q8_0 blocks
 KV_DTYPE_K8V4 = 3  # K as Q8_0, V as Q4 blocks
+KV_DTYPE_F16 = 4   # K and V as IEEE half; bf16 k, v, q and out
 KV_PAGE_NONE = 0xFFFFFFFF
 
 STATUS = {

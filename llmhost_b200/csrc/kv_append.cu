@@ -7,12 +7,14 @@
 // k'[d] = k[d]*cos + k[d-32]*sin, each as two rounded products and a rounded
 // sum (Rust does not contract to FMA).  cos/sin come from the pool's table,
 // computed with the same libm calls as rope.rs:30-41, so the stored K is
-// bit-identical to the CPU path's (after bf16 rounding to nearest even).
+// bit-identical to the CPU path's (after bf16 or f16 rounding to nearest even).
 //
 // Thread mapping: 4 threads per (token, kv head); thread qd owns dims
 // [8qd, 8qd+8) and their rotation partners [8qd+32, 8qd+40), so the four
 // threads of a head write its 128-byte (bf16) row as 16-byte stores.
 #include <cuda_fp16.h>
+
+#include <type_traits>
 
 #include "kv_common.cuh"
 #include "kv_pool_impl.h"
@@ -65,6 +67,12 @@ __device__ __forceinline__ void store8(__nv_bfloat16* p, const float (&x)[8]) {
     u.w = float2_to_bf16x2(x[6], x[7]);
     *reinterpret_cast<uint4*>(p) = u;
 }
+__device__ __forceinline__ void store8(__half* p, const float (&x)[8]) {
+    __half2 h[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) h[i] = __floats2half2_rn(x[2 * i], x[2 * i + 1]);  // low half: x[2i]
+    *reinterpret_cast<uint4*>(p) = *reinterpret_cast<const uint4*>(h);
+}
 __device__ __forceinline__ void store8(float* p, const float (&x)[8]) {
     reinterpret_cast<float4*>(p)[0] = make_float4(x[0], x[1], x[2], x[3]);
     reinterpret_cast<float4*>(p)[1] = make_float4(x[4], x[5], x[6], x[7]);
@@ -79,8 +87,11 @@ __device__ __forceinline__ void copy8(float* dst, const float* src) {
     reinterpret_cast<float4*>(dst)[1] = __ldg(reinterpret_cast<const float4*>(src) + 1);
 }
 
-template <typename T>
-__global__ void __launch_bounds__(256) append_kernel(T* __restrict__ pages, const AppendArgs a) {
+// S: the page element (bf16, fp32, or IEEE half for KV_DTYPE_F16); I: the
+// appended k / v element (S, or bf16 for half pages, whose V is then widened
+// and rounded to half rather than copied).
+template <typename S, typename I = S>
+__global__ void __launch_bounds__(256) append_kernel(S* __restrict__ pages, const AppendArgs a) {
     const long long gtid = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
     const int per_tok = a.nkv * 4;
     const long long tok = gtid / per_tok;
@@ -113,11 +124,11 @@ __global__ void __launch_bounds__(256) append_kernel(T* __restrict__ pages, cons
     }
     const int j = slot % kPageTokens;
     const size_t page_elems = static_cast<size_t>(2) * a.nkv * kPageTokens * kHeadDim;
-    T* kdst = pages + page * page_elems + (static_cast<size_t>(h) * kPageTokens + j) * kHeadDim;
-    T* vdst = pages + page * page_elems +
+    S* kdst = pages + page * page_elems + (static_cast<size_t>(h) * kPageTokens + j) * kHeadDim;
+    S* vdst = pages + page * page_elems +
               (static_cast<size_t>(a.nkv + h) * kPageTokens + j) * kHeadDim;
-    const T* ksrc = static_cast<const T*>(a.k) + (tok * a.nkv + h) * kHeadDim;
-    const T* vsrc = static_cast<const T*>(a.v) + (tok * a.nkv + h) * kHeadDim;
+    const I* ksrc = static_cast<const I*>(a.k) + (tok * a.nkv + h) * kHeadDim;
+    const I* vsrc = static_cast<const I*>(a.v) + (tok * a.nkv + h) * kHeadDim;
 
     float x[8], y[8], xo[8], yo[8];
     load8(ksrc + 8 * qd, x);
@@ -131,8 +142,15 @@ __global__ void __launch_bounds__(256) append_kernel(T* __restrict__ pages, cons
     }
     store8(kdst + 8 * qd, xo);
     store8(kdst + 8 * qd + 32, yo);
-    copy8(vdst + 8 * qd, vsrc + 8 * qd);
-    copy8(vdst + 8 * qd + 32, vsrc + 8 * qd + 32);
+    if constexpr (std::is_same_v<S, I>) {
+        copy8(vdst + 8 * qd, vsrc + 8 * qd);
+        copy8(vdst + 8 * qd + 32, vsrc + 8 * qd + 32);
+    } else {
+        load8(vsrc + 8 * qd, x);
+        load8(vsrc + 8 * qd + 32, y);
+        store8(vdst + 8 * qd, x);
+        store8(vdst + 8 * qd + 32, y);
+    }
 }
 
 // ---- quantised pools (KV_DTYPE_Q8, KV_DTYPE_K8V4) ---------------------------
@@ -283,7 +301,7 @@ int launch_append(kv_pool* pool, const void* k, const void* v, const int32_t* to
                   const int32_t* tok_slot, const int32_t* tok_pos, const int32_t* seq_lens,
                   int32_t n_tokens, int32_t n_seqs, const uint32_t* bt, int32_t bt_stride,
                   cudaStream_t stream, const float* k_norm, float eps) {
-    if (k_norm && !is_quant(pool->cfg.dtype)) return KV_ERR_UNSUPPORTED;  // bf16 / fp32 fold it into the decode
+    if (k_norm && !is_quant(pool->cfg.dtype)) return KV_ERR_UNSUPPORTED;  // bf16 / f16 / fp32 fold it into the decode
     AppendArgs a;
     a.k = k;
     a.v = v;
@@ -308,6 +326,8 @@ int launch_append(kv_pool* pool, const void* k, const void* v, const int32_t* to
     if (pool->cfg.dtype == KV_DTYPE_BF16)
         append_kernel<__nv_bfloat16><<<grid, block, 0, stream>>>(
             static_cast<__nv_bfloat16*>(pool->pages), a);
+    else if (pool->cfg.dtype == KV_DTYPE_F16)
+        append_kernel<__half, __nv_bfloat16><<<grid, block, 0, stream>>>(static_cast<__half*>(pool->pages), a);
     else if (pool->cfg.dtype == KV_DTYPE_Q8)
         append_q_kernel<false><<<grid, block, 0, stream>>>(static_cast<uint8_t*>(pool->pages), a);
     else if (pool->cfg.dtype == KV_DTYPE_K8V4)

@@ -904,7 +904,7 @@ int raise_smem_limit(const void* fn, int device, size_t bytes) {
 
 int decode_setup(kv_pool* pool) {
     const auto& c = pool->cfg;
-    if (c.dtype == KV_DTYPE_BF16 || is_quant(c.dtype)) return decode_tc_setup(pool);
+    if (is_half_page(c.dtype) || is_quant(c.dtype)) return decode_tc_setup(pool);
     const DecodeVariant* v = find_variant(c.dtype, c.n_kv_heads, c.n_q_heads / c.n_kv_heads);
     if (!v) return KV_ERR_UNSUPPORTED;
     const size_t smem = v->smem(c.max_seqs);
@@ -923,7 +923,7 @@ int decode_setup(kv_pool* pool) {
     return KV_OK;
 }
 
-// Partial rows: two per CTA; the tensor-core kernel (bf16 pools) keeps two
+// Partial rows: two per CTA; the tensor-core kernel (bf16, f16 and quantised pools) keeps two
 // more per CTA for the run partials of a long sequence's two-level merge.
 size_t decode_workspace_slots(const kv_pool* pool) {
     return (pool->cfg.dtype == KV_DTYPE_F32 ? 2 : 4) * static_cast<size_t>(pool->decode_grid);
@@ -939,7 +939,7 @@ int launch_decode(kv_pool* pool, const void* q, const uint32_t* bt, int32_t bt_s
                   cudaStream_t stream, const void* new_k, const void* new_v, const float* q_norm,
                   const float* k_norm, float eps) {
     const auto& c = pool->cfg;
-    if (c.dtype == KV_DTYPE_BF16)
+    if (is_half_page(c.dtype))
         return launch_decode_tc(pool, q, bt, bt_stride, seq_lens, n_seqs, window, out, stream, new_k, new_v, q_norm,
                                 k_norm, eps);
     if (is_quant(c.dtype)) {

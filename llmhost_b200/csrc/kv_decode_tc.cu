@@ -80,7 +80,7 @@ constexpr int kSoftRegsQ = 160;
 constexpr int kConvPages = kUnitPages / kConvWarps;   // pages of a unit per converter warp
 constexpr int kPrefetchStages = 4;                    // L2 prefetch distance of quantised page blocks
 template <int kQ>
-__host__ __device__ constexpr int block_threads() { return kQ ? 512 : kThreads; }
+__host__ __device__ constexpr int block_threads() { return (kQ == 1 || kQ == 2) ? 512 : kThreads; }
 constexpr uint32_t kTmemCols = 256;
 constexpr uint32_t kColS = 0;   // S of buffer sb, unit u: columns kColS + 32 sb + 16 u ..
 constexpr uint32_t kColO = 64;  // O of segment buffer e, accumulator c: kColO + 64 e + 16 c; unit u's queries at + 8 u
@@ -117,8 +117,12 @@ struct TcArgs {
     float eps;
 };
 
+// kQ: the page storage.  0 bf16 and 3 IEEE half (TMA boxes straight into the
+// tile ring); 1 Q8 and 2 K8V4 (codes copied raw and converted in the CTA).
+// Every kQ but 0 runs the MMAs on f16 operands.
 template <int NKV, int G, int kQ = 0>
 struct TcShape {
+    static constexpr bool kConv = kQ == 1 || kQ == 2;
     static_assert(G >= 1 && G <= 4, "query heads per kv head");
     static_assert(NKV == 1 || NKV == 2 || NKV == 4 || NKV == 8, "kv heads");
     static constexpr int NQ = NKV * G;
@@ -127,11 +131,11 @@ struct TcShape {
     // Tile ring: three stages for bf16 pools; two for quantised pools, which
     // also keep two stages of raw page blocks (8 pages x 2 units) that the
     // converter warps expand into the tiles.
-    static constexpr int kRing = kQ ? 2 : kStagesBf16;
-    static constexpr int kHeadBlock = kQ ? kPageTokens * (kHeadDim + (kQ == 2 ? 32 : 64) + 8) : 0;
+    static constexpr int kRing = kConv ? 2 : kStagesBf16;
+    static constexpr int kHeadBlock = kConv ? kPageTokens * (kHeadDim + (kQ == 2 ? 32 : 64) + 8) : 0;
     static constexpr int kRawStage = 2 * kUnitPages * kHeadBlock;
     static constexpr int kOffRaw = kRing * kStageBytes;
-    static constexpr int kOffQ = kOffRaw + (kQ ? kRing * kRawStage : 0);  // Q tiles: head h at + 1024 h (8 rows)
+    static constexpr int kOffQ = kOffRaw + (kConv ? kRing * kRawStage : 0);  // Q tiles: head h at + 1024 h (8 rows)
     static constexpr int kOffP = kOffQ + (NKV + 1) * 1024;          // P, two buffers
     static constexpr int kOffStg = kOffP + 2 * kPBytes;             // fused append inputs
     static constexpr int kStgBytes = NKV * 256 + 256;               // per head K row, V row; RoPE row
@@ -394,6 +398,8 @@ __global__ void __launch_bounds__(block_threads<kQ>(), 1) decode_tc_kernel(const
                                                                            const TcArgs a) {
     constexpr int kNT = block_threads<kQ>();
     using Sh = TcShape<NKV, G, kQ>;
+    constexpr bool kConv = Sh::kConv;  // quantised pages: converter warps
+    constexpr bool kF16 = kQ != 0;     // f16 MMA operands (Q, P and the K / V tiles)
     constexpr int kRing = Sh::kRing;
     constexpr int NQ = Sh::NQ;
     constexpr int kPairs = Sh::kPairs;
@@ -439,7 +445,7 @@ __global__ void __launch_bounds__(block_threads<kQ>(), 1) decode_tc_kernel(const
     if (warp == kProducerWarp) {
         if (lane == 0) {
             for (int i = 0; i < kRing; ++i) {
-                mbar_init(&full[i], kQ ? kConvWarps * 32 : 1);  // TMA arrival, or every converter thread
+                mbar_init(&full[i], kConv ? kConvWarps * 32 : 1);  // TMA arrival, or every converter thread
                 mbar_init(&rfull[i], 1);
                 mbar_init(&rempty[i], kConvWarps * 32);
                 mbar_init(&empty[i], 1);
@@ -459,7 +465,7 @@ __global__ void __launch_bounds__(block_threads<kQ>(), 1) decode_tc_kernel(const
             }
             *abort_flag = 0;
             fence_mbar_init();
-            if constexpr (kQ == 0) prefetch_tmap(&hmap);
+            if constexpr (!kConv) prefetch_tmap(&hmap);
         }
         grid_dep_wait();  // the inputs are read from here on
         __syncwarp();
@@ -544,7 +550,7 @@ __global__ void __launch_bounds__(block_threads<kQ>(), 1) decode_tc_kernel(const
         };
         // k RMSNorm weights of this lane's dims (2 ii, 2 ii + 1, 32 + 2 ii, 33 + 2 ii)
         float2 kwx = make_float2(1.f, 1.f), kwy = make_float2(1.f, 1.f);
-        if constexpr (kNorm && kQ == 0) {  // quantised pools normalise k in their append launch (no k_norm here)
+        if constexpr (kNorm && !kConv) {  // quantised pools normalise k in their append launch (no k_norm here)
             kwx = __ldg(reinterpret_cast<const float2*>(a.k_norm) + (lane & 15));
             kwy = __ldg(reinterpret_cast<const float2*>(a.k_norm + 32) + (lane & 15));
         }
@@ -566,7 +572,7 @@ __global__ void __launch_bounds__(block_threads<kQ>(), 1) decode_tc_kernel(const
                 hpf = NKV >= 2 ? 2 * pp + u : 0;
             }
         };
-        if constexpr (kQ != 0) {
+        if constexpr (kConv) {
             for (int d = 0; d < kPrefetchStages && !pfc.done; ++d) pfc.next(a, pstart);
             fetch_pf();
         }
@@ -617,7 +623,7 @@ __global__ void __launch_bounds__(block_threads<kQ>(), 1) decode_tc_kernel(const
             if (issuing) {
                 bool ok = true;
                 if (lane == 0 && i >= kRing)
-                    ok = wait_bar(kQ ? &rempty[st] : &empty[st], static_cast<uint32_t>(i / kRing - 1) & 1u, abort_flag,
+                    ok = wait_bar(kConv ? &rempty[st] : &empty[st], static_cast<uint32_t>(i / kRing - 1) & 1u, abort_flag,
                                   a.err);
                 issuing = __shfl_sync(kAll, ok, 0);
             }
@@ -659,11 +665,18 @@ __global__ void __launch_bounds__(block_threads<kQ>(), 1) decode_tc_kernel(const
                                 const float y0 = __fadd_rn(__fmul_rn(y.x, c.x), __fmul_rn(x.x, c.y));
                                 const float y1 = __fadd_rn(__fmul_rn(y.y, c.z), __fmul_rn(x.y, c.w));
                                 uint8_t* row = gpage + (h * kPageTokens + jslot) * 128;
-                                *reinterpret_cast<uint32_t*>(row + 4 * ii) = float2_to_bf16x2(x0, x1);
-                                *reinterpret_cast<uint32_t*>(row + 64 + 4 * ii) = float2_to_bf16x2(y0, y1);
+                                *reinterpret_cast<uint32_t*>(row + 4 * ii) = pack_ab<kF16>(x0, x1);
+                                *reinterpret_cast<uint32_t*>(row + 64 + 4 * ii) = pack_ab<kF16>(y0, y1);
                             } else {
                                 uint8_t* row = gpage + ((NKV + h) * kPageTokens + jslot) * 128;
-                                *reinterpret_cast<uint2*>(row + 8 * ii) = *reinterpret_cast<const uint2*>(in + 128 + 8 * ii);
+                                const uint2 vb = *reinterpret_cast<const uint2*>(in + 128 + 8 * ii);
+                                if constexpr (kF16) {  // half pages: bf16 V widened and rounded to half
+                                    const float2 v0 = bf16x2_to_float2(vb.x), v1 = bf16x2_to_float2(vb.y);
+                                    *reinterpret_cast<uint2*>(row + 8 * ii) =
+                                        make_uint2(pack_ab<true>(v0.x, v0.y), pack_ab<true>(v1.x, v1.y));
+                                } else {
+                                    *reinterpret_cast<uint2*>(row + 8 * ii) = vb;
+                                }
                             }
                         }
                         asm volatile("fence.proxy.async.global;" ::: "memory");
@@ -671,7 +684,7 @@ __global__ void __launch_bounds__(block_threads<kQ>(), 1) decode_tc_kernel(const
                     __syncwarp();
                 }
                 const int hu = NKV >= 2 ? 2 * p + u : 0;
-                if constexpr (kQ == 0) {
+                if constexpr (!kConv) {
                     if (lane == 0) mbar_arrive_expect_tx(&full[st], kStageBytes);
                     __syncwarp();
                     int row = total_rows;  // out of range: zero fill
@@ -725,7 +738,7 @@ __global__ void __launch_bounds__(block_threads<kQ>(), 1) decode_tc_kernel(const
         if (lane == 0) {
             for (int st = 0; st < kRing && st < issued; ++st) {
                 const int last = st + ((issued - 1 - st) / kRing) * kRing;
-                mbar_wait(kQ ? &rfull[st] : &full[st], static_cast<uint32_t>(last / kRing) & 1u);
+                mbar_wait(kConv ? &rfull[st] : &full[st], static_cast<uint32_t>(last / kRing) & 1u);
             }
         }
     } else if (warp == kMmaWarp) {
@@ -736,8 +749,8 @@ __global__ void __launch_bounds__(block_threads<kQ>(), 1) decode_tc_kernel(const
         // its stage back to the producer) never queues behind the next
         // stage's copy.  PV(pi) is issued only after S(pi).
         if (lane == 0) {
-            constexpr uint32_t kIdS = instr_desc(16, 128, false, false, kQ != 0);
-            constexpr uint32_t kIdPV = instr_desc(16, 128, false, true, kQ != 0);
+            constexpr uint32_t kIdS = instr_desc(16, 128, false, false, kF16);
+            constexpr uint32_t kIdPV = instr_desc(16, 128, false, true, kF16);
             const uint32_t st_addr = smem_addr(base), q_addr = smem_addr(base + Sh::kOffQ);
             const uint32_t p_addr = smem_addr(base + Sh::kOffP);
             StageCursor<NKV> sc, pc;
@@ -810,7 +823,7 @@ __global__ void __launch_bounds__(block_threads<kQ>(), 1) decode_tc_kernel(const
     } else if (warp < kProducerWarp) {
         // ---------------- softmax and Q tiles (warps 0-3) ----------------
         // (quantised pools: with the registers the converter warpgroup gives up)
-        if constexpr (kQ != 0) asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kSoftRegsQ));
+        if constexpr (kConv) asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kSoftRegsQ));
         const int t = threadIdx.x;
         const uint32_t lane_base = tmem + (static_cast<uint32_t>(32 * warp) << 16);
         const int kp = t >> 4, slot = t & 15;  // page of the block and slot of this thread's key
@@ -874,8 +887,8 @@ __global__ void __launch_bounds__(block_threads<kQ>(), 1) decode_tc_kernel(const
                     const float a1 = __fadd_rn(__fmul_rn(x.y, c1.x), __fmul_rn(-y.y, c1.y)) * a.qscale;
                     const float b0 = __fadd_rn(__fmul_rn(y.x, c0.x), __fmul_rn(x.x, c0.y)) * a.qscale;
                     const float b1 = __fadd_rn(__fmul_rn(y.y, c1.x), __fmul_rn(x.y, c1.y)) * a.qscale;
-                    lo[e] = pack_ab<kQ != 0>(a0, a1);
-                    hi[e] = pack_ab<kQ != 0>(b0, b1);
+                    lo[e] = pack_ab<kF16>(a0, a1);
+                    hi[e] = pack_ab<kF16>(b0, b1);
                 }
                 uint8_t* row = base + Sh::kOffQ + h * 1024 + n_ * 128;
                 *reinterpret_cast<uint4*>(row + ((c ^ n_) << 4)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
@@ -1019,8 +1032,8 @@ __global__ void __launch_bounds__(block_threads<kQ>(), 1) decode_tc_kernel(const
 #pragma unroll
                     for (int c = 0; c < G; ++c) {
                         float r0, r1;
-                        const unsigned short p0 = round_ab<kQ != 0>(v0 ? ex2f(s0[c] - m[h0][c]) : 0.f, r0);
-                        const unsigned short p1 = round_ab<kQ != 0>(v1 ? ex2f(s1[c] - m[h1][c]) : 0.f, r1);
+                        const unsigned short p0 = round_ab<kF16>(v0 ? ex2f(s0[c] - m[h0][c]) : 0.f, r0);
+                        const unsigned short p1 = round_ab<kF16>(v1 ? ex2f(s1[c] - m[h1][c]) : 0.f, r1);
                         l[h0][c] += r0;
                         l[h1][c] += r1;
                         *reinterpret_cast<unsigned short*>(prow + c * 128 + ((chunk ^ c) << 4) + within) = p0;
@@ -1067,7 +1080,7 @@ __global__ void __launch_bounds__(block_threads<kQ>(), 1) decode_tc_kernel(const
             ++segk;
             if (!more) break;
         }
-    } else if (kQ != 0 && warp >= kConvWarp0) {
+    } else if (kConv && warp >= kConvWarp0) {
         // ---------------- converters (quantised pools, warps 12-15) ----------------
         // Warp w expands pages [w P, w P + P) (P = kConvPages) of both units
         // of a stage from its raw slot (head blocks the producer copied) into
@@ -1076,7 +1089,7 @@ __global__ void __launch_bounds__(block_threads<kQ>(), 1) decode_tc_kernel(const
         // as four 16-byte chunks of f16 in the 128-byte-swizzled tile row
         // (the layout the TMA boxes give bf16 pools).  A page not loaded
         // (past the block's end, or a bad id) is written as zeros.
-        if constexpr (kQ != 0) {
+        if constexpr (kConv) {
             asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kConvRegs));
             constexpr int kVRow = kQ == 2 ? 32 : 64;
             constexpr int kHB = Sh::kHeadBlock;
@@ -1365,9 +1378,12 @@ struct TcVariant {
     const void* fn_k8v4;  // KV_DTYPE_K8V4 pages
     const void* fn_q8_norm;  // the same with the q RMSNorm
     const void* fn_k8v4_norm;
+    const void* fn_f16;       // KV_DTYPE_F16 pages (TMA, f16 operands)
+    const void* fn_f16_norm;
     size_t (*smem)(int);  // dynamic shared memory of each, by max_seqs
     size_t (*smem_q8)(int);
     size_t (*smem_k8v4)(int);
+    size_t (*smem_f16)(int);
 };
 
 template <int NKV, int G>
@@ -1380,8 +1396,10 @@ TcVariant make_tc_variant() {
                      reinterpret_cast<const void*>(&decode_tc_kernel<NKV, G, false, 2>),
                      reinterpret_cast<const void*>(&decode_tc_kernel<NKV, G, true, 1>),
                      reinterpret_cast<const void*>(&decode_tc_kernel<NKV, G, true, 2>),
+                     reinterpret_cast<const void*>(&decode_tc_kernel<NKV, G, false, 3>),
+                     reinterpret_cast<const void*>(&decode_tc_kernel<NKV, G, true, 3>),
                      &TcShape<NKV, G, 0>::smem_bytes, &TcShape<NKV, G, 1>::smem_bytes,
-                     &TcShape<NKV, G, 2>::smem_bytes};
+                     &TcShape<NKV, G, 2>::smem_bytes, &TcShape<NKV, G, 3>::smem_bytes};
 }
 
 const TcVariant* find_tc_variant(int nkv, int group) {
@@ -1394,10 +1412,11 @@ const TcVariant* find_tc_variant(int nkv, int group) {
     return nullptr;
 }
 
-// The kernel for a pool's storage type (and the norm form for bf16 pools).
+// The kernel for a pool's storage type, plain or with the q/k RMSNorm.
 const void* tc_kernel_for(const TcVariant* v, int dtype, bool norm) {
     if (dtype == KV_DTYPE_Q8) return norm ? v->fn_q8_norm : v->fn_q8;
     if (dtype == KV_DTYPE_K8V4) return norm ? v->fn_k8v4_norm : v->fn_k8v4;
+    if (dtype == KV_DTYPE_F16) return norm ? v->fn_f16_norm : v->fn_f16;
     return norm ? v->fn_norm : v->fn;
 }
 
@@ -1409,7 +1428,10 @@ int decode_tc_setup(kv_pool* pool) {
     const auto& c = pool->cfg;
     const TcVariant* v = find_tc_variant(c.n_kv_heads, c.n_q_heads / c.n_kv_heads);
     if (!v) return KV_ERR_UNSUPPORTED;
-    const size_t smem = (c.dtype == KV_DTYPE_Q8 ? v->smem_q8 : c.dtype == KV_DTYPE_K8V4 ? v->smem_k8v4 : v->smem)(c.max_seqs);
+    const size_t smem = (c.dtype == KV_DTYPE_Q8     ? v->smem_q8
+                         : c.dtype == KV_DTYPE_K8V4 ? v->smem_k8v4
+                         : c.dtype == KV_DTYPE_F16  ? v->smem_f16
+                                                    : v->smem)(c.max_seqs);
     int optin = 0;
     if (cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, c.device) != cudaSuccess)
         return KV_ERR_CUDA;

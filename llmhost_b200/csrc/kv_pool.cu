@@ -36,7 +36,8 @@ struct DeviceScope {
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 bool valid_config(const kv_pool_config& c) {
-    if (c.dtype != KV_DTYPE_F32 && c.dtype != KV_DTYPE_BF16 && c.dtype != KV_DTYPE_Q8 && c.dtype != KV_DTYPE_K8V4)
+    if (c.dtype != KV_DTYPE_F32 && c.dtype != KV_DTYPE_BF16 && c.dtype != KV_DTYPE_Q8 && c.dtype != KV_DTYPE_K8V4 &&
+        c.dtype != KV_DTYPE_F16)
         return false;
     if (c.head_dim != kvb200::kHeadDim || c.page_tokens != kvb200::kPageTokens) return false;
     if (c.n_kv_heads != 1 && c.n_kv_heads != 2 && c.n_kv_heads != 4 && c.n_kv_heads != 8) return false;
@@ -91,7 +92,8 @@ int encode_row_map(kv_pool* p, CUtensorMap* map, cuuint32_t box_rows) {
     const cuuint64_t gstride[1] = {128};
     const cuuint32_t box[2] = {static_cast<cuuint32_t>(row_elems), box_rows};
     const cuuint32_t estride[2] = {1, 1};
-    const CUtensorMapDataType dt = p->cfg.dtype == KV_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+    const CUtensorMapDataType dt = p->cfg.dtype == KV_DTYPE_BF16  ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                   : p->cfg.dtype == KV_DTYPE_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
                                                                   : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
     const CUresult r = encode(map, dt, 2, p->pages, gdim, gstride, box, estride,
                               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -163,7 +165,7 @@ int kv_pool_create(const kv_pool_config* cfg, kv_pool** out) {
     kv_pool* p = new (std::nothrow) kv_pool();
     if (!p) return KV_ERR_OOM;
     p->cfg = *cfg;
-    p->elem_bytes = cfg->dtype == KV_DTYPE_F32 ? 4 : 2;  // quantised pools take bf16 k, v, q, out
+    p->elem_bytes = cfg->dtype == KV_DTYPE_F32 ? 4 : 2;  // f16 and quantised pools take bf16 k, v, q, out
     p->page_bytes = kvb200::is_quant(cfg->dtype)
                         ? kvb200::quant_page_bytes(cfg->dtype, cfg->n_kv_heads)
                         : 2ull * cfg->n_kv_heads * cfg->page_tokens * cfg->head_dim * p->elem_bytes;

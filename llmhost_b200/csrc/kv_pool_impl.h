@@ -36,6 +36,8 @@ namespace kvb200 {
 // V.  A page is n_kv head blocks: K codes [16][64], V codes [16][vrow],
 // scales [16 tokens][2 blocks][K, V].
 inline bool is_quant(int dtype) { return dtype == KV_DTYPE_Q8 || dtype == KV_DTYPE_K8V4; }
+// 16-bit float pages (bf16 or IEEE half) in the bf16 page layout.
+inline bool is_half_page(int dtype) { return dtype == KV_DTYPE_BF16 || dtype == KV_DTYPE_F16; }
 inline int quant_vrow(int dtype) { return dtype == KV_DTYPE_Q8 ? 64 : 32; }
 inline size_t quant_head_block(int dtype) { return static_cast<size_t>(16) * (64 + quant_vrow(dtype) + 8); }
 inline size_t quant_page_bytes(int dtype, int nkv) { return static_cast<size_t>(nkv) * quant_head_block(dtype); }

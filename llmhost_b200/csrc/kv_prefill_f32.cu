@@ -7,9 +7,10 @@
 // 1e-5 relative bound of attention_forward (crates/llm-engine/src/lfm2.rs:
 // 1058-1111).
 //
-// Quantised pools (KV_DTYPE_Q8, KV_DTYPE_K8V4) run the same kernel: their
-// pages are dequantised into the fp32 staging (code x f16 block scale, exact
-// in fp32) and their q and out are bf16.
+// Quantised pools (KV_DTYPE_Q8, KV_DTYPE_K8V4) and half pools (KV_DTYPE_F16)
+// run the same kernel: their pages are widened into the fp32 staging (code x
+// f16 block scale, or the half value; both exact in fp32) and their q and out
+// are bf16.
 //
 // One CTA (8 warps) per (sequence, kv head, kTokens query tokens); a row is a
 // (token, query head of the group) pair, up to 32 rows per CTA.  Per page of
@@ -63,7 +64,7 @@ struct Stage {
     float v[kPageTokens * kHeadDim];
 };
 
-// kQ: 0 fp32 pages; 1 Q8, 2 K8V4 pages (bf16 q and out)
+// kQ: 0 fp32 pages; 1 Q8, 2 K8V4, 3 IEEE-half pages (bf16 q and out)
 template <int kQ>
 __global__ void __launch_bounds__(kWarps * 32) prefill_f32_kernel(const PrefillF32Args a) {
     const int s = blockIdx.z, h = blockIdx.y;
@@ -135,6 +136,23 @@ __global__ void __launch_bounds__(kWarps * 32) prefill_f32_kernel(const PrefillF
             kdst[2] = kv.z;
             kdst[3] = kv.w;
             cp_async16(vdst, vb + kk * kHeadDim + 4 * c4);
+        } else if constexpr (kQ == 3) {
+            // half pages in the bf16 layout: K block [nkv][16][64], then V
+            const __half* kb = reinterpret_cast<const __half*>(static_cast<const uint8_t*>(a.pages) +
+                                                               static_cast<size_t>(phys) * a.page_bytes) +
+                               static_cast<size_t>(h) * kPageTokens * kHeadDim;
+            const __half* vb = kb + static_cast<size_t>(a.nkv) * kPageTokens * kHeadDim;
+            const uint2 kw = __ldg(reinterpret_cast<const uint2*>(kb + kk * kHeadDim + 4 * c4));
+            const uint2 vw = __ldg(reinterpret_cast<const uint2*>(vb + kk * kHeadDim + 4 * c4));
+            const float2 k0 = __half22float2(*reinterpret_cast<const __half2*>(&kw.x));
+            const float2 k1 = __half22float2(*reinterpret_cast<const __half2*>(&kw.y));
+            const float2 v0 = __half22float2(*reinterpret_cast<const __half2*>(&vw.x));
+            const float2 v1 = __half22float2(*reinterpret_cast<const __half2*>(&vw.y));
+            kdst[0] = k0.x;
+            kdst[1] = k0.y;
+            kdst[2] = k1.x;
+            kdst[3] = k1.y;
+            *reinterpret_cast<float4*>(vdst) = make_float4(v0.x, v0.y, v1.x, v1.y);
         } else {
             // head block of the page: K codes [16][64], V codes [16][vrow],
             // scales [16][2 blocks][K, V]; dims 4 c4 .. lie in block c4 / 8
@@ -287,6 +305,8 @@ int launch_prefill_f32(kv_pool* pool, const void* q, const int32_t* q_pos, const
         prefill_f32_kernel<1><<<grid, kWarps * 32, 0, stream>>>(a);
     else if (c.dtype == KV_DTYPE_K8V4)
         prefill_f32_kernel<2><<<grid, kWarps * 32, 0, stream>>>(a);
+    else if (c.dtype == KV_DTYPE_F16)
+        prefill_f32_kernel<3><<<grid, kWarps * 32, 0, stream>>>(a);
     else
         prefill_f32_kernel<0><<<grid, kWarps * 32, 0, stream>>>(a);
     return cudaGetLastError() == cudaSuccess ? KV_OK : KV_ERR_CUDA;

@@ -13,12 +13,12 @@ import numpy as np
 import torch
 
 from . import _capi
-from ._capi import KV_DTYPE_BF16, KV_DTYPE_F32, KV_DTYPE_K8V4, KV_DTYPE_Q8, KvPoolConfig, check
+from ._capi import KV_DTYPE_BF16, KV_DTYPE_F16, KV_DTYPE_F32, KV_DTYPE_K8V4, KV_DTYPE_Q8, KvPoolConfig, check
 from .plans import tree_masks  # noqa: F401  (ancestor-or-self masks for prefill_attn)
 
 # The dtype of k, v, q and out: quantised pools take bf16 and store codes.
 _TORCH_DTYPE = {KV_DTYPE_F32: torch.float32, KV_DTYPE_BF16: torch.bfloat16, KV_DTYPE_Q8: torch.bfloat16,
-                KV_DTYPE_K8V4: torch.bfloat16}
+                KV_DTYPE_K8V4: torch.bfloat16, KV_DTYPE_F16: torch.bfloat16}
 
 
 def dtype_code(dtype) -> int:
@@ -30,6 +30,8 @@ def dtype_code(dtype) -> int:
         return KV_DTYPE_Q8
     if dtype in ("k8v4", KV_DTYPE_K8V4):
         return KV_DTYPE_K8V4
+    if dtype in ("f16", KV_DTYPE_F16):  # half pages; k, v, q and out stay bf16
+        return KV_DTYPE_F16
     raise ValueError(f"unsupported KV dtype {dtype!r}")
 
 
@@ -118,10 +120,11 @@ class KvPool:
         check(self.last_error(), "device error word")
 
     def read_pages(self, page_ids) -> np.ndarray:
-        """Pages as a host array [n, page_elems] (bf16 returned as uint16 bits,
-        quantised pages as bytes)."""
+        """Pages as a host array [n, page_elems] (bf16 and f16 returned as
+        uint16 bits, quantised pages as bytes)."""
         ids = np.ascontiguousarray(page_ids, dtype=np.uint32)
-        np_dt = {KV_DTYPE_BF16: np.uint16, KV_DTYPE_F32: np.float32}.get(self.shape.dtype, np.uint8)
+        np_dt = {KV_DTYPE_BF16: np.uint16, KV_DTYPE_F16: np.uint16, KV_DTYPE_F32: np.float32}.get(
+            self.shape.dtype, np.uint8)
         out = np.empty((len(ids), self.shape.page_elems), dtype=np_dt)
         check(self._lib.kv_pool_read_pages(self._h, ids.ctypes.data, len(ids), out.ctypes.data),
               "kv_pool_read_pages")

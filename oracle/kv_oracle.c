@@ -333,13 +333,16 @@ void orc_attention_masked(const float *q, const float *k, const float *v, size_t
 /* ---- paged layout (build-defined) ---------------------------------------- */
 
 static inline float load_elem(const void *base, int dtype, size_t i) {
-    return dtype == ORC_BF16 ? orc_bf16_to_f32(((const uint16_t *)base)[i])
-                             : ((const float *)base)[i];
+    if (dtype == ORC_BF16) return orc_bf16_to_f32(((const uint16_t *)base)[i]);
+    if (dtype == ORC_F16) return orc_f16_to_f32(((const uint16_t *)base)[i]);
+    return ((const float *)base)[i];
 }
 
 static inline void store_elem(void *base, int dtype, size_t i, float x) {
     if (dtype == ORC_BF16)
         ((uint16_t *)base)[i] = orc_f32_to_bf16(x);
+    else if (dtype == ORC_F16)
+        ((uint16_t *)base)[i] = orc_f32_to_f16(x);
     else
         ((float *)base)[i] = x;
 }
@@ -369,11 +372,12 @@ void orc_rms_norm(const float *x, const float *weight, float eps, size_t dim, si
  * [P][64] int8 (Q8) or [P][32] packed nibbles (K8V4), scales [P][2 blocks]
  * [K, V] f16.  Queries, outputs and the appended k/v stay bf16. */
 static inline int is_quant(int dtype) { return dtype == ORC_Q8 || dtype == ORC_K8V4; }
-static inline int io_dtype(int dtype) { return is_quant(dtype) ? ORC_BF16 : dtype; }
+/* Element type of the appended k / v, q and out: bf16 for quantised and half pages. */
+static inline int io_dtype(int dtype) { return (is_quant(dtype) || dtype == ORC_F16) ? ORC_BF16 : dtype; }
 static inline size_t q_vrow(int dtype) { return dtype == ORC_Q8 ? 64 : 32; }
 size_t orc_page_bytes(int dtype, size_t n_kv, size_t P, size_t d) {
     if (is_quant(dtype)) return n_kv * P * (d + q_vrow(dtype) + 8);
-    return 2 * n_kv * P * d * (dtype == ORC_BF16 ? 2 : 4);
+    return 2 * n_kv * P * d * ((dtype == ORC_BF16 || dtype == ORC_F16) ? 2 : 4);
 }
 static inline size_t q_head(size_t P, int dtype, size_t h) { return h * P * (64 + q_vrow(dtype) + 8); }
 static inline size_t q_koff(size_t n_kv, size_t P, int dtype, size_t h, size_t j) {
@@ -456,7 +460,7 @@ static void append_token_impl(void *pages, int dtype, size_t n_kv, size_t P, siz
         size_t vofs = (size_t)page * page_elems + ((n_kv + h) * P + j) * d;
         for (size_t e = 0; e < d; e++) {
             store_elem(pages, dtype, kofs + e, kr[h * d + e]);
-            store_elem(pages, dtype, vofs + e, load_elem(v, dtype, h * d + e));
+            store_elem(pages, dtype, vofs + e, load_elem(v, io_dtype(dtype), h * d + e));
         }
     }
     free(kr);

@@ -33,7 +33,9 @@
 extern "C" {
 #endif
 
-enum { ORC_F32 = 0, ORC_BF16 = 1, ORC_Q8 = 2, ORC_K8V4 = 3 };
+/* Page storage.  ORC_F16: K and V as IEEE half in the bf16 page layout, with
+ * bf16 k / v / q inputs (the library's KV_DTYPE_F16; the reference's tag F16). */
+enum { ORC_F32 = 0, ORC_BF16 = 1, ORC_Q8 = 2, ORC_K8V4 = 3, ORC_F16 = 4 };
 #define ORC_PAGE_NONE 0xFFFFFFFFu
 
 /* bf16 <-> f32, round to nearest even (the build's bf16 storage rule). */

@@ -22,6 +22,7 @@ F32 = 0
 BF16 = 1
 Q8 = 2     # K and V as Q8_0 blocks (crates/llm-quant/src/lib.rs:14-46)
 K8V4 = 3   # K as Q8_0, V as Q4 blocks (lib.rs:48-101)
+F16 = 4    # K and V as IEEE half, bf16 layout; bf16 k / v / q in
 PAGE_NONE = 0xFFFFFFFF
 
 _lib = None
@@ -203,7 +204,7 @@ class HostPages:
             np_dt = np.uint8
         else:
             self.page_elems = 2 * n_kv * page_tokens * head_dim
-            np_dt = np.uint16 if dtype == BF16 else np.float32
+            np_dt = np.uint16 if dtype in (BF16, F16) else np.float32
         if data is None:
             data = np.zeros((n_pages, self.page_elems), np_dt)
         assert data.dtype == np_dt and data.shape == (n_pages, self.page_elems)
@@ -211,7 +212,7 @@ class HostPages:
         self.inv = inv_freq(head_dim, theta)
 
     def _raw(self, a) -> np.ndarray:
-        np_dt = np.uint16 if self.dtype in (BF16, Q8, K8V4) else np.float32
+        np_dt = np.uint16 if self.dtype in (BF16, Q8, K8V4, F16) else np.float32
         a = np.ascontiguousarray(a)
         assert a.dtype == np_dt, (a.dtype, np_dt)
         return a

@@ -32,12 +32,12 @@ def to_numpy_f32(t) -> np.ndarray:
     return t.detach().to(torch.float32).cpu().numpy()
 
 
-ORACLE_DTYPE = {"bf16": O.BF16, "f32": O.F32, "q8": O.Q8, "k8v4": O.K8V4}
+ORACLE_DTYPE = {"bf16": O.BF16, "f32": O.F32, "q8": O.Q8, "k8v4": O.K8V4, "f16": O.F16}
 
 
 class DecodeCase:
     """`dtype` is the k / v / q type; `store` the pool's storage type when it
-    differs (quantised pools "q8" / "k8v4" take bf16 k, v, q)."""
+    differs (half pools "f16" and quantised pools "q8" / "k8v4" take bf16 k, v, q)."""
 
     def __init__(self, dtype: str, n_q: int, n_kv: int, lens, seed: int = 0, window: int = 0,
                  extra_pages: int = 8, evict_below_window: bool = False, store: str | None = None):

@@ -57,11 +57,11 @@ def test_invalid_config_rejected_before_touching_cuda():
     assert h.value is None
 
 
-def test_quantised_dtypes_accepted_by_the_config_check():
-    # Q8 (2) and K8V4 (3) pass the shape check (without a GPU the call then
-    # fails on CUDA), unlike an unknown dtype, which the check rejects
+def test_quantised_and_half_dtypes_accepted_by_the_config_check():
+    # Q8 (2), K8V4 (3) and F16 (4) pass the shape check (without a GPU the
+    # call then fails on CUDA), unlike an unknown dtype, which the check rejects
     lib = _capi.lib()
-    for dt in (_capi.KV_DTYPE_Q8, _capi.KV_DTYPE_K8V4):
+    for dt in (_capi.KV_DTYPE_Q8, _capi.KV_DTYPE_K8V4, _capi.KV_DTYPE_F16):
         h = _capi.c_void_p()
         cfg = _capi.KvPoolConfig(dt, 24, 8, 64, 16, 1024, 1e6, 1024, 64, 0)
         rc = lib.kv_pool_create(cfg, h)

@@ -66,7 +66,7 @@ def _token_layout(lens):
 
 
 # ---- config 2 -----------------------------------------------------------------------
-@pytest.mark.parametrize("store", ["bf16", "q8", "k8v4"])
+@pytest.mark.parametrize("store", ["bf16", "q8", "k8v4", "f16"])
 def test_config2_batched_decode_full_size(cuda, store):
     import torch
     from llmhost_b200.kv import KvPool

@@ -19,14 +19,14 @@ pytestmark = pytest.mark.gpu
 NONE = 0xFFFFFFFF
 
 
-@pytest.mark.parametrize("store", ["bf16", "q8", "k8v4"])
+@pytest.mark.parametrize("store", ["bf16", "q8", "k8v4", "f16"])
 def test_copy_pages_bit_exact(cuda, store):
     import torch
     from llmhost_b200.kv import KvPool
 
     rng = np.random.default_rng(0)
     with KvPool(dtype=store, n_q_heads=24, n_kv_heads=8, n_pages=64, max_positions=64, max_seqs=4) as pool:
-        if store == "bf16":
+        if store in ("bf16", "f16"):  # 16-bit elements, read back as uint16 bits
             data = rng.integers(0, 1 << 16, size=(64, 2 * 8 * 16 * 64), dtype=np.uint16)
         else:
             data = rng.integers(0, 256, size=(64, pool.page_bytes), dtype=np.uint8)
@@ -62,7 +62,7 @@ def _replay_moves(host, moves):
             v[dp, :, ds, :] = v[sp, :, ss, :]
 
 
-@pytest.mark.parametrize("seed,store", [(1, "bf16"), (2, "bf16"), (3, "q8"), (4, "k8v4")])
+@pytest.mark.parametrize("seed,store", [(1, "bf16"), (2, "bf16"), (3, "q8"), (4, "k8v4"), (5, "f16")])
 def test_speculative_round_matches_oracle(cuda, seed, store):
     import torch
     from llmhost_b200.kv import KvPool
