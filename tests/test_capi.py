@@ -81,3 +81,14 @@ def test_missing_library_fails_loudly(monkeypatch, tmp_path):
     monkeypatch.setattr(_capi, "_lib", None)
     with pytest.raises(RuntimeError, match="no CPU fallback"):
         _capi.lib()
+
+
+def test_noalloc_refuses_half_and_quantised_pages_without_gpu():
+    # the allocation-free decode serves fp32 and bf16 pages only; the dtype
+    # is checked before any pointer or device is touched
+    lib = _capi.lib()
+    status = _capi.c_void_p(0)
+    for dt in (_capi.KV_DTYPE_Q8, _capi.KV_DTYPE_K8V4, _capi.KV_DTYPE_F16, 7):
+        rc = lib.kv_decode_attn_noalloc(None, 16, dt, 24, 8, None, 64, None, None, 4, None, 1, 0, None,
+                                        status, None)
+        assert rc == 1  # KV_ERR_INVALID
