@@ -32,6 +32,8 @@ device at most):
   decode_k8v4  tcgen05 decode of the converted tiles; K8V4: 4-bit V): the batched-decode
                configuration's 64 session lengths (U[128, 8192]) and six
                layers' block tables taken in turn, as bench.py does
+  decode_f16   the same sessions on a half (KV_DTYPE_F16) pool: the append
+               fused into the tcgen05 decode, f16 operands
 
 Algorithmic bytes: append reads k, v and writes them (4 n_kv d e per token);
 a page copy reads and writes a page; a token move reads and writes one
@@ -305,16 +307,22 @@ def _decode_quant(d: _Dev, store: str):
     q, k, v = d.bf16((n_seq, n_q, 64)), d.bf16((n_seq, n_kv, 64)), d.bf16((n_seq, n_kv, 64))
     seq_lens = d.i32(lens + 1)
     out = d.torch.empty_like(q)
-    key_bytes = 64 + (64 if store == "q8" else 32) + 8
     n_tok = lens + 1
-    byts = int((n_kv * key_bytes * n_tok + 2 * n_kv * 64 * 2 + 2 * n_q * 64 * 2 + 4 * (-(-n_tok // 16))).sum())
+    if store == "f16":  # half pages: the bf16 byte count (the fused append reads and writes the new row)
+        byts = int((n_kv * 256 * n_tok + 2 * n_kv * 64 * 4 + 2 * n_q * 64 * 2 + 4 * (-(-n_tok // 16))).sum())
+    else:
+        key_bytes = 64 + (64 if store == "q8" else 32) + 8
+        byts = int((n_kv * key_bytes * n_tok + 2 * n_kv * 64 * 2 + 2 * n_q * 64 * 2
+                    + 4 * (-(-n_tok // 16))).sum())
     state = {"i": 0}
 
     def launch():
         pool.append_decode_attn(k, v, q, tables[state["i"] % n_layers], seq_lens, out=out)
         state["i"] += 1
 
-    return pool, launch, {"kernel": f"append_q_kernel + decode_tc_kernel with converter warps ({store} pool)",
+    kernel = ("decode_tc_kernel, append fused, f16 operands (f16 pool)" if store == "f16" else
+              f"append_q_kernel + decode_tc_kernel with converter warps ({store} pool)")
+    return pool, launch, {"kernel": kernel,
                           "bound": "hbm", "bytes": byts, "sessions": n_seq, "keys": int(n_tok.sum()),
                           "layers_in_turn": n_layers, "bf16_equivalent_bytes":
                               int((n_kv * 256 * n_tok + 2 * n_kv * 64 * 4 + 2 * n_q * 64 * 2
@@ -329,10 +337,14 @@ def case_decode_k8v4(d: _Dev):
     return _decode_quant(d, "k8v4")
 
 
+def case_decode_f16(d: _Dev):
+    return _decode_quant(d, "f16")
+
+
 CASES = {"append": case_append, "copy": case_copy, "move": case_move, "decode_f32": case_decode_f32,
          "prefill_f32": case_prefill_f32, "verify": case_verify, "verify_shared": case_verify_shared,
          "decode_q8": case_decode_q8,
-         "decode_k8v4": case_decode_k8v4}
+         "decode_k8v4": case_decode_k8v4, "decode_f16": case_decode_f16}
 
 
 def main() -> None:
